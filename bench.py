@@ -1,0 +1,438 @@
+#!/usr/bin/env python
+"""bench.py — MoE-layer decode throughput of libmoe_cuda on B200.
+
+Workload: one Qwen3-30B-A3B-shaped MoE layer,
+hidden 2048, 128 experts, moe_intermediate 768, top-8, Q8 experts, decode of
+T tokens (default 16; T=1 and T=4 are reported beside it). A "step" is one
+moe_ffn call (router -> top-k -> routed experts -> k-ordered combine +
+residual) on one batch of T tokens. Steps rotate through NL resident layers
+(default 16, 9.7 GB of Q8 experts) and a pool of input batches, so every step
+streams its experts from HBM (a layer's routed experts plus the other layers'
+exceed the 126 MB L2 between two visits of the same layer).
+
+Synthetic data: random-init weights of the real shapes (seeded, see
+moe.cc_b200/synth.py), hidden states ~ N(0,1).
+
+N>1 (torchrun): expert parallelism, rank r holds experts [16r/… ) — 128/N per
+GPU; every rank routes all T tokens (identical results), computes its own
+experts' slots, one NCCL all-reduce (sum) of the [T*8, 2048] slot outputs
+(exactly one rank contributes each slot, so the sum is exact), then the
+k-ordered combine. Total work is fixed as N grows: "strong" scaling.
+
+--impl reference: the reference's own C (kernels.c + test_model_trace.c MoE
+block, compiled from source into oracle/_ref; else this repo's C port) on the
+host cores, same metric and config.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "moe.cc_b200"))
+
+E, D, F, TOPK = 128, 2048, 768, 8
+METRIC = "MoE-layer decode tok/s (Q8, Qwen3-30B-A3B layer shape)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=16)
+    ap.add_argument("--dtype", default="q8", choices=["q8", "q4"])
+    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--extra-t", default="1,4", help="other T values reported beside the headline")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), \
+        int(os.environ.get("LOCAL_RANK", 0))
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx, self.rows, self.stop = gpu_index, [], threading.Event()
+        self.th = threading.Thread(target=self.run, daemon=True)
+
+    def run(self):
+        while not self.stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True,
+                                     text=True, timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([c.strip() for c in out.split(",")])
+            except Exception:
+                pass
+            self.stop.wait(0.2)
+
+    def __enter__(self):
+        self.th.start()
+        return self
+
+    def __exit__(self, *a):
+        self.stop.set()
+        self.th.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = sorted(float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None,
+                "sm_max_mhz": float(self.rows[0][2]) if self.rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_table():
+    """Per-launch DRAM bytes of each kernel from a committed ncu summary, if any."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+def alg_bytes(kernel, T, U, dt):
+    """Algorithmic HBM bytes of one launch (weights + scales read once, token
+    activations in/out). U = distinct experts routed in that step."""
+    gu_rb = D if dt == 2 else D // 2
+    d_rb = F if dt == 2 else F // 2
+    if kernel == "gateup":
+        return U * (2 * F * gu_rb + 2 * F * 4)
+    if kernel == "down":
+        return U * (D * d_rb + D * 4) + T * D * 4 * 2   # + residual read, output write
+    if kernel == "router_logits":
+        return E * D * 4 + T * D * 4 + T * E * 4
+    return None
+
+
+def layer_bytes_step(T, U, dt):
+    return sum(alg_bytes(k, T, U, dt) for k in ("router_logits", "gateup", "down"))
+
+
+def build_layers(torch, mc, sy, nl, dt):
+    for l in range(nl):
+        Ld = sy.make_layer_dev(torch, 1, l, E, D, F, dt, bias=False)
+        mc.upload_layer(l, Ld, device_arrays=True)
+        del Ld
+    torch.cuda.synchronize()
+    mc.check_status()
+
+
+def make_inputs(torch, mc, T, pool, seed):
+    xs, xa = [], []
+    for i in range(pool):
+        a = torch.empty(T, D, device="cuda")
+        b = torch.empty(T, D, device="cuda")
+        mc.synth_normal_dev(seed * 7919 + 2 * i, a, 1.0)
+        mc.synth_normal_dev(seed * 7919 + 2 * i + 1, b, 1.0)
+        xs.append(a); xa.append(b)
+    return xs, xa
+
+
+class Runner:
+    """One decode step on this rank (N=1: moe_ffn; N>1: partial + all-reduce + combine)."""
+
+    def __init__(self, torch, mc, dist, world, T, nl, pool):
+        self.torch, self.mc, self.dist, self.world = torch, mc, dist, world
+        self.T, self.nl = T, nl
+        self.xs, self.xa = make_inputs(torch, mc, T, pool, seed=T)
+        self.out = [x.clone() for x in self.xa]
+        self.y = torch.empty(T * TOPK, D, device="cuda") if world > 1 else None
+        self.p = torch.empty(T, TOPK, device="cuda") if world > 1 else None
+        self.stream = torch.cuda.current_stream()
+
+    def step(self, i, topk_idx=None):
+        j = i % len(self.xs)
+        layer = i % self.nl
+        if self.world == 1:
+            self.mc.moe_ffn_dev(layer, self.xs[j], self.out[j], topk_idx, None, stream=self.stream)
+        else:
+            self.mc.moe_ffn_partial(layer, self.xs[j], self.y, topk_idx, self.p, stream=self.stream)
+            self.dist.all_reduce(self.y)
+            self.mc.moe_ffn_combine(self.y, self.p, self.out[j], TOPK, stream=self.stream)
+
+    def timed(self, steps, warmup, barrier=True):
+        torch = self.torch
+        for i in range(warmup):
+            self.step(i)
+        torch.cuda.synchronize()
+        if barrier and self.world > 1:
+            self.dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(self.stream)
+        for i in range(steps):
+            self.step(warmup + i)
+        b.record(self.stream)
+        torch.cuda.synchronize()
+        if barrier and self.world > 1:
+            self.dist.barrier()
+        ms = a.elapsed_time(b)
+        if self.world > 1:
+            t = torch.tensor([ms], device="cuda")
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+            ms = float(t.item())
+        self.mc.check_status()
+        return ms
+
+    def distinct_experts(self, steps, warmup):
+        """U per step (routing is a pure function of layer and input)."""
+        torch = self.torch
+        idx = torch.empty(steps, self.T, TOPK, dtype=torch.int32, device="cuda")
+        for i in range(steps):
+            self.step(warmup + i, idx[i])
+        torch.cuda.synchronize()
+        h = idx.cpu().numpy()
+        return [len(set(h[i].ravel().tolist())) for i in range(steps)]
+
+
+def e2e_host(torch, mc, T, steps, warmup, nl):
+    """Same metric through the C-ABI with pinned HOST buffers: every step copies
+    x_norm2 and x_inout in, the result and top-k out (inside the timed region)."""
+    import numpy as np
+    xs = [torch.from_numpy(mc.synth_normal_host(5000 + i, T * D, 1.0).reshape(T, D)).pin_memory()
+          for i in range(8)]
+    xo = [torch.from_numpy(mc.synth_normal_host(6000 + i, T * D, 1.0).reshape(T, D)).pin_memory()
+          for i in range(8)]
+    idx = torch.empty(T, TOPK, dtype=torch.int32).pin_memory()
+    p = torch.empty(T, TOPK, dtype=torch.float32).pin_memory()
+    lib = mc.lib()
+
+    def call(i):
+        mc.check(lib.moe_ffn(i % nl, xs[i % 8].data_ptr(), xo[i % 8].data_ptr(), T, idx.data_ptr(),
+                             p.data_ptr(), mc.HOST_PTRS, None))
+    for i in range(warmup):
+        call(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(torch.cuda.default_stream())
+    for i in range(steps):
+        call(warmup + i)
+    b.record(torch.cuda.default_stream())
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    return {"value": T * steps / (ms / 1e3), "unit": "tok/s",
+            "h2d_bytes_per_step": 2 * T * D * 4, "d2h_bytes_per_step": T * D * 4 + T * TOPK * 8,
+            "ms_per_step": ms / steps}
+
+
+def host_layer_from_device(torch, mc, sy, dt):
+    """Layer 0 rebuilt on the GPU and copied to host numpy (CPU-baseline input)."""
+    Ld = sy.make_layer_dev(torch, 1, 0, E, D, F, dt, bias=False)
+    torch.cuda.synchronize()
+    L = {k: (v.cpu().numpy() if hasattr(v, "cpu") else v) for k, v in Ld.items()}
+    L["topk"] = TOPK
+    L.setdefault("router_b", None)
+    return L
+
+
+def host_layer(mc, dt):
+    """Layer 0 built on the host (no GPU), same seeds as synth.make_layer_dev."""
+    import numpy as np
+    import synth as sy
+    from oracle.oracle import Port
+    port = Port()
+    L = {"dtype": dt, "topk": TOPK, "router_b": None,
+         "router_w": mc.synth_normal_host(sy.stream_seed(1, 0, 0), E * D, 0.02).reshape(E, D)}
+    shapes = {"g": (F, D), "u": (F, D), "d": (D, F)}
+    for j, nm in enumerate("gud"):
+        rows, cols = shapes[nm]
+        qs, ss = [], []
+        for e in range(E):
+            w = mc.synth_normal_host(sy.stream_seed(1, 0, 2 + 3 * e + j), rows * cols, 0.02)
+            q, s = port.quantize(w.reshape(rows, cols), dt)
+            qs.append(q); ss.append(s)
+        L[nm + "q"] = np.ascontiguousarray(np.stack(qs))
+        L[nm + "s"] = np.ascontiguousarray(np.stack(ss))
+    return L
+
+
+def cpu_engine():
+    from oracle.oracle import Port, Ref
+    if Ref.available():
+        return "reference", Ref()
+    return "port", Port()
+
+
+def cpu_step(kind, eng, L, xn, xa):
+    if kind == "reference":
+        # the reference's layer_forward_f32 with zero attention: MoE input = rmsnorm(x)
+        eng.moe_layer(xa, L)
+    else:
+        eng.moe_block(xn, xa, L)
+
+
+def cpu_baseline(mc, L, T, budget_s=12.0):
+    """The reference's own CPU path (oracle/_ref, single-threaded as shipped) on a
+    bounded sample of the same workload: whole T-token steps until ~budget_s."""
+    kind, eng = cpu_engine()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        xn = mc.synth_normal_host(7000 + n, T * D, 1.0).reshape(T, D)
+        xa = mc.synth_normal_host(7500 + n, T * D, 1.0).reshape(T, D)
+        cpu_step(kind, eng, L, xn, xa)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    cores = 1 if kind == "reference" else (os.cpu_count() or 1)
+    return {"value": n * T / dt, "unit": "tok/s", "cores": cores, "kind": kind,
+            "sample": f"{n} steps of T={T} tokens (one Q8 layer each), {dt:.1f} s"}
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import synth  # noqa: F401  (seed helper)
+    import moe_cuda as mc
+    dt = 2 if args.dtype == "q8" else 3
+    L = host_layer(mc, dt)
+    kind, eng = cpu_engine()
+    T = args.tokens
+    xs = [(mc.synth_normal_host(7000 + i, T * D, 1.0).reshape(T, D),
+           mc.synth_normal_host(7500 + i, T * D, 1.0).reshape(T, D)) for i in range(4)]
+    for i in range(args.warmup):
+        cpu_step(kind, eng, L, *xs[i % 4])
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        cpu_step(kind, eng, L, *xs[i % 4])
+    sec = time.perf_counter() - t0
+    v = T * args.steps / sec
+    cores = 1 if kind == "reference" else (os.cpu_count() or 1)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int32-acc q8" if dt == 2 else "int32-acc q4", "data": "synthetic",
+            "config": {"workload": f"configs[1]: Qwen3-30B-A3B MoE layer decode, T={T}",
+                       "tokens": T, "experts": E, "hidden": D, "moe_intermediate": F, "top_k": TOPK},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind,
+                             "sample": f"{args.steps} timed steps of T={T} on the host"},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    import moe_cuda as mc
+    import synth as sy
+    mc.init(local, world, rank)
+    dt = 2 if args.dtype == "q8" else 3
+    nl = args.layers
+    build_layers(torch, mc, sy, nl, dt)
+    T = args.tokens
+    steps, warmup = args.steps, max(args.warmup, 3)
+    pool = 64
+
+    run = Runner(torch, mc, dist, world, T, nl, pool)
+    with ClockSampler(local) as clk:
+        ms = run.timed(steps, warmup)
+    clocks = clk.summary()
+    value = T * steps / (ms / 1e3)
+
+    # routed experts per step and per-kernel device times (separate profiled pass)
+    Us = run.distinct_experts(min(steps, 64), warmup)
+    U = sum(Us) / len(Us)
+    mc.profile(True)
+    run.timed(steps, 0)
+    prof = mc.profile_read()
+    mc.profile(False)
+    peak, peak_kind = peaks()
+    kern = {}
+    for name, (tot, cnt) in prof.items():
+        avg_ms = tot / max(cnt, 1)
+        b = alg_bytes(name, T, U / 1.0 if world == 1 else U / world, dt)
+        kern[name] = {"avg_us": avg_ms * 1e3, "launches": cnt,
+                      "share": tot / max(sum(v[0] for v in prof.values()), 1e-9),
+                      "alg_bytes": b, "gbs": (b / (avg_ms * 1e-3) / 1e9) if b else None}
+    dom = max((k for k in kern if kern[k]["alg_bytes"]), key=lambda k: kern[k]["share"])
+    tr = traffic_table().get(f"{dom}_T{T}_{args.dtype}")
+    roof = {"kernel": dom, "bound": "hbm", "achieved": kern[dom]["gbs"], "peak": peak,
+            "unit": "GB/s", "frac": kern[dom]["gbs"] / peak, "peak_source": peak_kind,
+            "traffic": tr, "alg_bytes_per_launch": kern[dom]["alg_bytes"]}
+    layer_gbs = layer_bytes_step(T, U, dt) / (ms / steps * 1e-3) / 1e9
+    launches_per_step = sum(v["launches"] for v in kern.values()) / steps
+
+    extra = {}
+    if world == 1:
+        for t in [int(v) for v in args.extra_t.split(",") if v]:
+            if t == T:
+                continue
+            r2 = Runner(torch, mc, dist, world, t, nl, pool)
+            ms2 = r2.timed(steps, warmup)
+            u2 = r2.distinct_experts(min(steps, 64), warmup)
+            extra[f"T{t}"] = {"tok_s": t * steps / (ms2 / 1e3), "us_per_step": ms2 * 1e3 / steps,
+                              "distinct_experts": sum(u2) / len(u2),
+                              "layer_gbs": layer_bytes_step(t, sum(u2) / len(u2), dt)
+                              / (ms2 / steps * 1e-3) / 1e9}
+    e2e = None
+    if world == 1:
+        e2e = e2e_host(torch, mc, T, steps, warmup, nl)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(mc, host_layer_from_device(torch, mc, sy, dt), T)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+                "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "int32-acc q8" if dt == 2 else "int32-acc q4", "data": "synthetic",
+                "config": {"workload": f"configs[1]: Qwen3-30B-A3B MoE layer decode, T={T}",
+                           "tokens": T, "experts": E, "hidden": D, "moe_intermediate": F,
+                           "top_k": TOPK, "resident_layers": nl, "input_pool": pool,
+                           "parallelism": f"ep{world}",
+                           "l2": "inputs larger than L2: steps rotate over resident layers"},
+                "roofline": roof,
+                "layer": {"alg_gbs": layer_gbs, "frac_hbm": layer_gbs / peak,
+                          "distinct_experts": U, "us_per_step": ms * 1e3 / steps},
+                "kernels": kern, "gpu_launches": int(round(launches_per_step * steps)),
+                "gpu_launches_per_step": launches_per_step,
+                "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu, "extra": extra}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

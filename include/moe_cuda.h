@@ -1,0 +1,199 @@
+/*
+ * moe_cuda.h — C-ABI of libmoe_cuda.so, the B200 (sm_100a) implementation of
+ * moe.cc's MoE expert-FFN hot path.
+ *
+ * Plain C99: pointers, sizes and int status codes only. A C host that today
+ * links kernels.o (moe.cc Makefile:8-9) links libmoe_cuda.so instead and keeps
+ * calling matmul_adaptive() unchanged; the fused moe_ffn() replaces the whole
+ * MoE block of layer_forward_f32 (test_model_trace.c:463-517).
+ *
+ * Arithmetic contract (identical to the reference, not "dequant(W)·x"):
+ *   Q8:  C[m,n] = ((float)Σ_k (int32)(A[m,k]*127f) * q[n,k] / 127f) * s[n]
+ *   Q4:  C[m,n] = ((float)Σ_k (int32)(A[m,k]*7f) * (nib[n,k]-8) / 7f) * s[n]
+ * with truncation toward zero, exact int32 accumulation (two's-complement
+ * wrap), IEEE round-to-nearest divide and multiply (kernels.c:51-74, 96-128).
+ *
+ * Status codes: every int-returning entry point returns MOE_OK (0) or one of
+ * the MOE_ERR_* codes below; moe_cuda_last_error() gives a message. The
+ * void-returning reference-shaped entry points (matmul_f32_q8/_q4,
+ * matmul_adaptive) cannot return a status: on failure they print the message
+ * to stderr and abort(), because the reference host has no error path and a
+ * silently wrong result is worse than a crash.
+ *
+ * Threading: one host thread per device; all device work is ordered on the
+ * stream passed in (NULL = the legacy default stream).
+ */
+#ifndef MOE_CUDA_H
+#define MOE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same layout as moe.cc model.h:26-32, so a QwenLayerWeights' Wg_q/Wu_q/Wd_q
+ * arrays can be passed as they are. */
+#ifndef QUANTIZED_WEIGHT_DEFINED
+typedef struct {
+  const int8_t* q;      /* Q8: int8 [rows][cols]; Q4: uint8 [rows][cols/2] */
+  const float* s;       /* per-row fp32 scale [rows] */
+  int rows, cols;       /* logical shape (Q4: cols = 2 * packed bytes) */
+  int dtype;            /* 2 = Q8, 3 = Q4 (TensorBin dtype enum) */
+} QuantizedWeight;
+#define QUANTIZED_WEIGHT_DEFINED
+#endif
+
+#define MOE_OK               0
+#define MOE_ERR_INVALID      1  /* bad argument / shape / dtype */
+#define MOE_ERR_CUDA         2  /* a CUDA runtime call failed */
+#define MOE_ERR_NOT_INIT     3  /* moe_cuda_init() not called / layer missing */
+#define MOE_ERR_RANGE        4  /* an activation left the integer range the
+                                   kernels accept (see moe_ffn) or was NaN */
+#define MOE_ERR_UNSUPPORTED  5  /* valid for the reference, not built here */
+#define MOE_ERR_NOMEM        6  /* device allocation failed */
+
+#define MOE_DTYPE_Q8 2
+#define MOE_DTYPE_Q4 3
+
+/* moe_ffn flags */
+#define MOE_FFN_HOST_PTRS   0x1 /* x/out/topk pointers are host memory: the
+                                   call copies in, computes, copies out and
+                                   synchronises the stream */
+#define MOE_FFN_DEVICE_PTRS 0x0 /* all pointers are device memory; async */
+#define MOE_FFN_FORCE_GEMV  0x4 /* always use the decode (GEMV) kernels */
+#define MOE_FFN_FORCE_GEMM  0x8 /* always use the grouped tcgen05 GEMM */
+
+/* ---- runtime -------------------------------------------------------------
+ * No reference counterpart (moe.cc has no device); the reference's process
+ * state is only io.c's progress globals (io.c:14-33).
+ * ep_world/ep_rank: expert-parallel group. Rank r owns experts
+ * [r*E/ep_world, (r+1)*E/ep_world) of every layer it uploads. nccl_uid is
+ * reserved and must be NULL (the cross-rank exchange is driven by the caller
+ * through moe_ffn_partial + its own communicator). */
+int moe_cuda_init(int device, int ep_world, int ep_rank, const void* nccl_uid);
+int moe_cuda_shutdown(void);
+const char* moe_cuda_last_error(void);
+/* Synchronise the device and report (then clear) any error a kernel flagged
+ * asynchronously (MOE_ERR_RANGE from device-pointer moe_ffn calls). */
+int moe_cuda_check_status(void);
+
+/* ---- reference kernel surface (kernels.c / kernels.h) --------------------
+ * Host pointers, synchronous. If B_q/B_s are host pointers previously given
+ * to moe_cuda_upload_layer (or moe_cuda_register_weight), the resident device
+ * copy is used; otherwise the weight is copied for this call only. */
+/* replaces static matmul_f32_q8, kernels.c:51 (same parameter list) */
+void matmul_f32_q8(const float* A, const int8_t* B_q, const float* B_s,
+                   float* C, int M, int N, int K);
+/* replaces static matmul_f32_q4, kernels.c:96 (same parameter list; K even,
+ * see DESIGN notes on the reference's odd-K read past the row) */
+void matmul_f32_q4(const float* A, const uint8_t* B_q, const float* B_s,
+                   float* C, int M, int N, int K);
+/* replaces matmul_adaptive, kernels.h:16-17 / kernels.c:149-181:
+ * W_q_ptr == NULL -> sequential fp32 dot; dtype 2/3 -> Q8/Q4; any other
+ * dtype -> C zero-filled (kernels.c:172-180). */
+void matmul_adaptive(const float* A, const float* W_fp32, const void* W_q_ptr,
+                     float* C, int M, int N, int K);
+
+/* Device-pointer, stream-ordered forms of the three above (same math).
+ * stream is a cudaStream_t (NULL = default stream). */
+int moe_matmul_q8_dev(const float* A, const int8_t* B_q, const float* B_s,
+                      float* C, int M, int N, int K, void* stream);
+int moe_matmul_q4_dev(const float* A, const uint8_t* B_q, const float* B_s,
+                      float* C, int M, int N, int K, void* stream);
+int moe_matmul_f32_dev(const float* A, const float* W, float* C,
+                       int M, int N, int K, void* stream);
+/* Many independent GEMVs of one activation row against n_mat Q8/Q4 matrices
+ * of identical shape (the "all experts' gate matrices in one launch" form of
+ * config C1): C[i][n] = matmul(A[1,K], W_i[N,K]). W_q/W_s are device arrays
+ * of n_mat device pointers. No reference counterpart (one loop of calls to
+ * matmul_adaptive with M=1 in the reference). */
+int moe_matmul_batched_dev(const float* A, const void* const* W_q,
+                           const float* const* W_s, float* C, int n_mat,
+                           int N, int K, int dtype, void* stream);
+
+/* ---- quantisers (export.py:23-36) -----------------------------------------
+ * Bit-exact with export._rowwise_q8 / _rowwise_q4: s = max(max|row|,1e-8)/127
+ * (or /7), q = round-half-even(w/s) (Q4: clamped to [-8,7], +8, two nibbles a
+ * byte, even column in the low nibble). Device pointers. */
+int moe_quantize_rowwise_q8_dev(const float* W, int rows, int cols,
+                                int8_t* q, float* s, void* stream);
+int moe_quantize_rowwise_q4_dev(const float* W, int rows, int cols,
+                                uint8_t* q, float* s, void* stream);
+
+/* ---- weight residency (model.h:220-305 + io.c:193-320) --------------------
+ * Copies one layer's experts (host QuantizedWeight arrays of length E, as in
+ * QwenLayerWeights.Wg_q/Wu_q/Wd_q, model.h:55-57) and router (model.h:44-45;
+ * router_b may be NULL, model.h:217-218) into device memory: one slab per
+ * expert holding [gate q | up q | down q | gate s | up s | down s], every
+ * part 128-byte aligned. Under expert parallelism only this rank's experts
+ * are copied. The host q/s pointers are remembered, so later matmul_f32_q8/
+ * _q4/matmul_adaptive calls on them run on the resident copy. */
+int moe_cuda_upload_layer(int layer, const QuantizedWeight* Wg,
+                          const QuantizedWeight* Wu, const QuantizedWeight* Wd,
+                          const float* router_w, const float* router_b, int E);
+/* Same, but every q/s pointer in Wg/Wu/Wd and router_w/router_b is DEVICE
+ * memory (e.g. the output of moe_quantize_rowwise_*_dev). Sizes as above. */
+int moe_cuda_upload_layer_dev(int layer, const QuantizedWeight* Wg,
+                              const QuantizedWeight* Wu,
+                              const QuantizedWeight* Wd,
+                              const float* router_w, const float* router_b,
+                              int E);
+int moe_cuda_free_layer(int layer);
+/* Bytes of device memory the layer's expert slabs occupy on this rank. */
+size_t moe_cuda_layer_bytes(int layer);
+
+/* ---- fused MoE block --------------------------------------------------------
+ * Replaces test_model_trace.c:463-517 (router matmul + bias, topk_desc,
+ * top-k softmax, per-(token,k) gate/up/SiLU·up/down, k-ordered weighted
+ * combine, residual add):
+ *   x_inout[t] = x_inout[t] + Σ_{k=0..top_k-1} p[t,k] · down_e(silu(gate_e x)·up_e x)
+ * x_norm2: [T][D] fp32 input to the experts; x_inout: [T][D] fp32, holds
+ * x_after on entry and x on return (test_model_trace.c:517).
+ * topk_idx_out/topk_p_out: optional [T][top_k] (NULL to skip).
+ * Integer range: Q8 needs |x| < 258 (trunc(127x) fits 16 bits) and
+ * |silu(g)u| < 258; Q4 needs trunc(7x) in [-128,127]. Outside that the call
+ * returns MOE_ERR_RANGE (device-pointer calls: reported by
+ * moe_cuda_check_status) instead of a wrong answer.
+ * With ep_world > 1 use moe_ffn_partial instead. */
+int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T,
+            int* topk_idx_out, float* topk_p_out, int flags, void* stream);
+
+/* Expert-parallel form: computes router/top-k on every rank (identical
+ * results), and for this rank's experts only, writes y_slots[T*top_k][D]
+ * (y of slot t*top_k+k, zero where the slot's expert lives on another rank)
+ * and topk_p [T*top_k]. After the caller sums y_slots over ranks (a
+ * reduce — exact, because exactly one rank contributes each slot), call
+ * moe_ffn_combine to apply the k-ordered combine and residual. Device
+ * pointers, async. */
+int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots,
+                    int* topk_idx_out, float* topk_p_out, void* stream);
+int moe_ffn_combine(const float* y_slots, const float* topk_p, float* x_inout,
+                    int T, int D, int top_k, void* stream);
+
+/* ---- profiling -------------------------------------------------------------
+ * Per-kernel device time of moe_ffn / moe_ffn_partial (CUDA events recorded
+ * on the launching stream around each launch). Counterpart of the
+ * reference's PROF_START/PROF_ENDF profiler (test_model_trace.c:64-199).
+ * moe_cuda_profile(1) clears and starts, (0) stops. moe_cuda_profile_read
+ * synchronises and fills up to max_kernels entries: names (name_len bytes
+ * each), total milliseconds and launch counts; returns the entry count. */
+int moe_cuda_profile(int enable);
+int moe_cuda_profile_read(int max_kernels, char* names, int name_len,
+                          double* total_ms, long* launches);
+
+/* ---- synthetic inputs -----------------------------------------------------
+ * out[i] = std * N(0,1) sample i of the counter-based stream `seed`
+ * (splitmix64 -> Box-Muller in double -> float), i = offset .. offset+n-1.
+ * Host and device forms produce the same stream. Harness convenience only;
+ * no reference counterpart. */
+void moe_synth_normal_host(uint64_t seed, uint64_t offset, size_t n, float std,
+                           float* out);
+int moe_synth_normal_dev(uint64_t seed, uint64_t offset, size_t n, float std,
+                         float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_CUDA_H */

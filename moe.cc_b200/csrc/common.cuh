@@ -1,0 +1,104 @@
+// common.cuh — shared device helpers for libmoe_cuda (sm_100a).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moe {
+
+// Exactly-rounded scalar ops used wherever the reference's arithmetic must be
+// reproduced bit for bit (no FMA contraction, IEEE round-to-nearest).
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
+
+// expf(v) rounded once from a double-precision exp. glibc's expf (the
+// reference's, test_model_trace.c:233,485) is accurate to within about half
+// an ulp, so the two agree except where the exact value lies within a hair of
+// a rounding midpoint.
+__device__ __forceinline__ float exp_f32(float v) { return (float)exp((double)v); }
+
+// silu_f32 (test_model_trace.c:229-236): v / (1 + expf(-v)).
+__device__ __forceinline__ float silu_ref(float v) {
+  return fdiv(v, fadd(1.0f, exp_f32(-v)));
+}
+
+// (int32_t)(a * scale) — kernels.c:66 / :113, truncation toward zero.
+// Returns INT32_MIN for NaN (x86 cvttss2si gives the same "indefinite" value).
+__device__ __forceinline__ int trunc_scale(float a, float scale) {
+  float v = fmul(a, scale);
+  if (v != v) return INT32_MIN;
+  return __float2int_rz(v);
+}
+
+// dp4a with signed A bytes and unsigned B bytes: d = c + Σ a_i * b_i.
+__device__ __forceinline__ int dp4a_su(int a, unsigned b, int c) {
+  int d;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// signed × signed
+__device__ __forceinline__ int dp4a_ss(int a, int b, int c) { return __dp4a(a, b, c); }
+// unsigned A × signed B (int8 weights against the low activation limb)
+__device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// 16-byte read-only streaming load (weights: read once, keep out of L1).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Q8 activation limbs: a = lo + 256 * hi with lo in [0,255], hi in [-128,127]
+// (|a| <= 32767). Σ w*a = Σ w*lo + 256 Σ w*hi, exact mod 2^32.
+// Q8 chunk dot: 16 weight bytes against 16 lo bytes and 16 hi bytes.
+__device__ __forceinline__ void dot16_q8(const uint4 w, const uint4 lo, const uint4 hi,
+                                         int& acc_lo, int& acc_hi) {
+  acc_lo = dp4a_us(lo.x, (int)w.x, acc_lo);
+  acc_lo = dp4a_us(lo.y, (int)w.y, acc_lo);
+  acc_lo = dp4a_us(lo.z, (int)w.z, acc_lo);
+  acc_lo = dp4a_us(lo.w, (int)w.w, acc_lo);
+  acc_hi = dp4a_ss((int)hi.x, (int)w.x, acc_hi);
+  acc_hi = dp4a_ss((int)hi.y, (int)w.y, acc_hi);
+  acc_hi = dp4a_ss((int)hi.z, (int)w.z, acc_hi);
+  acc_hi = dp4a_ss((int)hi.w, (int)w.w, acc_hi);
+}
+
+// Q4 chunk dot: 16 packed bytes (32 nibbles, k = 32c..32c+31) against 32
+// signed activation bytes stored as words [E0,O0,E1,O1] [E2,O2,E3,O3], where
+// word j of the weights holds k=8j..8j+7 with even k in low nibbles:
+// Ej = (a[8j],a[8j+2],a[8j+4],a[8j+6]), Oj = (a[8j+1],a[8j+3],a[8j+5],a[8j+7]).
+// Accumulates Σ a * nibble (nibble in [0,15]); the caller subtracts 8 Σ a.
+__device__ __forceinline__ int dot16_q4(const uint4 w, const uint4 a0, const uint4 a1, int acc) {
+  acc = dp4a_su((int)a0.x, w.x & 0x0F0F0F0Fu, acc);
+  acc = dp4a_su((int)a0.y, (w.x >> 4) & 0x0F0F0F0Fu, acc);
+  acc = dp4a_su((int)a0.z, w.y & 0x0F0F0F0Fu, acc);
+  acc = dp4a_su((int)a0.w, (w.y >> 4) & 0x0F0F0F0Fu, acc);
+  acc = dp4a_su((int)a1.x, w.z & 0x0F0F0F0Fu, acc);
+  acc = dp4a_su((int)a1.y, (w.z >> 4) & 0x0F0F0F0Fu, acc);
+  acc = dp4a_su((int)a1.z, w.w & 0x0F0F0F0Fu, acc);
+  acc = dp4a_su((int)a1.w, (w.w >> 4) & 0x0F0F0F0Fu, acc);
+  return acc;
+}
+
+// Position of activation element k inside the Q4 permuted layout
+// (byte offset within the token's row of K bytes).
+__host__ __device__ __forceinline__ int q4_act_pos(int k) {
+  const int j = k >> 3, r = k & 7;           // word j of weights, nibble r
+  return (j << 3) + ((r & 1) << 2) + (r >> 1);  // E_j at 8j..8j+3, O_j at 8j+4..
+}
+
+// Error flag bits written by kernels (read by the host).
+enum : int { kErrRange = 1 };
+
+}  // namespace moe

@@ -1,0 +1,748 @@
+// kernels.cu — CUDA-core kernels of libmoe_cuda (sm_100a): activation
+// truncation, router, top-k, routing lists, the decode-regime fused expert
+// GEMVs (gate/up + SiLU·up, down + k-ordered combine), the plain Q8/Q4 GEMV of
+// the matmul_* entry points, rowwise quantisers and the synthetic generator.
+//
+// Arithmetic follows the reference exactly (kernels.c:51-128,
+// test_model_trace.c:213-288, 463-517): activations are truncated to integers
+// once per row, dots are exact integer sums (order-free), and every float step
+// is one IEEE round-to-nearest op in the reference's order.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace moe {
+
+// --------------------------------------------------------------------------
+// geometry of the warp GEMV: a row of `rb` bytes is read by a group of LPR
+// lanes, each lane loading `cpl` 16-byte chunks per pass, `np` passes.
+// --------------------------------------------------------------------------
+struct Geo { int lpr = 0, cpl = 0, np = 0; };
+
+static bool pick_geo(int rb, Geo& g) {
+  if (rb <= 0 || rb % 16) return false;
+  const int nc = rb / 16;
+  if (nc >= 128) {
+    if (nc % 32) return false;
+    const int per = nc / 32;
+    for (int c = 4; c >= 1; --c)
+      if (per % c == 0) { g.lpr = 32; g.cpl = c; g.np = per / c; return true; }
+    return false;
+  }
+  for (int l = 1; l <= 32; l <<= 1)
+    if (nc % l == 0 && nc / l <= 4) { g.lpr = l; g.cpl = nc / l; g.np = 1; return true; }
+  return false;
+}
+
+bool fast_geometry_ok(int dtype, int K) {
+  Geo g;
+  const int rb = dtype == 2 ? K : K / 2;
+  if (dtype == 3 && (K & 1)) return false;
+  return pick_geo(rb, g);
+}
+
+// one 16-byte weight chunk `c` against the activation row `act` (row of K
+// logical elements; Q8: lo plane [0,K), hi plane [K,2K); Q4: K permuted bytes)
+template <int DT>
+__device__ __forceinline__ void chunk_dot(const uint4 w, const uint8_t* act, int K, int c,
+                                          int& a0, int& a1) {
+  if (DT == 8) {
+    const uint4 lo = __ldg(reinterpret_cast<const uint4*>(act + (size_t)c * 16));
+    const uint4 hi = __ldg(reinterpret_cast<const uint4*>(act + K + (size_t)c * 16));
+    dot16_q8(w, lo, hi, a0, a1);
+  } else {
+    const uint4 p0 = __ldg(reinterpret_cast<const uint4*>(act + (size_t)c * 32));
+    const uint4 p1 = __ldg(reinterpret_cast<const uint4*>(act + (size_t)c * 32 + 16));
+    a0 = dot16_q4(w, p0, p1, a0);
+  }
+}
+
+// combine limb accumulators into the per-lane partial (mod 2^32)
+template <int DT>
+__device__ __forceinline__ int lane_partial(int a0, int a1) {
+  return DT == 8 ? (int)((unsigned)a0 + ((unsigned)a1 << 8)) : a0;
+}
+
+template <int LPR>
+__device__ __forceinline__ int group_sum(int v) {
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ((float)dot / S) * s — kernels.c:71 / :126
+template <int DT>
+__device__ __forceinline__ float dequant_out(int dot, int asum, float s) {
+  constexpr float S = DT == 8 ? 127.0f : 7.0f;
+  if (DT == 4) dot = (int)((unsigned)dot - 8u * (unsigned)asum);
+  return fmul(fdiv(__int2float_rn(dot), S), s);
+}
+
+// --------------------------------------------------------------------------
+// activation truncation (kernels.c:66 / :113), once per row
+// --------------------------------------------------------------------------
+template <int DT>
+__global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restrict__ x, int K,
+                                                           uint8_t* __restrict__ act, int act_stride,
+                                                           int* __restrict__ asum, int* err) {
+  const int m = blockIdx.x;
+  const float* xr = x + (size_t)m * K;
+  uint8_t* ar = act + (size_t)m * act_stride;
+  int sum = 0, bad = 0;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const int a = trunc_scale(xr[k], DT == 8 ? 127.0f : 7.0f);
+    if (DT == 8) {
+      bad |= (a < -32768 || a > 32767);
+      ar[k] = (uint8_t)(a & 0xFF);
+      ar[K + k] = (uint8_t)((a >> 8) & 0xFF);
+    } else {
+      bad |= (a < -128 || a > 127);
+      ar[q4_act_pos(k)] = (uint8_t)(a & 0xFF);
+      sum += a;
+    }
+  }
+  if (bad) atomicOr(err, kErrRange);
+  if (DT == 4) {
+    __shared__ int red[8];
+    sum = warp_sum(sum);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int s = 0;
+      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += red[i];
+      asum[m] = s;
+    }
+  }
+}
+
+void launch_quantize_act(const float* x, int M, int K, int dtype, uint8_t* act, int act_stride,
+                         int* asum, int* err, cudaStream_t st) {
+  if (M <= 0) return;
+  if (dtype == 2)
+    quantize_act_kernel<8><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err);
+  else
+    quantize_act_kernel<4><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err);
+}
+
+// --------------------------------------------------------------------------
+// sequential fp32 dot per output (test_model_trace.c:213-227, kernels.c:153-165)
+// one dependent add chain per (m, n), exactly the reference's order
+// --------------------------------------------------------------------------
+template <bool VEC>
+__global__ void __launch_bounds__(32) f32_seq_kernel(const float* __restrict__ A,
+                                                     const float* __restrict__ W,
+                                                     const float* __restrict__ b, float* __restrict__ C,
+                                                     int M, int N, int K) {
+  const long c = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= (long)M * N) return;
+  const int m = (int)(c / N), n = (int)(c % N);
+  const float* a = A + (size_t)m * K;
+  const float* w = W + (size_t)n * K;
+  float acc = 0.0f;
+  if (VEC) {
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll 4
+    for (int k = 0; k < K / 4; ++k) {
+      const float4 av = __ldg(a4 + k), wv = __ldg(w4 + k);
+      acc = fadd(acc, fmul(av.x, wv.x));
+      acc = fadd(acc, fmul(av.y, wv.y));
+      acc = fadd(acc, fmul(av.z, wv.z));
+      acc = fadd(acc, fmul(av.w, wv.w));
+    }
+  } else {
+    for (int k = 0; k < K; ++k) acc = fadd(acc, fmul(__ldg(a + k), __ldg(w + k)));
+  }
+  if (b) acc = fadd(acc, __ldg(b + n));   // logits += router_b (:466-468)
+  C[c] = acc;
+}
+
+void launch_f32_seq_matmul(const float* A, const float* W, const float* b, float* C, int M, int N,
+                           int K, cudaStream_t st) {
+  const long total = (long)M * N;
+  if (total <= 0) return;
+  const bool vec = (K % 4 == 0) && ((uintptr_t)A % 16 == 0) && ((uintptr_t)W % 16 == 0);
+  const unsigned grid = (unsigned)((total + 31) / 32);
+  if (vec)
+    f32_seq_kernel<true><<<grid, 32, 0, st>>>(A, W, b, C, M, N, K);
+  else
+    f32_seq_kernel<false><<<grid, 32, 0, st>>>(A, W, b, C, M, N, K);
+}
+
+// --------------------------------------------------------------------------
+// top-k (topk_desc, test_model_trace.c:275-288) + softmax (:481-487)
+// --------------------------------------------------------------------------
+constexpr int kMaxTopK = 32;
+
+__global__ void topk_softmax_kernel(const float* __restrict__ logits, int T, int E, int K,
+                                    int* __restrict__ idx, float* __restrict__ p) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  float val[kMaxTopK];
+  int id[kMaxTopK];
+  for (int i = 0; i < K; ++i) { val[i] = -INFINITY; id[i] = -1; }
+  const float* x = logits + (size_t)t * E;
+  for (int e = 0; e < E; ++e) {
+    const float v = x[e];
+    int pos = -1;
+    for (int i = 0; i < K; ++i) if (v > val[i]) { pos = i; break; }
+    if (pos < 0) continue;
+    for (int j = K - 1; j > pos; --j) { val[j] = val[j - 1]; id[j] = id[j - 1]; }
+    val[pos] = v; id[pos] = e;
+  }
+  float mx = val[0];
+  for (int i = 1; i < K; ++i) if (val[i] > mx) mx = val[i];
+  float sum = 0.0f;
+  for (int i = 0; i < K; ++i) { val[i] = exp_f32(__fsub_rn(val[i], mx)); sum = fadd(sum, val[i]); }
+  const float inv = fdiv(1.0f, fadd(sum, 1e-9f));
+  for (int i = 0; i < K; ++i) {
+    idx[(size_t)t * K + i] = id[i];
+    p[(size_t)t * K + i] = fmul(val[i], inv);
+  }
+}
+
+void launch_topk_softmax(const float* logits, int T, int E, int K, int* idx, float* p,
+                         cudaStream_t st) {
+  if (T <= 0) return;
+  topk_softmax_kernel<<<(T + 127) / 128, 128, 0, st>>>(logits, T, E, K, idx, p);
+}
+
+// --------------------------------------------------------------------------
+// routing lists: for every local expert with tokens, its slots (t*K+k) in
+// ascending slot order; experts ascending. One CTA.
+// --------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) route_build_kernel(const int* __restrict__ idx, int TK,
+                                                           int e_begin, int E_local, int* route,
+                                                           int* hsum) {
+  extern __shared__ int sm[];
+  int* cnt = sm;              // [E_local]
+  int* start = sm + E_local;  // [E_local]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const RouteView r = route_view(route, E_local);
+  if (hsum)
+    for (int i = threadIdx.x; i < TK; i += blockDim.x) hsum[i] = 0;
+  for (int el = wid; el < E_local; el += nw) {
+    const int e = e_begin + el;
+    int c = 0;
+    for (int base = 0; base < TK; base += 32) {
+      const int v = base + lane < TK ? idx[base + lane] : -1;
+      c += __popc(__ballot_sync(0xffffffffu, v == e));
+    }
+    if (lane == 0) cnt[el] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int na = 0, off = 0;
+    for (int el = 0; el < E_local; ++el) {
+      start[el] = off;
+      if (cnt[el] > 0) { r.active[na] = el; r.exp_off[na] = off; off += cnt[el]; ++na; }
+    }
+    r.exp_off[na] = off;
+    *r.n_active = na;
+  }
+  __syncthreads();
+  const unsigned lt = (1u << lane) - 1u;
+  for (int el = wid; el < E_local; el += nw) {
+    if (cnt[el] == 0) continue;
+    const int e = e_begin + el;
+    int pos = start[el];
+    for (int base = 0; base < TK; base += 32) {
+      const int v = base + lane < TK ? idx[base + lane] : -1;
+      const unsigned m = __ballot_sync(0xffffffffu, v == e);
+      if (v == e) r.slot_list[pos + __popc(m & lt)] = base + lane;
+      pos += __popc(m);
+    }
+  }
+}
+
+void launch_route_build(const int* idx, int T, int K, int e_begin, int e_end, int* route,
+                        int E_local, int* hsum, cudaStream_t st) {
+  (void)e_end;
+  const size_t smem = sizeof(int) * 2 * (size_t)E_local;
+  route_build_kernel<<<1, 1024, smem, st>>>(idx, T * K, e_begin, E_local, route, hsum);
+}
+
+// --------------------------------------------------------------------------
+// plain warp GEMV (matmul_f32_q8/_q4 fast path, and the batched C1 form)
+// --------------------------------------------------------------------------
+struct GemvArgs {
+  const uint8_t* const* Wq;  // device array of n_mat pointers, or null
+  const float* const* Ws;
+  const uint8_t* W0;         // single matrix (when Wq == null)
+  const float* S0;
+  int n_mat, N, K, rb, cpl, np, items_per_mat, M, act_stride;
+  const uint8_t* act;
+  const int* asum;
+  float* C;
+};
+
+template <int DT, int LPR, int RPG>
+__global__ void __launch_bounds__(256) gemv_kernel(const GemvArgs a) {
+  constexpr int GPW = 32 / LPR;
+  const int lane = threadIdx.x & 31, grp = lane / LPR, lig = lane % LPR;
+  const long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int mat = (int)(w / a.items_per_mat);
+  if (mat >= a.n_mat) return;
+  const int item = (int)(w % a.items_per_mat);
+  const uint8_t* W = a.Wq ? a.Wq[mat] : a.W0;
+  const float* S = a.Ws ? a.Ws[mat] : a.S0;
+  int n[RPG];
+  bool ok[RPG];
+#pragma unroll
+  for (int j = 0; j < RPG; ++j) { n[j] = (item * GPW + grp) * RPG + j; ok[j] = n[j] < a.N; }
+  uint4 wr[RPG][4];
+  auto load = [&](int p) {
+#pragma unroll
+    for (int j = 0; j < RPG; ++j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = (p * a.cpl + i) * LPR + lig;
+        wr[j][i] = (i < a.cpl && ok[j]) ? ldg_stream(W + (size_t)n[j] * a.rb + (size_t)c * 16)
+                                        : make_uint4(0, 0, 0, 0);
+      }
+  };
+  if (a.np == 1) load(0);
+  for (int m = 0; m < a.M; ++m) {
+    const uint8_t* act = a.act + (size_t)m * a.act_stride;
+    int a0[RPG], a1[RPG];
+#pragma unroll
+    for (int j = 0; j < RPG; ++j) a0[j] = a1[j] = 0;
+    for (int p = 0; p < a.np; ++p) {
+      if (a.np > 1) load(p);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (i >= a.cpl) break;
+        const int c = (p * a.cpl + i) * LPR + lig;
+#pragma unroll
+        for (int j = 0; j < RPG; ++j) chunk_dot<DT>(wr[j][i], act, a.K, c, a0[j], a1[j]);
+      }
+    }
+    const int as = DT == 4 ? __ldg(a.asum + m) : 0;
+#pragma unroll
+    for (int j = 0; j < RPG; ++j) {
+      const int v = group_sum<LPR>(lane_partial<DT>(a0[j], a1[j]));
+      if (lig == 0 && ok[j])
+        a.C[((size_t)mat * a.M + m) * a.N + n[j]] = dequant_out<DT>(v, as, __ldg(S + n[j]));
+    }
+  }
+}
+
+template <int DT, int RPG>
+static void gemv_dispatch(const Geo& g, const GemvArgs& a, unsigned grid, cudaStream_t st) {
+  switch (g.lpr) {
+    case 1: gemv_kernel<DT, 1, RPG><<<grid, 256, 0, st>>>(a); break;
+    case 2: gemv_kernel<DT, 2, RPG><<<grid, 256, 0, st>>>(a); break;
+    case 4: gemv_kernel<DT, 4, RPG><<<grid, 256, 0, st>>>(a); break;
+    case 8: gemv_kernel<DT, 8, RPG><<<grid, 256, 0, st>>>(a); break;
+    case 16: gemv_kernel<DT, 16, RPG><<<grid, 256, 0, st>>>(a); break;
+    default: gemv_kernel<DT, 32, RPG><<<grid, 256, 0, st>>>(a); break;
+  }
+}
+
+bool launch_gemv(int dtype, const uint8_t* const* Wq, const float* const* Ws, int n_mat,
+                 bool ptr_arrays_on_device, int N, int K, const uint8_t* act, int act_stride,
+                 const int* asum, int M, float* C, cudaStream_t st) {
+  Geo g;
+  const int rb = dtype == 2 ? K : K / 2;
+  if (dtype == 3 && (K & 1)) return false;
+  if (!pick_geo(rb, g)) return false;
+  constexpr int RPG = 2;
+  GemvArgs a{};
+  if (ptr_arrays_on_device) { a.Wq = Wq; a.Ws = Ws; }
+  else { a.W0 = Wq[0]; a.S0 = Ws[0]; }
+  a.n_mat = n_mat; a.N = N; a.K = K; a.rb = rb; a.cpl = g.cpl; a.np = g.np;
+  const int rows_per_item = (32 / g.lpr) * RPG;
+  a.items_per_mat = (N + rows_per_item - 1) / rows_per_item;
+  a.M = M; a.act_stride = act_stride; a.act = act; a.asum = asum; a.C = C;
+  const long warps = (long)a.items_per_mat * n_mat;
+  const unsigned grid = (unsigned)((warps + 7) / 8);
+  if (dtype == 2) gemv_dispatch<8, RPG>(g, a, grid, st);
+  else gemv_dispatch<4, RPG>(g, a, grid, st);
+  return true;
+}
+
+// generic exact kernel for any shape / any activation magnitude: one thread
+// per output, int32 activation, plain integer multiply-accumulate.
+template <int DT>
+__global__ void gemv_generic_kernel(const float* __restrict__ A, const uint8_t* __restrict__ Wq,
+                                    const float* __restrict__ Ws, float* __restrict__ C, int M,
+                                    int N, int K) {
+  const long c = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= (long)M * N) return;
+  const int m = (int)(c / N), n = (int)(c % N);
+  const float* a = A + (size_t)m * K;
+  unsigned acc = 0;
+  if (DT == 8) {
+    const int8_t* w = reinterpret_cast<const int8_t*>(Wq) + (size_t)n * K;
+    for (int k = 0; k < K; ++k) acc += (unsigned)(trunc_scale(__ldg(a + k), 127.0f) * (int)w[k]);
+    C[c] = fmul(fdiv(__int2float_rn((int)acc), 127.0f), __ldg(Ws + n));
+  } else {
+    const uint8_t* w = Wq + (size_t)n * (K / 2);
+    for (int k = 0; k < K; k += 2) {
+      const uint8_t b = w[k >> 1];
+      acc += (unsigned)(trunc_scale(__ldg(a + k), 7.0f) * ((int)(b & 0xF) - 8));
+      acc += (unsigned)(trunc_scale(__ldg(a + k + 1), 7.0f) * ((int)(b >> 4) - 8));
+    }
+    C[c] = fmul(fdiv(__int2float_rn((int)acc), 7.0f), __ldg(Ws + n));
+  }
+}
+
+void launch_gemv_generic(int dtype, const float* A, const uint8_t* Wq, const float* Ws, float* C,
+                         int M, int N, int K, cudaStream_t st) {
+  const long total = (long)M * N;
+  if (total <= 0) return;
+  const unsigned grid = (unsigned)((total + 127) / 128);
+  if (dtype == 2) gemv_generic_kernel<8><<<grid, 128, 0, st>>>(A, Wq, Ws, C, M, N, K);
+  else gemv_generic_kernel<4><<<grid, 128, 0, st>>>(A, Wq, Ws, C, M, N, K);
+}
+
+// --------------------------------------------------------------------------
+// decode: fused gate/up GEMV + SiLU·up + re-truncation of h for the down
+// projection (test_model_trace.c:496-501). One warp item = GPW row indices of
+// one routed expert (each row index = one gate row and one up row), for every
+// slot routed to that expert; weights are read once per item.
+// --------------------------------------------------------------------------
+struct GateUpArgs {
+  const uint8_t* slab;
+  size_t stride, gq_off, uq_off, gs_off, us_off;
+  int F, D, rb, cpl, np, topk, items_per_expert;
+  const int* route;  // n_active | active | exp_off | slot_list
+  int E_local;
+  const uint8_t* xact; int xact_stride;
+  const int* xsum;
+  uint8_t* hact; int hact_stride;
+  int* hsum;
+  int* err;
+};
+
+template <int DT, int LPR>
+__global__ void __launch_bounds__(256) gateup_kernel(const GateUpArgs a) {
+  constexpr int GPW = 32 / LPR;
+  constexpr float S = DT == 8 ? 127.0f : 7.0f;
+  const int lane = threadIdx.x & 31, grp = lane / LPR, lig = lane % LPR;
+  const long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const RouteView r = route_view(const_cast<int*>(a.route), a.E_local);
+  const int u = (int)(w / a.items_per_expert);
+  if (u >= *r.n_active) return;
+  const int n = (int)(w % a.items_per_expert) * GPW + grp;
+  const bool ok = n < a.F;
+  const uint8_t* base = a.slab + (size_t)r.active[u] * a.stride;
+  const uint8_t* Wg = base + a.gq_off + (size_t)n * a.rb;
+  const uint8_t* Wu = base + a.uq_off + (size_t)n * a.rb;
+  uint4 wg[4], wu[4];
+  auto load = [&](int p) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = (p * a.cpl + i) * LPR + lig;
+      const bool v = i < a.cpl && ok;
+      wg[i] = v ? ldg_stream(Wg + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+      wu[i] = v ? ldg_stream(Wu + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  if (a.np == 1) load(0);
+  const float sg = ok ? __ldg(reinterpret_cast<const float*>(base + a.gs_off) + n) : 0.f;
+  const float su = ok ? __ldg(reinterpret_cast<const float*>(base + a.us_off) + n) : 0.f;
+  const int j0 = r.exp_off[u], j1 = r.exp_off[u + 1];
+  for (int j = j0; j < j1; ++j) {
+    const int s = r.slot_list[j];
+    const int t = s / a.topk;
+    const uint8_t* act = a.xact + (size_t)t * a.xact_stride;
+    int g0 = 0, g1 = 0, u0 = 0, u1 = 0;
+    for (int p = 0; p < a.np; ++p) {
+      if (a.np > 1) load(p);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (i >= a.cpl) break;
+        const int c = (p * a.cpl + i) * LPR + lig;
+        chunk_dot<DT>(wg[i], act, a.D, c, g0, g1);
+        chunk_dot<DT>(wu[i], act, a.D, c, u0, u1);
+      }
+    }
+    const int dg = group_sum<LPR>(lane_partial<DT>(g0, g1));
+    const int du = group_sum<LPR>(lane_partial<DT>(u0, u1));
+    if (lig == 0 && ok) {
+      const int as = DT == 4 ? __ldg(a.xsum + t) : 0;
+      const float g = dequant_out<DT>(dg, as, sg);
+      const float uu = dequant_out<DT>(du, as, su);
+      const float h = fmul(silu_ref(g), uu);        // silu then g *= u (:498-501)
+      const int ha = trunc_scale(h, S);             // down's activation truncation
+      uint8_t* hr = a.hact + (size_t)s * a.hact_stride;
+      if (DT == 8) {
+        if (ha < -32768 || ha > 32767) atomicOr(a.err, kErrRange);
+        hr[n] = (uint8_t)(ha & 0xFF);
+        hr[a.F + n] = (uint8_t)((ha >> 8) & 0xFF);
+      } else {
+        if (ha < -128 || ha > 127) atomicOr(a.err, kErrRange);
+        hr[q4_act_pos(n)] = (uint8_t)(ha & 0xFF);
+        atomicAdd(a.hsum + s, ha);
+      }
+    }
+  }
+}
+
+void launch_gateup(const LayerDev& L, const Workspace& ws, int T, int* err, cudaStream_t st) {
+  Geo g;
+  pick_geo(L.gu_rb, g);
+  GateUpArgs a{};
+  a.slab = L.slab; a.stride = L.expert_stride;
+  a.gq_off = L.gq_off; a.uq_off = L.uq_off; a.gs_off = L.gs_off; a.us_off = L.us_off;
+  a.F = L.F; a.D = L.D; a.rb = L.gu_rb; a.cpl = g.cpl; a.np = g.np; a.topk = L.topk;
+  const int gpw = 32 / g.lpr;
+  a.items_per_expert = (L.F + gpw - 1) / gpw;
+  const int E_local = L.e_end - L.e_begin;
+  a.route = ws.route; a.E_local = E_local;
+  a.xact = ws.xact; a.xact_stride = 2 * L.D; a.xsum = ws.xsum;
+  a.hact = ws.hact; a.hact_stride = 2 * L.F; a.hsum = ws.hsum; a.err = err;
+  const int max_experts = E_local < T * L.topk ? E_local : T * L.topk;
+  const long warps = (long)max_experts * a.items_per_expert;
+  const unsigned grid = (unsigned)((warps + 7) / 8);
+#define GU(DT)                                                                   \
+  switch (g.lpr) {                                                               \
+    case 1: gateup_kernel<DT, 1><<<grid, 256, 0, st>>>(a); break;                \
+    case 2: gateup_kernel<DT, 2><<<grid, 256, 0, st>>>(a); break;                \
+    case 4: gateup_kernel<DT, 4><<<grid, 256, 0, st>>>(a); break;                \
+    case 8: gateup_kernel<DT, 8><<<grid, 256, 0, st>>>(a); break;                \
+    case 16: gateup_kernel<DT, 16><<<grid, 256, 0, st>>>(a); break;              \
+    default: gateup_kernel<DT, 32><<<grid, 256, 0, st>>>(a); break;              \
+  }
+  if (L.dtype == 2) { GU(8) } else { GU(4) }
+#undef GU
+}
+
+// --------------------------------------------------------------------------
+// decode: down projection (test_model_trace.c:502-503) and, fused, the
+// k-ordered weighted combine + residual (:513, :517). The last warp to finish
+// a row block (an arrival counter per block reaches n_active) combines it.
+// --------------------------------------------------------------------------
+struct DownArgs {
+  const uint8_t* slab;
+  size_t stride, dq_off, ds_off;
+  int D, F, rb, cpl, np, topk, items_per_expert, T;
+  const int* route; int E_local;
+  const uint8_t* hact; int hact_stride;
+  const int* hsum;
+  float* y;
+  int* cnt;
+  const int* topk_idx;
+  const float* topk_p;
+  const float* xres;
+  float* out;
+  int fuse;
+};
+
+template <int DT, int LPR, int RPG>
+__global__ void __launch_bounds__(256) down_kernel(const DownArgs a) {
+  constexpr int GPW = 32 / LPR;
+  const int lane = threadIdx.x & 31, grp = lane / LPR, lig = lane % LPR;
+  const long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const RouteView r = route_view(const_cast<int*>(a.route), a.E_local);
+  const int na = *r.n_active;
+  const int u = (int)(w / a.items_per_expert);
+  if (u >= na) return;
+  const int item = (int)(w % a.items_per_expert);
+  const uint8_t* base = a.slab + (size_t)r.active[u] * a.stride;
+  const uint8_t* W = base + a.dq_off;
+  const float* S = reinterpret_cast<const float*>(base + a.ds_off);
+  int n[RPG];
+  bool ok[RPG];
+  float sc[RPG];
+#pragma unroll
+  for (int j = 0; j < RPG; ++j) {
+    n[j] = (item * GPW + grp) * RPG + j;
+    ok[j] = n[j] < a.D;
+    sc[j] = ok[j] ? __ldg(S + n[j]) : 0.f;
+  }
+  uint4 wr[RPG][4];
+  auto load = [&](int p) {
+#pragma unroll
+    for (int j = 0; j < RPG; ++j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = (p * a.cpl + i) * LPR + lig;
+        wr[j][i] = (i < a.cpl && ok[j]) ? ldg_stream(W + (size_t)n[j] * a.rb + (size_t)c * 16)
+                                        : make_uint4(0, 0, 0, 0);
+      }
+  };
+  if (a.np == 1) load(0);
+  const int j0 = r.exp_off[u], j1 = r.exp_off[u + 1];
+  for (int jj = j0; jj < j1; ++jj) {
+    const int s = r.slot_list[jj];
+    const uint8_t* act = a.hact + (size_t)s * a.hact_stride;
+    int a0[RPG], a1[RPG];
+#pragma unroll
+    for (int j = 0; j < RPG; ++j) a0[j] = a1[j] = 0;
+    for (int p = 0; p < a.np; ++p) {
+      if (a.np > 1) load(p);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (i >= a.cpl) break;
+        const int c = (p * a.cpl + i) * LPR + lig;
+#pragma unroll
+        for (int j = 0; j < RPG; ++j) chunk_dot<DT>(wr[j][i], act, a.F, c, a0[j], a1[j]);
+      }
+    }
+    const int as = DT == 4 ? __ldcg(a.hsum + s) : 0;
+#pragma unroll
+    for (int j = 0; j < RPG; ++j) {
+      const int v = group_sum<LPR>(lane_partial<DT>(a0[j], a1[j]));
+      if (lig == 0 && ok[j]) a.y[(size_t)s * a.D + n[j]] = dequant_out<DT>(v, as, sc[j]);
+    }
+  }
+  if (!a.fuse) return;
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = atomicAdd(a.cnt + item, 1) == na - 1;
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  constexpr int ROWS = GPW * RPG;
+  const int row0 = item * ROWS;
+  for (int q = lane; q < a.T * ROWS; q += 32) {
+    const int t = q / ROWS, nn = row0 + q % ROWS;
+    if (nn >= a.D) continue;
+    float acc = 0.0f;
+    for (int k = 0; k < a.topk; ++k) {
+      const int s = t * a.topk + k;
+      if (__ldcg(a.topk_idx + s) < 0) continue;
+      acc = fadd(acc, fmul(__ldcg(a.topk_p + s), __ldcg(a.y + (size_t)s * a.D + nn)));
+    }
+    const size_t o = (size_t)t * a.D + nn;
+    a.out[o] = fadd(a.xres[o], acc);
+  }
+  if (lane == 0) atomicExch(a.cnt + item, 0);
+}
+
+void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y, bool fuse_combine,
+                 const float* xres, float* out, cudaStream_t st) {
+  Geo g;
+  pick_geo(L.d_rb, g);
+  constexpr int RPG = 2;
+  DownArgs a{};
+  a.slab = L.slab; a.stride = L.expert_stride; a.dq_off = L.dq_off; a.ds_off = L.ds_off;
+  a.D = L.D; a.F = L.F; a.rb = L.d_rb; a.cpl = g.cpl; a.np = g.np; a.topk = L.topk; a.T = T;
+  const int rows_per_item = (32 / g.lpr) * RPG;
+  a.items_per_expert = (L.D + rows_per_item - 1) / rows_per_item;
+  const int E_local = L.e_end - L.e_begin;
+  a.route = ws.route; a.E_local = E_local;
+  a.hact = ws.hact; a.hact_stride = 2 * L.F; a.hsum = ws.hsum;
+  a.y = y; a.cnt = ws.cnt; a.topk_idx = ws.topk_idx; a.topk_p = ws.topk_p;
+  a.xres = xres; a.out = out; a.fuse = fuse_combine ? 1 : 0;
+  const int max_experts = E_local < T * L.topk ? E_local : T * L.topk;
+  const long warps = (long)max_experts * a.items_per_expert;
+  const unsigned grid = (unsigned)((warps + 7) / 8);
+#define DN(DT)                                                                   \
+  switch (g.lpr) {                                                               \
+    case 1: down_kernel<DT, 1, RPG><<<grid, 256, 0, st>>>(a); break;             \
+    case 2: down_kernel<DT, 2, RPG><<<grid, 256, 0, st>>>(a); break;             \
+    case 4: down_kernel<DT, 4, RPG><<<grid, 256, 0, st>>>(a); break;             \
+    case 8: down_kernel<DT, 8, RPG><<<grid, 256, 0, st>>>(a); break;             \
+    case 16: down_kernel<DT, 16, RPG><<<grid, 256, 0, st>>>(a); break;           \
+    default: down_kernel<DT, 32, RPG><<<grid, 256, 0, st>>>(a); break;           \
+  }
+  if (L.dtype == 2) { DN(8) } else { DN(4) }
+#undef DN
+}
+
+// k-ordered combine + residual as a separate pass (prefill, expert parallel)
+__global__ void combine_kernel(const float* __restrict__ y, const float* __restrict__ p,
+                               const float* xres, float* out, int T, int D, int K) {
+  const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= (long)T * D) return;
+  const int t = (int)(q / D), n = (int)(q % D);
+  float acc = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    const int s = t * K + k;
+    acc = fadd(acc, fmul(p[s], y[(size_t)s * D + n]));
+  }
+  out[q] = fadd(xres[q], acc);
+}
+
+void launch_combine(const float* y, const float* p, const float* xres, float* out, int T, int D,
+                    int K, cudaStream_t st) {
+  const long total = (long)T * D;
+  if (total <= 0) return;
+  combine_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(y, p, xres, out, T, D, K);
+}
+
+// --------------------------------------------------------------------------
+// rowwise quantisers, export.py:23-36 (bit-exact): s = max(amax,1e-8)/127 or
+// /7 in fp32; q = round-half-even(w / s) (Q4: clamp [-8,7], +8, pack pairs)
+// --------------------------------------------------------------------------
+template <int DT>
+__global__ void __launch_bounds__(256) quantize_rowwise_kernel(const float* __restrict__ W,
+                                                               int cols, void* q, float* s) {
+  const int r = blockIdx.x;
+  const float* w = W + (size_t)r * cols;
+  float amax = 0.0f;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) amax = fmaxf(amax, fabsf(w[c]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+    red[0] = fdiv(fmaxf(m, 1e-8f), DT == 8 ? 127.0f : 7.0f);
+  }
+  __syncthreads();
+  const float sc = red[0];
+  if (threadIdx.x == 0) s[r] = sc;
+  if (DT == 8) {
+    int8_t* qr = reinterpret_cast<int8_t*>(q) + (size_t)r * cols;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) qr[c] = (int8_t)__float2int_rn(fdiv(w[c], sc));
+  } else {
+    uint8_t* qr = reinterpret_cast<uint8_t*>(q) + (size_t)r * (cols / 2);
+    for (int c = threadIdx.x; c < cols / 2; c += blockDim.x) {
+      int v0 = __float2int_rn(fdiv(w[2 * c], sc)), v1 = __float2int_rn(fdiv(w[2 * c + 1], sc));
+      v0 = min(max(v0, -8), 7) + 8;
+      v1 = min(max(v1, -8), 7) + 8;
+      qr[c] = (uint8_t)(v0 | (v1 << 4));
+    }
+  }
+}
+
+void launch_quantize_rowwise(int dtype, const float* W, int rows, int cols, void* q, float* s,
+                             cudaStream_t st) {
+  if (rows <= 0) return;
+  if (dtype == 2) quantize_rowwise_kernel<8><<<rows, 256, 0, st>>>(W, cols, q, s);
+  else quantize_rowwise_kernel<4><<<rows, 256, 0, st>>>(W, cols, q, s);
+}
+
+// --------------------------------------------------------------------------
+// synthetic N(0, std²): sample i = Box-Muller of outputs 2i, 2i+1 of
+// splitmix64 seeded with `seed`, in double, rounded once to float
+// --------------------------------------------------------------------------
+__device__ inline uint64_t splitmix_at(uint64_t seed, uint64_t i) {
+  uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__global__ void synth_normal_kernel(uint64_t seed, uint64_t offset, size_t n, float std, float* out) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t j = offset + i;
+  const double u1 = (double)(splitmix_at(seed, 2 * j) >> 11) * 0x1.0p-53;
+  const double u2 = (double)(splitmix_at(seed, 2 * j + 1) >> 11) * 0x1.0p-53;
+  const double z = sqrt(-2.0 * log(1.0 - u1)) * cos(6.283185307179586 * u2);
+  out[i] = (float)(z * (double)std);
+}
+
+void launch_synth_normal(uint64_t seed, uint64_t offset, size_t n, float std, float* out,
+                         cudaStream_t st) {
+  if (!n) return;
+  synth_normal_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(seed, offset, n, std, out);
+}
+
+__global__ void zero_kernel(float* C, size_t n) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) C[i] = 0.0f;
+}
+void launch_zero_fill(float* C, size_t n, cudaStream_t st) {
+  if (!n) return;
+  zero_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(C, n);
+}
+
+}  // namespace moe

@@ -1,0 +1,89 @@
+// kernels.cuh — kernel launch interfaces shared by the .cu files of libmoe_cuda.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace moe {
+
+// Device-resident layer (one expert-parallel shard of one MoE layer).
+// Each local expert owns one slab of `expert_stride` bytes:
+//   [gate q | up q | down q | gate s | up s | down s], parts 128 B aligned.
+struct LayerDev {
+  int E = 0, D = 0, F = 0, dtype = 0, topk = 8;
+  int e_begin = 0, e_end = 0;         // this rank's experts [e_begin, e_end)
+  int gu_rb = 0, d_rb = 0;            // row bytes: gate/up (D or D/2), down (F or F/2)
+  uint8_t* slab = nullptr;
+  size_t expert_stride = 0;
+  size_t gq_off = 0, uq_off = 0, dq_off = 0, gs_off = 0, us_off = 0, ds_off = 0;
+  float* router_w = nullptr;          // [E][D]
+  float* router_b = nullptr;          // [E] or null
+  size_t bytes = 0;
+};
+
+// Per-call scratch of moe_ffn (capacity for up to cap_T tokens).
+struct Workspace {
+  int cap_T = 0, cap_D = 0, cap_E = 0, cap_F = 0, cap_K = 0;
+  float* logits = nullptr;    // [T][E]
+  int* topk_idx = nullptr;    // [T][K]
+  float* topk_p = nullptr;    // [T][K]
+  int* route = nullptr;       // n_active | active[E] | exp_off[E+1] | slot_list[T*K]
+  uint8_t* xact = nullptr;    // token activations, 2*D bytes per token
+  int* xsum = nullptr;        // [T]  Σ activation (Q4 zero-point correction)
+  uint8_t* hact = nullptr;    // slot activations, 2*F bytes per slot
+  int* hsum = nullptr;        // [T*K]
+  float* y = nullptr;         // [T*K][D]
+  int* cnt = nullptr;         // [D] combine arrival counters (kept zero between calls)
+  float* xn = nullptr;        // staging for host-pointer calls [T][D]
+  float* xo = nullptr;        // [T][D]
+};
+
+struct RouteView {
+  int* n_active; int* active; int* exp_off; int* slot_list;
+};
+__host__ __device__ inline RouteView route_view(int* route, int E) {
+  RouteView r;
+  r.n_active = route;
+  r.active = route + 1;
+  r.exp_off = route + 1 + E;
+  r.slot_list = route + 2 + 2 * E;
+  return r;
+}
+
+// ---- launchers (all asynchronous on `st`) ----
+// xact planes from fp32 rows: Q8 -> [lo K][hi K] per row, Q4 -> permuted K
+// bytes per row + rowsum. Sets err bit kErrRange on out-of-range values.
+void launch_quantize_act(const float* x, int M, int K, int dtype, uint8_t* act,
+                         int act_stride, int* asum, int* err, cudaStream_t st);
+// C[m][n] = sequential fp32 Σ_k A[m][k] W[n][k] (+ b[n]).
+void launch_f32_seq_matmul(const float* A, const float* W, const float* b,
+                           float* C, int M, int N, int K, cudaStream_t st);
+void launch_topk_softmax(const float* logits, int T, int E, int K, int* idx,
+                         float* p, cudaStream_t st);
+void launch_route_build(const int* idx, int T, int K, int e_begin, int e_end,
+                        int* route, int E_local, int* hsum, cudaStream_t st);
+// Fast warp GEMV over n_mat matrices: C[mat][m][n]. Returns false if the
+// shape has no fast-path geometry (caller uses the generic kernel).
+bool launch_gemv(int dtype, const uint8_t* const* Wq, const float* const* Ws,
+                 int n_mat, bool ptr_arrays_on_device, int N, int K,
+                 const uint8_t* act, int act_stride, const int* asum, int M,
+                 float* C, cudaStream_t st);
+void launch_gemv_generic(int dtype, const float* A, const uint8_t* Wq,
+                         const float* Ws, float* C, int M, int N, int K,
+                         cudaStream_t st);
+bool fast_geometry_ok(int dtype, int K);
+void launch_gateup(const LayerDev& L, const Workspace& ws, int T, int* err,
+                   cudaStream_t st);
+// down projection; if fuse_combine, also out[t] = xres[t] + Σ_k p y (k order)
+void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y,
+                 bool fuse_combine, const float* xres, float* out,
+                 cudaStream_t st);
+void launch_combine(const float* y, const float* p, const float* xres,
+                    float* out, int T, int D, int K, cudaStream_t st);
+void launch_quantize_rowwise(int dtype, const float* W, int rows, int cols,
+                             void* q, float* s, cudaStream_t st);
+void launch_synth_normal(uint64_t seed, uint64_t offset, size_t n, float std,
+                         float* out, cudaStream_t st);
+void launch_zero_fill(float* C, size_t n, cudaStream_t st);
+
+}  // namespace moe

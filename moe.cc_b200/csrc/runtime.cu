@@ -1,0 +1,676 @@
+// runtime.cu — host side of libmoe_cuda: the extern "C" boundary declared in
+// include/moe_cuda.h, device residency of the expert weights, the per-call
+// workspace and the orchestration of the fused MoE block.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/moe_cuda.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace moe {
+
+struct Alias { const void* dev; size_t bytes; };
+
+struct State {
+  bool init = false;
+  int device = 0, ep_world = 1, ep_rank = 0, sm_count = 0;
+  std::map<int, LayerDev> layers;
+  std::unordered_map<const void*, Alias> alias;  // host q/s pointer -> device copy
+  Workspace ws;
+  int* d_err = nullptr;                          // kernel-flagged errors
+  std::string last_error;
+  std::recursive_mutex mu;
+};
+
+static State g;
+
+static int set_err(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g.last_error = buf;
+  return code;
+}
+
+#define CU(call)                                                                         \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      return set_err(MOE_ERR_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                     __FILE__, __LINE__);                                                \
+  } while (0)
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+static int ensure_init() {
+  if (!g.init) return set_err(MOE_ERR_NOT_INIT, "moe_cuda_init() has not been called");
+  return MOE_OK;
+}
+
+// Grow the workspace to hold T tokens for a layer of shape (E, D, F, K).
+static int ensure_workspace(int T, int E, int D, int F, int K) {
+  Workspace& w = g.ws;
+  if (T <= w.cap_T && E <= w.cap_E && D <= w.cap_D && F <= w.cap_F && K <= w.cap_K) return MOE_OK;
+  const int nT = T > w.cap_T ? (T > 2 * w.cap_T ? T : 2 * w.cap_T) : w.cap_T;
+  const int nE = E > w.cap_E ? E : w.cap_E, nD = D > w.cap_D ? D : w.cap_D;
+  const int nF = F > w.cap_F ? F : w.cap_F, nK = K > w.cap_K ? K : w.cap_K;
+  CU(cudaDeviceSynchronize());
+  void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum,
+                  w.hact, w.hsum, w.y, w.cnt, w.xn, w.xo};
+  for (void* p : ptrs) if (p) cudaFree(p);
+  w = Workspace{};
+  const size_t TK = (size_t)nT * nK;
+#define ALLOC(field, bytes)                                                    \
+  do {                                                                         \
+    if (cudaMalloc((void**)&w.field, (bytes)) != cudaSuccess) {                \
+      w = Workspace{};                                                         \
+      return set_err(MOE_ERR_NOMEM, "workspace allocation of %zu bytes failed", \
+                     (size_t)(bytes));                                         \
+    }                                                                          \
+  } while (0)
+  ALLOC(logits, sizeof(float) * (size_t)nT * nE);
+  ALLOC(topk_idx, sizeof(int) * TK);
+  ALLOC(topk_p, sizeof(float) * TK);
+  ALLOC(route, sizeof(int) * (2 + 2 * (size_t)nE + TK));
+  ALLOC(xact, (size_t)2 * nD * nT);
+  ALLOC(xsum, sizeof(int) * (size_t)nT);
+  ALLOC(hact, (size_t)2 * nF * TK);
+  ALLOC(hsum, sizeof(int) * TK);
+  ALLOC(y, sizeof(float) * TK * nD);
+  ALLOC(cnt, sizeof(int) * (size_t)nD);
+  ALLOC(xn, sizeof(float) * (size_t)nT * nD);
+  ALLOC(xo, sizeof(float) * (size_t)nT * nD);
+#undef ALLOC
+  CU(cudaMemset(w.cnt, 0, sizeof(int) * (size_t)nD));
+  w.cap_T = nT; w.cap_E = nE; w.cap_D = nD; w.cap_F = nF; w.cap_K = nK;
+  return MOE_OK;
+}
+
+// Read (and clear) the kernel error flag. Synchronises the device.
+static int consume_device_error() {
+  int h = 0;
+  CU(cudaDeviceSynchronize());
+  CU(cudaMemcpy(&h, g.d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h) {
+    CU(cudaMemset(g.d_err, 0, sizeof(int)));
+    if (h & kErrRange)
+      return set_err(MOE_ERR_RANGE,
+                     "an activation was NaN/inf or outside the integer range of the "
+                     "quantised kernels (Q8: |x| < 258, Q4: trunc(7x) in [-128,127])");
+  }
+  return MOE_OK;
+}
+
+}  // namespace moe
+
+using namespace moe;
+
+// ---------------------------------------------------------------------------
+// scratch for the matmul_* entry points (grown on demand, never shrunk)
+// ---------------------------------------------------------------------------
+namespace moe {
+struct Buf { void* p = nullptr; size_t cap = 0; };
+static Buf s_A, s_C, s_W, s_S, s_act, s_asum;
+
+static int grow(Buf& b, size_t bytes) {
+  if (bytes <= b.cap) return MOE_OK;
+  if (b.p) { CU(cudaDeviceSynchronize()); cudaFree(b.p); b.p = nullptr; b.cap = 0; }
+  size_t n = align_up(bytes, 1 << 20);
+  if (cudaMalloc(&b.p, n) != cudaSuccess)
+    return set_err(MOE_ERR_NOMEM, "scratch allocation of %zu bytes failed", n);
+  b.cap = n;
+  return MOE_OK;
+}
+
+static const void* lookup_alias(const void* host) {
+  auto it = g.alias.find(host);
+  return it == g.alias.end() ? nullptr : it->second.dev;
+}
+
+static int check_mnk(int M, int N, int K) {
+  if (M < 0 || N < 0 || K < 0) return set_err(MOE_ERR_INVALID, "negative M/N/K (%d,%d,%d)", M, N, K);
+  return MOE_OK;
+}
+
+// Q8/Q4 matmul on device pointers. If `exact_fallback` is set the caller
+// checks the range flag and reruns on the generic kernel.
+static int matmul_q_dev(int dtype, const float* A, const void* Bq, const float* Bs, float* C,
+                        int M, int N, int K, cudaStream_t st) {
+  int rc = check_mnk(M, N, K);
+  if (rc) return rc;
+  if (dtype == MOE_DTYPE_Q4 && (K & 1))
+    return set_err(MOE_ERR_UNSUPPORTED,
+                   "Q4 with odd K=%d: the reference reads one byte past the packed row "
+                   "(kernels.c:108,116); not reproduced", K);
+  if ((long)M * N == 0) return MOE_OK;
+  if (K == 0) { launch_zero_fill(C, (size_t)M * N, st); return MOE_OK; }
+  const bool aligned = ((uintptr_t)Bq % 16 == 0);
+  if (aligned && fast_geometry_ok(dtype, K)) {
+    if ((rc = grow(s_act, (size_t)2 * K * M))) return rc;
+    if ((rc = grow(s_asum, sizeof(int) * (size_t)M))) return rc;
+    launch_quantize_act(A, M, K, dtype, (uint8_t*)s_act.p, 2 * K, (int*)s_asum.p, g.d_err, st);
+    const uint8_t* wq = (const uint8_t*)Bq;
+    launch_gemv(dtype, &wq, &Bs, 1, false, N, K, (const uint8_t*)s_act.p, 2 * K,
+                (const int*)s_asum.p, M, C, st);
+  } else {
+    launch_gemv_generic(dtype, A, (const uint8_t*)Bq, Bs, C, M, N, K, st);
+  }
+  CU(cudaGetLastError());
+  return MOE_OK;
+}
+
+// Host-pointer synchronous matmul (the reference's calling convention).
+static int matmul_q_host(int dtype, const float* A, const void* Bq, const float* Bs, float* C,
+                         int M, int N, int K) {
+  int rc = ensure_init();
+  if (rc) return rc;
+  if ((rc = check_mnk(M, N, K))) return rc;
+  if ((long)M * N == 0) return MOE_OK;
+  const size_t wbytes = (size_t)N * (dtype == MOE_DTYPE_Q8 ? K : K / 2);
+  const void* dq = lookup_alias(Bq);
+  const float* ds = (const float*)lookup_alias(Bs);
+  if (!dq || !ds) {
+    if ((rc = grow(s_W, wbytes + 16)) || (rc = grow(s_S, sizeof(float) * (size_t)N))) return rc;
+    CU(cudaMemcpy(s_W.p, Bq, wbytes, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(s_S.p, Bs, sizeof(float) * N, cudaMemcpyHostToDevice));
+    dq = s_W.p; ds = (const float*)s_S.p;
+  }
+  if ((rc = grow(s_A, sizeof(float) * (size_t)M * K + 16)) ||
+      (rc = grow(s_C, sizeof(float) * (size_t)M * N)))
+    return rc;
+  CU(cudaMemcpy(s_A.p, A, sizeof(float) * (size_t)M * K, cudaMemcpyHostToDevice));
+  if ((rc = matmul_q_dev(dtype, (const float*)s_A.p, dq, ds, (float*)s_C.p, M, N, K, 0))) return rc;
+  rc = consume_device_error();
+  if (rc == MOE_ERR_RANGE) {
+    // Large activations: rerun on the exact int32 kernel (any magnitude).
+    launch_gemv_generic(dtype, (const float*)s_A.p, (const uint8_t*)dq, ds, (float*)s_C.p, M, N, K, 0);
+    CU(cudaGetLastError());
+    rc = MOE_OK;
+  }
+  if (rc) return rc;
+  CU(cudaMemcpy(C, s_C.p, sizeof(float) * (size_t)M * N, cudaMemcpyDeviceToHost));
+  return MOE_OK;
+}
+
+static void die_on(int rc, const char* who) {
+  if (rc == MOE_OK) return;
+  fprintf(stderr, "libmoe_cuda: %s failed (%d): %s\n", who, rc, g.last_error.c_str());
+  abort();
+}
+}  // namespace moe
+
+extern "C" {
+
+int moe_cuda_init(int device, int ep_world, int ep_rank, const void* nccl_uid) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  if (nccl_uid) return set_err(MOE_ERR_UNSUPPORTED, "nccl_uid must be NULL");
+  if (ep_world < 1 || ep_rank < 0 || ep_rank >= ep_world)
+    return set_err(MOE_ERR_INVALID, "bad expert-parallel group (world %d rank %d)", ep_world, ep_rank);
+  if (g.init) {
+    if (device == g.device && ep_world == g.ep_world && ep_rank == g.ep_rank) return MOE_OK;
+    return set_err(MOE_ERR_INVALID, "already initialised on device %d (world %d rank %d)",
+                   g.device, g.ep_world, g.ep_rank);
+  }
+  CU(cudaSetDevice(device));
+  CU(cudaDeviceGetAttribute(&g.sm_count, cudaDevAttrMultiProcessorCount, device));
+  CU(cudaMalloc((void**)&g.d_err, sizeof(int)));
+  CU(cudaMemset(g.d_err, 0, sizeof(int)));
+  g.device = device; g.ep_world = ep_world; g.ep_rank = ep_rank;
+  g.init = true;
+  return MOE_OK;
+}
+
+int moe_cuda_shutdown(void) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  if (!g.init) return MOE_OK;
+  cudaDeviceSynchronize();
+  for (auto& kv : g.layers) {
+    cudaFree(kv.second.slab); cudaFree(kv.second.router_w);
+    if (kv.second.router_b) cudaFree(kv.second.router_b);
+  }
+  g.layers.clear();
+  g.alias.clear();
+  Workspace& w = g.ws;
+  void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum,
+                  w.hact, w.hsum, w.y, w.cnt, w.xn, w.xo};
+  for (void* p : ptrs) if (p) cudaFree(p);
+  w = Workspace{};
+  Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum};
+  for (Buf* b : bufs) { if (b->p) cudaFree(b->p); *b = Buf{}; }
+  cudaFree(g.d_err); g.d_err = nullptr;
+  g.init = false;
+  return MOE_OK;
+}
+
+const char* moe_cuda_last_error(void) { return g.last_error.c_str(); }
+
+int moe_cuda_check_status(void) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  int rc = ensure_init();
+  if (rc) return rc;
+  CU(cudaGetLastError());
+  return consume_device_error();
+}
+
+void matmul_f32_q8(const float* A, const int8_t* B_q, const float* B_s, float* C, int M, int N, int K) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  die_on(matmul_q_host(MOE_DTYPE_Q8, A, B_q, B_s, C, M, N, K), "matmul_f32_q8");
+}
+
+void matmul_f32_q4(const float* A, const uint8_t* B_q, const float* B_s, float* C, int M, int N, int K) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  die_on(matmul_q_host(MOE_DTYPE_Q4, A, B_q, B_s, C, M, N, K), "matmul_f32_q4");
+}
+
+static int matmul_f32_host(const float* A, const float* W, float* C, int M, int N, int K) {
+  int rc = ensure_init();
+  if (rc || (rc = check_mnk(M, N, K))) return rc;
+  if ((long)M * N == 0) return MOE_OK;
+  const float* dW = (const float*)lookup_alias(W);
+  if (!dW) {
+    if ((rc = grow(s_W, sizeof(float) * (size_t)N * K + 16))) return rc;
+    CU(cudaMemcpy(s_W.p, W, sizeof(float) * (size_t)N * K, cudaMemcpyHostToDevice));
+    dW = (const float*)s_W.p;
+  }
+  if ((rc = grow(s_A, sizeof(float) * (size_t)M * K + 16)) ||
+      (rc = grow(s_C, sizeof(float) * (size_t)M * N)))
+    return rc;
+  CU(cudaMemcpy(s_A.p, A, sizeof(float) * (size_t)M * K, cudaMemcpyHostToDevice));
+  launch_f32_seq_matmul((const float*)s_A.p, dW, nullptr, (float*)s_C.p, M, N, K, 0);
+  CU(cudaGetLastError());
+  CU(cudaMemcpy(C, s_C.p, sizeof(float) * (size_t)M * N, cudaMemcpyDeviceToHost));
+  return MOE_OK;
+}
+
+void matmul_adaptive(const float* A, const float* W_fp32, const void* W_q_ptr, float* C, int M,
+                     int N, int K) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  const QuantizedWeight* w = (const QuantizedWeight*)W_q_ptr;
+  int rc;
+  if (!w) rc = matmul_f32_host(A, W_fp32, C, M, N, K);
+  else if (w->dtype == MOE_DTYPE_Q8 || w->dtype == MOE_DTYPE_Q4)
+    rc = matmul_q_host(w->dtype, A, w->q, w->s, C, M, N, K);
+  else {
+    // unsupported dtype: zero output, as kernels.c:172-180
+    if (M > 0 && N > 0) memset(C, 0, sizeof(float) * (size_t)M * N);
+    rc = MOE_OK;
+  }
+  die_on(rc, "matmul_adaptive");
+}
+
+int moe_matmul_q8_dev(const float* A, const int8_t* B_q, const float* B_s, float* C, int M, int N,
+                      int K, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  int rc = ensure_init();
+  return rc ? rc : matmul_q_dev(MOE_DTYPE_Q8, A, B_q, B_s, C, M, N, K, (cudaStream_t)stream);
+}
+
+int moe_matmul_q4_dev(const float* A, const uint8_t* B_q, const float* B_s, float* C, int M, int N,
+                      int K, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  int rc = ensure_init();
+  return rc ? rc : matmul_q_dev(MOE_DTYPE_Q4, A, B_q, B_s, C, M, N, K, (cudaStream_t)stream);
+}
+
+int moe_matmul_f32_dev(const float* A, const float* W, float* C, int M, int N, int K, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  int rc = ensure_init();
+  if (rc || (rc = check_mnk(M, N, K))) return rc;
+  launch_f32_seq_matmul(A, W, nullptr, C, M, N, K, (cudaStream_t)stream);
+  CU(cudaGetLastError());
+  return MOE_OK;
+}
+
+int moe_matmul_batched_dev(const float* A, const void* const* W_q, const float* const* W_s, float* C,
+                           int n_mat, int N, int K, int dtype, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  int rc = ensure_init();
+  if (rc) return rc;
+  if (dtype != MOE_DTYPE_Q8 && dtype != MOE_DTYPE_Q4) return set_err(MOE_ERR_INVALID, "dtype %d", dtype);
+  if (n_mat <= 0 || N <= 0 || K <= 0) return set_err(MOE_ERR_INVALID, "empty batched matmul");
+  if (!fast_geometry_ok(dtype, K))
+    return set_err(MOE_ERR_UNSUPPORTED, "batched matmul needs K with 16-byte rows (K=%d)", K);
+  cudaStream_t st = (cudaStream_t)stream;
+  if ((rc = grow(s_act, (size_t)2 * K)) || (rc = grow(s_asum, sizeof(int)))) return rc;
+  launch_quantize_act(A, 1, K, dtype, (uint8_t*)s_act.p, 2 * K, (int*)s_asum.p, g.d_err, st);
+  launch_gemv(dtype, (const uint8_t* const*)W_q, W_s, n_mat, true, N, K, (const uint8_t*)s_act.p,
+              2 * K, (const int*)s_asum.p, 1, C, st);
+  CU(cudaGetLastError());
+  return MOE_OK;
+}
+
+int moe_quantize_rowwise_q8_dev(const float* W, int rows, int cols, int8_t* q, float* s, void* stream) {
+  if (rows < 0 || cols <= 0) return set_err(MOE_ERR_INVALID, "bad shape %dx%d", rows, cols);
+  launch_quantize_rowwise(MOE_DTYPE_Q8, W, rows, cols, q, s, (cudaStream_t)stream);
+  CU(cudaGetLastError());
+  return MOE_OK;
+}
+
+int moe_quantize_rowwise_q4_dev(const float* W, int rows, int cols, uint8_t* q, float* s, void* stream) {
+  if (rows < 0 || cols <= 0 || (cols & 1))
+    return set_err(MOE_ERR_INVALID, "Q4 needs an even column count (%dx%d)", rows, cols);
+  launch_quantize_rowwise(MOE_DTYPE_Q4, W, rows, cols, q, s, (cudaStream_t)stream);
+  CU(cudaGetLastError());
+  return MOE_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// weight residency + fused MoE block
+// ---------------------------------------------------------------------------
+namespace moe {
+
+static int validate_layer(const QuantizedWeight* Wg, const QuantizedWeight* Wu,
+                          const QuantizedWeight* Wd, int E, int* D, int* F, int* dtype) {
+  if (E <= 0 || !Wg || !Wu || !Wd) return set_err(MOE_ERR_INVALID, "empty layer (E=%d)", E);
+  *dtype = Wg[0].dtype; *F = Wg[0].rows; *D = Wg[0].cols;
+  if (*dtype != MOE_DTYPE_Q8 && *dtype != MOE_DTYPE_Q4)
+    return set_err(MOE_ERR_UNSUPPORTED, "expert dtype %d (only Q8=2 / Q4=3)", *dtype);
+  for (int e = 0; e < E; ++e) {
+    const QuantizedWeight* w[3] = {&Wg[e], &Wu[e], &Wd[e]};
+    for (int i = 0; i < 3; ++i) {
+      const int rows = i < 2 ? *F : *D, cols = i < 2 ? *D : *F;
+      if (w[i]->dtype != *dtype || w[i]->rows != rows || w[i]->cols != cols || !w[i]->q || !w[i]->s)
+        return set_err(MOE_ERR_INVALID, "expert %d projection %d: shape/dtype mismatch", e, i);
+    }
+  }
+  if (!fast_geometry_ok(*dtype, *D) || !fast_geometry_ok(*dtype, *F))
+    return set_err(MOE_ERR_UNSUPPORTED,
+                   "moe_ffn needs D and F whose packed rows are multiples of 16 bytes "
+                   "(D=%d F=%d dtype %d)", *D, *F, *dtype);
+  return MOE_OK;
+}
+
+static int upload_layer(int layer, const QuantizedWeight* Wg, const QuantizedWeight* Wu,
+                        const QuantizedWeight* Wd, const float* router_w, const float* router_b,
+                        int E, cudaMemcpyKind kind) {
+  int rc = ensure_init();
+  if (rc) return rc;
+  int D, F, dtype;
+  if ((rc = validate_layer(Wg, Wu, Wd, E, &D, &F, &dtype))) return rc;
+  if (!router_w) return set_err(MOE_ERR_INVALID, "router_w is NULL");
+  if (g.layers.count(layer)) moe_cuda_free_layer(layer);
+  LayerDev L;
+  L.E = E; L.D = D; L.F = F; L.dtype = dtype; L.topk = 8;
+  L.e_begin = (int)((long)E * g.ep_rank / g.ep_world);
+  L.e_end = (int)((long)E * (g.ep_rank + 1) / g.ep_world);
+  L.gu_rb = dtype == MOE_DTYPE_Q8 ? D : D / 2;
+  L.d_rb = dtype == MOE_DTYPE_Q8 ? F : F / 2;
+  const size_t gub = (size_t)F * L.gu_rb, db = (size_t)D * L.d_rb;
+  L.gq_off = 0;
+  L.uq_off = align_up(gub, 128);
+  L.dq_off = L.uq_off + align_up(gub, 128);
+  L.gs_off = L.dq_off + align_up(db, 128);
+  L.us_off = L.gs_off + align_up(sizeof(float) * F, 128);
+  L.ds_off = L.us_off + align_up(sizeof(float) * F, 128);
+  L.expert_stride = align_up(L.ds_off + sizeof(float) * D, 128);
+  const int El = L.e_end - L.e_begin;
+  L.bytes = L.expert_stride * (size_t)(El > 0 ? El : 0);
+  if (El > 0 && cudaMalloc((void**)&L.slab, L.bytes) != cudaSuccess)
+    return set_err(MOE_ERR_NOMEM, "layer %d: %zu bytes of expert slabs", layer, L.bytes);
+  if (cudaMalloc((void**)&L.router_w, sizeof(float) * (size_t)E * D) != cudaSuccess) {
+    cudaFree(L.slab);
+    return set_err(MOE_ERR_NOMEM, "layer %d router", layer);
+  }
+  if (router_b && cudaMalloc((void**)&L.router_b, sizeof(float) * E) != cudaSuccess) {
+    cudaFree(L.slab); cudaFree(L.router_w);
+    return set_err(MOE_ERR_NOMEM, "layer %d router bias", layer);
+  }
+  g.layers[layer] = L;  // registered before the copies so free_layer cleans up on error
+  CU(cudaMemcpy(L.router_w, router_w, sizeof(float) * (size_t)E * D, kind));
+  if (router_b) CU(cudaMemcpy(L.router_b, router_b, sizeof(float) * E, kind));
+  for (int e = L.e_begin; e < L.e_end; ++e) {
+    uint8_t* base = L.slab + (size_t)(e - L.e_begin) * L.expert_stride;
+    struct Part { const void* src; size_t off, bytes; } parts[6] = {
+        {Wg[e].q, L.gq_off, gub}, {Wu[e].q, L.uq_off, gub}, {Wd[e].q, L.dq_off, db},
+        {Wg[e].s, L.gs_off, sizeof(float) * F}, {Wu[e].s, L.us_off, sizeof(float) * F},
+        {Wd[e].s, L.ds_off, sizeof(float) * D}};
+    for (const Part& p : parts) {
+      CU(cudaMemcpy(base + p.off, p.src, p.bytes, kind));
+      if (kind == cudaMemcpyHostToDevice) g.alias[p.src] = Alias{base + p.off, p.bytes};
+    }
+  }
+  if (kind == cudaMemcpyHostToDevice) g.alias[router_w] = Alias{L.router_w, sizeof(float) * (size_t)E * D};
+  return MOE_OK;
+}
+
+// Optional per-kernel timing of moe_ffn (bench.py uses it for the roofline):
+// events recorded on the launching stream around each launch.
+struct ProfRec { const char* name; cudaEvent_t a, b; };
+static bool g_prof = false;
+static std::vector<ProfRec> g_prof_pending;
+static std::map<std::string, std::pair<double, long>> g_prof_acc;
+
+template <class F>
+static void timed(const char* name, cudaStream_t st, F&& launch) {
+  if (!g_prof) { launch(); return; }
+  ProfRec r{name, nullptr, nullptr};
+  cudaEventCreate(&r.a); cudaEventCreate(&r.b);
+  cudaEventRecord(r.a, st);
+  launch();
+  cudaEventRecord(r.b, st);
+  g_prof_pending.push_back(r);
+}
+
+static void prof_drain() {
+  for (ProfRec& r : g_prof_pending) {
+    float ms = 0.f;
+    cudaEventSynchronize(r.b);
+    cudaEventElapsedTime(&ms, r.a, r.b);
+    auto& acc = g_prof_acc[r.name];
+    acc.first += ms; acc.second += 1;
+    cudaEventDestroy(r.a); cudaEventDestroy(r.b);
+  }
+  g_prof_pending.clear();
+}
+
+// Router + top-k + routing lists + token activation truncation.
+static void route_tokens(const LayerDev& L, const float* xn, int T, cudaStream_t st) {
+  const Workspace& w = g.ws;
+  timed("quantize_act", st, [&] {
+    launch_quantize_act(xn, T, L.D, L.dtype, w.xact, 2 * L.D, w.xsum, g.d_err, st);
+  });
+  timed("router_logits", st, [&] {
+    launch_f32_seq_matmul(xn, L.router_w, L.router_b, w.logits, T, L.E, L.D, st);
+  });
+  timed("topk_softmax", st, [&] {
+    launch_topk_softmax(w.logits, T, L.E, L.topk, w.topk_idx, w.topk_p, st);
+  });
+  timed("route_build", st, [&] {
+    launch_route_build(w.topk_idx, T, L.topk, L.e_begin, L.e_end, w.route, L.e_end - L.e_begin,
+                       L.dtype == MOE_DTYPE_Q4 ? w.hsum : nullptr, st);
+  });
+}
+
+static int get_layer(int layer, const LayerDev** out) {
+  int rc = ensure_init();
+  if (rc) return rc;
+  auto it = g.layers.find(layer);
+  if (it == g.layers.end()) return set_err(MOE_ERR_NOT_INIT, "layer %d was not uploaded", layer);
+  *out = &it->second;
+  return MOE_OK;
+}
+
+// Tokens at or below this count use the fused down+combine epilogue.
+constexpr int kFuseCombineMaxT = 64;
+
+}  // namespace moe
+
+extern "C" {
+
+int moe_cuda_upload_layer(int layer, const QuantizedWeight* Wg, const QuantizedWeight* Wu,
+                          const QuantizedWeight* Wd, const float* router_w, const float* router_b,
+                          int E) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  return upload_layer(layer, Wg, Wu, Wd, router_w, router_b, E, cudaMemcpyHostToDevice);
+}
+
+int moe_cuda_upload_layer_dev(int layer, const QuantizedWeight* Wg, const QuantizedWeight* Wu,
+                              const QuantizedWeight* Wd, const float* router_w,
+                              const float* router_b, int E) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  return upload_layer(layer, Wg, Wu, Wd, router_w, router_b, E, cudaMemcpyDeviceToDevice);
+}
+
+int moe_cuda_free_layer(int layer) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  auto it = g.layers.find(layer);
+  if (it == g.layers.end()) return set_err(MOE_ERR_NOT_INIT, "layer %d was not uploaded", layer);
+  cudaDeviceSynchronize();
+  LayerDev& L = it->second;
+  for (auto a = g.alias.begin(); a != g.alias.end();) {
+    const uint8_t* d = (const uint8_t*)a->second.dev;
+    const bool in_slab = L.slab && d >= L.slab && d < L.slab + L.bytes;
+    if (in_slab || d == (const uint8_t*)L.router_w) a = g.alias.erase(a);
+    else ++a;
+  }
+  cudaFree(L.slab); cudaFree(L.router_w);
+  if (L.router_b) cudaFree(L.router_b);
+  g.layers.erase(it);
+  return MOE_OK;
+}
+
+size_t moe_cuda_layer_bytes(int layer) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  auto it = g.layers.find(layer);
+  return it == g.layers.end() ? 0 : it->second.bytes;
+}
+
+int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_idx_out,
+            float* topk_p_out, int flags, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  const LayerDev* Lp;
+  int rc = get_layer(layer, &Lp);
+  if (rc) return rc;
+  const LayerDev& L = *Lp;
+  if (T < 0) return set_err(MOE_ERR_INVALID, "T=%d", T);
+  if (T == 0) return MOE_OK;
+  if (g.ep_world > 1)
+    return set_err(MOE_ERR_INVALID, "expert-parallel run: use moe_ffn_partial + moe_ffn_combine");
+  if ((rc = ensure_workspace(T, L.E, L.D, L.F, L.topk))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool host = flags & MOE_FFN_HOST_PTRS;
+  const Workspace& w = g.ws;
+  const size_t xb = sizeof(float) * (size_t)T * L.D;
+  const float* xn = x_norm2;
+  float* xo = x_inout;
+  if (host) {
+    CU(cudaMemcpyAsync(w.xn, x_norm2, xb, cudaMemcpyHostToDevice, st));
+    CU(cudaMemcpyAsync(w.xo, x_inout, xb, cudaMemcpyHostToDevice, st));
+    xn = w.xn; xo = w.xo;
+  }
+  route_tokens(L, xn, T, st);
+  timed("gateup", st, [&] { launch_gateup(L, w, T, g.d_err, st); });
+  const bool fuse = T <= kFuseCombineMaxT;
+  timed("down", st, [&] { launch_down(L, w, T, w.y, fuse, xo, xo, st); });
+  if (!fuse) timed("combine", st, [&] { launch_combine(w.y, w.topk_p, xo, xo, T, L.D, L.topk, st); });
+  CU(cudaGetLastError());
+  const size_t kb = sizeof(int) * (size_t)T * L.topk;
+  const cudaMemcpyKind out_kind = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+  if (topk_idx_out) CU(cudaMemcpyAsync(topk_idx_out, w.topk_idx, kb, out_kind, st));
+  if (topk_p_out) CU(cudaMemcpyAsync(topk_p_out, w.topk_p, kb, out_kind, st));
+  if (host) {
+    CU(cudaMemcpyAsync(x_inout, xo, xb, cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    return consume_device_error();
+  }
+  return MOE_OK;
+}
+
+int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots, int* topk_idx_out,
+                    float* topk_p_out, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  const LayerDev* Lp;
+  int rc = get_layer(layer, &Lp);
+  if (rc) return rc;
+  const LayerDev& L = *Lp;
+  if (T < 0) return set_err(MOE_ERR_INVALID, "T=%d", T);
+  if (T == 0) return MOE_OK;
+  if ((rc = ensure_workspace(T, L.E, L.D, L.F, L.topk))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const Workspace& w = g.ws;
+  const size_t TK = (size_t)T * L.topk;
+  CU(cudaMemsetAsync(y_slots, 0, sizeof(float) * TK * L.D, st));
+  route_tokens(L, x_norm2, T, st);
+  if (L.e_end > L.e_begin) {
+    timed("gateup", st, [&] { launch_gateup(L, w, T, g.d_err, st); });
+    timed("down", st, [&] { launch_down(L, w, T, y_slots, false, nullptr, nullptr, st); });
+  }
+  if (topk_idx_out) CU(cudaMemcpyAsync(topk_idx_out, w.topk_idx, sizeof(int) * TK, cudaMemcpyDeviceToDevice, st));
+  if (topk_p_out) CU(cudaMemcpyAsync(topk_p_out, w.topk_p, sizeof(float) * TK, cudaMemcpyDeviceToDevice, st));
+  CU(cudaGetLastError());
+  return MOE_OK;
+}
+
+int moe_ffn_combine(const float* y_slots, const float* topk_p, float* x_inout, int T, int D,
+                    int top_k, void* stream) {
+  if (T < 0 || D <= 0 || top_k <= 0) return set_err(MOE_ERR_INVALID, "bad combine shape");
+  launch_combine(y_slots, topk_p, x_inout, x_inout, T, D, top_k, (cudaStream_t)stream);
+  CU(cudaGetLastError());
+  return MOE_OK;
+}
+
+static inline uint64_t splitmix_at_host(uint64_t seed, uint64_t i) {
+  uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+void moe_synth_normal_host(uint64_t seed, uint64_t offset, size_t n, float std, float* out) {
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < (long long)n; ++i) {
+    const uint64_t j = offset + (uint64_t)i;
+    const double u1 = (double)(splitmix_at_host(seed, 2 * j) >> 11) * 0x1.0p-53;
+    const double u2 = (double)(splitmix_at_host(seed, 2 * j + 1) >> 11) * 0x1.0p-53;
+    const double z = sqrt(-2.0 * log(1.0 - u1)) * cos(6.283185307179586 * u2);
+    out[i] = (float)(z * (double)std);
+  }
+}
+
+int moe_synth_normal_dev(uint64_t seed, uint64_t offset, size_t n, float std, float* out,
+                         void* stream) {
+  launch_synth_normal(seed, offset, n, std, out, (cudaStream_t)stream);
+  CU(cudaGetLastError());
+  return MOE_OK;
+}
+
+}  // extern "C"
+
+extern "C" {
+int moe_cuda_profile(int enable) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  prof_drain();
+  g_prof = enable != 0;
+  if (enable) g_prof_acc.clear();
+  return MOE_OK;
+}
+
+int moe_cuda_profile_read(int max_kernels, char* names, int name_len, double* total_ms, long* launches) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  prof_drain();
+  int i = 0;
+  for (auto& kv : g_prof_acc) {
+    if (i >= max_kernels) break;
+    snprintf(names + (size_t)i * name_len, (size_t)name_len, "%s", kv.first.c_str());
+    total_ms[i] = kv.second.first;
+    launches[i] = kv.second.second;
+    ++i;
+  }
+  return i;
+}
+}  // extern "C"

@@ -1,0 +1,111 @@
+"""Generate tests/golden/*.npz from the REFERENCE itself.
+
+Run in a container where the reference sources are present (default
+/root/reference, override with MOE_REF_DIR) after `make -C oracle`:
+
+    python tests/golden/make_golden.py
+
+* quant.npz  — export._rowwise_q8 / _rowwise_q4 (export.py:23-36), imported
+  from the reference and run on seeded and hand-made edge-case rows.
+* gemv.npz   — the reference's matmul_adaptive (kernels.c:149-181, compiled
+  from source into oracle/_ref) on config C1 (768x2048, Q8 and Q4) and on
+  small ragged shapes.
+* moe_small.npz — the reference's layer_forward_f32 MoE block
+  (test_model_trace.c:463-517, via oracle/ref_shim.c) on a small seeded layer.
+
+Inputs come from the counter-based normal stream moe_synth_normal_host of
+libmoe_cuda.so (host code, no GPU needed), so tests can rebuild them.
+"""
+import hashlib
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "moe.cc_b200"))
+REF_DIR = os.environ.get("MOE_REF_DIR", "/root/reference")
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+
+def synth(seed, n, std):
+    import moe_cuda as mc
+    return mc.synth_normal_host(seed, n, std)
+
+
+def edge_rows():
+    """Rows that hit round-half-even ties, the 1e-8 clamp and the Q4 clamp."""
+    r0 = np.zeros(64, np.float32)                                  # all-zero row
+    r1 = np.array([127.0] + [k + 0.5 for k in range(-31, 32)], np.float32)  # s=1 ties (Q8)
+    r2 = np.array([7.0] + [((k % 15) - 7) + 0.5 for k in range(63)], np.float32)  # s=1 ties (Q4)
+    r3 = np.full(64, 1e-12, np.float32)                            # below the clamp
+    r4 = np.linspace(-3.0, 3.0, 64).astype(np.float32)
+    return np.stack([r0, r1, r2, r3, r4])
+
+
+def main():
+    sys.path.insert(0, REF_DIR)
+    import torch
+    import export  # the reference's exporter (its quantisers)
+    from oracle.oracle import Ref
+
+    ref = Ref()
+    # ---- quantisers ----
+    Wq = np.concatenate([synth(11, 8 * 64, 0.02).reshape(8, 64), edge_rows()])
+    s8, q8 = export._rowwise_q8(torch.from_numpy(Wq))
+    s4, q4 = export._rowwise_q4(torch.from_numpy(Wq))
+    np.savez(os.path.join(OUT, "quant.npz"), W=Wq, s8=s8.numpy(), q8=q8.numpy(),
+             s4=s4.numpy(), q4=q4.numpy())
+
+    # ---- GEMV: config C1 + small ragged shapes ----
+    g = {}
+    W = synth(1, 768 * 2048, 0.02).reshape(768, 2048)
+    x = synth(2, 2048, 1.0).reshape(1, 2048)
+    for dt, fn in ((2, export._rowwise_q8), (3, export._rowwise_q4)):
+        s, q = fn(torch.from_numpy(W))
+        s, q = s.numpy(), q.numpy()
+        g[f"c1_y_{dt}"] = ref.matmul(x, q, s, 768, 2048, dt)[0]
+        g[f"c1_qsha_{dt}"] = np.frombuffer(hashlib.sha256(q.tobytes() + s.tobytes()).digest(), np.uint8)
+    for (M, N, K) in ((3, 40, 96), (1, 17, 64), (5, 8, 2)):
+        Ws = synth(21 + K, N * K, 0.02).reshape(N, K)
+        A = synth(22 + K, M * K, 1.0).reshape(M, K)
+        for dt, fn in ((2, export._rowwise_q8), (3, export._rowwise_q4)):
+            s, q = fn(torch.from_numpy(Ws))
+            g[f"y_{M}_{N}_{K}_{dt}"] = ref.matmul(A, q.numpy(), s.numpy(), N, K, dt)
+        g[f"y_{M}_{N}_{K}_0"] = ref.matmul(A, Ws, None, N, K, 0)
+    np.savez(os.path.join(OUT, "gemv.npz"), **g)
+
+    # ---- small MoE layer through the reference's layer_forward_f32 ----
+    m = {}
+    E, D, F, T = 16, 256, 64, 5
+    for dt, fn, bias in ((2, export._rowwise_q8, False), (3, export._rowwise_q4, True)):
+        L = small_layer(E, D, F, dt, bias, fn, torch)
+        xin = synth(40 + dt, T * D, 1.0).reshape(T, D)
+        xo, xn, lg, idx, p = ref.moe_layer(xin, L)
+        m.update({f"x_{dt}": xin, f"xo_{dt}": xo, f"xn_{dt}": xn, f"logits_{dt}": lg,
+                  f"idx_{dt}": idx, f"p_{dt}": p})
+    np.savez(os.path.join(OUT, "moe_small.npz"), **m)
+    print("golden fixtures written to", OUT)
+
+
+def small_layer(E, D, F, dt, bias, quant, torch=None):
+    """Seeded small layer; `quant` maps a [rows, cols] float32 array to (s, q)."""
+    L = {"dtype": dt, "topk": 8,
+         "router_w": synth(30 + dt, E * D, 0.02).reshape(E, D)}
+    L["router_b"] = synth(31 + dt, E, 1.0) if bias else None
+    shapes = {"g": (F, D), "u": (F, D), "d": (D, F)}
+    for j, nm in enumerate("gud"):
+        rows, cols = shapes[nm]
+        ss, qs = [], []
+        for e in range(E):
+            w = synth(1000 * dt + 3 * e + j, rows * cols, 0.02).reshape(rows, cols)
+            s, q = quant(torch.from_numpy(w) if torch is not None else w)
+            ss.append(np.asarray(s)); qs.append(np.asarray(q))
+        L[nm + "s"] = np.ascontiguousarray(np.stack(ss))
+        L[nm + "q"] = np.ascontiguousarray(np.stack(qs))
+    return L
+
+
+if __name__ == "__main__":
+    main()
