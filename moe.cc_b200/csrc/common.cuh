@@ -99,6 +99,6 @@ __host__ __device__ __forceinline__ int q4_act_pos(int k) {
 }
 
 // Error flag bits written by kernels (read by the host).
-enum : int { kErrRange = 1 };
+enum : int { kErrRange = 1, kErrTimeout = 2 };
 
 }  // namespace moe

@@ -156,16 +156,87 @@ __global__ void __launch_bounds__(32) f32_seq_kernel(const float* __restrict__ A
   C[c] = acc;
 }
 
+// Tiled form for the router: a CTA owns 16 experts x 16 tokens (one chain per
+// thread); K is staged through shared memory in tiles of 256 with coalesced
+// float4 loads, the next tile prefetched into registers while the current one
+// is consumed. Each chain still adds its products one by one in k order.
+constexpr int kRT = 16, kRE = 16, kRK = 128, kRPad = kRK + 4;
+
+__global__ void __launch_bounds__(256) f32_seq_tiled_kernel(const float* __restrict__ A,
+                                                           const float* __restrict__ W,
+                                                           const float* __restrict__ b,
+                                                           float* __restrict__ C, int M, int N,
+                                                           int K) {
+  __shared__ __align__(16) float xs[2][kRT][kRPad];
+  __shared__ __align__(16) float ws[2][kRE][kRPad];
+  const int tid = threadIdx.x;
+  const int tt = tid / kRE, et = tid % kRE;
+  const int m0 = blockIdx.y * kRT, n0 = blockIdx.x * kRE;
+  // loader mapping: 16 rows x 32 float4 per tile; thread loads 2 float4 of each
+  const int lrow = tid / 16, lcol = (tid % 16) * 2;   // 2 consecutive float4 per thread
+  float4 rx[2], rw[2];
+  auto gload = [&](int kt) {
+    const int k0 = kt * kRK;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int kk = k0 + (lcol + i) * 4;
+      const int m = m0 + lrow, n = n0 + lrow;
+      rx[i] = (m < M && kk < K) ? __ldg(reinterpret_cast<const float4*>(A + (size_t)m * K + kk))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+      rw[i] = (n < N && kk < K) ? __ldg(reinterpret_cast<const float4*>(W + (size_t)n * K + kk))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto sstore = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      *reinterpret_cast<float4*>(&xs[buf][lrow][(lcol + i) * 4]) = rx[i];
+      *reinterpret_cast<float4*>(&ws[buf][lrow][(lcol + i) * 4]) = rw[i];
+    }
+  };
+  const int ntiles = (K + kRK - 1) / kRK;
+  float acc = 0.0f;
+  gload(0);
+  sstore(0);
+  __syncthreads();
+  for (int kt = 0; kt < ntiles; ++kt) {
+    const int buf = kt & 1;
+    if (kt + 1 < ntiles) gload(kt + 1);
+    const int kn = min(kRK, K - kt * kRK);
+    const float* xr = xs[buf][tt];
+    const float* wr = ws[buf][et];
+    for (int k = 0; k < kn; k += 4) {
+      const float4 xv = *reinterpret_cast<const float4*>(xr + k);
+      const float4 wv = *reinterpret_cast<const float4*>(wr + k);
+      acc = fadd(acc, fmul(xv.x, wv.x));
+      acc = fadd(acc, fmul(xv.y, wv.y));
+      acc = fadd(acc, fmul(xv.z, wv.z));
+      acc = fadd(acc, fmul(xv.w, wv.w));
+    }
+    if (kt + 1 < ntiles) {
+      sstore(buf ^ 1);
+    }
+    __syncthreads();
+  }
+  const int m = m0 + tt, n = n0 + et;
+  if (m < M && n < N) {
+    if (b) acc = fadd(acc, __ldg(b + n));
+    C[(size_t)m * N + n] = acc;
+  }
+}
+
 void launch_f32_seq_matmul(const float* A, const float* W, const float* b, float* C, int M, int N,
                            int K, cudaStream_t st) {
   const long total = (long)M * N;
   if (total <= 0) return;
-  const bool vec = (K % 4 == 0) && ((uintptr_t)A % 16 == 0) && ((uintptr_t)W % 16 == 0);
+  const bool aligned = ((uintptr_t)A % 16 == 0) && ((uintptr_t)W % 16 == 0);
+  if (K % 4 == 0 && aligned) {
+    dim3 grid((N + kRE - 1) / kRE, (M + kRT - 1) / kRT);
+    f32_seq_tiled_kernel<<<grid, 256, 0, st>>>(A, W, b, C, M, N, K);
+    return;
+  }
   const unsigned grid = (unsigned)((total + 31) / 32);
-  if (vec)
-    f32_seq_kernel<true><<<grid, 32, 0, st>>>(A, W, b, C, M, N, K);
-  else
-    f32_seq_kernel<false><<<grid, 32, 0, st>>>(A, W, b, C, M, N, K);
+  f32_seq_kernel<false><<<grid, 32, 0, st>>>(A, W, b, C, M, N, K);
 }
 
 // --------------------------------------------------------------------------
@@ -200,10 +271,70 @@ __global__ void topk_softmax_kernel(const float* __restrict__ logits, int T, int
   }
 }
 
+// Warp per token: K rounds of a warp arg-max (larger value first, lower
+// expert index on ties; NaN and -inf never chosen) — the same list topk_desc's
+// insertion produces — then the softmax of :481-487 on lane 0.
+constexpr int kTopkMaxPerLane = 8;   // E <= 256
+
+__global__ void __launch_bounds__(256) topk_softmax_warp_kernel(const float* __restrict__ logits,
+                                                               int T, int E, int K,
+                                                               int* __restrict__ idx,
+                                                               float* __restrict__ p) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  float v[kTopkMaxPerLane];
+  const float* x = logits + (size_t)t * E;
+#pragma unroll
+  for (int i = 0; i < kTopkMaxPerLane; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? x[e] : -INFINITY;
+  }
+  float val[kMaxTopK];
+  int id[kMaxTopK];
+  for (int r = 0; r < K; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kTopkMaxPerLane; ++i) {
+      const int e = lane + 32 * i;
+      if (v[i] > bv) { bv = v[i]; bi = e; }   // ascending e: first max kept
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    const bool found = bi != 0x7fffffff;
+    val[r] = found ? bv : -INFINITY;
+    id[r] = found ? bi : -1;
+    if (found && (bi & 31) == lane) {
+#pragma unroll
+      for (int i = 0; i < kTopkMaxPerLane; ++i)
+        if (lane + 32 * i == bi) v[i] = -INFINITY;
+    }
+  }
+  if (lane != 0) return;
+  float mx = val[0];
+  for (int i = 1; i < K; ++i) if (val[i] > mx) mx = val[i];
+  float sum = 0.0f;
+  for (int i = 0; i < K; ++i) { val[i] = exp_f32(__fsub_rn(val[i], mx)); sum = fadd(sum, val[i]); }
+  const float inv = fdiv(1.0f, fadd(sum, 1e-9f));
+  for (int i = 0; i < K; ++i) {
+    idx[(size_t)t * K + i] = id[i];
+    p[(size_t)t * K + i] = fmul(val[i], inv);
+  }
+}
+
 void launch_topk_softmax(const float* logits, int T, int E, int K, int* idx, float* p,
                          cudaStream_t st) {
   if (T <= 0) return;
-  topk_softmax_kernel<<<(T + 127) / 128, 128, 0, st>>>(logits, T, E, K, idx, p);
+  if (E <= 32 * kTopkMaxPerLane) {
+    topk_softmax_warp_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, T, E, K, idx, p);
+  } else {
+    topk_softmax_kernel<<<(T + 127) / 128, 128, 0, st>>>(logits, T, E, K, idx, p);
+  }
 }
 
 // --------------------------------------------------------------------------

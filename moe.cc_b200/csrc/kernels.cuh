@@ -87,3 +87,4 @@ void launch_synth_normal(uint64_t seed, uint64_t offset, size_t n, float std,
 void launch_zero_fill(float* C, size_t n, cudaStream_t st);
 
 }  // namespace moe
+

@@ -110,6 +110,8 @@ static int consume_device_error() {
       return set_err(MOE_ERR_RANGE,
                      "an activation was NaN/inf or outside the integer range of the "
                      "quantised kernels (Q8: |x| < 258, Q4: trunc(7x) in [-128,127])");
+    if (h & kErrTimeout)
+      return set_err(MOE_ERR_CUDA, "a pipelined kernel gave up waiting on a copy (bounded wait)");
   }
   return MOE_OK;
 }
@@ -164,7 +166,7 @@ static int matmul_q_dev(int dtype, const float* A, const void* Bq, const float* 
     launch_quantize_act(A, M, K, dtype, (uint8_t*)s_act.p, 2 * K, (int*)s_asum.p, g.d_err, st);
     const uint8_t* wq = (const uint8_t*)Bq;
     launch_gemv(dtype, &wq, &Bs, 1, false, N, K, (const uint8_t*)s_act.p, 2 * K,
-                (const int*)s_asum.p, M, C, st);
+                  (const int*)s_asum.p, M, C, st);
   } else {
     launch_gemv_generic(dtype, A, (const uint8_t*)Bq, Bs, C, M, N, K, st);
   }
@@ -347,7 +349,7 @@ int moe_matmul_batched_dev(const float* A, const void* const* W_q, const float* 
   if ((rc = grow(s_act, (size_t)2 * K)) || (rc = grow(s_asum, sizeof(int)))) return rc;
   launch_quantize_act(A, 1, K, dtype, (uint8_t*)s_act.p, 2 * K, (int*)s_asum.p, g.d_err, st);
   launch_gemv(dtype, (const uint8_t* const*)W_q, W_s, n_mat, true, N, K, (const uint8_t*)s_act.p,
-              2 * K, (const int*)s_asum.p, 1, C, st);
+                2 * K, (const int*)s_asum.p, 1, C, st);
   CU(cudaGetLastError());
   return MOE_OK;
 }
@@ -505,6 +507,15 @@ static int get_layer(int layer, const LayerDev** out) {
   return MOE_OK;
 }
 
+static void run_gateup(const LayerDev& L, const Workspace& w, int T, cudaStream_t st) {
+  launch_gateup(L, w, T, g.d_err, st);
+}
+
+static void run_down(const LayerDev& L, const Workspace& w, int T, float* y, bool fuse,
+                     const float* xres, float* out, cudaStream_t st) {
+  launch_down(L, w, T, y, fuse, xres, out, st);
+}
+
 // Tokens at or below this count use the fused down+combine epilogue.
 constexpr int kFuseCombineMaxT = 64;
 
@@ -574,9 +585,9 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
     xn = w.xn; xo = w.xo;
   }
   route_tokens(L, xn, T, st);
-  timed("gateup", st, [&] { launch_gateup(L, w, T, g.d_err, st); });
   const bool fuse = T <= kFuseCombineMaxT;
-  timed("down", st, [&] { launch_down(L, w, T, w.y, fuse, xo, xo, st); });
+  timed("gateup", st, [&] { run_gateup(L, w, T, st); });
+  timed("down", st, [&] { run_down(L, w, T, w.y, fuse, xo, xo, st); });
   if (!fuse) timed("combine", st, [&] { launch_combine(w.y, w.topk_p, xo, xo, T, L.D, L.topk, st); });
   CU(cudaGetLastError());
   const size_t kb = sizeof(int) * (size_t)T * L.topk;
@@ -607,8 +618,8 @@ int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots, int*
   CU(cudaMemsetAsync(y_slots, 0, sizeof(float) * TK * L.D, st));
   route_tokens(L, x_norm2, T, st);
   if (L.e_end > L.e_begin) {
-    timed("gateup", st, [&] { launch_gateup(L, w, T, g.d_err, st); });
-    timed("down", st, [&] { launch_down(L, w, T, y_slots, false, nullptr, nullptr, st); });
+    timed("gateup", st, [&] { run_gateup(L, w, T, st); });
+    timed("down", st, [&] { run_down(L, w, T, y_slots, false, nullptr, nullptr, st); });
   }
   if (topk_idx_out) CU(cudaMemcpyAsync(topk_idx_out, w.topk_idx, sizeof(int) * TK, cudaMemcpyDeviceToDevice, st));
   if (topk_p_out) CU(cudaMemcpyAsync(topk_p_out, w.topk_p, sizeof(float) * TK, cudaMemcpyDeviceToDevice, st));

