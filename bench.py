@@ -122,6 +122,7 @@ def alg_bytes(kernel, T, U, dt):
     activations in/out). U = distinct experts routed in that step."""
     gu_rb = D if dt == 2 else D // 2
     d_rb = F if dt == 2 else F // 2
+    kernel = kernel.replace("mma_", "")
     if kernel == "gateup":
         return U * (2 * F * gu_rb + 2 * F * 4)
     if kernel == "down":

@@ -339,36 +339,55 @@ void launch_topk_softmax(const float* logits, int T, int E, int K, int* idx, flo
 
 // --------------------------------------------------------------------------
 // routing lists: for every local expert with tokens, its slots (t*K+k) in
-// ascending slot order; experts ascending. One CTA.
+// ascending slot order; experts ascending. Optionally (nt > 0) also the tensor-
+// core tile table (nt slots per tile) and the slot -> sorted-row map. One CTA;
+// the token choices are staged in shared memory first.
 // --------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) route_build_kernel(const int* __restrict__ idx, int TK,
                                                            int e_begin, int E_local, int* route,
-                                                           int* hsum) {
+                                                           int* hsum, int nt, int max_tiles,
+                                                           int* slot_pos) {
   extern __shared__ int sm[];
-  int* cnt = sm;              // [E_local]
-  int* start = sm + E_local;  // [E_local]
+  int* cnt = sm;                   // [E_local]
+  int* start = sm + E_local;       // [E_local]
+  int* sidx = sm + 2 * E_local;    // [TK]
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const RouteView r = route_view(route, E_local);
-  if (hsum)
-    for (int i = threadIdx.x; i < TK; i += blockDim.x) hsum[i] = 0;
+  for (int i = threadIdx.x; i < TK; i += blockDim.x) {
+    sidx[i] = idx[i];
+    if (hsum) hsum[i] = 0;
+  }
+  __syncthreads();
   for (int el = wid; el < E_local; el += nw) {
     const int e = e_begin + el;
     int c = 0;
     for (int base = 0; base < TK; base += 32) {
-      const int v = base + lane < TK ? idx[base + lane] : -1;
+      const int v = base + lane < TK ? sidx[base + lane] : -1;
       c += __popc(__ballot_sync(0xffffffffu, v == e));
     }
     if (lane == 0) cnt[el] = c;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    int na = 0, off = 0;
+    int na = 0, off = 0, ntl = 0;
+    int* tab = route + 2 + 2 * E_local + TK;   // tile table: n | u[] | j0[] | cnt[]
     for (int el = 0; el < E_local; ++el) {
       start[el] = off;
-      if (cnt[el] > 0) { r.active[na] = el; r.exp_off[na] = off; off += cnt[el]; ++na; }
+      if (cnt[el] == 0) continue;
+      r.active[na] = el;
+      r.exp_off[na] = off;
+      if (nt > 0)
+        for (int j0 = off; j0 < off + cnt[el] && ntl < max_tiles; j0 += nt, ++ntl) {
+          tab[1 + ntl] = na;
+          tab[1 + max_tiles + ntl] = j0;
+          tab[1 + 2 * max_tiles + ntl] = min(nt, off + cnt[el] - j0);
+        }
+      off += cnt[el];
+      ++na;
     }
     r.exp_off[na] = off;
     *r.n_active = na;
+    if (nt > 0) tab[0] = ntl;
   }
   __syncthreads();
   const unsigned lt = (1u << lane) - 1u;
@@ -377,19 +396,34 @@ __global__ void __launch_bounds__(1024) route_build_kernel(const int* __restrict
     const int e = e_begin + el;
     int pos = start[el];
     for (int base = 0; base < TK; base += 32) {
-      const int v = base + lane < TK ? idx[base + lane] : -1;
+      const int v = base + lane < TK ? sidx[base + lane] : -1;
       const unsigned m = __ballot_sync(0xffffffffu, v == e);
-      if (v == e) r.slot_list[pos + __popc(m & lt)] = base + lane;
+      if (v == e) {
+        const int j = pos + __popc(m & lt);
+        r.slot_list[j] = base + lane;
+        if (slot_pos) slot_pos[base + lane] = j;
+      }
       pos += __popc(m);
     }
   }
 }
 
+int route_max_tiles(int TK, int E_local, int nt) {
+  return TK / nt + (E_local < TK ? E_local : TK) + 1;
+}
+
 void launch_route_build(const int* idx, int T, int K, int e_begin, int e_end, int* route,
-                        int E_local, int* hsum, cudaStream_t st) {
+                        int E_local, int* hsum, int nt, int* slot_pos, cudaStream_t st) {
   (void)e_end;
-  const size_t smem = sizeof(int) * 2 * (size_t)E_local;
-  route_build_kernel<<<1, 1024, smem, st>>>(idx, T * K, e_begin, E_local, route, hsum);
+  const int TK = T * K;
+  const size_t smem = sizeof(int) * (2 * (size_t)E_local + (size_t)TK);
+  const int mt = nt > 0 ? route_max_tiles(TK, E_local, nt) : 0;
+  static size_t attr = 0;
+  if (smem > 48 * 1024 && smem > attr) {
+    cudaFuncSetAttribute(route_build_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = smem;
+  }
+  route_build_kernel<<<1, 1024, smem, st>>>(idx, TK, e_begin, E_local, route, hsum, nt, mt, slot_pos);
 }
 
 // --------------------------------------------------------------------------

@@ -34,6 +34,11 @@ struct Workspace {
   int* hsum = nullptr;        // [T*K]
   float* y = nullptr;         // [T*K][D]
   int* cnt = nullptr;         // [D] combine arrival counters (kept zero between calls)
+  uint8_t* xs0 = nullptr;     // expert-sorted token activations, plane 0 [T*K][D]
+  uint8_t* xs1 = nullptr;     //   plane 1 (Q8 high limb)
+  uint8_t* hs0 = nullptr;     // expert-sorted down-projection inputs [T*K][F]
+  uint8_t* hs1 = nullptr;
+  int* slot_pos = nullptr;    // [T*K] slot -> expert-sorted row
   float* xn = nullptr;        // staging for host-pointer calls [T][D]
   float* xo = nullptr;        // [T][D]
 };
@@ -41,6 +46,13 @@ struct Workspace {
 struct RouteView {
   int* n_active; int* active; int* exp_off; int* slot_list;
 };
+// tile table after the routing lists: n_tiles | tile_u[m] | tile_j0[m] | tile_n[m]
+struct TileView { const int* n; const int* u; const int* j0; const int* cnt; };
+__host__ __device__ inline TileView tile_view(const int* route, int E, int TK, int m) {
+  const int* t = route + 2 + 2 * E + TK;
+  return {t, t + 1, t + 1 + m, t + 1 + 2 * m};
+}
+
 __host__ __device__ inline RouteView route_view(int* route, int E) {
   RouteView r;
   r.n_active = route;
@@ -60,8 +72,11 @@ void launch_f32_seq_matmul(const float* A, const float* W, const float* b,
                            float* C, int M, int N, int K, cudaStream_t st);
 void launch_topk_softmax(const float* logits, int T, int E, int K, int* idx,
                          float* p, cudaStream_t st);
+// nt > 0: also the tensor-core tile table (nt slots per tile) and slot_pos
 void launch_route_build(const int* idx, int T, int K, int e_begin, int e_end,
-                        int* route, int E_local, int* hsum, cudaStream_t st);
+                        int* route, int E_local, int* hsum, int nt, int* slot_pos,
+                        cudaStream_t st);
+int route_max_tiles(int TK, int E_local, int nt);
 // Fast warp GEMV over n_mat matrices: C[mat][m][n]. Returns false if the
 // shape has no fast-path geometry (caller uses the generic kernel).
 bool launch_gemv(int dtype, const uint8_t* const* Wq, const float* const* Ws,
@@ -88,3 +103,14 @@ void launch_zero_fill(float* C, size_t n, cudaStream_t st);
 
 }  // namespace moe
 
+namespace moe {
+// moe_mma.cu: tcgen05 grouped GEMMs over the routed experts
+bool mma_supported(const LayerDev& L);
+int mma_tile_n(int T);
+void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream_t st);
+bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st);
+bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, float* ys, bool fuse,
+                     const float* xres, float* out, int* err, cudaStream_t st);
+void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
+                           const float* xres, float* out, int T, int D, int K, cudaStream_t st);
+}  // namespace moe

@@ -1,0 +1,444 @@
+// moe_mma.cu — routed-expert GEMMs on the 5th-generation tensor cores.
+//
+// D[128 weight rows][NT routed slots] = W_tile[128 x K] · X[NT x K]^T with
+// tcgen05.mma kind::i8 (exact int32 accumulation in TMEM). Weights are the A
+// operand (one 128-row block of one expert per tile, TMA 3-D tensor map over
+// the per-expert slabs, 128-byte swizzle); the routed tokens' truncated
+// activations, sorted by expert into contiguous rows, are the B operand
+// (TMA 2-D). Q8 activations need 16 bits, so they are two byte limbs (lo as
+// u8, hi as s8) and two MMAs; the epilogue recombines lo + 256*hi.
+//
+// Warp roles (persistent CTA, one per SM):
+//   warp 0      TMA producer (one elected thread), S-stage smem ring
+//   warp 1      TMEM allocator + MMA issuer (one elected thread)
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator, one weight row per
+//               thread, every (row, slot) finished in parallel:
+//                 GATEUP: h = silu(g)*u, re-truncated for the down projection
+//                         (test_model_trace.c:496-501, kernels.c:66/:113)
+//                 DOWN:   y = dot/S*s; with `fuse`, the last tile to finish a
+//                         row block applies the k-ordered combine (:502-517)
+// TMEM holds two accumulator buffers so the MMAs of tile i+1 overlap the
+// epilogue of tile i. Every wait is bounded (kWaitBudget polls); on expiry the
+// kernel flags kErrTimeout and leaves instead of hanging.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "tc.cuh"
+
+namespace moe {
+namespace mm {
+
+enum { GATEUP = 0, DOWN = 1 };
+constexpr int kThreads = 6 * 32;
+
+struct __align__(64) TMap { CUtensorMap m; };
+
+struct Args {
+  int rows;          // output rows per expert (F for GATEUP, D for DOWN)
+  int kchunks;       // K bytes / 128
+  int n_mblk;        // rows / 128
+  int stages, stage_bytes;
+  const int* route;  // routing lists + tile table (route_view / tile_view)
+  int E_local, TK, max_tiles;
+  const uint8_t* slab;
+  size_t stride, s0_off, s1_off;
+  int F;                                   // GATEUP: output plane row length
+  uint8_t* hs0; uint8_t* hs1;              // GATEUP outputs (expert-sorted rows)
+  float* ys;                               // DOWN output [J][D]
+  int fuse, T, topk;
+  int* cnt; const int* slot_pos; const float* topk_p; const int* topk_idx;
+  const float* xres; float* out;
+  int* err;
+};
+
+template <int DT, int MODE, int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_mma_kernel(const __grid_constant__ TMap tmA0, const __grid_constant__ TMap tmA1,
+                   const __grid_constant__ TMap tmB0, const __grid_constant__ TMap tmB1, const Args a) {
+  constexpr int NM = MODE == GATEUP ? 2 : 1;     // weight matrices per tile
+  constexpr int NL = DT == 8 ? 2 : 1;            // activation limbs
+  constexpr int ACC = NM * NL * NT;              // accumulator columns per buffer
+  constexpr uint32_t TCOLS = ACC * 2 <= 32 ? 32 : ACC * 2 <= 64 ? 64 : ACC * 2 <= 128 ? 128
+                             : ACC * 2 <= 256 ? 256 : 512;
+  static_assert(ACC * 2 <= 512, "accumulators exceed TMEM");
+  constexpr float S = DT == 8 ? 127.0f : 7.0f;
+  constexpr int A_BYTES = 128 * 128;
+  constexpr int B_BYTES = NT * 128;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)a.stages * a.stage_bytes);
+  uint64_t* empty = full + a.stages;
+  uint64_t* acc_full = empty + a.stages;     // [2]
+  uint64_t* acc_empty = acc_full + 2;        // [2]
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort, s_issued;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const TileView tv = tile_view(a.route, a.E_local, a.TK, a.max_tiles);
+  const int* active = a.route + 1;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0; s_issued = 0;
+    for (int s = 0; s < a.stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 4); }
+    fence_mbar_init();
+    tc::prefetch_tmap(&tmA0.m); tc::prefetch_tmap(&tmB0.m);
+    if (NM == 2) tc::prefetch_tmap(&tmA1.m);
+    if (NL == 2) tc::prefetch_tmap(&tmB1.m);
+  }
+  if (warp == 1) tc::tmem_alloc(&s_tmem, TCOLS);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = s_tmem;
+
+  const int n_units = *tv.n * a.n_mblk;
+  const int u0 = (int)((long)n_units * blockIdx.x / gridDim.x);
+  const int u1 = (int)((long)n_units * (blockIdx.x + 1) / gridDim.x);
+  volatile int* abort_flag = &s_abort;
+
+  if (warp == 0) {
+    // ------------------------- TMA producer -------------------------
+    if (lane == 0) {
+      const uint32_t bytes = NM * A_BYTES + NL * B_BYTES;
+      int it = 0;
+      for (int u = u0; u < u1 && !*abort_flag; ++u) {
+        const int tile = u / a.n_mblk, mb = u % a.n_mblk;
+        const int e = active[tv.u[tile]], j0 = tv.j0[tile];
+        for (int kc = 0; kc < a.kchunks; ++kc, ++it) {
+          const int st = it % a.stages;
+          if (it >= a.stages && !mbar_wait(&empty[st], ((it / a.stages) - 1) & 1, kWaitBudget)) {
+            atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
+          }
+          uint8_t* sb = smem + (size_t)st * a.stage_bytes;
+          mbar_arrive_expect_tx(&full[st], bytes);
+          tc::tma_load_3d(sb, &tmA0.m, kc * 128, mb * 128, e, &full[st]);
+          if (NM == 2) tc::tma_load_3d(sb + A_BYTES, &tmA1.m, kc * 128, mb * 128, e, &full[st]);
+          tc::tma_load_2d(sb + NM * A_BYTES, &tmB0.m, kc * 128, j0, &full[st]);
+          if (NL == 2) tc::tma_load_2d(sb + NM * A_BYTES + B_BYTES, &tmB1.m, kc * 128, j0, &full[st]);
+          s_issued = it + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------- MMA issuer ---------------------------
+    if (lane == 0) {
+      // Q8: A = s8 weights, B = u8 low limb / s8 high limb.
+      // Q4: A = u8 nibbles (0..15), B = s8 activations.
+      uint32_t idesc[2];
+      idesc[0] = tc::idesc_i8(128, NT, DT == 8, DT != 8);
+      idesc[1] = tc::idesc_i8(128, NT, true, true);
+      int it = 0, ul = 0;
+      for (int u = u0; u < u1 && !*abort_flag; ++u, ++ul) {
+        const int buf = ul & 1;
+        if (ul >= 2 && !mbar_wait(&acc_empty[buf], ((ul >> 1) - 1) & 1, kWaitBudget)) {
+          atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
+        }
+        tc::fence_after_sync();
+        const uint32_t dbase = tmem + buf * ACC;
+        for (int kc = 0; kc < a.kchunks; ++kc, ++it) {
+          const int st = it % a.stages;
+          if (!mbar_wait(&full[st], (it / a.stages) & 1, kWaitBudget)) {
+            atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
+          }
+          tc::fence_after_sync();
+          const uint8_t* sb = smem + (size_t)st * a.stage_bytes;
+          uint64_t da[NM], db[NL];
+#pragma unroll
+          for (int m = 0; m < NM; ++m) da[m] = tc::sw128_desc(sb + m * A_BYTES);
+#pragma unroll
+          for (int l = 0; l < NL; ++l) db[l] = tc::sw128_desc(sb + NM * A_BYTES + l * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)            // 4 x 32 bytes of K per 128-byte chunk
+#pragma unroll
+            for (int m = 0; m < NM; ++m)
+#pragma unroll
+              for (int l = 0; l < NL; ++l)
+                tc::mma_i8(dbase + (m * NL + l) * NT, da[m] + 2 * kk, db[l] + 2 * kk, idesc[l],
+                           (kc | kk) != 0);
+          tc::mma_commit(&empty[st]);               // stage free once these MMAs finish
+        }
+        if (*abort_flag) break;
+        tc::mma_commit(&acc_full[buf]);             // accumulator of this tile complete
+      }
+    }
+  } else {
+    // ------------------------- epilogue -----------------------------
+    const int q = warp & 3;                         // TMEM lane quarter of this warp
+    const int r = q * 32 + lane;                    // weight row within the 128-row block
+    int ul = 0;
+    for (int u = u0; u < u1; ++u, ++ul) {
+      const int buf = ul & 1;
+      if (!mbar_wait(&acc_full[buf], (ul >> 1) & 1, kWaitBudget)) {
+        if (lane == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; }
+        break;
+      }
+      tc::fence_after_sync();
+      const int tile = u / a.n_mblk, mb = u % a.n_mblk;
+      const int e = active[tv.u[tile]], j0 = tv.j0[tile], nt = tv.cnt[tile];
+      const int n = mb * 128 + r;
+      const uint8_t* ex = a.slab + (size_t)e * a.stride;
+      const float sc0 = __ldg(reinterpret_cast<const float*>(ex + a.s0_off) + n);
+      const float sc1 = NM == 2 ? __ldg(reinterpret_cast<const float*>(ex + a.s1_off) + n) : 0.f;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * ACC;
+      for (int c0 = 0; c0 < nt; c0 += 8) {
+        uint32_t v[NM * NL][8];
+#pragma unroll
+        for (int x = 0; x < NM * NL; ++x) tc::tmem_ld8(tbase + x * NT + c0, v[x]);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int jj = c0 + i;
+          if (jj >= nt) break;
+          const int j = j0 + jj;
+          int dot[NM];
+#pragma unroll
+          for (int m = 0; m < NM; ++m)
+            dot[m] = NL == 2 ? (int)(v[m * 2][i] + (v[m * 2 + 1][i] << 8)) : (int)v[m][i];
+          if (MODE == GATEUP) {
+            const float g = fmul(fdiv(__int2float_rn(dot[0]), S), sc0);
+            const float uu = fmul(fdiv(__int2float_rn(dot[NM - 1]), S), sc1);
+            const float h = fmul(silu_ref(g), uu);
+            const int ha = trunc_scale(h, S);
+            if (DT == 8) {
+              if (ha < -32768 || ha > 32767) atomicOr(a.err, kErrRange);
+              a.hs0[(size_t)j * a.F + n] = (uint8_t)(ha & 0xFF);
+              a.hs1[(size_t)j * a.F + n] = (uint8_t)((ha >> 8) & 0xFF);
+            }
+          } else {
+            a.ys[(size_t)j * a.rows + n] = fmul(fdiv(__int2float_rn(dot[0]), S), sc0);
+          }
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+
+      if (MODE == DOWN && a.fuse) {
+        // this warp's 32 rows of block mb are final once every tile has passed
+        // through them; the last warp to arrive applies the combine to them
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(a.cnt + mb * 4 + q, 1) == *tv.n - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          for (int t = 0; t < a.T; ++t) {
+            float accf = 0.0f;
+            for (int k = 0; k < a.topk; ++k) {
+              const int s = t * a.topk + k;
+              if (__ldcg(a.topk_idx + s) < 0) continue;
+              const int j = __ldcg(a.slot_pos + s);
+              accf = fadd(accf, fmul(__ldcg(a.topk_p + s), __ldcg(a.ys + (size_t)j * a.rows + n)));
+            }
+            const size_t o = (size_t)t * a.rows + n;
+            a.out[o] = fadd(a.xres[o], accf);
+          }
+          if (lane == 0) atomicExch(a.cnt + mb * 4 + q, 0);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && s_abort) {
+    // let the tensor copies still in flight land before the CTA's smem goes away
+    for (int it = max(0, s_issued - a.stages); it < s_issued; ++it)
+      mbar_wait(&full[it % a.stages], (it / a.stages) & 1, kWaitBudget);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, TCOLS);
+  }
+}
+
+}  // namespace mm
+}  // namespace moe
+
+// ===========================================================================
+// host side
+// ===========================================================================
+namespace moe {
+namespace mm {
+
+// Gather the routed tokens' activation rows into expert-sorted order:
+// row j of the output planes = token slot_list[j] / topk (B operand rows).
+__global__ void gather_rows_kernel(const uint8_t* __restrict__ xact, int act_stride, int D, int nplanes,
+                                   const int* __restrict__ route, int E_local, int topk,
+                                   uint8_t* __restrict__ xs0, uint8_t* __restrict__ xs1) {
+  const int j = blockIdx.x;
+  const RouteView r = route_view(const_cast<int*>(route), E_local);
+  if (j >= r.exp_off[*r.n_active]) return;
+  const int t = r.slot_list[j] / topk;
+  const uint4* src = reinterpret_cast<const uint4*>(xact + (size_t)t * act_stride);
+  uint4* d0 = reinterpret_cast<uint4*>(xs0 + (size_t)j * D);
+  for (int i = threadIdx.x; i < D / 16; i += blockDim.x) d0[i] = src[i];
+  if (nplanes == 2) {
+    uint4* d1 = reinterpret_cast<uint4*>(xs1 + (size_t)j * D);
+    for (int i = threadIdx.x; i < D / 16; i += blockDim.x) d1[i] = src[D / 16 + i];
+  }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// uint8 tensor map, 128-byte inner box with 128-byte swizzle.
+static bool map_u8(TMap& t, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                   const cuuint32_t* box) {
+  auto fn = encoder();
+  if (!fn) return false;
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(&t.m, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// weights of one projection over all local experts: (K bytes, rows, expert)
+static bool map_weights(TMap& t, const LayerDev& L, size_t off, int kbytes, int rows) {
+  const cuuint64_t dims[3] = {(cuuint64_t)kbytes, (cuuint64_t)rows, (cuuint64_t)(L.e_end - L.e_begin)};
+  const cuuint64_t strides[2] = {(cuuint64_t)kbytes, (cuuint64_t)L.expert_stride};
+  const cuuint32_t box[3] = {128, 128, 1};
+  return map_u8(t, L.slab + off, 3, dims, strides, box);
+}
+
+// expert-sorted activation plane: (K bytes, J rows); J >= the box height
+static bool map_rows(TMap& t, const uint8_t* base, int kbytes, int J, int nt) {
+  const cuuint64_t dims[2] = {(cuuint64_t)kbytes, (cuuint64_t)J};
+  const cuuint64_t strides[1] = {(cuuint64_t)kbytes};
+  const cuuint32_t box[2] = {128, (cuuint32_t)nt};
+  return map_u8(t, base, 2, dims, strides, box);
+}
+
+static int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int DT, int MODE, int NT>
+static bool launch_kernel(const TMap& a0, const TMap& a1, const TMap& b0, const TMap& b1, Args a, int grid,
+                          cudaStream_t st) {
+  constexpr int NM = MODE == GATEUP ? 2 : 1, NL = DT == 8 ? 2 : 1;
+  a.stage_bytes = NM * 128 * 128 + NL * NT * 128;
+  const int budget = 220 * 1024;
+  a.stages = (budget - 1024 - 256) / a.stage_bytes;
+  if (a.stages > 8) a.stages = 8;
+  if (a.stages < 2) return false;
+  const size_t smem = (size_t)a.stages * a.stage_bytes + 1024 + 8 * (2 * (size_t)a.stages + 4);
+  auto k = moe_mma_kernel<DT, MODE, NT>;
+  static size_t attr = 0;
+  if (smem > attr) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return false;
+    attr = smem;
+  }
+  k<<<grid, kThreads, smem, st>>>(a0, a1, b0, b1, a);
+  return true;
+}
+
+}  // namespace mm
+
+// ---- public launchers ------------------------------------------------------
+
+int mma_tile_n(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : 64; }
+
+bool mma_supported(const LayerDev& L) {
+  return L.dtype == 2 && L.D % 128 == 0 && L.F % 128 == 0 && mm::encoder() != nullptr;
+}
+
+void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream_t st) {
+  const int E_local = L.e_end - L.e_begin, TK = T * L.topk;
+  mm::gather_rows_kernel<<<TK, 128, 0, st>>>(ws.xact, 2 * L.D, L.D, L.dtype == 2 ? 2 : 1, ws.route, E_local,
+                                             L.topk, ws.xs0, ws.xs1);
+}
+
+#define NT_SWITCH(nt, CALL) \
+  switch (nt) {             \
+    case 16: { constexpr int NT = 16; CALL; } break; \
+    case 32: { constexpr int NT = 32; CALL; } break; \
+    default: { constexpr int NT = 64; CALL; } break; \
+  }
+
+bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st) {
+  const int E_local = L.e_end - L.e_begin, TK = T * L.topk, cap = ws.cap_T * ws.cap_K;
+  mm::TMap a0, a1, b0, b1;
+  if (!mm::map_weights(a0, L, L.gq_off, L.D, L.F) || !mm::map_weights(a1, L, L.uq_off, L.D, L.F) ||
+      !mm::map_rows(b0, ws.xs0, L.D, cap, nt) || !mm::map_rows(b1, ws.xs1, L.D, cap, nt))
+    return false;
+  mm::Args a{};
+  a.rows = L.F; a.kchunks = L.D / 128; a.n_mblk = L.F / 128;
+  a.route = ws.route; a.E_local = E_local; a.TK = TK; a.max_tiles = route_max_tiles(TK, E_local, nt);
+  a.slab = L.slab; a.stride = L.expert_stride; a.s0_off = L.gs_off; a.s1_off = L.us_off;
+  a.F = L.F; a.hs0 = ws.hs0; a.hs1 = ws.hs1; a.err = err;
+  const int units = a.max_tiles * a.n_mblk;
+  const int grid = units < mm::sm_count() ? units : mm::sm_count();
+  bool ok = false;
+  NT_SWITCH(nt, (ok = mm::launch_kernel<8, mm::GATEUP, NT>(a0, a1, b0, b1, a, grid, st)));
+  return ok;
+}
+
+bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, float* ys, bool fuse,
+                     const float* xres, float* out, int* err, cudaStream_t st) {
+  const int E_local = L.e_end - L.e_begin, TK = T * L.topk, cap = ws.cap_T * ws.cap_K;
+  mm::TMap a0, b0, b1;
+  if (!mm::map_weights(a0, L, L.dq_off, L.F, L.D) || !mm::map_rows(b0, ws.hs0, L.F, cap, nt) ||
+      !mm::map_rows(b1, ws.hs1, L.F, cap, nt))
+    return false;
+  mm::Args a{};
+  a.rows = L.D; a.kchunks = L.F / 128; a.n_mblk = L.D / 128;
+  a.route = ws.route; a.E_local = E_local; a.TK = TK; a.max_tiles = route_max_tiles(TK, E_local, nt);
+  a.slab = L.slab; a.stride = L.expert_stride; a.s0_off = L.ds_off;
+  a.ys = ys; a.fuse = fuse ? 1 : 0; a.T = T; a.topk = L.topk;
+  a.cnt = ws.cnt; a.slot_pos = ws.slot_pos; a.topk_p = ws.topk_p; a.topk_idx = ws.topk_idx;
+  a.xres = xres; a.out = out; a.err = err;
+  const int units = a.max_tiles * a.n_mblk;
+  const int grid = units < mm::sm_count() ? units : mm::sm_count();
+  bool ok = false;
+  NT_SWITCH(nt, (ok = mm::launch_kernel<8, mm::DOWN, NT>(a0, a0, b0, b1, a, grid, st)));
+  return ok;
+}
+
+// combine from expert-sorted y rows (prefill / non-fused path)
+__global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* __restrict__ slot_pos,
+                                      const float* __restrict__ p, const int* __restrict__ idx,
+                                      const float* xres, float* out, int T, int D, int K) {
+  const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= (long)T * D) return;
+  const int t = (int)(q / D), n = (int)(q % D);
+  float acc = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    const int s = t * K + k;
+    if (idx[s] < 0) continue;
+    acc = fadd(acc, fmul(p[s], ys[(size_t)slot_pos[s] * D + n]));
+  }
+  out[q] = fadd(xres[q], acc);
+}
+
+void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
+                           const float* xres, float* out, int T, int D, int K, cudaStream_t st) {
+  const long total = (long)T * D;
+  if (total <= 0) return;
+  combine_sorted_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(ys, slot_pos, p, idx, xres, out, T, D, K);
+}
+
+}  // namespace moe

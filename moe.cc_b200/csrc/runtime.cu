@@ -64,15 +64,17 @@ static int ensure_init() {
 static int ensure_workspace(int T, int E, int D, int F, int K) {
   Workspace& w = g.ws;
   if (T <= w.cap_T && E <= w.cap_E && D <= w.cap_D && F <= w.cap_F && K <= w.cap_K) return MOE_OK;
-  const int nT = T > w.cap_T ? (T > 2 * w.cap_T ? T : 2 * w.cap_T) : w.cap_T;
+  int nT = T > w.cap_T ? (T > 2 * w.cap_T ? T : 2 * w.cap_T) : w.cap_T;
+  if (nT < 8) nT = 8;   // >= 64 sorted rows: the smallest tensor-core tile fits
   const int nE = E > w.cap_E ? E : w.cap_E, nD = D > w.cap_D ? D : w.cap_D;
   const int nF = F > w.cap_F ? F : w.cap_F, nK = K > w.cap_K ? K : w.cap_K;
   CU(cudaDeviceSynchronize());
-  void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum,
-                  w.hact, w.hsum, w.y, w.cnt, w.xn, w.xo};
+  void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum, w.hact, w.hsum,
+                  w.y, w.cnt, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
   const size_t TK = (size_t)nT * nK;
+  const size_t max_tiles = (size_t)route_max_tiles((int)TK, nE, 16);
 #define ALLOC(field, bytes)                                                    \
   do {                                                                         \
     if (cudaMalloc((void**)&w.field, (bytes)) != cudaSuccess) {                \
@@ -84,13 +86,18 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   ALLOC(logits, sizeof(float) * (size_t)nT * nE);
   ALLOC(topk_idx, sizeof(int) * TK);
   ALLOC(topk_p, sizeof(float) * TK);
-  ALLOC(route, sizeof(int) * (2 + 2 * (size_t)nE + TK));
+  ALLOC(route, sizeof(int) * (2 + 2 * (size_t)nE + TK + 1 + 3 * max_tiles));
   ALLOC(xact, (size_t)2 * nD * nT);
   ALLOC(xsum, sizeof(int) * (size_t)nT);
   ALLOC(hact, (size_t)2 * nF * TK);
   ALLOC(hsum, sizeof(int) * TK);
   ALLOC(y, sizeof(float) * TK * nD);
   ALLOC(cnt, sizeof(int) * (size_t)nD);
+  ALLOC(xs0, TK * nD);
+  ALLOC(xs1, TK * nD);
+  ALLOC(hs0, TK * nF);
+  ALLOC(hs1, TK * nF);
+  ALLOC(slot_pos, sizeof(int) * TK);
   ALLOC(xn, sizeof(float) * (size_t)nT * nD);
   ALLOC(xo, sizeof(float) * (size_t)nT * nD);
 #undef ALLOC
@@ -246,8 +253,8 @@ int moe_cuda_shutdown(void) {
   g.layers.clear();
   g.alias.clear();
   Workspace& w = g.ws;
-  void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum,
-                  w.hact, w.hsum, w.y, w.cnt, w.xn, w.xo};
+  void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum, w.hact, w.hsum,
+                  w.y, w.cnt, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
   Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum};
@@ -481,7 +488,7 @@ static void prof_drain() {
 }
 
 // Router + top-k + routing lists + token activation truncation.
-static void route_tokens(const LayerDev& L, const float* xn, int T, cudaStream_t st) {
+static void route_tokens(const LayerDev& L, const float* xn, int T, int nt, cudaStream_t st) {
   const Workspace& w = g.ws;
   timed("quantize_act", st, [&] {
     launch_quantize_act(xn, T, L.D, L.dtype, w.xact, 2 * L.D, w.xsum, g.d_err, st);
@@ -494,7 +501,7 @@ static void route_tokens(const LayerDev& L, const float* xn, int T, cudaStream_t
   });
   timed("route_build", st, [&] {
     launch_route_build(w.topk_idx, T, L.topk, L.e_begin, L.e_end, w.route, L.e_end - L.e_begin,
-                       L.dtype == MOE_DTYPE_Q4 ? w.hsum : nullptr, st);
+                       L.dtype == MOE_DTYPE_Q4 ? w.hsum : nullptr, nt, nt > 0 ? w.slot_pos : nullptr, st);
   });
 }
 
@@ -514,6 +521,19 @@ static void run_gateup(const LayerDev& L, const Workspace& w, int T, cudaStream_
 static void run_down(const LayerDev& L, const Workspace& w, int T, float* y, bool fuse,
                      const float* xres, float* out, cudaStream_t st) {
   launch_down(L, w, T, y, fuse, xres, out, st);
+}
+
+// Tensor-core (tcgen05) expert GEMMs unless the caller forces the CUDA-core
+// GEMVs (MOE_FFN_FORCE_GEMV, or MOE_FFN_PATH=gemv in the environment).
+static bool use_tensor_cores(const LayerDev& L, int flags) {
+  if (flags & MOE_FFN_FORCE_GEMV) return false;
+  static int env = -1;
+  if (env < 0) {
+    const char* e = getenv("MOE_FFN_PATH");
+    env = (e && strcmp(e, "gemv") == 0) ? 0 : 1;
+  }
+  if (!env && !(flags & MOE_FFN_FORCE_GEMM)) return false;
+  return mma_supported(L);
 }
 
 // Tokens at or below this count use the fused down+combine epilogue.
@@ -584,11 +604,25 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
     CU(cudaMemcpyAsync(w.xo, x_inout, xb, cudaMemcpyHostToDevice, st));
     xn = w.xn; xo = w.xo;
   }
-  route_tokens(L, xn, T, st);
   const bool fuse = T <= kFuseCombineMaxT;
-  timed("gateup", st, [&] { run_gateup(L, w, T, st); });
-  timed("down", st, [&] { run_down(L, w, T, w.y, fuse, xo, xo, st); });
-  if (!fuse) timed("combine", st, [&] { launch_combine(w.y, w.topk_p, xo, xo, T, L.D, L.topk, st); });
+  if (use_tensor_cores(L, flags)) {
+    const int nt = mma_tile_n(T);
+    route_tokens(L, xn, T, nt, st);
+    timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
+    bool ok = true;
+    timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
+    if (ok) timed("mma_down", st, [&] { ok = launch_mma_down(L, w, T, nt, w.y, fuse, xo, xo, g.d_err, st); });
+    if (!ok) return set_err(MOE_ERR_CUDA, "tensor-core launch failed (tensor map or shared memory)");
+    if (!fuse)
+      timed("combine", st, [&] {
+        launch_combine_sorted(w.y, w.slot_pos, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, st);
+      });
+  } else {
+    route_tokens(L, xn, T, 0, st);
+    timed("gateup", st, [&] { run_gateup(L, w, T, st); });
+    timed("down", st, [&] { run_down(L, w, T, w.y, fuse, xo, xo, st); });
+    if (!fuse) timed("combine", st, [&] { launch_combine(w.y, w.topk_p, xo, xo, T, L.D, L.topk, st); });
+  }
   CU(cudaGetLastError());
   const size_t kb = sizeof(int) * (size_t)T * L.topk;
   const cudaMemcpyKind out_kind = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
@@ -616,7 +650,7 @@ int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots, int*
   const Workspace& w = g.ws;
   const size_t TK = (size_t)T * L.topk;
   CU(cudaMemsetAsync(y_slots, 0, sizeof(float) * TK * L.D, st));
-  route_tokens(L, x_norm2, T, st);
+  route_tokens(L, x_norm2, T, 0, st);
   if (L.e_end > L.e_begin) {
     timed("gateup", st, [&] { run_gateup(L, w, T, st); });
     timed("down", st, [&] { run_down(L, w, T, y_slots, false, nullptr, nullptr, st); });

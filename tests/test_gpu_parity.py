@@ -183,6 +183,23 @@ def test_moe_ffn_qwen_shape_vs_port(gpu, port, dt, T, bias):
     assert float(np.mean(p == ref_p)) >= 0.999
 
 
+@pytest.mark.parametrize("T", [1, 16, 40, 100])
+def test_moe_ffn_tensor_core_path_equals_gemv_path(gpu, T):
+    """The tcgen05 grouped-GEMM path and the CUDA-core GEMV path compute the
+    same integers, so their outputs are identical bit for bit."""
+    lid, L = qwen_layer(gpu, 2, False)
+    xn = torch.from_numpy(synth(960 + T, T * 2048, 1.0).reshape(T, 2048)).cuda()
+    xa = torch.from_numpy(synth(961 + T, T * 2048, 1.0).reshape(T, 2048)).cuda()
+    outs = []
+    for flags in (gpu.FORCE_GEMM, gpu.FORCE_GEMV):
+        o = xa.clone()
+        gpu.moe_ffn_dev(lid, xn, o, flags=flags)
+        torch.cuda.synchronize()
+        gpu.check_status()
+        outs.append(o.cpu().numpy())
+    assert np.array_equal(outs[0], outs[1])
+
+
 def test_moe_ffn_device_ptrs_and_partial_combine(gpu, port):
     lid, L = qwen_layer(gpu, 2, False)
     T = 8
