@@ -113,6 +113,21 @@ int moe_matmul_batched_dev(const float* A, const void* const* W_q,
                            const float* const* W_s, float* C, int n_mat,
                            int N, int K, int dtype, void* stream);
 
+/* Allocation-free form of moe_matmul_q8_dev / moe_matmul_q4_dev (dtype 2 or 3),
+ * for callers that must not allocate GPU memory at call time (code inside a
+ * memory-pool or allocator callback, hosts whose device memory is entirely
+ * reserved up front, latency-critical paths that cannot take cudaMalloc's
+ * implicit synchronisation). No counterpart in the reference. Same results as
+ * moe_matmul_q8_dev/_q4_dev, bit for bit, for any input magnitude. Scratch is
+ * a fixed 1 MiB + 16.25 KiB device array inside the library (held by every GPU
+ * that loads it until exit): M <= 4096 and M*K <= 524288, larger calls return
+ * MOE_ERR_INVALID. Needs no moe_cuda_init. The first call on each device
+ * resolves the array's address (make it before any stream capture). All
+ * calls share the array: calls whose GPU work overlaps race on it. */
+int moe_matmul_q_dev_noalloc(const float* A, const void* B_q, const float* B_s,
+                             float* C, int M, int N, int K, int dtype,
+                             void* stream);
+
 /* ---- quantisers (export.py:23-36) -----------------------------------------
  * Bit-exact with export._rowwise_q8 / _rowwise_q4: s = max(max|row|,1e-8)/127
  * (or /7), q = round-half-even(w/s) (Q4: clamped to [-8,7], +8, two nibbles a

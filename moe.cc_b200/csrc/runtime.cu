@@ -45,6 +45,9 @@ static int set_err(int code, const char* fmt, ...) {
   return code;
 }
 
+// Error reporting for entry points defined in other .cu files of the library.
+int set_error_message(int code, const char* msg) { return set_err(code, "%s", msg); }
+
 #define CU(call)                                                                         \
   do {                                                                                   \
     cudaError_t e_ = (call);                                                             \

@@ -32,7 +32,7 @@ EXPORTS = (
     "moe_cuda_upload_layer", "moe_cuda_upload_layer_dev", "moe_cuda_free_layer",
     "moe_cuda_layer_bytes", "moe_ffn", "moe_ffn_partial", "moe_ffn_combine",
     "moe_synth_normal_host", "moe_synth_normal_dev",
-    "moe_cuda_profile", "moe_cuda_profile_read",
+    "moe_cuda_profile", "moe_cuda_profile_read", "moe_matmul_q_dev_noalloc",
 )
 
 
@@ -80,6 +80,7 @@ def lib():
             "moe_synth_normal_host": ([u64, u64, sz, f, vp], None),
             "moe_synth_normal_dev": ([u64, u64, sz, f, vp, vp], i),
             "moe_cuda_profile": ([i], i),
+            "moe_matmul_q_dev_noalloc": ([vp, vp, vp, vp, i, i, i, i, vp], i),
             "moe_cuda_profile_read": ([i, vp, i, vp, vp], i),
         }
         for name, (args, res) in sig.items():
