@@ -34,6 +34,7 @@ struct Workspace {
   int* hsum = nullptr;        // [T*K]
   float* y = nullptr;         // [T*K][D]
   int* cnt = nullptr;         // [D] combine arrival counters (kept zero between calls)
+  int* route_counter = nullptr;  // arrival counter of the fused routing kernel (kept zero)
   uint8_t* xs0 = nullptr;     // expert-sorted token activations, plane 0 [T*K][D]
   uint8_t* xs1 = nullptr;     //   plane 1 (Q8 high limb)
   uint8_t* hs0 = nullptr;     // expert-sorted down-projection inputs [T*K][F]
@@ -113,4 +114,11 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
                      const float* xres, float* out, int* err, cudaStream_t st);
 void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
                            const float* xres, float* out, int T, int D, int K, cudaStream_t st);
+}  // namespace moe
+
+namespace moe {
+// router.cu: decode routing prologue in one launch
+bool decode_route_supported(const LayerDev& L, int T, const float* x);
+void launch_decode_route(const LayerDev& L, const Workspace& ws, const float* x, int T, int nt,
+                         int* counter, int* err, cudaStream_t st);
 }  // namespace moe

@@ -1,0 +1,289 @@
+// router.cu — the decode-regime routing prologue in one launch.
+//
+// grid = (E/8 expert blocks) x (ceil(T/16) token blocks), 128 threads. Each
+// CTA bulk-copies its 8 router rows and 16 token rows into shared memory once
+// (1-D bulk async copies, one mbarrier), then every thread runs one exact
+// sequential fp32 chain logits[t][e] = Σ_k x[t][k]·W[e][k] (+b[e]) in k order
+// (test_model_trace.c:213-227, :465-468) straight from shared memory, and the
+// CTA truncates its slice of the token activations for the expert kernels
+// (kernels.c:66 / :113). The last CTA to finish (arrival counter) then does,
+// for all tokens: top-k (topk_desc, :275-288, as K warp arg-max rounds), the
+// top-k softmax (:481-487), and the routing lists, tensor-core tile table and
+// slot -> expert-sorted-row map. That phase keeps its tables in shared memory
+// (per-expert counts by shared atomics, one warp-shuffle scan over experts)
+// and writes them out with all threads: a single thread issuing hundreds of
+// scattered global stores was measured at ~15 us per table.
+#include "common.cuh"
+#include "kernels.cuh"
+#include "pipeline.cuh"
+
+namespace moe {
+namespace rt {
+
+constexpr int kE = 8, kT = 16, kThreads = 128;
+constexpr int kMaxTK = 256;     // T*K handled by the last CTA (decode sizes)
+constexpr int kMaxE = 256;
+constexpr int kMaxTiles = kMaxTK / 16 + kMaxE + 1;
+
+struct Args {
+  const float* x; const float* W; const float* b;
+  int T, E, D, K;
+  float* logits; int* idx; float* p;
+  int* route; int e_begin, E_local; int* hsum; int nt, max_tiles; int* slot_pos;
+  uint8_t* xact; int* xsum;
+  int* counter; int* err;
+};
+
+template <int DT>
+__global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int pitch = a.D + 4;                                   // floats; padding spreads banks
+  float* sw = reinterpret_cast<float*>(smem);                  // [kE][pitch]
+  float* sx = sw + kE * pitch;                                 // [kT][pitch]
+  __shared__ uint64_t bar;
+  __shared__ int s_last;
+  const int e0 = blockIdx.x * kE, t0 = blockIdx.y * kT;
+  const int ne = min(kE, a.E - e0), nt = min(kT, a.T - t0);
+  const int tid = threadIdx.x;
+
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&bar, (uint32_t)((ne + nt) * a.D * 4));
+    for (int i = 0; i < ne; ++i) bulk_g2s(sw + i * pitch, a.W + (size_t)(e0 + i) * a.D, a.D * 4, &bar);
+    for (int i = 0; i < nt; ++i) bulk_g2s(sx + i * pitch, a.x + (size_t)(t0 + i) * a.D, a.D * 4, &bar);
+  }
+  __syncthreads();
+  // A timed-out copy flags the call as failed; the CTA still reports its
+  // arrival below so the arrival counter stays consistent for later calls.
+  const bool ok = mbar_wait(&bar, 0, kWaitBudget);
+  if (!ok && tid == 0) atomicOr(a.err, kErrTimeout);
+
+  // ---- exact sequential chain: one (token, expert) per thread ----
+  const int tt = tid / kE, ee = tid % kE;
+  if (ok && tt < nt && ee < ne) {
+    const float* xr = sx + tt * pitch;
+    const float* wr = sw + ee * pitch;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int k = 0; k < a.D; k += 4) {
+      const float4 xv = *reinterpret_cast<const float4*>(xr + k);
+      const float4 wv = *reinterpret_cast<const float4*>(wr + k);
+      acc = fadd(acc, fmul(xv.x, wv.x));
+      acc = fadd(acc, fmul(xv.y, wv.y));
+      acc = fadd(acc, fmul(xv.z, wv.z));
+      acc = fadd(acc, fmul(xv.w, wv.w));
+    }
+    if (a.b) acc = fadd(acc, __ldg(a.b + e0 + ee));
+    a.logits[(size_t)(t0 + tt) * a.E + e0 + ee] = acc;
+  }
+
+  // ---- truncated activations: this CTA's column slice of its tokens ----
+  if (ok) {
+    const int c0 = (int)((long)a.D * blockIdx.x / gridDim.x);
+    const int c1 = (int)((long)a.D * (blockIdx.x + 1) / gridDim.x);
+    const int w = c1 - c0;
+    int bad = 0;
+    for (int q = tid; q < nt * w; q += kThreads) {
+      const int t = q / w, k = c0 + q % w;
+      const int v = trunc_scale(sx[t * pitch + k], DT == 8 ? 127.0f : 7.0f);
+      uint8_t* ar = a.xact + (size_t)(t0 + t) * 2 * a.D;
+      if (DT == 8) {
+        bad |= (v < -32768 || v > 32767);
+        ar[k] = (uint8_t)(v & 0xFF);
+        ar[a.D + k] = (uint8_t)((v >> 8) & 0xFF);
+      } else {
+        bad |= (v < -128 || v > 127);
+        ar[q4_act_pos(k)] = (uint8_t)(v & 0xFF);
+      }
+    }
+    if (bad) atomicOr(a.err, kErrRange);
+    if (DT == 4 && blockIdx.x == 0) {       // Σ activation per token (Q4 zero point)
+      for (int t = tid / 32; t < nt; t += kThreads / 32) {
+        int s = 0;
+        for (int k = tid % 32; k < a.D; k += 32) s += trunc_scale(sx[t * pitch + k], 7.0f);
+        s = warp_sum(s);
+        if ((tid & 31) == 0) a.xsum[t0 + t] = s;
+      }
+    }
+  }
+
+  // ---- last CTA: top-k, softmax, routing ----
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(a.counter, 1) == (int)(gridDim.x * gridDim.y) - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+
+  __shared__ int sidx[kMaxTK];
+  __shared__ int cnt[kMaxE], start[kMaxE], s_tab[1 + 3 * kMaxTiles];
+  __shared__ int s_route[2 + 2 * kMaxE + kMaxTK];
+  const int lane = tid & 31, warp = tid >> 5;
+  const int TK = a.T * a.K;
+  for (int i = tid; i < a.E_local; i += kThreads) cnt[i] = 0;
+  // top-k per token: warp per token, K rounds of a warp arg-max; lane r keeps
+  // round r's winner, so the softmax and the stores are spread over lanes
+  for (int t = warp; t < a.T; t += kThreads / 32) {
+    float v[kMaxE / 32];
+#pragma unroll
+    for (int i = 0; i < kMaxE / 32; ++i) {
+      const int e = lane + 32 * i;
+      v[i] = e < a.E ? __ldcg(a.logits + (size_t)t * a.E + e) : -INFINITY;
+    }
+    float myv = -INFINITY;
+    int myi = -1;
+    for (int r = 0; r < a.K; ++r) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < kMaxE / 32; ++i)
+        if (v[i] > bv) { bv = v[i]; bi = lane + 32 * i; }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      const bool found = bi != 0x7fffffff;
+      if (lane == r) { myv = found ? bv : -INFINITY; myi = found ? bi : -1; }
+      if (found && (bi & 31) == lane) {
+#pragma unroll
+        for (int i = 0; i < kMaxE / 32; ++i)
+          if (lane + 32 * i == bi) v[i] = -INFINITY;
+      }
+    }
+    // softmax over the K selected (:481-487): max is exact in any order; the
+    // sum is accumulated in the reference's order i = 0..K-1
+    float mx = __shfl_sync(0xffffffffu, myv, 0);
+    for (int i = 1; i < a.K; ++i) {
+      const float vi = __shfl_sync(0xffffffffu, myv, i);
+      if (vi > mx) mx = vi;
+    }
+    const float ev = lane < a.K ? exp_f32(__fsub_rn(myv, mx)) : 0.0f;
+    float sum = 0.0f;
+    for (int i = 0; i < a.K; ++i) sum = fadd(sum, __shfl_sync(0xffffffffu, ev, i));
+    const float inv = fdiv(1.0f, fadd(sum, 1e-9f));
+    if (lane < a.K) {
+      a.idx[t * a.K + lane] = myi;
+      a.p[t * a.K + lane] = fmul(ev, inv);
+      sidx[t * a.K + lane] = myi;
+    }
+  }
+  __syncthreads();
+  for (int s = tid; s < TK; s += kThreads) {
+    const int el = sidx[s] - a.e_begin;
+    if (el >= 0 && el < a.E_local) atomicAdd(&cnt[el], 1);
+  }
+  if (a.hsum)
+    for (int s = tid; s < TK; s += kThreads) a.hsum[s] = 0;
+  __syncthreads();
+  // one warp: exclusive scans over experts of (slots, active flag, tiles)
+  int* r_active = s_route + 1;
+  int* r_off = s_route + 1 + a.E_local;
+  const int mt = a.max_tiles;
+  if (warp == 0) {
+    constexpr int PER = kMaxE / 32;
+    int c[PER], sl = 0, sa = 0, stl = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int el = lane * PER + i;
+      c[i] = el < a.E_local ? cnt[el] : 0;
+      sl += c[i];
+      sa += c[i] > 0;
+      stl += a.nt > 0 ? (c[i] + a.nt - 1) / a.nt : 0;
+    }
+    int xl = sl, xa = sa, xt = stl;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int yl = __shfl_up_sync(0xffffffffu, xl, o), ya = __shfl_up_sync(0xffffffffu, xa, o),
+                yt = __shfl_up_sync(0xffffffffu, xt, o);
+      if (lane >= o) { xl += yl; xa += ya; xt += yt; }
+    }
+    int off = xl - sl, na = xa - sa, ntl = xt - stl;      // exclusive prefixes
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int el = lane * PER + i;
+      if (el >= a.E_local) break;
+      start[el] = off;
+      if (c[i] > 0) {
+        r_active[na] = el;
+        r_off[na] = off;
+        if (a.nt > 0)
+          for (int j0 = off; j0 < off + c[i] && ntl < mt; j0 += a.nt, ++ntl) {
+            s_tab[1 + ntl] = na;
+            s_tab[1 + mt + ntl] = j0;
+            s_tab[1 + 2 * mt + ntl] = min(a.nt, off + c[i] - j0);
+          }
+        ++na;
+      }
+      off += c[i];
+    }
+    if (lane == 31) {
+      r_off[na] = off;
+      s_route[0] = na;
+      s_tab[0] = ntl < mt ? ntl : mt;
+    }
+  }
+  __syncthreads();
+  // slot lists in ascending slot order within each expert
+  int* r_slots = s_route + 2 + 2 * a.E_local;
+  for (int s = tid; s < TK; s += kThreads) {
+    const int el = sidx[s] - a.e_begin;
+    if (el < 0 || el >= a.E_local) continue;
+    int rank = 0;
+    for (int s2 = 0; s2 < s; ++s2) rank += sidx[s2] == sidx[s];
+    const int j = start[el] + rank;
+    r_slots[j] = s;
+    if (a.slot_pos) a.slot_pos[s] = j;
+  }
+  __syncthreads();
+  // copy the tables out with all threads
+  const int nr = 2 + 2 * a.E_local + TK;
+  for (int i = tid; i < nr; i += kThreads) a.route[i] = s_route[i];
+  if (a.nt > 0) {
+    int* tab = a.route + nr;
+    for (int i = tid; i < 1 + 3 * mt; i += kThreads) tab[i] = s_tab[i];
+  }
+  if (tid == 0) *a.counter = 0;
+}
+
+}  // namespace rt
+
+bool decode_route_supported(const LayerDev& L, int T, const float* x) {
+  const int El = L.e_end - L.e_begin;
+  return T * L.topk <= rt::kMaxTK && L.E <= rt::kMaxE && El <= rt::kMaxE && L.topk <= 32 &&
+         L.D % 4 == 0 && (size_t)(rt::kE + rt::kT) * (L.D + 4) * 4 <= 200 * 1024 &&
+         ((uintptr_t)x % 16) == 0 && ((uintptr_t)L.router_w % 16) == 0;
+}
+
+void launch_decode_route(const LayerDev& L, const Workspace& ws, const float* x, int T, int nt,
+                         int* counter, int* err, cudaStream_t st) {
+  rt::Args a{};
+  a.x = x; a.W = L.router_w; a.b = L.router_b; a.T = T; a.E = L.E; a.D = L.D; a.K = L.topk;
+  a.logits = ws.logits; a.idx = ws.topk_idx; a.p = ws.topk_p;
+  a.route = ws.route; a.e_begin = L.e_begin; a.E_local = L.e_end - L.e_begin;
+  a.hsum = L.dtype == 3 ? ws.hsum : nullptr;
+  a.nt = nt; a.max_tiles = nt > 0 ? route_max_tiles(T * L.topk, a.E_local, nt) : 0;
+  a.slot_pos = nt > 0 ? ws.slot_pos : nullptr;
+  a.xact = ws.xact; a.xsum = ws.xsum; a.counter = counter; a.err = err;
+  const size_t smem = (size_t)(rt::kE + rt::kT) * (L.D + 4) * 4;
+  dim3 grid((L.E + rt::kE - 1) / rt::kE, (T + rt::kT - 1) / rt::kT);
+  if (L.dtype == 2) {
+    static size_t attr = 0;
+    if (smem > attr) {
+      cudaFuncSetAttribute(rt::decode_route_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr = smem;
+    }
+    rt::decode_route_kernel<8><<<grid, rt::kThreads, smem, st>>>(a);
+  } else {
+    static size_t attr = 0;
+    if (smem > attr) {
+      cudaFuncSetAttribute(rt::decode_route_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr = smem;
+    }
+    rt::decode_route_kernel<4><<<grid, rt::kThreads, smem, st>>>(a);
+  }
+}
+
+}  // namespace moe

@@ -73,7 +73,7 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   const int nF = F > w.cap_F ? F : w.cap_F, nK = K > w.cap_K ? K : w.cap_K;
   CU(cudaDeviceSynchronize());
   void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum, w.hact, w.hsum,
-                  w.y, w.cnt, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos};
+                  w.y, w.cnt, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
   const size_t TK = (size_t)nT * nK;
@@ -101,10 +101,12 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   ALLOC(hs0, TK * nF);
   ALLOC(hs1, TK * nF);
   ALLOC(slot_pos, sizeof(int) * TK);
+  ALLOC(route_counter, sizeof(int));
   ALLOC(xn, sizeof(float) * (size_t)nT * nD);
   ALLOC(xo, sizeof(float) * (size_t)nT * nD);
 #undef ALLOC
   CU(cudaMemset(w.cnt, 0, sizeof(int) * (size_t)nD));
+  CU(cudaMemset(w.route_counter, 0, sizeof(int)));
   w.cap_T = nT; w.cap_E = nE; w.cap_D = nD; w.cap_F = nF; w.cap_K = nK;
   return MOE_OK;
 }
@@ -257,7 +259,7 @@ int moe_cuda_shutdown(void) {
   g.alias.clear();
   Workspace& w = g.ws;
   void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum, w.hact, w.hsum,
-                  w.y, w.cnt, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos};
+                  w.y, w.cnt, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
   Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum};
@@ -492,6 +494,12 @@ static void prof_drain() {
 
 // Router + top-k + routing lists + token activation truncation.
 static void route_tokens(const LayerDev& L, const float* xn, int T, int nt, cudaStream_t st) {
+  if (decode_route_supported(L, T, xn)) {
+    timed("route", st, [&] {
+      launch_decode_route(L, g.ws, xn, T, nt, g.ws.route_counter, g.d_err, st);
+    });
+    return;
+  }
   const Workspace& w = g.ws;
   timed("quantize_act", st, [&] {
     launch_quantize_act(xn, T, L.D, L.dtype, w.xact, 2 * L.D, w.xsum, g.d_err, st);
@@ -607,9 +615,17 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
     CU(cudaMemcpyAsync(w.xo, x_inout, xb, cudaMemcpyHostToDevice, st));
     xn = w.xn; xo = w.xo;
   }
-  const bool fuse = T <= kFuseCombineMaxT;
   if (use_tensor_cores(L, flags)) {
     const int nt = mma_tile_n(T);
+    // The combine runs as its own kernel: fused into the down epilogue it left
+    // the last warp through each row block with T*K dependent loads at the
+    // end of the kernel (measured 90 us vs 39 + 6 us). MOE_MMA_FUSE=1 restores it.
+    static int fuse_env = -1;
+    if (fuse_env < 0) {
+      const char* e = getenv("MOE_MMA_FUSE");
+      fuse_env = e ? atoi(e) : 0;
+    }
+    const bool fuse = fuse_env && T <= kFuseCombineMaxT;
     route_tokens(L, xn, T, nt, st);
     timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
     bool ok = true;
@@ -621,6 +637,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
         launch_combine_sorted(w.y, w.slot_pos, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, st);
       });
   } else {
+    const bool fuse = T <= kFuseCombineMaxT;
     route_tokens(L, xn, T, 0, st);
     timed("gateup", st, [&] { run_gateup(L, w, T, st); });
     timed("down", st, [&] { run_down(L, w, T, w.y, fuse, xo, xo, st); });
