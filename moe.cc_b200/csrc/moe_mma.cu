@@ -27,6 +27,8 @@
 #include "kernels.cuh"
 #include "tc.cuh"
 
+#include <stdlib.h>
+
 namespace moe {
 namespace mm {
 
@@ -325,6 +327,20 @@ static bool map_rows(TMap& t, const uint8_t* base, int kbytes, int J, int nt) {
   return map_u8(t, base, 2, dims, strides, box);
 }
 
+// Resident CTAs per SM. Two independent producer/MMA/epilogue pipelines per
+// SM measured faster than one with twice the stages (T=16 decode: gate/up 58
+// -> 51 us, down 39 -> 32 us); three leave too few stages. MOE_MMA_CTAS
+// overrides, for tuning runs.
+static int ctas_per_sm() {
+  static int c = 0;
+  if (!c) {
+    const char* e = getenv("MOE_MMA_CTAS");
+    c = e ? atoi(e) : 2;
+    if (c < 1 || c > 3) c = 2;
+  }
+  return c;
+}
+
 static int sm_count() {
   static int n = 0;
   if (!n) {
@@ -332,7 +348,7 @@ static int sm_count() {
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   }
-  return n;
+  return n * ctas_per_sm();
 }
 
 template <int DT, int MODE, int NT>
@@ -340,7 +356,7 @@ static bool launch_kernel(const TMap& a0, const TMap& a1, const TMap& b0, const 
                           cudaStream_t st) {
   constexpr int NM = MODE == GATEUP ? 2 : 1, NL = DT == 8 ? 2 : 1;
   a.stage_bytes = NM * 128 * 128 + NL * NT * 128;
-  const int budget = 220 * 1024;
+  const int budget = 220 * 1024 / ctas_per_sm();
   a.stages = (budget - 1024 - 256) / a.stage_bytes;
   if (a.stages > 8) a.stages = 8;
   if (a.stages < 2) return false;
