@@ -20,7 +20,7 @@
 namespace moe {
 namespace rt {
 
-constexpr int kE = 8, kT = 16, kThreads = 128;
+constexpr int kE = 8, kT = 16, kThreads = 256, kChainThreads = kE * kT, kChunks = 4;
 constexpr int kMaxTK = 256;     // T*K handled by the last CTA (decode sizes)
 constexpr int kMaxE = 256;
 constexpr int kMaxTiles = kMaxTK / 16 + kMaxE + 1;
@@ -40,73 +40,104 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
   const int pitch = a.D + 4;                                   // floats; padding spreads banks
   float* sw = reinterpret_cast<float*>(smem);                  // [kE][pitch]
   float* sx = sw + kE * pitch;                                 // [kT][pitch]
-  __shared__ uint64_t bar;
+  __shared__ uint64_t bar[kChunks];
   __shared__ int s_last;
   const int e0 = blockIdx.x * kE, t0 = blockIdx.y * kT;
   const int ne = min(kE, a.E - e0), nt = min(kT, a.T - t0);
   const int tid = threadIdx.x;
+  const int dc = a.D / kChunks;                                // columns per chunk
 
+  // the rows arrive in kChunks column chunks, each on its own barrier, so the
+  // chains start on chunk 0 while the rest is still in flight
   if (tid == 0) {
-    mbar_init(&bar, 1);
+    for (int c = 0; c < kChunks; ++c) mbar_init(&bar[c], 1);
     fence_mbar_init();
-    mbar_arrive_expect_tx(&bar, (uint32_t)((ne + nt) * a.D * 4));
-    for (int i = 0; i < ne; ++i) bulk_g2s(sw + i * pitch, a.W + (size_t)(e0 + i) * a.D, a.D * 4, &bar);
-    for (int i = 0; i < nt; ++i) bulk_g2s(sx + i * pitch, a.x + (size_t)(t0 + i) * a.D, a.D * 4, &bar);
+    for (int c = 0; c < kChunks; ++c) {
+      mbar_arrive_expect_tx(&bar[c], (uint32_t)((ne + nt) * dc * 4));
+      for (int i = 0; i < ne; ++i)
+        bulk_g2s(sw + i * pitch + c * dc, a.W + (size_t)(e0 + i) * a.D + c * dc, dc * 4, &bar[c]);
+      for (int i = 0; i < nt; ++i)
+        bulk_g2s(sx + i * pitch + c * dc, a.x + (size_t)(t0 + i) * a.D + c * dc, dc * 4, &bar[c]);
+    }
   }
   __syncthreads();
   // A timed-out copy flags the call as failed; the CTA still reports its
   // arrival below so the arrival counter stays consistent for later calls.
-  const bool ok = mbar_wait(&bar, 0, kWaitBudget);
-  if (!ok && tid == 0) atomicOr(a.err, kErrTimeout);
+  bool ok = true;
 
-  // ---- exact sequential chain: one (token, expert) per thread ----
-  const int tt = tid / kE, ee = tid % kE;
-  if (ok && tt < nt && ee < ne) {
+  if (tid < kChainThreads) {
+    // ---- exact sequential chain: one (token, expert) per thread ----
+    const int tt = tid / kE, ee = tid % kE;
+    const bool mine = tt < nt && ee < ne;
     const float* xr = sx + tt * pitch;
     const float* wr = sw + ee * pitch;
     float acc = 0.0f;
-#pragma unroll 8
-    for (int k = 0; k < a.D; k += 4) {
-      const float4 xv = *reinterpret_cast<const float4*>(xr + k);
-      const float4 wv = *reinterpret_cast<const float4*>(wr + k);
-      acc = fadd(acc, fmul(xv.x, wv.x));
-      acc = fadd(acc, fmul(xv.y, wv.y));
-      acc = fadd(acc, fmul(xv.z, wv.z));
-      acc = fadd(acc, fmul(xv.w, wv.w));
-    }
-    if (a.b) acc = fadd(acc, __ldg(a.b + e0 + ee));
-    a.logits[(size_t)(t0 + tt) * a.E + e0 + ee] = acc;
-  }
-
-  // ---- truncated activations: this CTA's column slice of its tokens ----
-  if (ok) {
-    const int c0 = (int)((long)a.D * blockIdx.x / gridDim.x);
-    const int c1 = (int)((long)a.D * (blockIdx.x + 1) / gridDim.x);
-    const int w = c1 - c0;
-    int bad = 0;
-    for (int q = tid; q < nt * w; q += kThreads) {
-      const int t = q / w, k = c0 + q % w;
-      const int v = trunc_scale(sx[t * pitch + k], DT == 8 ? 127.0f : 7.0f);
-      uint8_t* ar = a.xact + (size_t)(t0 + t) * 2 * a.D;
-      if (DT == 8) {
-        bad |= (v < -32768 || v > 32767);
-        ar[k] = (uint8_t)(v & 0xFF);
-        ar[a.D + k] = (uint8_t)((v >> 8) & 0xFF);
-      } else {
-        bad |= (v < -128 || v > 127);
-        ar[q4_act_pos(k)] = (uint8_t)(v & 0xFF);
+    for (int c = 0; c < kChunks; ++c) {
+      if (!mbar_wait(&bar[c], 0, kWaitBudget)) { ok = false; break; }
+      if (!mine) continue;
+      // 16-k register blocks, the next block loaded before the current
+      // block's 16 dependent adds, so shared-memory latency overlaps the chain
+      const float4* xc = reinterpret_cast<const float4*>(xr + c * dc);
+      const float4* wc = reinterpret_cast<const float4*>(wr + c * dc);
+      const int nb = dc / 16;
+      float4 xb[4], wb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) { xb[i] = xc[i]; wb[i] = wc[i]; }
+      for (int blk = 0; blk < nb; ++blk) {
+        float4 xn[4], wn[4];
+        const int nxt = blk + 1 < nb ? blk + 1 : blk;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { xn[i] = xc[4 * nxt + i]; wn[i] = wc[4 * nxt + i]; }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc = fadd(acc, fmul(xb[i].x, wb[i].x));
+          acc = fadd(acc, fmul(xb[i].y, wb[i].y));
+          acc = fadd(acc, fmul(xb[i].z, wb[i].z));
+          acc = fadd(acc, fmul(xb[i].w, wb[i].w));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { xb[i] = xn[i]; wb[i] = wn[i]; }
       }
     }
-    if (bad) atomicOr(a.err, kErrRange);
-    if (DT == 4 && blockIdx.x == 0) {       // Σ activation per token (Q4 zero point)
-      for (int t = tid / 32; t < nt; t += kThreads / 32) {
-        int s = 0;
-        for (int k = tid % 32; k < a.D; k += 32) s += trunc_scale(sx[t * pitch + k], 7.0f);
-        s = warp_sum(s);
-        if ((tid & 31) == 0) a.xsum[t0 + t] = s;
+    if (ok && mine) {
+      if (a.b) acc = fadd(acc, __ldg(a.b + e0 + ee));
+      a.logits[(size_t)(t0 + tt) * a.E + e0 + ee] = acc;
+    }
+  } else {
+    // ---- truncated activations: this CTA's column slice of its tokens ----
+    const int q0 = tid - kChainThreads, nq = kThreads - kChainThreads;
+    for (int c = 0; c < kChunks; ++c)
+      if (!mbar_wait(&bar[c], 0, kWaitBudget)) { ok = false; break; }
+    if (ok) {
+      const int c0 = (int)((long)a.D * blockIdx.x / gridDim.x);
+      const int c1 = (int)((long)a.D * (blockIdx.x + 1) / gridDim.x);
+      const int w = c1 - c0;
+      int bad = 0;
+      for (int q = q0; q < nt * w; q += nq) {
+        const int t = q / w, k = c0 + q % w;
+        const int v = trunc_scale(sx[t * pitch + k], DT == 8 ? 127.0f : 7.0f);
+        uint8_t* ar = a.xact + (size_t)(t0 + t) * 2 * a.D;
+        if (DT == 8) {
+          bad |= (v < -32768 || v > 32767);
+          ar[k] = (uint8_t)(v & 0xFF);
+          ar[a.D + k] = (uint8_t)((v >> 8) & 0xFF);
+        } else {
+          bad |= (v < -128 || v > 127);
+          ar[q4_act_pos(k)] = (uint8_t)(v & 0xFF);
+        }
+      }
+      if (bad) atomicOr(a.err, kErrRange);
+      if (DT == 4 && blockIdx.x == 0) {       // Σ activation per token (Q4 zero point)
+        for (int t = q0 / 32; t < nt; t += nq / 32) {
+          int sacc = 0;
+          for (int k = q0 % 32; k < a.D; k += 32) sacc += trunc_scale(sx[t * pitch + k], 7.0f);
+          sacc = warp_sum(sacc);
+          if ((q0 & 31) == 0) a.xsum[t0 + t] = sacc;
+        }
       }
     }
   }
+  if (!ok && (tid & 31) == 0) atomicOr(a.err, kErrTimeout);
 
   // ---- last CTA: top-k, softmax, routing ----
   __threadfence();
@@ -122,39 +153,43 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
   const int lane = tid & 31, warp = tid >> 5;
   const int TK = a.T * a.K;
   for (int i = tid; i < a.E_local; i += kThreads) cnt[i] = 0;
-  // top-k per token: warp per token, K rounds of a warp arg-max; lane r keeps
-  // round r's winner, so the softmax and the stores are spread over lanes
+  // top-k per token: one warp per token, K rounds; each round is two warp
+  // reductions (redux.sync): the largest order-preserving key, then the lowest
+  // expert index among the lanes holding it. Keys of NaN and -inf are 0 (never
+  // chosen) and -0 is keyed as +0, so equal values tie exactly as in
+  // topk_desc's strict-'>' insertion (lower index first). Lane r keeps round
+  // r's winner; the softmax (:481-487) then runs across lanes, summing in order.
+  constexpr int PERL = kMaxE / 32;
   for (int t = warp; t < a.T; t += kThreads / 32) {
-    float v[kMaxE / 32];
+    unsigned key[PERL];
 #pragma unroll
-    for (int i = 0; i < kMaxE / 32; ++i) {
+    for (int i = 0; i < PERL; ++i) {
       const int e = lane + 32 * i;
-      v[i] = e < a.E ? __ldcg(a.logits + (size_t)t * a.E + e) : -INFINITY;
+      float v = e < a.E ? __ldcg(a.logits + (size_t)t * a.E + e) : -INFINITY;
+      if (v == 0.0f) v = 0.0f;
+      const unsigned u = __float_as_uint(v);
+      key[i] = !(v > -INFINITY) ? 0u : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
     }
     float myv = -INFINITY;
     int myi = -1;
     for (int r = 0; r < a.K; ++r) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
+      unsigned hk = 0; int hi = 0x7fffffff;
 #pragma unroll
-      for (int i = 0; i < kMaxE / 32; ++i)
-        if (v[i] > bv) { bv = v[i]; bi = lane + 32 * i; }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      for (int i = 0; i < PERL; ++i)
+        if (key[i] > hk) { hk = key[i]; hi = lane + 32 * i; }   // ascending index: first max kept
+      const unsigned M = __reduce_max_sync(0xffffffffu, hk);
+      const unsigned I = __reduce_min_sync(0xffffffffu, (M != 0u && hk == M) ? (unsigned)hi : 0x7fffffffu);
+      if (lane == r && M != 0u) {
+        const unsigned u = (M & 0x80000000u) ? (M & 0x7fffffffu) : ~M;
+        myv = __uint_as_float(u);
+        myi = (int)I;
       }
-      const bool found = bi != 0x7fffffff;
-      if (lane == r) { myv = found ? bv : -INFINITY; myi = found ? bi : -1; }
-      if (found && (bi & 31) == lane) {
+      if (M != 0u && (int)(I & 31) == lane) {
 #pragma unroll
-        for (int i = 0; i < kMaxE / 32; ++i)
-          if (lane + 32 * i == bi) v[i] = -INFINITY;
+        for (int i = 0; i < PERL; ++i)
+          if (lane + 32 * i == (int)I) key[i] = 0u;
       }
     }
-    // softmax over the K selected (:481-487): max is exact in any order; the
-    // sum is accumulated in the reference's order i = 0..K-1
     float mx = __shfl_sync(0xffffffffu, myv, 0);
     for (int i = 1; i < a.K; ++i) {
       const float vi = __shfl_sync(0xffffffffu, myv, i);
@@ -253,7 +288,7 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
 bool decode_route_supported(const LayerDev& L, int T, const float* x) {
   const int El = L.e_end - L.e_begin;
   return T * L.topk <= rt::kMaxTK && L.E <= rt::kMaxE && El <= rt::kMaxE && L.topk <= 32 &&
-         L.D % 4 == 0 && (size_t)(rt::kE + rt::kT) * (L.D + 4) * 4 <= 200 * 1024 &&
+         L.D % (16 * rt::kChunks) == 0 && (size_t)(rt::kE + rt::kT) * (L.D + 4) * 4 <= 200 * 1024 &&
          ((uintptr_t)x % 16) == 0 && ((uintptr_t)L.router_w % 16) == 0;
 }
 
