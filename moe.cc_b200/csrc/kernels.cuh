@@ -114,6 +114,7 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
                      const float* xres, float* out, int* err, cudaStream_t st);
 void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
                            const float* xres, float* out, int T, int D, int K, cudaStream_t st);
+void launch_unsort_rows(const LayerDev& L, const Workspace& ws, int T, float* y_slots, cudaStream_t st);
 }  // namespace moe
 
 namespace moe {

@@ -457,4 +457,25 @@ void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p,
   combine_sorted_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(ys, slot_pos, p, idx, xres, out, T, D, K);
 }
 
+// Expert-parallel output: slot-ordered rows of this rank's slots, zeros for
+// slots whose expert lives on another rank (so a sum over ranks is exact).
+__global__ void unsort_rows_kernel(const float* __restrict__ ys, const int* __restrict__ slot_pos,
+                                   const int* __restrict__ idx, int e_begin, int e_end,
+                                   float* __restrict__ y_slots, int D) {
+  const int s = blockIdx.x;
+  const int e = idx[s];
+  float4* dst = reinterpret_cast<float4*>(y_slots + (size_t)s * D);
+  if (e < e_begin || e >= e_end) {
+    for (int i = threadIdx.x; i < D / 4; i += blockDim.x) dst[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
+  }
+  const float4* src = reinterpret_cast<const float4*>(ys + (size_t)slot_pos[s] * D);
+  for (int i = threadIdx.x; i < D / 4; i += blockDim.x) dst[i] = src[i];
+}
+
+void launch_unsort_rows(const LayerDev& L, const Workspace& ws, int T, float* y_slots, cudaStream_t st) {
+  unsort_rows_kernel<<<T * L.topk, 128, 0, st>>>(ws.y, ws.slot_pos, ws.topk_idx, L.e_begin, L.e_end,
+                                                 y_slots, L.D);
+}
+
 }  // namespace moe

@@ -669,11 +669,25 @@ int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots, int*
   cudaStream_t st = (cudaStream_t)stream;
   const Workspace& w = g.ws;
   const size_t TK = (size_t)T * L.topk;
-  CU(cudaMemsetAsync(y_slots, 0, sizeof(float) * TK * L.D, st));
-  route_tokens(L, x_norm2, T, 0, st);
-  if (L.e_end > L.e_begin) {
-    timed("gateup", st, [&] { run_gateup(L, w, T, st); });
-    timed("down", st, [&] { run_down(L, w, T, y_slots, false, nullptr, nullptr, st); });
+  if (use_tensor_cores(L, 0)) {
+    const int nt = mma_tile_n(T);
+    route_tokens(L, x_norm2, T, nt, st);
+    timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
+    bool ok = true;
+    timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
+    if (ok)
+      timed("mma_down", st, [&] {
+        ok = launch_mma_down(L, w, T, nt, w.y, false, nullptr, nullptr, g.d_err, st);
+      });
+    if (!ok) return set_err(MOE_ERR_CUDA, "tensor-core launch failed (tensor map or shared memory)");
+    timed("unsort", st, [&] { launch_unsort_rows(L, w, T, y_slots, st); });
+  } else {
+    CU(cudaMemsetAsync(y_slots, 0, sizeof(float) * TK * L.D, st));
+    route_tokens(L, x_norm2, T, 0, st);
+    if (L.e_end > L.e_begin) {
+      timed("gateup", st, [&] { run_gateup(L, w, T, st); });
+      timed("down", st, [&] { run_down(L, w, T, y_slots, false, nullptr, nullptr, st); });
+    }
   }
   if (topk_idx_out) CU(cudaMemcpyAsync(topk_idx_out, w.topk_idx, sizeof(int) * TK, cudaMemcpyDeviceToDevice, st));
   if (topk_p_out) CU(cudaMemcpyAsync(topk_p_out, w.topk_p, sizeof(float) * TK, cudaMemcpyDeviceToDevice, st));

@@ -1,0 +1,62 @@
+"""One expert-parallel rank for tests/test_gpu_ep.py (run as a child process).
+
+Rank r owns experts [r*E/W, (r+1)*E/W): it routes all tokens, computes its own
+experts' slots with moe_ffn_partial, exchanges the slot outputs (sum over
+ranks: NCCL when each rank has its own GPU, gloo over host copies when the
+ranks share one GPU) and applies moe_ffn_combine. Rank 0 saves the result.
+"""
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "moe.cc_b200"))
+import moe_cuda as mc  # noqa: E402
+import synth as sy  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    out_path, T, dt = sys.argv[1], int(sys.argv[2]), int(sys.argv[3])
+    ngpu = torch.cuda.device_count()
+    dev = rank if ngpu >= world else 0
+    torch.cuda.set_device(dev)
+    backend = "nccl" if ngpu >= world else "gloo"
+    if backend == "nccl":
+        dist.init_process_group(backend, device_id=torch.device("cuda", dev))
+    else:
+        dist.init_process_group(backend)
+    mc.init(dev, world, rank)
+    L = sy.make_layer_dev(torch, 1, 0, 128, 2048, 768, dt)
+    mc.upload_layer(0, L, device_arrays=True)
+    xn = sy.make_tokens_dev(torch, 501, T, 2048)
+    xa = sy.make_tokens_dev(torch, 502, T, 2048)
+    y = torch.empty(T * 8, 2048, device="cuda")
+    p = torch.empty(T, 8, device="cuda")
+    mc.moe_ffn_partial(0, xn, y, None, p)
+    torch.cuda.synchronize()
+    mc.check_status()
+    if backend == "nccl":
+        dist.all_reduce(y)
+    else:
+        yc = y.cpu()
+        dist.all_reduce(yc)
+        y.copy_(yc)
+    out = xa.clone()
+    mc.moe_ffn_combine(y, p, out)
+    torch.cuda.synchronize()
+    mc.check_status()
+    if rank == 0:
+        Lh = {k: (v.cpu().numpy() if hasattr(v, "cpu") else v) for k, v in L.items()}
+        np.savez(out_path, out=out.cpu().numpy(), xn=xn.cpu().numpy(), xa=xa.cpu().numpy(), **{
+            k: v for k, v in Lh.items() if isinstance(v, np.ndarray)})
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
