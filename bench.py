@@ -126,14 +126,16 @@ def alg_bytes(kernel, T, U, dt):
     if kernel == "gateup":
         return U * (2 * F * gu_rb + 2 * F * 4)
     if kernel == "down":
-        return U * (D * d_rb + D * 4) + T * D * 4 * 2   # + residual read, output write
-    if kernel == "router_logits":
+        return U * (D * d_rb + D * 4)
+    if kernel in ("router_logits", "route"):
         return E * D * 4 + T * D * 4 + T * E * 4
+    if kernel == "combine":
+        return T * TOPK * D * 4 + 2 * T * D * 4    # slot outputs in, residual in, result out
     return None
 
 
 def layer_bytes_step(T, U, dt):
-    return sum(alg_bytes(k, T, U, dt) for k in ("router_logits", "gateup", "down"))
+    return sum(alg_bytes(k, T, U, dt) for k in ("route", "gateup", "down", "combine"))
 
 
 def build_layers(torch, mc, sy, nl, dt):
@@ -157,60 +159,109 @@ def make_inputs(torch, mc, T, pool, seed):
 
 
 class Runner:
-    """One decode step on this rank (N=1: moe_ffn; N>1: partial + all-reduce + combine)."""
+    """One decode step on this rank.
 
-    def __init__(self, torch, mc, dist, world, T, nl, pool):
-        self.torch, self.mc, self.dist, self.world = torch, mc, dist, world
+    N=1: moe_ffn on the T resident tokens.
+    N>1 (expert parallel, T tokens per rank): all-gather the ranks' tokens,
+    moe_ffn_partial on all T*N tokens (every rank routes all of them; each
+    computes only its own experts' slots), reduce-scatter the slot outputs so
+    each rank receives its own tokens' slots (exactly one rank contributes each
+    slot, so the sum is exact), then the k-ordered combine + residual.
+    """
+
+    def __init__(self, torch, mc, dist, world, rank, T, nl, pool):
+        self.torch, self.mc, self.dist, self.world, self.rank = torch, mc, dist, world, rank
         self.T, self.nl = T, nl
-        self.xs, self.xa = make_inputs(torch, mc, T, pool, seed=T)
+        self.xs, self.xa = make_inputs(torch, mc, T, pool, seed=T * 131 + rank)
         self.out = [x.clone() for x in self.xa]
-        self.y = torch.empty(T * TOPK, D, device="cuda") if world > 1 else None
-        self.p = torch.empty(T, TOPK, device="cuda") if world > 1 else None
         self.stream = torch.cuda.current_stream()
+        if world > 1:
+            TN = T * world
+            self.x_all = torch.empty(TN, D, device="cuda")
+            self.y_all = torch.empty(TN * TOPK, D, device="cuda")
+            self.p_all = torch.empty(TN, TOPK, device="cuda")
+            self.y_loc = torch.empty(T * TOPK, D, device="cuda")
 
-    def step(self, i, topk_idx=None):
+    def step(self, i, topk_idx=None, x_in=None, out=None):
         j = i % len(self.xs)
         layer = i % self.nl
+        x = self.xs[j] if x_in is None else x_in
+        o = self.out[j] if out is None else out
         if self.world == 1:
-            self.mc.moe_ffn_dev(layer, self.xs[j], self.out[j], topk_idx, None, stream=self.stream)
+            self.mc.moe_ffn_dev(layer, x, o, topk_idx, None, stream=self.stream)
         else:
-            self.mc.moe_ffn_partial(layer, self.xs[j], self.y, topk_idx, self.p, stream=self.stream)
-            self.dist.all_reduce(self.y)
-            self.mc.moe_ffn_combine(self.y, self.p, self.out[j], TOPK, stream=self.stream)
+            self.dist.all_gather_into_tensor(self.x_all, x)
+            self.mc.moe_ffn_partial(layer, self.x_all, self.y_all, topk_idx, self.p_all, stream=self.stream)
+            self.dist.reduce_scatter_tensor(self.y_loc, self.y_all)
+            p = self.p_all[self.rank * self.T:(self.rank + 1) * self.T]
+            self.mc.moe_ffn_combine(self.y_loc, p, o, TOPK, stream=self.stream)
 
-    def timed(self, steps, warmup, barrier=True):
+    def _bracket(self):
+        self.torch.cuda.synchronize()
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def _max_over_ranks(self, ms):
+        if self.world > 1:
+            t = self.torch.tensor([ms], device="cuda")
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    def timed(self, steps, warmup):
         torch = self.torch
         for i in range(warmup):
             self.step(i)
-        torch.cuda.synchronize()
-        if barrier and self.world > 1:
-            self.dist.barrier()
-        torch.cuda.synchronize()
+        self._bracket()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(self.stream)
         for i in range(steps):
             self.step(warmup + i)
         b.record(self.stream)
-        torch.cuda.synchronize()
-        if barrier and self.world > 1:
-            self.dist.barrier()
-        ms = a.elapsed_time(b)
-        if self.world > 1:
-            t = torch.tensor([ms], device="cuda")
-            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
-            ms = float(t.item())
+        self._bracket()
+        ms = self._max_over_ranks(a.elapsed_time(b))
         self.mc.check_status()
         return ms
 
-    def distinct_experts(self, steps, warmup):
-        """U per step (routing is a pure function of layer and input)."""
+    def timed_host(self, steps, warmup):
+        """Same steps with the tokens coming from pinned host memory and the
+        result going back to it, copies inside the timed region (N>1 e2e)."""
         torch = self.torch
-        idx = torch.empty(steps, self.T, TOPK, dtype=torch.int32, device="cuda")
+        hx = [torch.empty(self.T, D).pin_memory() for _ in range(4)]
+        for i, h in enumerate(hx):
+            h.copy_(self.xs[i].cpu())
+        ho = torch.empty(self.T, D).pin_memory()
+        xd, od = torch.empty(self.T, D, device="cuda"), torch.empty(self.T, D, device="cuda")
+
+        def one(i):
+            xd.copy_(hx[i % 4], non_blocking=True)
+            od.copy_(self.xa[i % len(self.xa)])
+            self.step(i, x_in=xd, out=od)
+            ho.copy_(od, non_blocking=True)
+        for i in range(warmup):
+            one(i)
+        self._bracket()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(self.stream)
+        for i in range(steps):
+            one(warmup + i)
+        b.record(self.stream)
+        self._bracket()
+        return self._max_over_ranks(a.elapsed_time(b))
+
+    def distinct_experts(self, steps, warmup):
+        """Distinct experts this rank computes per step (routing is a pure
+        function of layer and input)."""
+        torch = self.torch
+        TN = self.T * self.world
+        idx = torch.empty(steps, TN, TOPK, dtype=torch.int32, device="cuda")
         for i in range(steps):
             self.step(warmup + i, idx[i])
         torch.cuda.synchronize()
         h = idx.cpu().numpy()
-        return [len(set(h[i].ravel().tolist())) for i in range(steps)]
+        lo, hi = E * self.rank // self.world, E * (self.rank + 1) // self.world
+        return [len({e for e in h[i].ravel().tolist() if lo <= e < hi}) for i in range(steps)]
 
 
 def e2e_host(torch, mc, T, steps, warmup, nl):
@@ -357,11 +408,12 @@ def run_ours(args):
     steps, warmup = args.steps, max(args.warmup, 3)
     pool = 64
 
-    run = Runner(torch, mc, dist, world, T, nl, pool)
+    run = Runner(torch, mc, dist, world, rank, T, nl, pool)
     with ClockSampler(local) as clk:
         ms = run.timed(steps, warmup)
     clocks = clk.summary()
-    value = T * steps / (ms / 1e3)
+    TN = T * world                       # tokens per step over all ranks
+    value = TN * steps / (ms / 1e3)
 
     # routed experts per step and per-kernel device times (separate profiled pass)
     Us = run.distinct_experts(min(steps, 64), warmup)
@@ -374,7 +426,7 @@ def run_ours(args):
     kern = {}
     for name, (tot, cnt) in prof.items():
         avg_ms = tot / max(cnt, 1)
-        b = alg_bytes(name, T, U / 1.0 if world == 1 else U / world, dt)
+        b = alg_bytes(name, TN if name == "route" else T, U, dt)
         kern[name] = {"avg_us": avg_ms * 1e3, "launches": cnt,
                       "share": tot / max(sum(v[0] for v in prof.values()), 1e-9),
                       "alg_bytes": b, "gbs": (b / (avg_ms * 1e-3) / 1e9) if b else None}
@@ -383,7 +435,7 @@ def run_ours(args):
     roof = {"kernel": dom, "bound": "hbm", "achieved": kern[dom]["gbs"], "peak": peak,
             "unit": "GB/s", "frac": kern[dom]["gbs"] / peak, "peak_source": peak_kind,
             "traffic": tr, "alg_bytes_per_launch": kern[dom]["alg_bytes"]}
-    layer_gbs = layer_bytes_step(T, U, dt) / (ms / steps * 1e-3) / 1e9
+    layer_gbs = layer_bytes_step(T, U, dt) / (ms / steps * 1e-3) / 1e9   # this rank's bytes
     launches_per_step = sum(v["launches"] for v in kern.values()) / steps
 
     extra = {}
@@ -391,16 +443,20 @@ def run_ours(args):
         for t in [int(v) for v in args.extra_t.split(",") if v]:
             if t == T:
                 continue
-            r2 = Runner(torch, mc, dist, world, t, nl, pool)
+            r2 = Runner(torch, mc, dist, world, rank, t, nl, pool)
             ms2 = r2.timed(steps, warmup)
             u2 = r2.distinct_experts(min(steps, 64), warmup)
             extra[f"T{t}"] = {"tok_s": t * steps / (ms2 / 1e3), "us_per_step": ms2 * 1e3 / steps,
                               "distinct_experts": sum(u2) / len(u2),
                               "layer_gbs": layer_bytes_step(t, sum(u2) / len(u2), dt)
                               / (ms2 / steps * 1e-3) / 1e9}
-    e2e = None
     if world == 1:
         e2e = e2e_host(torch, mc, T, steps, warmup, nl)
+    else:
+        ms_h = run.timed_host(steps, warmup)
+        e2e = {"value": TN * steps / (ms_h / 1e3), "unit": "tok/s",
+               "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4,
+               "ms_per_step": ms_h / steps, "note": "per rank: tokens in from pinned host, result out"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(mc, host_layer_from_device(torch, mc, sy, dt), T)
@@ -408,10 +464,10 @@ def run_ours(args):
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
                 "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,
-                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "int32-acc q8" if dt == 2 else "int32-acc q4", "data": "synthetic",
-                "config": {"workload": f"configs[1]: Qwen3-30B-A3B MoE layer decode, T={T}",
-                           "tokens": T, "experts": E, "hidden": D, "moe_intermediate": F,
+                "config": {"workload": f"configs[1]: Qwen3-30B-A3B MoE layer decode, T={T} per GPU",
+                           "tokens": T, "tokens_per_step": TN, "experts": E, "hidden": D, "moe_intermediate": F,
                            "top_k": TOPK, "resident_layers": nl, "input_pool": pool,
                            "parallelism": f"ep{world}",
                            "l2": "inputs larger than L2: steps rotate over resident layers"},

@@ -21,7 +21,7 @@ namespace moe {
 namespace rt {
 
 constexpr int kE = 8, kT = 16, kThreads = 256, kChainThreads = kE * kT, kChunks = 4;
-constexpr int kMaxTK = 256;     // T*K handled by the last CTA (decode sizes)
+constexpr int kMaxTK = 2048;    // T*K handled by the last CTA (decode and EP-gathered sizes)
 constexpr int kMaxE = 256;
 constexpr int kMaxTiles = kMaxTK / 16 + kMaxE + 1;
 
@@ -261,16 +261,32 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
     }
   }
   __syncthreads();
-  // slot lists in ascending slot order within each expert
+  // slot lists: placed with shared-memory atomics, then each expert's list is
+  // sorted by slot id (one thread per expert) so the order is deterministic:
+  // ascending slot within each expert, experts ascending
   int* r_slots = s_route + 2 + 2 * a.E_local;
+  for (int i = tid; i < a.E_local; i += kThreads) cnt[i] = 0;
+  __syncthreads();
   for (int s = tid; s < TK; s += kThreads) {
     const int el = sidx[s] - a.e_begin;
     if (el < 0 || el >= a.E_local) continue;
-    int rank = 0;
-    for (int s2 = 0; s2 < s; ++s2) rank += sidx[s2] == sidx[s];
-    const int j = start[el] + rank;
-    r_slots[j] = s;
-    if (a.slot_pos) a.slot_pos[s] = j;
+    r_slots[start[el] + atomicAdd(&cnt[el], 1)] = s;
+  }
+  __syncthreads();
+  for (int el = tid; el < a.E_local; el += kThreads) {
+    int* lst = r_slots + start[el];
+    const int c = cnt[el];
+    for (int i = 1; i < c; ++i) {
+      const int v = lst[i];
+      int j = i - 1;
+      while (j >= 0 && lst[j] > v) { lst[j + 1] = lst[j]; --j; }
+      lst[j + 1] = v;
+    }
+  }
+  __syncthreads();
+  if (a.slot_pos) {
+    const int J = r_off[s_route[0]];
+    for (int j = tid; j < J; j += kThreads) a.slot_pos[r_slots[j]] = j;
   }
   __syncthreads();
   // copy the tables out with all threads
