@@ -98,6 +98,14 @@ __host__ __device__ __forceinline__ int q4_act_pos(int k) {
   return (j << 3) + ((r & 1) << 2) + (r >> 1);  // E_j at 8j..8j+3, O_j at 8j+4..
 }
 
+// Position of activation element k in the tensor-core Q4 layout: within each
+// 32-element group, the even elements first, then the odd ones. This matches
+// how the tensor-core path unpacks 16 packed weight bytes (32 nibbles) into 16
+// low-nibble bytes followed by 16 high-nibble bytes.
+__host__ __device__ __forceinline__ int q4_mma_pos(int k) {
+  return (k & ~31) + ((k & 1) << 4) + ((k & 31) >> 1);
+}
+
 // Error flag bits written by kernels (read by the host).
 enum : int { kErrRange = 1, kErrTimeout = 2 };
 

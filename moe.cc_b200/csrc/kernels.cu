@@ -83,7 +83,8 @@ __device__ __forceinline__ float dequant_out(int dot, int asum, float s) {
 template <int DT>
 __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restrict__ x, int K,
                                                            uint8_t* __restrict__ act, int act_stride,
-                                                           int* __restrict__ asum, int* err) {
+                                                           int* __restrict__ asum, int* err,
+                                                           int mma_layout) {
   const int m = blockIdx.x;
   const float* xr = x + (size_t)m * K;
   uint8_t* ar = act + (size_t)m * act_stride;
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
       ar[K + k] = (uint8_t)((a >> 8) & 0xFF);
     } else {
       bad |= (a < -128 || a > 127);
-      ar[q4_act_pos(k)] = (uint8_t)(a & 0xFF);
+      ar[mma_layout ? q4_mma_pos(k) : q4_act_pos(k)] = (uint8_t)(a & 0xFF);
       sum += a;
     }
   }
@@ -115,12 +116,12 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
 }
 
 void launch_quantize_act(const float* x, int M, int K, int dtype, uint8_t* act, int act_stride,
-                         int* asum, int* err, cudaStream_t st) {
+                         int* asum, int* err, cudaStream_t st, int mma_layout) {
   if (M <= 0) return;
   if (dtype == 2)
-    quantize_act_kernel<8><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err);
+    quantize_act_kernel<8><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err, mma_layout);
   else
-    quantize_act_kernel<4><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err);
+    quantize_act_kernel<4><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err, mma_layout);
 }
 
 // --------------------------------------------------------------------------

@@ -66,8 +66,10 @@ __host__ __device__ inline RouteView route_view(int* route, int E) {
 // ---- launchers (all asynchronous on `st`) ----
 // xact planes from fp32 rows: Q8 -> [lo K][hi K] per row, Q4 -> permuted K
 // bytes per row + rowsum. Sets err bit kErrRange on out-of-range values.
+// mma_layout: Q4 activations in the tensor-core order (q4_mma_pos)
 void launch_quantize_act(const float* x, int M, int K, int dtype, uint8_t* act,
-                         int act_stride, int* asum, int* err, cudaStream_t st);
+                         int act_stride, int* asum, int* err, cudaStream_t st,
+                         int mma_layout = 0);
 // C[m][n] = sequential fp32 Σ_k A[m][k] W[n][k] (+ b[n]).
 void launch_f32_seq_matmul(const float* A, const float* W, const float* b,
                            float* C, int M, int N, int K, cudaStream_t st);

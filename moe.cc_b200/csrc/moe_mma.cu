@@ -33,7 +33,9 @@ namespace moe {
 namespace mm {
 
 enum { GATEUP = 0, DOWN = 1 };
-constexpr int kThreads = 6 * 32;
+constexpr int kThreads = 6 * 32;        // Q8: producer, MMA, 4 epilogue warps
+constexpr int kThreadsQ4 = 10 * 32;     // Q4: + 4 nibble-expander warps
+constexpr int kPackedBytes = 128 * 64;  // one packed Q4 tile: 128 rows x 128 nibbles
 
 struct __align__(64) TMap { CUtensorMap m; };
 
@@ -51,12 +53,13 @@ struct Args {
   float* ys;                               // DOWN output [J][D]
   int fuse, T, topk;
   int* cnt; const int* slot_pos; const float* topk_p; const int* topk_idx;
+  const int* xsum; int* hsum;                // Q4 zero-point sums (token / slot)
   const float* xres; float* out;
   int* err;
 };
 
 template <int DT, int MODE, int NT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
     moe_mma_kernel(const __grid_constant__ TMap tmA0, const __grid_constant__ TMap tmA1,
                    const __grid_constant__ TMap tmB0, const __grid_constant__ TMap tmB1, const Args a) {
   constexpr int NM = MODE == GATEUP ? 2 : 1;     // weight matrices per tile
@@ -75,6 +78,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + a.stages;
   uint64_t* acc_full = empty + a.stages;     // [2]
   uint64_t* acc_empty = acc_full + 2;        // [2]
+  uint64_t* ready = acc_empty + 2;           // [stages] Q4: expanded A tiles written
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_issued;
 
@@ -86,6 +90,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     s_abort = 0; s_issued = 0;
     for (int s = 0; s < a.stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 4); }
+    if (DT == 4)
+      for (int s = 0; s < a.stages; ++s) mbar_init(&ready[s], 4);
     fence_mbar_init();
     tc::prefetch_tmap(&tmA0.m); tc::prefetch_tmap(&tmB0.m);
     if (NM == 2) tc::prefetch_tmap(&tmA1.m);
@@ -105,7 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------- TMA producer -------------------------
     if (lane == 0) {
-      const uint32_t bytes = NM * A_BYTES + NL * B_BYTES;
+      const uint32_t bytes = (DT == 4 ? NM * kPackedBytes : NM * A_BYTES) + NL * B_BYTES;
       int it = 0;
       for (int u = u0; u < u1 && !*abort_flag; ++u) {
         const int tile = u / a.n_mblk, mb = u % a.n_mblk;
@@ -117,8 +123,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sb = smem + (size_t)st * a.stage_bytes;
           mbar_arrive_expect_tx(&full[st], bytes);
-          tc::tma_load_3d(sb, &tmA0.m, kc * 128, mb * 128, e, &full[st]);
-          if (NM == 2) tc::tma_load_3d(sb + A_BYTES, &tmA1.m, kc * 128, mb * 128, e, &full[st]);
+          if (DT == 8) {
+            tc::tma_load_3d(sb, &tmA0.m, kc * 128, mb * 128, e, &full[st]);
+            if (NM == 2) tc::tma_load_3d(sb + A_BYTES, &tmA1.m, kc * 128, mb * 128, e, &full[st]);
+          } else {   // packed nibbles into the staging area; expanders build the A tiles
+            uint8_t* stg = sb + NM * A_BYTES + NL * B_BYTES;
+            tc::tma_load_3d(stg, &tmA0.m, kc * 64, mb * 128, e, &full[st]);
+            if (NM == 2) tc::tma_load_3d(stg + kPackedBytes, &tmA1.m, kc * 64, mb * 128, e, &full[st]);
+          }
           tc::tma_load_2d(sb + NM * A_BYTES, &tmB0.m, kc * 128, j0, &full[st]);
           if (NL == 2) tc::tma_load_2d(sb + NM * A_BYTES + B_BYTES, &tmB1.m, kc * 128, j0, &full[st]);
           s_issued = it + 1;
@@ -143,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t dbase = tmem + buf * ACC;
         for (int kc = 0; kc < a.kchunks; ++kc, ++it) {
           const int st = it % a.stages;
-          if (!mbar_wait(&full[st], (it / a.stages) & 1, kWaitBudget)) {
+          if (!mbar_wait(DT == 4 ? &ready[st] : &full[st], (it / a.stages) & 1, kWaitBudget)) {
             atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
           }
           tc::fence_after_sync();
@@ -165,6 +177,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (*abort_flag) break;
         tc::mma_commit(&acc_full[buf]);             // accumulator of this tile complete
+      }
+    }
+  } else if (DT == 4 && warp >= 6) {
+    // ------------------- Q4 nibble expanders ------------------------
+    // row r of each packed tile (64 bytes = 128 nibbles) becomes 128 bytes of
+    // the 128B-swizzled u8 A tile: packed 16-byte chunk c -> chunk 2c holds its
+    // 16 low nibbles, chunk 2c+1 its 16 high nibbles (the activations use the
+    // same k order, q4_mma_pos). 16-byte chunk h of row r sits at h ^ (r & 7).
+    const int r = (warp - 6) * 32 + lane;
+    int it = 0;
+    for (int u = u0; u < u1 && !*abort_flag; ++u) {
+      for (int kc = 0; kc < a.kchunks; ++kc, ++it) {
+        const int st = it % a.stages;
+        if (!mbar_wait(&full[st], (it / a.stages) & 1, kWaitBudget)) {
+          if (lane == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; }
+          break;
+        }
+        uint8_t* sb = smem + (size_t)st * a.stage_bytes;
+        const uint8_t* stg = sb + NM * A_BYTES + NL * B_BYTES;
+#pragma unroll
+        for (int m = 0; m < NM; ++m) {
+          const uint4* src = reinterpret_cast<const uint4*>(stg + m * kPackedBytes + r * 64);
+          uint8_t* dst = sb + m * A_BYTES + r * 128;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 w = src[c];
+            const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
+            const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu,
+                                        (w.z >> 4) & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
+            *reinterpret_cast<uint4*>(dst + (((2 * c) ^ (r & 7)) << 4)) = lo;
+            *reinterpret_cast<uint4*>(dst + (((2 * c + 1) ^ (r & 7)) << 4)) = hi;
+          }
+        }
+        tc::fence_proxy_async_smem();     // generic-proxy writes -> visible to the MMA
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[st]);
       }
     }
   } else {
@@ -200,6 +248,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int m = 0; m < NM; ++m)
             dot[m] = NL == 2 ? (int)(v[m * 2][i] + (v[m * 2 + 1][i] << 8)) : (int)v[m][i];
+          if (DT == 4) {   // nibbles are stored +8: subtract 8 * Σ activation (exact mod 2^32)
+            const int as = MODE == GATEUP ? __ldg(a.xsum + __ldg(a.route + 2 + 2 * a.E_local + j) / a.topk)
+                                          : __ldcg(a.hsum + j);
+#pragma unroll
+            for (int m = 0; m < NM; ++m) dot[m] = (int)((unsigned)dot[m] - 8u * (unsigned)as);
+          }
           if (MODE == GATEUP) {
             const float g = fmul(fdiv(__int2float_rn(dot[0]), S), sc0);
             const float uu = fmul(fdiv(__int2float_rn(dot[NM - 1]), S), sc1);
@@ -209,6 +263,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (ha < -32768 || ha > 32767) atomicOr(a.err, kErrRange);
               a.hs0[(size_t)j * a.F + n] = (uint8_t)(ha & 0xFF);
               a.hs1[(size_t)j * a.F + n] = (uint8_t)((ha >> 8) & 0xFF);
+            } else {
+              if (ha < -128 || ha > 127) atomicOr(a.err, kErrRange);
+              a.hs0[(size_t)j * a.F + q4_mma_pos(n)] = (uint8_t)(ha & 0xFF);
+              // Σ h of slot j for the down projection's zero-point correction
+              const int ws = __reduce_add_sync(0xffffffffu, ha);
+              if (lane == 0) atomicAdd(a.hsum + j, ws);
             }
           } else {
             a.ys[(size_t)j * a.rows + n] = fmul(fdiv(__int2float_rn(dot[0]), S), sc0);
@@ -301,22 +361,26 @@ static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 
 // uint8 tensor map, 128-byte inner box with 128-byte swizzle.
 static bool map_u8(TMap& t, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
-                   const cuuint32_t* box) {
+                   const cuuint32_t* box, bool swizzle = true) {
   auto fn = encoder();
   if (!fn) return false;
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = fn(&t.m, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), dims, strides, box, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-// weights of one projection over all local experts: (K bytes, rows, expert)
-static bool map_weights(TMap& t, const LayerDev& L, size_t off, int kbytes, int rows) {
-  const cuuint64_t dims[3] = {(cuuint64_t)kbytes, (cuuint64_t)rows, (cuuint64_t)(L.e_end - L.e_begin)};
-  const cuuint64_t strides[2] = {(cuuint64_t)kbytes, (cuuint64_t)L.expert_stride};
-  const cuuint32_t box[3] = {128, 128, 1};
-  return map_u8(t, L.slab + off, 3, dims, strides, box);
+// weights of one projection over all local experts: (row bytes, rows, expert).
+// Q8: 128-byte boxes, 128-byte swizzle (the MMA operand layout itself);
+// Q4: 64-byte boxes of packed nibbles, unswizzled (expanded in shared memory).
+static bool map_weights(TMap& t, const LayerDev& L, size_t off, int kelems, int rows) {
+  const bool q4 = L.dtype == 3;
+  const int rb = q4 ? kelems / 2 : kelems;
+  const cuuint64_t dims[3] = {(cuuint64_t)rb, (cuuint64_t)rows, (cuuint64_t)(L.e_end - L.e_begin)};
+  const cuuint64_t strides[2] = {(cuuint64_t)rb, (cuuint64_t)L.expert_stride};
+  const cuuint32_t box[3] = {q4 ? 64u : 128u, 128, 1};
+  return map_u8(t, L.slab + off, 3, dims, strides, box, !q4);
 }
 
 // expert-sorted activation plane: (K bytes, J rows); J >= the box height
@@ -341,26 +405,31 @@ static int ctas_per_sm() {
   return c;
 }
 
-static int sm_count() {
+static int sms() {
   static int n = 0;
   if (!n) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   }
-  return n * ctas_per_sm();
+  return n;
 }
+
+// Q4 stages carry the packed staging tiles too, so Q4 runs one CTA per SM
+// with the whole shared-memory budget.
+static int ctas_for(int dt) { return dt == 4 ? 1 : ctas_per_sm(); }
+static int grid_ctas(int dt) { return sms() * ctas_for(dt); }
 
 template <int DT, int MODE, int NT>
 static bool launch_kernel(const TMap& a0, const TMap& a1, const TMap& b0, const TMap& b1, Args a, int grid,
                           cudaStream_t st) {
   constexpr int NM = MODE == GATEUP ? 2 : 1, NL = DT == 8 ? 2 : 1;
-  a.stage_bytes = NM * 128 * 128 + NL * NT * 128;
-  const int budget = 220 * 1024 / ctas_per_sm();
+  a.stage_bytes = NM * 128 * 128 + NL * NT * 128 + (DT == 4 ? NM * kPackedBytes : 0);
+  const int budget = 220 * 1024 / ctas_for(DT);
   a.stages = (budget - 1024 - 256) / a.stage_bytes;
   if (a.stages > 8) a.stages = 8;
   if (a.stages < 2) return false;
-  const size_t smem = (size_t)a.stages * a.stage_bytes + 1024 + 8 * (2 * (size_t)a.stages + 4);
+  const size_t smem = (size_t)a.stages * a.stage_bytes + 1024 + 8 * (3 * (size_t)a.stages + 4);
   auto k = moe_mma_kernel<DT, MODE, NT>;
   static size_t attr = 0;
   if (smem > attr) {
@@ -368,7 +437,7 @@ static bool launch_kernel(const TMap& a0, const TMap& a1, const TMap& b0, const 
       return false;
     attr = smem;
   }
-  k<<<grid, kThreads, smem, st>>>(a0, a1, b0, b1, a);
+  k<<<grid, DT == 4 ? kThreadsQ4 : kThreads, smem, st>>>(a0, a1, b0, b1, a);
   return true;
 }
 
@@ -379,7 +448,7 @@ static bool launch_kernel(const TMap& a0, const TMap& a1, const TMap& b0, const 
 int mma_tile_n(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : 64; }
 
 bool mma_supported(const LayerDev& L) {
-  return L.dtype == 2 && L.D % 128 == 0 && L.F % 128 == 0 && mm::encoder() != nullptr;
+  return (L.dtype == 2 || L.dtype == 3) && L.D % 128 == 0 && L.F % 128 == 0 && mm::encoder() != nullptr;
 }
 
 void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream_t st) {
@@ -399,17 +468,19 @@ bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, in
   const int E_local = L.e_end - L.e_begin, TK = T * L.topk, cap = ws.cap_T * ws.cap_K;
   mm::TMap a0, a1, b0, b1;
   if (!mm::map_weights(a0, L, L.gq_off, L.D, L.F) || !mm::map_weights(a1, L, L.uq_off, L.D, L.F) ||
-      !mm::map_rows(b0, ws.xs0, L.D, cap, nt) || !mm::map_rows(b1, ws.xs1, L.D, cap, nt))
+      !mm::map_rows(b0, ws.xs0, L.D, cap, nt) || !mm::map_rows(b1, L.dtype == 2 ? ws.xs1 : ws.xs0, L.D, cap, nt))
     return false;
   mm::Args a{};
   a.rows = L.F; a.kchunks = L.D / 128; a.n_mblk = L.F / 128;
   a.route = ws.route; a.E_local = E_local; a.TK = TK; a.max_tiles = route_max_tiles(TK, E_local, nt);
   a.slab = L.slab; a.stride = L.expert_stride; a.s0_off = L.gs_off; a.s1_off = L.us_off;
   a.F = L.F; a.hs0 = ws.hs0; a.hs1 = ws.hs1; a.err = err;
-  const int units = a.max_tiles * a.n_mblk;
-  const int grid = units < mm::sm_count() ? units : mm::sm_count();
+  a.xsum = ws.xsum; a.hsum = ws.hsum; a.topk = L.topk;
+  const int units = a.max_tiles * a.n_mblk, gc = mm::grid_ctas(L.dtype == 2 ? 8 : 4);
+  const int grid = units < gc ? units : gc;
   bool ok = false;
-  NT_SWITCH(nt, (ok = mm::launch_kernel<8, mm::GATEUP, NT>(a0, a1, b0, b1, a, grid, st)));
+  if (L.dtype == 2) { NT_SWITCH(nt, (ok = mm::launch_kernel<8, mm::GATEUP, NT>(a0, a1, b0, b1, a, grid, st))); }
+  else { NT_SWITCH(nt, (ok = mm::launch_kernel<4, mm::GATEUP, NT>(a0, a1, b0, b0, a, grid, st))); }
   return ok;
 }
 
@@ -418,7 +489,7 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
   const int E_local = L.e_end - L.e_begin, TK = T * L.topk, cap = ws.cap_T * ws.cap_K;
   mm::TMap a0, b0, b1;
   if (!mm::map_weights(a0, L, L.dq_off, L.F, L.D) || !mm::map_rows(b0, ws.hs0, L.F, cap, nt) ||
-      !mm::map_rows(b1, ws.hs1, L.F, cap, nt))
+      !mm::map_rows(b1, L.dtype == 2 ? ws.hs1 : ws.hs0, L.F, cap, nt))
     return false;
   mm::Args a{};
   a.rows = L.D; a.kchunks = L.F / 128; a.n_mblk = L.D / 128;
@@ -427,10 +498,12 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
   a.ys = ys; a.fuse = fuse ? 1 : 0; a.T = T; a.topk = L.topk;
   a.cnt = ws.cnt; a.slot_pos = ws.slot_pos; a.topk_p = ws.topk_p; a.topk_idx = ws.topk_idx;
   a.xres = xres; a.out = out; a.err = err;
-  const int units = a.max_tiles * a.n_mblk;
-  const int grid = units < mm::sm_count() ? units : mm::sm_count();
+  a.xsum = ws.xsum; a.hsum = ws.hsum;
+  const int units = a.max_tiles * a.n_mblk, gc = mm::grid_ctas(L.dtype == 2 ? 8 : 4);
+  const int grid = units < gc ? units : gc;
   bool ok = false;
-  NT_SWITCH(nt, (ok = mm::launch_kernel<8, mm::DOWN, NT>(a0, a0, b0, b1, a, grid, st)));
+  if (L.dtype == 2) { NT_SWITCH(nt, (ok = mm::launch_kernel<8, mm::DOWN, NT>(a0, a0, b0, b1, a, grid, st))); }
+  else { NT_SWITCH(nt, (ok = mm::launch_kernel<4, mm::DOWN, NT>(a0, a0, b0, b0, a, grid, st))); }
   return ok;
 }
 

@@ -30,7 +30,7 @@ struct Args {
   int T, E, D, K;
   float* logits; int* idx; float* p;
   int* route; int e_begin, E_local; int* hsum; int nt, max_tiles; int* slot_pos;
-  uint8_t* xact; int* xsum;
+  uint8_t* xact; int* xsum; int q4_mma;
   int* counter; int* err;
 };
 
@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
           ar[a.D + k] = (uint8_t)((v >> 8) & 0xFF);
         } else {
           bad |= (v < -128 || v > 127);
-          ar[q4_act_pos(k)] = (uint8_t)(v & 0xFF);
+          ar[a.q4_mma ? q4_mma_pos(k) : q4_act_pos(k)] = (uint8_t)(v & 0xFF);
         }
       }
       if (bad) atomicOr(a.err, kErrRange);
@@ -317,7 +317,7 @@ void launch_decode_route(const LayerDev& L, const Workspace& ws, const float* x,
   a.hsum = L.dtype == 3 ? ws.hsum : nullptr;
   a.nt = nt; a.max_tiles = nt > 0 ? route_max_tiles(T * L.topk, a.E_local, nt) : 0;
   a.slot_pos = nt > 0 ? ws.slot_pos : nullptr;
-  a.xact = ws.xact; a.xsum = ws.xsum; a.counter = counter; a.err = err;
+  a.xact = ws.xact; a.xsum = ws.xsum; a.q4_mma = nt > 0; a.counter = counter; a.err = err;
   const size_t smem = (size_t)(rt::kE + rt::kT) * (L.D + 4) * 4;
   dim3 grid((L.E + rt::kE - 1) / rt::kE, (T + rt::kT - 1) / rt::kT);
   if (L.dtype == 2) {

@@ -502,7 +502,7 @@ static void route_tokens(const LayerDev& L, const float* xn, int T, int nt, cuda
   }
   const Workspace& w = g.ws;
   timed("quantize_act", st, [&] {
-    launch_quantize_act(xn, T, L.D, L.dtype, w.xact, 2 * L.D, w.xsum, g.d_err, st);
+    launch_quantize_act(xn, T, L.D, L.dtype, w.xact, 2 * L.D, w.xsum, g.d_err, st, nt > 0);
   });
   timed("router_logits", st, [&] {
     launch_f32_seq_matmul(xn, L.router_w, L.router_b, w.logits, T, L.E, L.D, st);

@@ -183,11 +183,12 @@ def test_moe_ffn_qwen_shape_vs_port(gpu, port, dt, T, bias):
     assert float(np.mean(p == ref_p)) >= 0.999
 
 
-@pytest.mark.parametrize("T", [1, 16, 40, 100])
-def test_moe_ffn_tensor_core_path_equals_gemv_path(gpu, T):
+@pytest.mark.parametrize("dt,T", [(2, 1), (2, 16), (2, 40), (2, 100), (3, 1), (3, 16), (3, 64), (3, 300)])
+def test_moe_ffn_tensor_core_path_equals_gemv_path(gpu, dt, T):
     """The tcgen05 grouped-GEMM path and the CUDA-core GEMV path compute the
-    same integers, so their outputs are identical bit for bit."""
-    lid, L = qwen_layer(gpu, 2, False)
+    same integers, so their outputs are identical bit for bit (Q8: two
+    activation limbs; Q4: nibbles unpacked in shared memory)."""
+    lid, L = qwen_layer(gpu, dt, False)
     xn = torch.from_numpy(synth(960 + T, T * 2048, 1.0).reshape(T, 2048)).cuda()
     xa = torch.from_numpy(synth(961 + T, T * 2048, 1.0).reshape(T, 2048)).cuda()
     outs = []
