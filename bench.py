@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=16)
     ap.add_argument("--extra-t", default="1,4", help="other T values reported beside the headline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-t", default="512,2048",
+                    help="configs[2] Q4 prefill sizes reported beside the headline ('' to skip)")
     return ap.parse_args()
 
 
@@ -390,6 +392,53 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def prefill_bench(torch, mc, sy, steps, warmup, ts):
+    """the same layer with Q4 experts, prefill of T tokens,
+    router logits skewed by a seeded per-expert bias ~ N(0,1) (ragged expert
+    loads). Four resident Q4 layers (each 304 MB > L2), steps rotate over them.
+    Reported beside the decode headline; the expert GEMMs' tensor throughput is
+    the grouped-GEMM evidence (int8 MMAs, counted as 2 ops per MAC)."""
+    ids = [1000 + i for i in range(4)]
+    for k, lid in enumerate(ids):
+        Ld = sy.make_layer_dev(torch, 3, k, E, D, F, 3, bias=True)
+        mc.upload_layer(lid, Ld, device_arrays=True)
+        del Ld
+    torch.cuda.synchronize()
+    out = {}
+    for T in ts:
+        xs = [sy.make_tokens_dev(torch, 4000 + T + i, T, D) for i in range(4)]
+        xo = [x.clone() for x in xs]
+        st = torch.cuda.current_stream()
+
+        def run(n, w0):
+            for i in range(n):
+                j = (w0 + i) % 4
+                mc.moe_ffn_dev(ids[j], xs[j], xo[j], stream=st)
+        run(warmup, 0)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        run(steps, warmup)
+        b.record(st)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        mc.profile(True)
+        run(steps, 0)
+        prof = mc.profile_read()
+        mc.profile(False)
+        mc.check_status()
+        kern = {n: v[0] / max(v[1], 1) * 1e3 for n, v in prof.items()}
+        mac = T * TOPK * 3 * F * D                      # gate + up + down MACs
+        gemm_us = kern.get("mma_gateup", 0) + kern.get("mma_down", 0)
+        out[f"T{T}"] = {"tok_s": T / (ms / 1e3), "us_per_step": ms * 1e3,
+                        "kernels_us": {n: round(v, 1) for n, v in kern.items()},
+                        "gemm_tops_int8": 2 * mac / (gemm_us * 1e-6) / 1e12 if gemm_us else None,
+                        "gemm_us": gemm_us}
+    for lid in ids:
+        mc.free_layer(lid)
+    return out
+
+
 def run_ours(args):
     import torch
     rank, world, local = dist_env()
@@ -457,6 +506,9 @@ def run_ours(args):
         e2e = {"value": TN * steps / (ms_h / 1e3), "unit": "tok/s",
                "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4,
                "ms_per_step": ms_h / steps, "note": "per rank: tokens in from pinned host, result out"}
+    prefill = None
+    if world == 1 and args.prefill_t:
+        prefill = prefill_bench(torch, mc, sy, 30, 3, [int(v) for v in args.prefill_t.split(",") if v])
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(mc, host_layer_from_device(torch, mc, sy, dt), T)
@@ -476,7 +528,8 @@ def run_ours(args):
                           "distinct_experts": U, "us_per_step": ms * 1e3 / steps},
                 "kernels": kern, "gpu_launches": int(round(launches_per_step * steps)),
                 "gpu_launches_per_step": launches_per_step,
-                "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu, "extra": extra}
+                "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu, "extra": extra,
+                "prefill_q4": prefill}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -109,7 +109,7 @@ void launch_zero_fill(float* C, size_t n, cudaStream_t st);
 namespace moe {
 // moe_mma.cu: tcgen05 grouped GEMMs over the routed experts
 bool mma_supported(const LayerDev& L);
-int mma_tile_n(int T);
+int mma_tile_n(int T, int dtype);
 void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream_t st);
 bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st);
 bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, float* ys, bool fuse,

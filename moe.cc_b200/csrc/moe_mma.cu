@@ -33,8 +33,10 @@ namespace moe {
 namespace mm {
 
 enum { GATEUP = 0, DOWN = 1 };
-constexpr int kThreads = 6 * 32;        // Q8: producer, MMA, 4 epilogue warps
-constexpr int kThreadsQ4 = 10 * 32;     // Q4: + 4 nibble-expander warps
+constexpr int kEpiWarps = 8;           // two per TMEM lane quarter, splitting the slot columns
+constexpr int kThreads = (2 + kEpiWarps) * 32;       // Q8: producer, MMA, epilogue
+constexpr int kThreadsQ4 = (2 + kEpiWarps + 4) * 32; // Q4: + 4 nibble-expander warps
+constexpr int kExpWarp0 = 2 + kEpiWarps;
 constexpr int kPackedBytes = 128 * 64;  // one packed Q4 tile: 128 rows x 128 nibbles
 
 struct __align__(64) TMap { CUtensorMap m; };
@@ -78,7 +80,11 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
   uint64_t* empty = full + a.stages;
   uint64_t* acc_full = empty + a.stages;     // [2]
   uint64_t* acc_empty = acc_full + 2;        // [2]
-  uint64_t* ready = acc_empty + 2;           // [stages] Q4: expanded A tiles written
+  uint64_t* afull = acc_empty + 2;           // [2] Q4: expanded A tiles written
+  uint64_t* aempty = afull + 2;              // [2] Q4: expanded A tiles consumed by the MMAs
+  // Q4: the stage ring holds [packed tiles | B]; the expanded A tiles live in
+  // their own 2-deep ring after the barriers (1024-aligned)
+  uint8_t* aring = smem + (((size_t)a.stages * a.stage_bytes + 16 * (size_t)a.stages + 64 + 1023) & ~(size_t)1023);
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_issued;
 
@@ -89,9 +95,9 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
   if (threadIdx.x == 0) {
     s_abort = 0; s_issued = 0;
     for (int s = 0; s < a.stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 4); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiWarps); }
     if (DT == 4)
-      for (int s = 0; s < a.stages; ++s) mbar_init(&ready[s], 4);
+      for (int b = 0; b < 2; ++b) { mbar_init(&afull[b], 4); mbar_init(&aempty[b], 1); }
     fence_mbar_init();
     tc::prefetch_tmap(&tmA0.m); tc::prefetch_tmap(&tmB0.m);
     if (NM == 2) tc::prefetch_tmap(&tmA1.m);
@@ -103,9 +109,10 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = s_tmem;
 
+  // units are dealt round-robin: tiles of heavily loaded experts (full slot
+  // columns, the costliest epilogues) sit next to each other in the tile table
   const int n_units = *tv.n * a.n_mblk;
-  const int u0 = (int)((long)n_units * blockIdx.x / gridDim.x);
-  const int u1 = (int)((long)n_units * (blockIdx.x + 1) / gridDim.x);
+  const int u0 = blockIdx.x, ustep = gridDim.x;
   volatile int* abort_flag = &s_abort;
 
   if (warp == 0) {
@@ -113,7 +120,7 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
     if (lane == 0) {
       const uint32_t bytes = (DT == 4 ? NM * kPackedBytes : NM * A_BYTES) + NL * B_BYTES;
       int it = 0;
-      for (int u = u0; u < u1 && !*abort_flag; ++u) {
+      for (int u = u0; u < n_units && !*abort_flag; u += ustep) {
         const int tile = u / a.n_mblk, mb = u % a.n_mblk;
         const int e = active[tv.u[tile]], j0 = tv.j0[tile];
         for (int kc = 0; kc < a.kchunks; ++kc, ++it) {
@@ -126,12 +133,11 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
           if (DT == 8) {
             tc::tma_load_3d(sb, &tmA0.m, kc * 128, mb * 128, e, &full[st]);
             if (NM == 2) tc::tma_load_3d(sb + A_BYTES, &tmA1.m, kc * 128, mb * 128, e, &full[st]);
-          } else {   // packed nibbles into the staging area; expanders build the A tiles
-            uint8_t* stg = sb + NM * A_BYTES + NL * B_BYTES;
-            tc::tma_load_3d(stg, &tmA0.m, kc * 64, mb * 128, e, &full[st]);
-            if (NM == 2) tc::tma_load_3d(stg + kPackedBytes, &tmA1.m, kc * 64, mb * 128, e, &full[st]);
+          } else {   // packed nibbles; the expanders build the A tiles from them
+            tc::tma_load_3d(sb, &tmA0.m, kc * 64, mb * 128, e, &full[st]);
+            if (NM == 2) tc::tma_load_3d(sb + kPackedBytes, &tmA1.m, kc * 64, mb * 128, e, &full[st]);
           }
-          tc::tma_load_2d(sb + NM * A_BYTES, &tmB0.m, kc * 128, j0, &full[st]);
+          tc::tma_load_2d(sb + (DT == 4 ? NM * kPackedBytes : NM * A_BYTES), &tmB0.m, kc * 128, j0, &full[st]);
           if (NL == 2) tc::tma_load_2d(sb + NM * A_BYTES + B_BYTES, &tmB1.m, kc * 128, j0, &full[st]);
           s_issued = it + 1;
         }
@@ -146,7 +152,7 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
       idesc[0] = tc::idesc_i8(128, NT, DT == 8, DT != 8);
       idesc[1] = tc::idesc_i8(128, NT, true, true);
       int it = 0, ul = 0;
-      for (int u = u0; u < u1 && !*abort_flag; ++u, ++ul) {
+      for (int u = u0; u < n_units && !*abort_flag; u += ustep, ++ul) {
         const int buf = ul & 1;
         if (ul >= 2 && !mbar_wait(&acc_empty[buf], ((ul >> 1) - 1) & 1, kWaitBudget)) {
           atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
@@ -155,16 +161,20 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
         const uint32_t dbase = tmem + buf * ACC;
         for (int kc = 0; kc < a.kchunks; ++kc, ++it) {
           const int st = it % a.stages;
-          if (!mbar_wait(DT == 4 ? &ready[st] : &full[st], (it / a.stages) & 1, kWaitBudget)) {
+          const int ab = it & 1;
+          if (!mbar_wait(DT == 4 ? &afull[ab] : &full[st], DT == 4 ? (it >> 1) & 1 : (it / a.stages) & 1,
+                         kWaitBudget)) {
             atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
           }
           tc::fence_after_sync();
           const uint8_t* sb = smem + (size_t)st * a.stage_bytes;
+          const uint8_t* atile = DT == 4 ? aring + (size_t)ab * NM * A_BYTES : sb;
+          const uint8_t* btile = sb + (DT == 4 ? NM * kPackedBytes : NM * A_BYTES);
           uint64_t da[NM], db[NL];
 #pragma unroll
-          for (int m = 0; m < NM; ++m) da[m] = tc::sw128_desc(sb + m * A_BYTES);
+          for (int m = 0; m < NM; ++m) da[m] = tc::sw128_desc(atile + m * A_BYTES);
 #pragma unroll
-          for (int l = 0; l < NL; ++l) db[l] = tc::sw128_desc(sb + NM * A_BYTES + l * B_BYTES);
+          for (int l = 0; l < NL; ++l) db[l] = tc::sw128_desc(btile + l * B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)            // 4 x 32 bytes of K per 128-byte chunk
 #pragma unroll
@@ -174,32 +184,34 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
                 tc::mma_i8(dbase + (m * NL + l) * NT, da[m] + 2 * kk, db[l] + 2 * kk, idesc[l],
                            (kc | kk) != 0);
           tc::mma_commit(&empty[st]);               // stage free once these MMAs finish
+          if (DT == 4) tc::mma_commit(&aempty[ab]);  // and the expanded A tiles
         }
         if (*abort_flag) break;
         tc::mma_commit(&acc_full[buf]);             // accumulator of this tile complete
       }
     }
-  } else if (DT == 4 && warp >= 6) {
+  } else if (DT == 4 && warp >= kExpWarp0) {
     // ------------------- Q4 nibble expanders ------------------------
     // row r of each packed tile (64 bytes = 128 nibbles) becomes 128 bytes of
     // the 128B-swizzled u8 A tile: packed 16-byte chunk c -> chunk 2c holds its
     // 16 low nibbles, chunk 2c+1 its 16 high nibbles (the activations use the
     // same k order, q4_mma_pos). 16-byte chunk h of row r sits at h ^ (r & 7).
-    const int r = (warp - 6) * 32 + lane;
+    const int r = (warp - kExpWarp0) * 32 + lane;
     int it = 0;
-    for (int u = u0; u < u1 && !*abort_flag; ++u) {
+    for (int u = u0; u < n_units && !*abort_flag; u += ustep) {
       for (int kc = 0; kc < a.kchunks; ++kc, ++it) {
-        const int st = it % a.stages;
-        if (!mbar_wait(&full[st], (it / a.stages) & 1, kWaitBudget)) {
+        const int st = it % a.stages, ab = it & 1;
+        if (!mbar_wait(&full[st], (it / a.stages) & 1, kWaitBudget) ||
+            (it >= 2 && !mbar_wait(&aempty[ab], ((it >> 1) - 1) & 1, kWaitBudget))) {
           if (lane == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; }
           break;
         }
-        uint8_t* sb = smem + (size_t)st * a.stage_bytes;
-        const uint8_t* stg = sb + NM * A_BYTES + NL * B_BYTES;
+        const uint8_t* stg = smem + (size_t)st * a.stage_bytes;
+        uint8_t* at = aring + (size_t)ab * NM * A_BYTES;
 #pragma unroll
         for (int m = 0; m < NM; ++m) {
           const uint4* src = reinterpret_cast<const uint4*>(stg + m * kPackedBytes + r * 64);
-          uint8_t* dst = sb + m * A_BYTES + r * 128;
+          uint8_t* dst = at + m * A_BYTES + r * 128;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             const uint4 w = src[c];
@@ -212,15 +224,16 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
         }
         tc::fence_proxy_async_smem();     // generic-proxy writes -> visible to the MMA
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ready[st]);
+        if (lane == 0) mbar_arrive(&afull[ab]);
       }
     }
   } else {
     // ------------------------- epilogue -----------------------------
     const int q = warp & 3;                         // TMEM lane quarter of this warp
+    const int half = (warp - 2) >> 2;               // which 8-column chunks this warp takes
     const int r = q * 32 + lane;                    // weight row within the 128-row block
     int ul = 0;
-    for (int u = u0; u < u1; ++u, ++ul) {
+    for (int u = u0; u < n_units; u += ustep, ++ul) {
       const int buf = ul & 1;
       if (!mbar_wait(&acc_full[buf], (ul >> 1) & 1, kWaitBudget)) {
         if (lane == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; }
@@ -234,7 +247,7 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
       const float sc0 = __ldg(reinterpret_cast<const float*>(ex + a.s0_off) + n);
       const float sc1 = NM == 2 ? __ldg(reinterpret_cast<const float*>(ex + a.s1_off) + n) : 0.f;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * ACC;
-      for (int c0 = 0; c0 < nt; c0 += 8) {
+      for (int c0 = 8 * half; c0 < nt; c0 += 16) {
         uint32_t v[NM * NL][8];
 #pragma unroll
         for (int x = 0; x < NM * NL; ++x) tc::tmem_ld8(tbase + x * NT + c0, v[x]);
@@ -285,7 +298,7 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
         __threadfence();
         __syncwarp();
         int last = 0;
-        if (lane == 0) last = atomicAdd(a.cnt + mb * 4 + q, 1) == *tv.n - 1;
+        if (lane == 0) last = atomicAdd(a.cnt + mb * 4 + q, 1) == 2 * *tv.n - 1;
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
           __threadfence();
@@ -424,12 +437,13 @@ template <int DT, int MODE, int NT>
 static bool launch_kernel(const TMap& a0, const TMap& a1, const TMap& b0, const TMap& b1, Args a, int grid,
                           cudaStream_t st) {
   constexpr int NM = MODE == GATEUP ? 2 : 1, NL = DT == 8 ? 2 : 1;
-  a.stage_bytes = NM * 128 * 128 + NL * NT * 128 + (DT == 4 ? NM * kPackedBytes : 0);
-  const int budget = 220 * 1024 / ctas_for(DT);
+  a.stage_bytes = (DT == 4 ? NM * kPackedBytes : NM * 128 * 128) + NL * NT * 128;
+  const int aring = DT == 4 ? 2 * NM * 128 * 128 + 1024 : 0;   // Q4 expanded-A ring
+  const int budget = 220 * 1024 / ctas_for(DT) - aring;
   a.stages = (budget - 1024 - 256) / a.stage_bytes;
   if (a.stages > 8) a.stages = 8;
   if (a.stages < 2) return false;
-  const size_t smem = (size_t)a.stages * a.stage_bytes + 1024 + 8 * (3 * (size_t)a.stages + 4);
+  const size_t smem = (size_t)a.stages * a.stage_bytes + 1024 + 16 * (size_t)a.stages + 64 + aring;
   auto k = moe_mma_kernel<DT, MODE, NT>;
   static size_t attr = 0;
   if (smem > attr) {
@@ -445,7 +459,14 @@ static bool launch_kernel(const TMap& a0, const TMap& a1, const TMap& b0, const 
 
 // ---- public launchers ------------------------------------------------------
 
-int mma_tile_n(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : 64; }
+// Slots per tile: the smallest tile that holds a decode expert's slots; for
+// Q4 prefill 128 (two 128-column accumulators, double-buffered, fill TMEM at
+// one CTA per SM; weight blocks are re-read once per tile, so wider is better).
+int mma_tile_n(int T, int dtype) {
+  if (T <= 16) return 16;
+  if (T <= 32) return 32;
+  return dtype == 3 && T > 256 ? 128 : 64;
+}
 
 bool mma_supported(const LayerDev& L) {
   return (L.dtype == 2 || L.dtype == 3) && L.D % 128 == 0 && L.F % 128 == 0 && mm::encoder() != nullptr;
@@ -462,6 +483,13 @@ void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream
     case 16: { constexpr int NT = 16; CALL; } break; \
     case 32: { constexpr int NT = 32; CALL; } break; \
     default: { constexpr int NT = 64; CALL; } break; \
+  }
+#define NT_SWITCH_Q4(nt, CALL) \
+  switch (nt) {             \
+    case 16: { constexpr int NT = 16; CALL; } break; \
+    case 32: { constexpr int NT = 32; CALL; } break; \
+    case 64: { constexpr int NT = 64; CALL; } break; \
+    default: { constexpr int NT = 128; CALL; } break; \
   }
 
 bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st) {
@@ -480,7 +508,7 @@ bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, in
   const int grid = units < gc ? units : gc;
   bool ok = false;
   if (L.dtype == 2) { NT_SWITCH(nt, (ok = mm::launch_kernel<8, mm::GATEUP, NT>(a0, a1, b0, b1, a, grid, st))); }
-  else { NT_SWITCH(nt, (ok = mm::launch_kernel<4, mm::GATEUP, NT>(a0, a1, b0, b0, a, grid, st))); }
+  else { NT_SWITCH_Q4(nt, (ok = mm::launch_kernel<4, mm::GATEUP, NT>(a0, a1, b0, b0, a, grid, st))); }
   return ok;
 }
 
@@ -503,7 +531,7 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
   const int grid = units < gc ? units : gc;
   bool ok = false;
   if (L.dtype == 2) { NT_SWITCH(nt, (ok = mm::launch_kernel<8, mm::DOWN, NT>(a0, a0, b0, b1, a, grid, st))); }
-  else { NT_SWITCH(nt, (ok = mm::launch_kernel<4, mm::DOWN, NT>(a0, a0, b0, b0, a, grid, st))); }
+  else { NT_SWITCH_Q4(nt, (ok = mm::launch_kernel<4, mm::DOWN, NT>(a0, a0, b0, b0, a, grid, st))); }
   return ok;
 }
 

@@ -616,7 +616,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
     xn = w.xn; xo = w.xo;
   }
   if (use_tensor_cores(L, flags)) {
-    const int nt = mma_tile_n(T);
+    const int nt = mma_tile_n(T, L.dtype);
     // The combine runs as its own kernel: fused into the down epilogue it left
     // the last warp through each row block with T*K dependent loads at the
     // end of the kernel (measured 90 us vs 39 + 6 us). MOE_MMA_FUSE=1 restores it.
@@ -670,7 +670,7 @@ int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots, int*
   const Workspace& w = g.ws;
   const size_t TK = (size_t)T * L.topk;
   if (use_tensor_cores(L, 0)) {
-    const int nt = mma_tile_n(T);
+    const int nt = mma_tile_n(T, L.dtype);
     route_tokens(L, x_norm2, T, nt, st);
     timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
     bool ok = true;
