@@ -226,11 +226,105 @@ __global__ void __launch_bounds__(256) f32_seq_tiled_kernel(const float* __restr
   }
 }
 
+// Register-blocked form for many tokens (prefill): a CTA owns 32 tokens x 64
+// experts, each of its 128 threads 4 tokens x 4 experts = 16 independent
+// chains (instruction-level parallelism over the 16 dependent add chains;
+// a thread's experts are 16 rows apart so shared-memory reads hit distinct banks);
+// k-tiles of 32 are double-buffered through shared memory. Each output is
+// still one sequential fp32 sum over k in ascending order.
+constexpr int kGT = 32, kGE = 64, kGK = 32, kGPad = kGK + 4;
+
+__global__ void __launch_bounds__(128) f32_seq_gemm_kernel(const float* __restrict__ A,
+                                                          const float* __restrict__ W,
+                                                          const float* __restrict__ b,
+                                                          float* __restrict__ C, int M, int N, int K) {
+  __shared__ __align__(16) float xs[2][kGT][kGPad];
+  __shared__ __align__(16) float ws[2][kGE][kGPad];
+  const int tid = threadIdx.x;
+  const int tq = tid / 16, eq = tid % 16;          // token quad, expert quad
+  const int m0 = blockIdx.y * kGT, n0 = blockIdx.x * kGE;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+  // loader: x tile 32 x 32 floats = 256 float4 (2 per thread); w tile 64 x 32 = 512 float4 (4 per thread)
+  float4 rx[2], rw[4];
+  auto gload = [&](int kt) {
+    const int k0 = kt * kGK;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int q = tid + i * 128, row = q / 8, col = (q % 8) * 4;
+      const int m = m0 + row;
+      rx[i] = (m < M && k0 + col < K) ? __ldg(reinterpret_cast<const float4*>(A + (size_t)m * K + k0 + col))
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q = tid + i * 128, row = q / 8, col = (q % 8) * 4;
+      const int n = n0 + row;
+      rw[i] = (n < N && k0 + col < K) ? __ldg(reinterpret_cast<const float4*>(W + (size_t)n * K + k0 + col))
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto sstore = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int q = tid + i * 128;
+      *reinterpret_cast<float4*>(&xs[buf][q / 8][(q % 8) * 4]) = rx[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q = tid + i * 128;
+      *reinterpret_cast<float4*>(&ws[buf][q / 8][(q % 8) * 4]) = rw[i];
+    }
+  };
+  const int ntiles = (K + kGK - 1) / kGK;
+  gload(0);
+  sstore(0);
+  __syncthreads();
+  for (int kt = 0; kt < ntiles; ++kt) {
+    const int buf = kt & 1;
+    if (kt + 1 < ntiles) gload(kt + 1);
+    const int kn = min(kGK, K - kt * kGK);
+    for (int k = 0; k < kn; k += 4) {
+      float4 xv[4], wv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(&xs[buf][tq * 4 + i][k]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) wv[j] = *reinterpret_cast<const float4*>(&ws[buf][eq + 16 * j][k]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[i][j] = fadd(acc[i][j], fmul(xv[i].x, wv[j].x));
+          acc[i][j] = fadd(acc[i][j], fmul(xv[i].y, wv[j].y));
+          acc[i][j] = fadd(acc[i][j], fmul(xv[i].z, wv[j].z));
+          acc[i][j] = fadd(acc[i][j], fmul(xv[i].w, wv[j].w));
+        }
+    }
+    if (kt + 1 < ntiles) sstore(buf ^ 1);
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int m = m0 + tq * 4 + i, n = n0 + eq + 16 * j;
+      if (m < M && n < N) C[(size_t)m * N + n] = b ? fadd(acc[i][j], __ldg(b + n)) : acc[i][j];
+    }
+}
+
 void launch_f32_seq_matmul(const float* A, const float* W, const float* b, float* C, int M, int N,
                            int K, cudaStream_t st) {
   const long total = (long)M * N;
   if (total <= 0) return;
   const bool aligned = ((uintptr_t)A % 16 == 0) && ((uintptr_t)W % 16 == 0);
+  if (K % 4 == 0 && aligned && M >= 64) {
+    dim3 grid((N + kGE - 1) / kGE, (M + kGT - 1) / kGT);
+    f32_seq_gemm_kernel<<<grid, 128, 0, st>>>(A, W, b, C, M, N, K);
+    return;
+  }
   if (K % 4 == 0 && aligned) {
     dim3 grid((N + kRE - 1) / kRE, (M + kRT - 1) / kRT);
     f32_seq_tiled_kernel<<<grid, 256, 0, st>>>(A, W, b, C, M, N, K);
@@ -425,6 +519,94 @@ void launch_route_build(const int* idx, int T, int K, int e_begin, int e_end, in
     attr = smem;
   }
   route_build_kernel<<<1, 1024, smem, st>>>(idx, TK, e_begin, E_local, route, hsum, nt, mt, slot_pos);
+}
+
+// --------------------------------------------------------------------------
+// routing lists for many slots (prefill): histogram -> one-CTA scan (+ tile
+// table) -> scatter. Slots are placed by atomics, so their order within an
+// expert varies from call to call; each slot's result does not depend on it.
+// tmp = [count E | start E | fill E], kept zero between calls except start.
+// --------------------------------------------------------------------------
+__global__ void route_hist_kernel(const int* __restrict__ idx, int TK, int e_begin, int E_local,
+                                  int* __restrict__ cnt) {
+  extern __shared__ int h[];
+  for (int i = threadIdx.x; i < E_local; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < TK; s += gridDim.x * blockDim.x) {
+    const int el = idx[s] - e_begin;
+    if (el >= 0 && el < E_local) atomicAdd(&h[el], 1);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < E_local; i += blockDim.x)
+    if (h[i]) atomicAdd(&cnt[i], h[i]);
+}
+
+__global__ void route_scan_kernel(int* route, int E_local, int TK, int* tmp, int nt, int max_tiles) {
+  extern __shared__ int sm2[];
+  int* s_route = sm2;                       // n_active | active[E] | exp_off[E+1]
+  int* s_tab = sm2 + 2 + 2 * E_local;       // n_tiles | u[m] | j0[m] | cnt[m]
+  int* cnt = tmp;
+  int* start = tmp + E_local;
+  if (threadIdx.x == 0) {
+    int na = 0, off = 0, ntl = 0;
+    for (int el = 0; el < E_local; ++el) {
+      const int c = cnt[el];
+      start[el] = off;
+      if (c == 0) continue;
+      s_route[1 + na] = el;
+      s_route[1 + E_local + na] = off;
+      if (nt > 0)
+        for (int j0 = off; j0 < off + c && ntl < max_tiles; j0 += nt, ++ntl) {
+          s_tab[1 + ntl] = na;
+          s_tab[1 + max_tiles + ntl] = j0;
+          s_tab[1 + 2 * max_tiles + ntl] = min(nt, off + c - j0);
+        }
+      off += c;
+      ++na;
+    }
+    s_route[1 + E_local + na] = off;
+    s_route[0] = na;
+    s_tab[0] = ntl;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 2 + 2 * E_local; i += blockDim.x) route[i] = s_route[i];
+  if (nt > 0) {
+    int* tab = route + 2 + 2 * E_local + TK;
+    for (int i = threadIdx.x; i < 1 + 3 * max_tiles; i += blockDim.x) tab[i] = s_tab[i];
+  }
+  for (int i = threadIdx.x; i < E_local; i += blockDim.x) cnt[i] = 0;   // ready for the next call
+}
+
+__global__ void route_scatter_kernel(const int* __restrict__ idx, int TK, int e_begin, int E_local,
+                                     int* route, int* tmp, int* slot_pos, int* hsum) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= TK) return;
+  if (hsum) hsum[s] = 0;
+  const int el = idx[s] - e_begin;
+  if (el < 0 || el >= E_local) return;
+  const int j = tmp[E_local + el] + atomicAdd(&tmp[2 * E_local + el], 1);
+  route[2 + 2 * E_local + j] = s;
+  if (slot_pos) slot_pos[s] = j;
+}
+
+__global__ void route_fill_reset_kernel(int* tmp, int E_local) {
+  for (int i = threadIdx.x; i < E_local; i += blockDim.x) tmp[2 * E_local + i] = 0;
+}
+
+void launch_route_build_multi(const int* idx, int T, int K, int e_begin, int E_local, int* route, int* hsum,
+                              int nt, int* slot_pos, int* tmp, cudaStream_t st) {
+  const int TK = T * K;
+  const int mt = nt > 0 ? route_max_tiles(TK, E_local, nt) : 0;
+  route_hist_kernel<<<(TK + 1023) / 1024, 256, sizeof(int) * E_local, st>>>(idx, TK, e_begin, E_local, tmp);
+  const size_t smem = sizeof(int) * (2 + 2 * (size_t)E_local + 1 + 3 * (size_t)mt);
+  static size_t attr = 0;
+  if (smem > 48 * 1024 && smem > attr) {
+    cudaFuncSetAttribute(route_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = smem;
+  }
+  route_scan_kernel<<<1, 256, smem, st>>>(route, E_local, TK, tmp, nt, mt);
+  route_scatter_kernel<<<(TK + 255) / 256, 256, 0, st>>>(idx, TK, e_begin, E_local, route, tmp, slot_pos, hsum);
+  route_fill_reset_kernel<<<1, 256, 0, st>>>(tmp, E_local);
 }
 
 // --------------------------------------------------------------------------

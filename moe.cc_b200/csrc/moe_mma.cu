@@ -33,10 +33,11 @@ namespace moe {
 namespace mm {
 
 enum { GATEUP = 0, DOWN = 1 };
-constexpr int kEpiWarps = 8;           // two per TMEM lane quarter, splitting the slot columns
-constexpr int kThreads = (2 + kEpiWarps) * 32;       // Q8: producer, MMA, epilogue
-constexpr int kThreadsQ4 = (2 + kEpiWarps + 4) * 32; // Q4: + 4 nibble-expander warps
-constexpr int kExpWarp0 = 2 + kEpiWarps;
+// Epilogue warps: several per TMEM lane quarter, splitting the slot columns.
+// Wide (prefill) tiles need 16 to hide the epilogue's latency; decode tiles
+// (<= 32 slots) use 8, which keeps two CTAs resident per SM.
+__host__ __device__ constexpr int epi_warps(int nt) { return nt >= 64 ? 16 : 8; }
+__host__ __device__ constexpr int cta_threads(int dt, int nt) { return (2 + epi_warps(nt) + (dt == 4 ? 4 : 0)) * 32; }
 constexpr int kPackedBytes = 128 * 64;  // one packed Q4 tile: 128 rows x 128 nibbles
 
 struct __align__(64) TMap { CUtensorMap m; };
@@ -61,9 +62,10 @@ struct Args {
 };
 
 template <int DT, int MODE, int NT>
-__global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
+__global__ void __launch_bounds__(cta_threads(DT, NT), 1)
     moe_mma_kernel(const __grid_constant__ TMap tmA0, const __grid_constant__ TMap tmA1,
                    const __grid_constant__ TMap tmB0, const __grid_constant__ TMap tmB1, const Args a) {
+  constexpr int kEpiWarps = epi_warps(NT), kEpiPerQ = kEpiWarps / 4, kExpWarp0 = 2 + kEpiWarps;
   constexpr int NM = MODE == GATEUP ? 2 : 1;     // weight matrices per tile
   constexpr int NL = DT == 8 ? 2 : 1;            // activation limbs
   constexpr int ACC = NM * NL * NT;              // accumulator columns per buffer
@@ -230,7 +232,7 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
   } else {
     // ------------------------- epilogue -----------------------------
     const int q = warp & 3;                         // TMEM lane quarter of this warp
-    const int half = (warp - 2) >> 2;               // which 8-column chunks this warp takes
+    const int half = (warp - 2) >> 2;               // which 8-column chunks this warp takes (of kEpiPerQ)
     const int r = q * 32 + lane;                    // weight row within the 128-row block
     int ul = 0;
     for (int u = u0; u < n_units; u += ustep, ++ul) {
@@ -247,7 +249,7 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
       const float sc0 = __ldg(reinterpret_cast<const float*>(ex + a.s0_off) + n);
       const float sc1 = NM == 2 ? __ldg(reinterpret_cast<const float*>(ex + a.s1_off) + n) : 0.f;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * ACC;
-      for (int c0 = 8 * half; c0 < nt; c0 += 16) {
+      for (int c0 = 8 * half; c0 < nt; c0 += 8 * kEpiPerQ) {
         uint32_t v[NM * NL][8];
 #pragma unroll
         for (int x = 0; x < NM * NL; ++x) tc::tmem_ld8(tbase + x * NT + c0, v[x]);
@@ -298,7 +300,7 @@ __global__ void __launch_bounds__(DT == 4 ? kThreadsQ4 : kThreads, 1)
         __threadfence();
         __syncwarp();
         int last = 0;
-        if (lane == 0) last = atomicAdd(a.cnt + mb * 4 + q, 1) == 2 * *tv.n - 1;
+        if (lane == 0) last = atomicAdd(a.cnt + mb * 4 + q, 1) == kEpiPerQ * *tv.n - 1;
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
           __threadfence();
@@ -451,7 +453,7 @@ static bool launch_kernel(const TMap& a0, const TMap& a1, const TMap& b0, const 
       return false;
     attr = smem;
   }
-  k<<<grid, DT == 4 ? kThreadsQ4 : kThreads, smem, st>>>(a0, a1, b0, b1, a);
+  k<<<grid, cta_threads(DT, NT), smem, st>>>(a0, a1, b0, b1, a);
   return true;
 }
 
