@@ -226,41 +226,43 @@ __global__ void __launch_bounds__(256) f32_seq_tiled_kernel(const float* __restr
   }
 }
 
-// Register-blocked form for many tokens (prefill): a CTA owns 32 tokens x 64
-// experts, each of its 128 threads 4 tokens x 4 experts = 16 independent
-// chains (instruction-level parallelism over the 16 dependent add chains;
-// a thread's experts are 16 rows apart so shared-memory reads hit distinct banks);
-// k-tiles of 32 are double-buffered through shared memory. Each output is
-// still one sequential fp32 sum over k in ascending order.
-constexpr int kGT = 32, kGE = 64, kGK = 32, kGPad = kGK + 4;
+// Register-blocked form for many tokens (prefill): 128 threads; a thread
+// owns TT tokens x ET experts of independent chains (instruction-level
+// parallelism over dependent add chains); a CTA owns 8*TT tokens x 16*ET
+// experts; k-tiles of 32 are double-buffered through shared memory. A
+// thread's experts are 16 rows apart, so shared-memory reads hit distinct
+// banks. Each output is still one sequential fp32 sum over k in ascending order.
+constexpr int kGK = 32, kGPad = kGK + 4;
 
+template <int TT, int ET>
 __global__ void __launch_bounds__(128) f32_seq_gemm_kernel(const float* __restrict__ A,
                                                           const float* __restrict__ W,
                                                           const float* __restrict__ b,
                                                           float* __restrict__ C, int M, int N, int K) {
-  __shared__ __align__(16) float xs[2][kGT][kGPad];
-  __shared__ __align__(16) float ws[2][kGE][kGPad];
+  constexpr int GT = 8 * TT, GE = 16 * ET;
+  constexpr int XL = GT * 8 / 128, WL = GE * 8 / 128;   // float4 loads per thread per k-tile
+  __shared__ __align__(16) float xs[2][GT][kGPad];
+  __shared__ __align__(16) float ws[2][GE][kGPad];
   const int tid = threadIdx.x;
-  const int tq = tid / 16, eq = tid % 16;          // token quad, expert quad
-  const int m0 = blockIdx.y * kGT, n0 = blockIdx.x * kGE;
-  float acc[4][4];
+  const int tq = tid / 16, eq = tid % 16;
+  const int m0 = blockIdx.y * GT, n0 = blockIdx.x * GE;
+  float acc[TT][ET];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < TT; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-  // loader: x tile 32 x 32 floats = 256 float4 (2 per thread); w tile 64 x 32 = 512 float4 (4 per thread)
-  float4 rx[2], rw[4];
+    for (int j = 0; j < ET; ++j) acc[i][j] = 0.0f;
+  float4 rx[XL], rw[WL];
   auto gload = [&](int kt) {
     const int k0 = kt * kGK;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < XL; ++i) {
       const int q = tid + i * 128, row = q / 8, col = (q % 8) * 4;
       const int m = m0 + row;
       rx[i] = (m < M && k0 + col < K) ? __ldg(reinterpret_cast<const float4*>(A + (size_t)m * K + k0 + col))
                                       : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < WL; ++i) {
       const int q = tid + i * 128, row = q / 8, col = (q % 8) * 4;
       const int n = n0 + row;
       rw[i] = (n < N && k0 + col < K) ? __ldg(reinterpret_cast<const float4*>(W + (size_t)n * K + k0 + col))
@@ -269,12 +271,12 @@ __global__ void __launch_bounds__(128) f32_seq_gemm_kernel(const float* __restri
   };
   auto sstore = [&](int buf) {
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < XL; ++i) {
       const int q = tid + i * 128;
       *reinterpret_cast<float4*>(&xs[buf][q / 8][(q % 8) * 4]) = rx[i];
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < WL; ++i) {
       const int q = tid + i * 128;
       *reinterpret_cast<float4*>(&ws[buf][q / 8][(q % 8) * 4]) = rw[i];
     }
@@ -288,15 +290,15 @@ __global__ void __launch_bounds__(128) f32_seq_gemm_kernel(const float* __restri
     if (kt + 1 < ntiles) gload(kt + 1);
     const int kn = min(kGK, K - kt * kGK);
     for (int k = 0; k < kn; k += 4) {
-      float4 xv[4], wv[4];
+      float4 xv[TT], wv[ET];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(&xs[buf][tq * 4 + i][k]);
+      for (int i = 0; i < TT; ++i) xv[i] = *reinterpret_cast<const float4*>(&xs[buf][tq * TT + i][k]);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) wv[j] = *reinterpret_cast<const float4*>(&ws[buf][eq + 16 * j][k]);
+      for (int j = 0; j < ET; ++j) wv[j] = *reinterpret_cast<const float4*>(&ws[buf][eq + 16 * j][k]);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < TT; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < ET; ++j) {
           acc[i][j] = fadd(acc[i][j], fmul(xv[i].x, wv[j].x));
           acc[i][j] = fadd(acc[i][j], fmul(xv[i].y, wv[j].y));
           acc[i][j] = fadd(acc[i][j], fmul(xv[i].z, wv[j].z));
@@ -307,10 +309,10 @@ __global__ void __launch_bounds__(128) f32_seq_gemm_kernel(const float* __restri
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < TT; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int m = m0 + tq * 4 + i, n = n0 + eq + 16 * j;
+    for (int j = 0; j < ET; ++j) {
+      const int m = m0 + tq * TT + i, n = n0 + eq + 16 * j;
       if (m < M && n < N) C[(size_t)m * N + n] = b ? fadd(acc[i][j], __ldg(b + n)) : acc[i][j];
     }
 }
@@ -321,8 +323,15 @@ void launch_f32_seq_matmul(const float* A, const float* W, const float* b, float
   if (total <= 0) return;
   const bool aligned = ((uintptr_t)A % 16 == 0) && ((uintptr_t)W % 16 == 0);
   if (K % 4 == 0 && aligned && M >= 64) {
-    dim3 grid((N + kGE - 1) / kGE, (M + kGT - 1) / kGT);
-    f32_seq_gemm_kernel<<<grid, 128, 0, st>>>(A, W, b, C, M, N, K);
+    // 4 x 4 chains per thread once there are enough tokens for several CTAs
+    // per SM; 2 x 2 below that, so the grid still spreads over the SMs
+    if (M >= 2048) {
+      dim3 grid((N + 63) / 64, (M + 31) / 32);
+      f32_seq_gemm_kernel<4, 4><<<grid, 128, 0, st>>>(A, W, b, C, M, N, K);
+    } else {
+      dim3 grid((N + 31) / 32, (M + 15) / 16);
+      f32_seq_gemm_kernel<2, 2><<<grid, 128, 0, st>>>(A, W, b, C, M, N, K);
+    }
     return;
   }
   if (K % 4 == 0 && aligned) {
