@@ -57,6 +57,7 @@ struct Args {
   int fuse, T, topk;
   int* cnt; const int* slot_pos; const float* topk_p; const int* topk_idx;
   const int* xsum; int* hsum;                // Q4 zero-point sums (token / slot)
+  int tokb;                                  // GATEUP: B = all T token rows (decode, T <= NT)
   const float* xres; float* out;
   int* err;
 };
@@ -139,8 +140,9 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
             tc::tma_load_3d(sb, &tmA0.m, kc * 64, mb * 128, e, &full[st]);
             if (NM == 2) tc::tma_load_3d(sb + kPackedBytes, &tmA1.m, kc * 64, mb * 128, e, &full[st]);
           }
-          tc::tma_load_2d(sb + (DT == 4 ? NM * kPackedBytes : NM * A_BYTES), &tmB0.m, kc * 128, j0, &full[st]);
-          if (NL == 2) tc::tma_load_2d(sb + NM * A_BYTES + B_BYTES, &tmB1.m, kc * 128, j0, &full[st]);
+          const int by = a.tokb ? 0 : j0;   // decode: all token rows from row 0
+          tc::tma_load_2d(sb + (DT == 4 ? NM * kPackedBytes : NM * A_BYTES), &tmB0.m, kc * 128, by, &full[st]);
+          if (NL == 2) tc::tma_load_2d(sb + NM * A_BYTES + B_BYTES, &tmB1.m, kc * 128, by, &full[st]);
           s_issued = it + 1;
         }
       }
@@ -249,44 +251,70 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
       const float sc0 = __ldg(reinterpret_cast<const float*>(ex + a.s0_off) + n);
       const float sc1 = NM == 2 ? __ldg(reinterpret_cast<const float*>(ex + a.s1_off) + n) : 0.f;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * ACC;
-      for (int c0 = 8 * half; c0 < nt; c0 += 8 * kEpiPerQ) {
-        uint32_t v[NM * NL][8];
-#pragma unroll
-        for (int x = 0; x < NM * NL; ++x) tc::tmem_ld8(tbase + x * NT + c0, v[x]);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int jj = c0 + i;
-          if (jj >= nt) break;
-          const int j = j0 + jj;
-          int dot[NM];
-#pragma unroll
-          for (int m = 0; m < NM; ++m)
-            dot[m] = NL == 2 ? (int)(v[m * 2][i] + (v[m * 2 + 1][i] << 8)) : (int)v[m][i];
-          if (DT == 4) {   // nibbles are stored +8: subtract 8 * Σ activation (exact mod 2^32)
-            const int as = MODE == GATEUP ? __ldg(a.xsum + __ldg(a.route + 2 + 2 * a.E_local + j) / a.topk)
-                                          : __ldcg(a.hsum + j);
-#pragma unroll
-            for (int m = 0; m < NM; ++m) dot[m] = (int)((unsigned)dot[m] - 8u * (unsigned)as);
-          }
-          if (MODE == GATEUP) {
-            const float g = fmul(fdiv(__int2float_rn(dot[0]), S), sc0);
-            const float uu = fmul(fdiv(__int2float_rn(dot[NM - 1]), S), sc1);
-            const float h = fmul(silu_ref(g), uu);
-            const int ha = trunc_scale(h, S);
-            if (DT == 8) {
-              if (ha < -32768 || ha > 32767) atomicOr(a.err, kErrRange);
-              a.hs0[(size_t)j * a.F + n] = (uint8_t)(ha & 0xFF);
-              a.hs1[(size_t)j * a.F + n] = (uint8_t)((ha >> 8) & 0xFF);
-            } else {
-              if (ha < -128 || ha > 127) atomicOr(a.err, kErrRange);
-              a.hs0[(size_t)j * a.F + q4_mma_pos(n)] = (uint8_t)(ha & 0xFF);
-              // Σ h of slot j for the down projection's zero-point correction
-              const int ws = __reduce_add_sync(0xffffffffu, ha);
-              if (lane == 0) atomicAdd(a.hsum + j, ws);
-            }
+      // one (row n, sorted slot j) output from its raw accumulator words
+      auto emit = [&](const int j, const uint32_t (&raw)[NM * NL]) {
+        int dot[NM];
+  #pragma unroll
+        for (int m = 0; m < NM; ++m)
+          dot[m] = NL == 2 ? (int)(raw[m * 2] + (raw[m * 2 + 1] << 8)) : (int)raw[m];
+        if (DT == 4) {   // nibbles are stored +8: subtract 8 * Σ activation (exact mod 2^32)
+          const int as = MODE == GATEUP ? __ldg(a.xsum + __ldg(a.route + 2 + 2 * a.E_local + j) / a.topk)
+                                        : __ldcg(a.hsum + j);
+  #pragma unroll
+          for (int m = 0; m < NM; ++m) dot[m] = (int)((unsigned)dot[m] - 8u * (unsigned)as);
+        }
+        if (MODE == GATEUP) {
+          const float g = fmul(fdiv(__int2float_rn(dot[0]), S), sc0);
+          const float uu = fmul(fdiv(__int2float_rn(dot[NM - 1]), S), sc1);
+          const float h = fmul(silu_ref(g), uu);
+          const int ha = trunc_scale(h, S);
+          if (DT == 8) {
+            if (ha < -32768 || ha > 32767) atomicOr(a.err, kErrRange);
+            a.hs0[(size_t)j * a.F + n] = (uint8_t)(ha & 0xFF);
+            a.hs1[(size_t)j * a.F + n] = (uint8_t)((ha >> 8) & 0xFF);
           } else {
-            a.ys[(size_t)j * a.rows + n] = fmul(fdiv(__int2float_rn(dot[0]), S), sc0);
+            if (ha < -128 || ha > 127) atomicOr(a.err, kErrRange);
+            a.hs0[(size_t)j * a.F + q4_mma_pos(n)] = (uint8_t)(ha & 0xFF);
+            // Σ h of slot j for the down projection's zero-point correction
+            const int ws = __reduce_add_sync(0xffffffffu, ha);
+            if (lane == 0) atomicAdd(a.hsum + j, ws);
+          }
+        } else {
+          a.ys[(size_t)j * a.rows + n] = fmul(fdiv(__int2float_rn(dot[0]), S), sc0);
+        }
+      };
+      if (MODE == GATEUP && a.tokb) {
+        // decode: B held all T token rows, so accumulator column t is token t;
+        // each routed slot j of this expert reads its token's column
+        for (int jj = half; jj < nt; jj += kEpiPerQ) {
+          const int j = j0 + jj;
+          const int t = __ldg(a.route + 2 + 2 * a.E_local + j) / a.topk;   // warp-uniform
+          uint32_t v[NM * NL][8], raw[NM * NL];
+#pragma unroll
+          for (int x = 0; x < NM * NL; ++x) tc::tmem_ld8(tbase + x * NT + (t & ~7), v[x]);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int x = 0; x < NM * NL; ++x) {
+            raw[x] = v[x][0];
+#pragma unroll
+            for (int c = 1; c < 8; ++c) if ((t & 7) == c) raw[x] = v[x][c];
+          }
+          emit(j, raw);
+        }
+      } else {
+        for (int c0 = 8 * half; c0 < nt; c0 += 8 * kEpiPerQ) {
+          uint32_t v[NM * NL][8];
+#pragma unroll
+          for (int x = 0; x < NM * NL; ++x) tc::tmem_ld8(tbase + x * NT + c0, v[x]);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int jj = c0 + i;
+            if (jj >= nt) break;
+            uint32_t raw[NM * NL];
+#pragma unroll
+            for (int x = 0; x < NM * NL; ++x) raw[x] = v[x][i];
+            emit(j0 + jj, raw);
           }
         }
       }
@@ -398,10 +426,10 @@ static bool map_weights(TMap& t, const LayerDev& L, size_t off, int kelems, int 
   return map_u8(t, L.slab + off, 3, dims, strides, box, !q4);
 }
 
-// expert-sorted activation plane: (K bytes, J rows); J >= the box height
-static bool map_rows(TMap& t, const uint8_t* base, int kbytes, int J, int nt) {
+// activation rows: (K bytes, J rows, row pitch); J >= the box height
+static bool map_rows(TMap& t, const uint8_t* base, int kbytes, int J, int nt, int pitch = 0) {
   const cuuint64_t dims[2] = {(cuuint64_t)kbytes, (cuuint64_t)J};
-  const cuuint64_t strides[1] = {(cuuint64_t)kbytes};
+  const cuuint64_t strides[1] = {(cuuint64_t)(pitch ? pitch : kbytes)};
   const cuuint32_t box[2] = {128, (cuuint32_t)nt};
   return map_u8(t, base, 2, dims, strides, box);
 }
@@ -475,6 +503,7 @@ bool mma_supported(const LayerDev& L) {
 }
 
 void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream_t st) {
+  if (T <= mma_tile_n(T, L.dtype)) return;   // decode: the GEMM reads the token rows directly
   const int E_local = L.e_end - L.e_begin, TK = T * L.topk;
   mm::gather_rows_kernel<<<TK, 128, 0, st>>>(ws.xact, 2 * L.D, L.D, L.dtype == 2 ? 2 : 1, ws.route, E_local,
                                              L.topk, ws.xs0, ws.xs1);
@@ -497,15 +526,24 @@ void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream
 bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st) {
   const int E_local = L.e_end - L.e_begin, TK = T * L.topk, cap = ws.cap_T * ws.cap_K;
   mm::TMap a0, a1, b0, b1;
-  if (!mm::map_weights(a0, L, L.gq_off, L.D, L.F) || !mm::map_weights(a1, L, L.uq_off, L.D, L.F) ||
-      !mm::map_rows(b0, ws.xs0, L.D, cap, nt) || !mm::map_rows(b1, L.dtype == 2 ? ws.xs1 : ws.xs0, L.D, cap, nt))
+  // decode (every expert's slots fit one tile): B = the T token rows as they
+  // are (lo plane, then the hi plane D bytes further; rows 2D apart), no gather
+  const bool tokb = T <= nt;
+  bool mapped;
+  if (tokb)
+    mapped = mm::map_rows(b0, ws.xact, L.D, ws.cap_T, nt, 2 * L.D) &&
+             mm::map_rows(b1, ws.xact + (L.dtype == 2 ? L.D : 0), L.D, ws.cap_T, nt, 2 * L.D);
+  else
+    mapped = mm::map_rows(b0, ws.xs0, L.D, cap, nt) &&
+             mm::map_rows(b1, L.dtype == 2 ? ws.xs1 : ws.xs0, L.D, cap, nt);
+  if (!mapped || !mm::map_weights(a0, L, L.gq_off, L.D, L.F) || !mm::map_weights(a1, L, L.uq_off, L.D, L.F))
     return false;
   mm::Args a{};
   a.rows = L.F; a.kchunks = L.D / 128; a.n_mblk = L.F / 128;
   a.route = ws.route; a.E_local = E_local; a.TK = TK; a.max_tiles = route_max_tiles(TK, E_local, nt);
   a.slab = L.slab; a.stride = L.expert_stride; a.s0_off = L.gs_off; a.s1_off = L.us_off;
   a.F = L.F; a.hs0 = ws.hs0; a.hs1 = ws.hs1; a.err = err;
-  a.xsum = ws.xsum; a.hsum = ws.hsum; a.topk = L.topk;
+  a.xsum = ws.xsum; a.hsum = ws.hsum; a.topk = L.topk; a.tokb = tokb;
   const int units = a.max_tiles * a.n_mblk, gc = mm::grid_ctas(L.dtype == 2 ? 8 : 4);
   const int grid = units < gc ? units : gc;
   bool ok = false;

@@ -68,7 +68,7 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   Workspace& w = g.ws;
   if (T <= w.cap_T && E <= w.cap_E && D <= w.cap_D && F <= w.cap_F && K <= w.cap_K) return MOE_OK;
   int nT = T > w.cap_T ? (T > 2 * w.cap_T ? T : 2 * w.cap_T) : w.cap_T;
-  if (nT < 8) nT = 8;   // >= 64 sorted rows: the smallest tensor-core tile fits
+  if (nT < 32) nT = 32;  // >= the widest decode tile: token rows are read as a tile
   const int nE = E > w.cap_E ? E : w.cap_E, nD = D > w.cap_D ? D : w.cap_D;
   const int nF = F > w.cap_F ? F : w.cap_F, nK = K > w.cap_K ? K : w.cap_K;
   CU(cudaDeviceSynchronize());
@@ -634,7 +634,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
     }
     const bool fuse = fuse_env && T <= kFuseCombineMaxT;
     route_tokens(L, xn, T, nt, st);
-    timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
+    if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
     bool ok = true;
     timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
     if (ok) timed("mma_down", st, [&] { ok = launch_mma_down(L, w, T, nt, w.y, fuse, xo, xo, g.d_err, st); });
@@ -679,7 +679,7 @@ int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots, int*
   if (use_tensor_cores(L, 0)) {
     const int nt = mma_tile_n(T, L.dtype);
     route_tokens(L, x_norm2, T, nt, st);
-    timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
+    if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
     bool ok = true;
     timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
     if (ok)
