@@ -124,7 +124,7 @@ def alg_bytes(kernel, T, U, dt):
     activations in/out). U = distinct experts routed in that step."""
     gu_rb = D if dt == 2 else D // 2
     d_rb = F if dt == 2 else F // 2
-    kernel = kernel.replace("mma_", "")
+    kernel = kernel.replace("mma_", "").replace("down_ep", "down").replace("ep_combine", "combine")
     if kernel == "gateup":
         return U * (2 * F * gu_rb + 2 * F * 4)
     if kernel == "down":
@@ -169,6 +169,10 @@ class Runner:
     computes only its own experts' slots), reduce-scatter the slot outputs so
     each rank receives its own tokens' slots (exactly one rank contributes each
     slot, so the sum is exact), then the k-ordered combine + residual.
+    With MOE_EP_EXCHANGE=fused (the default when every rank has its own GPU)
+    the reduce-scatter is replaced by moe_ffn_ep: the down GEMM's epilogue
+    stores each slot row into the owning rank's receive buffer over NVLink
+    and the combine waits on the ranks' flags.
     """
 
     def __init__(self, torch, mc, dist, world, rank, T, nl, pool):
@@ -183,6 +187,13 @@ class Runner:
             self.y_all = torch.empty(TN * TOPK, D, device="cuda")
             self.p_all = torch.empty(TN, TOPK, device="cuda")
             self.y_loc = torch.empty(T * TOPK, D, device="cuda")
+            own_gpu = torch.cuda.device_count() >= world
+            self.fused = os.environ.get("MOE_EP_EXCHANGE", "fused" if own_gpu else "nccl") == "fused"
+            if self.fused:
+                handles = [None] * world
+                dist.all_gather_object(handles, mc.ep_setup(T, D, TOPK))
+                mc.ep_connect(handles)
+                dist.barrier()
 
     def step(self, i, topk_idx=None, x_in=None, out=None):
         j = i % len(self.xs)
@@ -191,6 +202,9 @@ class Runner:
         o = self.out[j] if out is None else out
         if self.world == 1:
             self.mc.moe_ffn_dev(layer, x, o, topk_idx, None, stream=self.stream)
+        elif self.fused and topk_idx is None:
+            self.dist.all_gather_into_tensor(self.x_all, x)
+            self.mc.moe_ffn_ep(layer, self.x_all, o, stream=self.stream)
         else:
             self.dist.all_gather_into_tensor(self.x_all, x)
             self.mc.moe_ffn_partial(layer, self.x_all, self.y_all, topk_idx, self.p_all, stream=self.stream)
@@ -522,6 +536,8 @@ def run_ours(args):
                            "tokens": T, "tokens_per_step": TN, "experts": E, "hidden": D, "moe_intermediate": F,
                            "top_k": TOPK, "resident_layers": nl, "input_pool": pool,
                            "parallelism": f"ep{world}",
+                           "ep_exchange": (None if world == 1 else
+                                           ("fused peer stores" if run.fused else "nccl reduce_scatter")),
                            "l2": "inputs larger than L2: steps rotate over resident layers"},
                 "roofline": roof,
                 "layer": {"alg_gbs": layer_gbs, "frac_hbm": layer_gbs / peak,

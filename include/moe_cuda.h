@@ -81,7 +81,7 @@ int moe_cuda_check_status(void);
 
 /* ---- reference kernel surface (kernels.c / kernels.h) --------------------
  * Host pointers, synchronous. If B_q/B_s are host pointers previously given
- * to moe_cuda_upload_layer (or moe_cuda_register_weight), the resident device
+ * to moe_cuda_upload_layer (or moe_cuda_upload_layer_dev), the resident device
  * copy is used; otherwise the weight is copied for this call only. */
 /* replaces static matmul_f32_q8, kernels.c:51 (same parameter list) */
 void matmul_f32_q8(const float* A, const int8_t* B_q, const float* B_s,
@@ -186,6 +186,33 @@ int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots,
                     int* topk_idx_out, float* topk_p_out, void* stream);
 int moe_ffn_combine(const float* y_slots, const float* topk_p, float* x_inout,
                     int T, int D, int top_k, void* stream);
+
+/* ---- expert parallelism with the exchange fused into the down GEMM ------
+ * The same split as moe_ffn_partial + reduce + moe_ffn_combine, without the
+ * reduce: the down projection's epilogue stores each slot's output row into
+ * the receive buffer of the rank that owns the slot's token (peer stores over
+ * NVLink), a one-warp kernel raises this rank's flag at every peer, and the
+ * combine waits (bounded; MOE_ERR_CUDA with a timeout message afterwards via
+ * moe_cuda_check_status) on all ranks' flags before the k-ordered combine.
+ * The reference runs the whole MoE block on one CPU (test_model_trace.c:
+ * 463-517); this is the multi-GPU form of that block and has no counterpart
+ * there. One GPU per rank (moe_cuda_init with ep_world > 1).
+ *   moe_cuda_ep_setup: allocate the receive buffer for max_tokens_local tokens
+ *     of width D with top_k slots each; write this rank's 64-byte CUDA IPC
+ *     handle to ipc_handle_out. Collective in the caller's sense: every rank
+ *     calls it, then exchanges the handles (e.g. an all-gather).
+ *   moe_cuda_ep_connect: ipc_handles = ep_world handles of 64 bytes, in rank
+ *     order; opens the peers' buffers.
+ *   moe_ffn_ep: x_norm2_all = the normalised tokens of ALL ranks, [T_local *
+ *     ep_world][D], rank-major (identical on every rank); x_inout = this
+ *     rank's residual stream [T_local][D] (rows rank*T_local ...), updated in
+ *     place. Every rank must call it with the same T_local. Tensor-core path
+ *     only (Q8/Q4 layers, D and F multiples of 128), else
+ *     MOE_ERR_UNSUPPORTED. Device pointers, async on `stream`. */
+int moe_cuda_ep_setup(int max_tokens_local, int D, int top_k, void* ipc_handle_out);
+int moe_cuda_ep_connect(const void* ipc_handles);
+int moe_ffn_ep(int layer, const float* x_norm2_all, int T_local, float* x_inout,
+               void* stream);
 
 /* ---- profiling -------------------------------------------------------------
  * Per-kernel device time of moe_ffn / moe_ffn_partial (CUDA events recorded

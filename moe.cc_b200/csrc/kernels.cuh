@@ -116,8 +116,12 @@ bool mma_supported(const LayerDev& L);
 int mma_tile_n(int T, int dtype);
 void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream_t st);
 bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st);
+// ep_y (device array of per-rank receive buffers) != null: expert-parallel
+// mode, each slot row is stored into the buffer of the rank owning its token
+// (ep_T tokens per rank)
 bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, float* ys, bool fuse,
-                     const float* xres, float* out, int* err, cudaStream_t st);
+                     const float* xres, float* out, int* err, cudaStream_t st,
+                     float* const* ep_y = nullptr, int ep_T = 0);
 void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
                            const float* xres, float* out, int T, int D, int K, cudaStream_t st);
 void launch_unsort_rows(const LayerDev& L, const Workspace& ws, int T, float* y_slots, cudaStream_t st);
@@ -128,4 +132,13 @@ namespace moe {
 bool decode_route_supported(const LayerDev& L, int T, const float* x);
 void launch_decode_route(const LayerDev& L, const Workspace& ws, const float* x, int T, int nt,
                          int* counter, int* err, cudaStream_t st);
+}  // namespace moe
+
+namespace moe {
+// ep.cu: cross-rank completion signal and the waiting combine
+void launch_ep_signal(unsigned long long* const* peer_flags, int rank, int world, unsigned long long seq,
+                      cudaStream_t st);
+void launch_ep_combine(const unsigned long long* flags, int world, unsigned long long seq, const float* y,
+                       const float* p, const int* idx, const float* xres, float* out, int T, int D, int K,
+                       int* err, cudaStream_t st);
 }  // namespace moe

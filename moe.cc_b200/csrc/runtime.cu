@@ -138,6 +138,7 @@ using namespace moe;
 // scratch for the matmul_* entry points (grown on demand, never shrunk)
 // ---------------------------------------------------------------------------
 namespace moe {
+static void ep_shutdown_hook();   // releases the expert-parallel buffers (defined below)
 struct Buf { void* p = nullptr; size_t cap = 0; };
 static Buf s_A, s_C, s_W, s_S, s_act, s_asum;
 
@@ -253,6 +254,7 @@ int moe_cuda_shutdown(void) {
   std::lock_guard<std::recursive_mutex> lk(g.mu);
   if (!g.init) return MOE_OK;
   cudaDeviceSynchronize();
+  ep_shutdown_hook();
   for (auto& kv : g.layers) {
     cudaFree(kv.second.slab); cudaFree(kv.second.router_w);
     if (kv.second.router_b) cudaFree(kv.second.router_b);
@@ -759,4 +761,132 @@ int moe_cuda_profile_read(int max_kernels, char* names, int name_len, double* to
   }
   return i;
 }
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// expert parallelism with the slot exchange fused into the down GEMM
+// ---------------------------------------------------------------------------
+namespace moe {
+constexpr int kMaxEpRanks = 64;
+struct EpCtx {
+  bool ready = false, connected = false;
+  int cap_tokens = 0, D = 0, K = 0;
+  // [flags: kMaxEpRanks u64][receive rows, call parity 0][receive rows, parity 1]
+  uint8_t* buf = nullptr;
+  size_t recv_bytes = 0;                     // one parity's receive rows
+  void* peer_base[kMaxEpRanks] = {};
+  float** d_peer_y = nullptr;                // device arrays of peer pointers, [2][world]
+  unsigned long long** d_peer_flags = nullptr;
+  unsigned long long seq = 0;
+};
+static EpCtx g_ep;
+constexpr size_t kEpFlagBytes = 8 * kMaxEpRanks;
+static void ep_release();
+static void ep_shutdown_hook() { ep_release(); }
+
+static void ep_release() {
+  for (int p = 0; p < kMaxEpRanks; ++p)
+    if (g_ep.peer_base[p] && g_ep.peer_base[p] != g_ep.buf) cudaIpcCloseMemHandle(g_ep.peer_base[p]);
+  if (g_ep.buf) cudaFree(g_ep.buf);
+  if (g_ep.d_peer_y) cudaFree(g_ep.d_peer_y);
+  if (g_ep.d_peer_flags) cudaFree(g_ep.d_peer_flags);
+  g_ep = EpCtx{};
+}
+}  // namespace moe
+
+extern "C" {
+
+int moe_cuda_ep_setup(int max_tokens_local, int D, int top_k, void* ipc_handle_out) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  int rc = ensure_init();
+  if (rc) return rc;
+  if (g.ep_world < 2) return set_err(MOE_ERR_INVALID, "moe_cuda_ep_setup needs an expert-parallel group (ep_world > 1)");
+  if (g.ep_world > kMaxEpRanks) return set_err(MOE_ERR_UNSUPPORTED, "at most %d ranks", kMaxEpRanks);
+  if (max_tokens_local <= 0 || D <= 0 || top_k <= 0 || !ipc_handle_out)
+    return set_err(MOE_ERR_INVALID, "moe_cuda_ep_setup: bad arguments");
+  ep_release();
+  // two receive buffers, used by alternate calls: a peer can store into the
+  // parity of call n+2 only after this rank signalled call n+1, which it does
+  // after its combine of call n has consumed that parity.
+  g_ep.recv_bytes = sizeof(float) * (size_t)max_tokens_local * top_k * D;
+  const size_t bytes = kEpFlagBytes + 2 * g_ep.recv_bytes;
+  if (cudaMalloc((void**)&g_ep.buf, bytes) != cudaSuccess)
+    return set_err(MOE_ERR_NOMEM, "expert-parallel receive buffer (%zu bytes)", bytes);
+  CU(cudaMemset(g_ep.buf, 0, kEpFlagBytes));
+  cudaIpcMemHandle_t h;
+  CU(cudaIpcGetMemHandle(&h, g_ep.buf));
+  memcpy(ipc_handle_out, &h, sizeof(h));
+  g_ep.cap_tokens = max_tokens_local; g_ep.D = D; g_ep.K = top_k;
+  g_ep.ready = true;
+  return MOE_OK;
+}
+
+int moe_cuda_ep_connect(const void* ipc_handles) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  if (!g_ep.ready) return set_err(MOE_ERR_NOT_INIT, "moe_cuda_ep_setup has not been called");
+  const int W = g.ep_world;
+  const cudaIpcMemHandle_t* hs = (const cudaIpcMemHandle_t*)ipc_handles;
+  std::vector<float*> py(2 * W);
+  std::vector<unsigned long long*> pf(W);
+  for (int p = 0; p < W; ++p) {
+    if (p == g.ep_rank) {
+      g_ep.peer_base[p] = g_ep.buf;
+    } else if (!g_ep.peer_base[p]) {
+      void* ptr = nullptr;
+      CU(cudaIpcOpenMemHandle(&ptr, hs[p], cudaIpcMemLazyEnablePeerAccess));
+      g_ep.peer_base[p] = ptr;
+    }
+    pf[p] = (unsigned long long*)g_ep.peer_base[p];
+    py[p] = (float*)((uint8_t*)g_ep.peer_base[p] + kEpFlagBytes);
+    py[W + p] = (float*)((uint8_t*)g_ep.peer_base[p] + kEpFlagBytes + g_ep.recv_bytes);
+  }
+  CU(cudaMalloc((void**)&g_ep.d_peer_y, sizeof(float*) * 2 * W));
+  CU(cudaMalloc((void**)&g_ep.d_peer_flags, sizeof(void*) * W));
+  CU(cudaMemcpy(g_ep.d_peer_y, py.data(), sizeof(float*) * 2 * W, cudaMemcpyHostToDevice));
+  CU(cudaMemcpy(g_ep.d_peer_flags, pf.data(), sizeof(void*) * W, cudaMemcpyHostToDevice));
+  g_ep.connected = true;
+  return MOE_OK;
+}
+
+int moe_ffn_ep(int layer, const float* x_all, int T_local, float* x_inout, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  const LayerDev* Lp;
+  int rc = get_layer(layer, &Lp);
+  if (rc) return rc;
+  const LayerDev& L = *Lp;
+  if (!g_ep.connected) return set_err(MOE_ERR_NOT_INIT, "moe_cuda_ep_connect has not been called");
+  if (T_local < 0 || T_local > g_ep.cap_tokens || L.D != g_ep.D || L.topk != g_ep.K)
+    return set_err(MOE_ERR_INVALID, "moe_ffn_ep: T_local=%d exceeds the receive buffer (%d) or shape differs",
+                   T_local, g_ep.cap_tokens);
+  if (!use_tensor_cores(L, 0))
+    return set_err(MOE_ERR_UNSUPPORTED, "moe_ffn_ep needs the tensor-core path (Q8/Q4, D and F multiples of 128)");
+  if (T_local == 0) return MOE_OK;
+  const int W = g.ep_world, T = T_local * W;
+  if ((rc = ensure_workspace(T, L.E, L.D, L.F, L.topk))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const Workspace& w = g.ws;
+  const int nt = mma_tile_n(T, L.dtype);
+  route_tokens(L, x_all, T, nt, st);
+  if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
+  const unsigned long long seq = g_ep.seq + 1;
+  const int par = (int)(seq & 1);
+  bool ok = true;
+  timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
+  if (ok)
+    timed("mma_down_ep", st, [&] {
+      ok = launch_mma_down(L, w, T, nt, w.y, false, nullptr, nullptr, g.d_err, st, g_ep.d_peer_y + par * W, T_local);
+    });
+  if (!ok) return set_err(MOE_ERR_CUDA, "tensor-core launch failed (tensor map or shared memory)");
+  g_ep.seq = seq;
+  timed("ep_signal", st, [&] { launch_ep_signal(g_ep.d_peer_flags, g.ep_rank, W, seq, st); });
+  const size_t off = (size_t)g.ep_rank * T_local * L.topk;
+  timed("ep_combine", st, [&] {
+    launch_ep_combine((const unsigned long long*)g_ep.buf, W, seq,
+                      (const float*)(g_ep.buf + kEpFlagBytes + par * g_ep.recv_bytes), w.topk_p + off, w.topk_idx + off, x_inout,
+                      x_inout, T_local, L.D, L.topk, g.d_err, st);
+  });
+  CU(cudaGetLastError());
+  return MOE_OK;
+}
+
 }  // extern "C"

@@ -33,6 +33,7 @@ EXPORTS = (
     "moe_cuda_layer_bytes", "moe_ffn", "moe_ffn_partial", "moe_ffn_combine",
     "moe_synth_normal_host", "moe_synth_normal_dev",
     "moe_cuda_profile", "moe_cuda_profile_read", "moe_matmul_q_dev_noalloc",
+    "moe_cuda_ep_setup", "moe_cuda_ep_connect", "moe_ffn_ep",
 )
 
 
@@ -82,6 +83,9 @@ def lib():
             "moe_cuda_profile": ([i], i),
             "moe_matmul_q_dev_noalloc": ([vp, vp, vp, vp, i, i, i, i, vp], i),
             "moe_cuda_profile_read": ([i, vp, i, vp, vp], i),
+            "moe_cuda_ep_setup": ([i, i, i, vp], i),
+            "moe_cuda_ep_connect": ([vp], i),
+            "moe_ffn_ep": ([i, vp, i, vp, vp], i),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -237,6 +241,24 @@ def moe_ffn_partial(layer, x_norm2, y_slots, topk_idx=None, topk_p=None, stream=
 def moe_ffn_combine(y_slots, topk_p, x_inout, topk=8, stream=None):
     T, D = x_inout.shape
     check(lib().moe_ffn_combine(_p(y_slots), _p(topk_p), _p(x_inout), T, D, topk, _stream(stream)))
+
+
+def ep_setup(max_tokens_local, D, topk=8):
+    """Allocate this rank's receive buffer; returns its 64-byte IPC handle."""
+    h = C.create_string_buffer(64)
+    check(lib().moe_cuda_ep_setup(max_tokens_local, D, topk, h))
+    return h.raw
+
+
+def ep_connect(handles):
+    """handles: every rank's ep_setup() bytes, in rank order."""
+    buf = b"".join(handles)
+    check(lib().moe_cuda_ep_connect(C.c_char_p(buf)))
+
+
+def moe_ffn_ep(layer, x_norm2_all, x_inout, stream=None):
+    """Fused expert-parallel MoE block (include/moe_cuda.h: moe_ffn_ep)."""
+    check(lib().moe_ffn_ep(layer, _p(x_norm2_all), x_inout.shape[0], _p(x_inout), _stream(stream)))
 
 
 def profile(enable):

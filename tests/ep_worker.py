@@ -19,9 +19,35 @@ import moe_cuda as mc  # noqa: E402
 import synth as sy  # noqa: E402
 
 
+def fused_exchange(rank, world, T, xn, xa):
+    """moe_ffn_ep: T tokens split into world shards of T/world; three calls
+    (both receive-buffer parities, growing flag sequence); returns all T rows
+    gathered from the ranks."""
+    Tl = T // world
+    handles = [None] * world
+    dist.all_gather_object(handles, mc.ep_setup(Tl, 2048, 8))
+    mc.ep_connect(handles)
+    dist.barrier()
+    mine = xa[rank * Tl:(rank + 1) * Tl]
+    outs = []
+    for _ in range(3):
+        x = mine.clone()
+        mc.moe_ffn_ep(0, xn, x)
+        outs.append(x)
+    torch.cuda.synchronize()
+    mc.check_status()
+    for x in outs[1:]:
+        assert torch.equal(x, outs[0]), "fused expert-parallel call is not repeatable"
+    full = [torch.empty_like(outs[0]) for _ in range(world)]
+    dist.all_gather(full, outs[0])
+    dist.barrier()
+    return torch.cat(full)
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     out_path, T, dt = sys.argv[1], int(sys.argv[2]), int(sys.argv[3])
+    mode = sys.argv[4] if len(sys.argv) > 4 else "nccl"
     ngpu = torch.cuda.device_count()
     dev = rank if ngpu >= world else 0
     torch.cuda.set_device(dev)
@@ -35,21 +61,24 @@ def main():
     mc.upload_layer(0, L, device_arrays=True)
     xn = sy.make_tokens_dev(torch, 501, T, 2048)
     xa = sy.make_tokens_dev(torch, 502, T, 2048)
-    y = torch.empty(T * 8, 2048, device="cuda")
-    p = torch.empty(T, 8, device="cuda")
-    mc.moe_ffn_partial(0, xn, y, None, p)
-    torch.cuda.synchronize()
-    mc.check_status()
-    if backend == "nccl":
-        dist.all_reduce(y)
+    if mode == "fused":
+        out = fused_exchange(rank, world, T, xn, xa)
     else:
-        yc = y.cpu()
-        dist.all_reduce(yc)
-        y.copy_(yc)
-    out = xa.clone()
-    mc.moe_ffn_combine(y, p, out)
-    torch.cuda.synchronize()
-    mc.check_status()
+        y = torch.empty(T * 8, 2048, device="cuda")
+        p = torch.empty(T, 8, device="cuda")
+        mc.moe_ffn_partial(0, xn, y, None, p)
+        torch.cuda.synchronize()
+        mc.check_status()
+        if backend == "nccl":
+            dist.all_reduce(y)
+        else:
+            yc = y.cpu()
+            dist.all_reduce(yc)
+            y.copy_(yc)
+        out = xa.clone()
+        mc.moe_ffn_combine(y, p, out)
+        torch.cuda.synchronize()
+        mc.check_status()
     if rank == 0:
         Lh = {k: (v.cpu().numpy() if hasattr(v, "cpu") else v) for k, v in L.items()}
         np.savez(out_path, out=out.cpu().numpy(), xn=xn.cpu().numpy(), xa=xa.cpu().numpy(), **{

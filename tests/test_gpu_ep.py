@@ -12,7 +12,20 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-@pytest.mark.parametrize("dt,T", [(2, 16), (2, 40)])
+def assert_matches_port(out, ref, T):
+    """Bit-exact for small batches. With many tokens a few SiLU / softmax
+    exponentials round differently in the last place (device: double exp
+    rounded once; oracle: glibc expf), so large batches are held to the
+    layer tolerance 1e-4*max|y| with at least 99.5% of outputs identical."""
+    if T <= 64:
+        assert np.array_equal(out, ref)
+        return
+    err = float(np.abs(out - ref).max())
+    assert err <= 1e-4 * float(np.abs(ref).max()), f"max-abs {err}"
+    assert float(np.mean(out == ref)) >= 0.995
+
+
+@pytest.mark.parametrize("dt,T", [(2, 16), (2, 40), (2, 256)])
 def test_expert_parallel_two_ranks_matches_oracle(tmp_path, dt, T):
     out = str(tmp_path / "ep.npz")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
@@ -26,4 +39,27 @@ def test_expert_parallel_two_ranks_matches_oracle(tmp_path, dt, T):
     for k in ("router_w", "gq", "gs", "uq", "us", "dq", "ds"):
         L[k] = z[k]
     ref, _, _, _ = Port().moe_block(z["xn"], z["xa"], L)
-    assert np.array_equal(z["out"], ref)
+    assert_matches_port(z["out"], ref, T)
+
+
+@pytest.mark.parametrize("dt,T", [(2, 16), (3, 40), (2, 256)])
+def test_fused_expert_parallel_two_gpus_matches_oracle(tmp_path, dt, T):
+    """moe_ffn_ep: the down GEMM stores slot rows into the owning rank's
+    receive buffer over NVLink and the combine waits on the ranks' flags.
+    Needs one GPU per rank (ranks spin on one another)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("the fused exchange needs one GPU per rank (2 GPUs)")
+    out = str(tmp_path / "epf.npz")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", str(29700 + T + dt),
+           os.path.join(HERE, "ep_worker.py"), out, str(T), str(dt), "fused"]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    from oracle.oracle import Port
+    z = np.load(out)
+    L = {"dtype": dt, "topk": 8, "router_b": None}
+    for k in ("router_w", "gq", "gs", "uq", "us", "dq", "ds"):
+        L[k] = z[k]
+    ref, _, _, _ = Port().moe_block(z["xn"], z["xa"], L)
+    assert_matches_port(z["out"], ref, T)
