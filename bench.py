@@ -124,7 +124,8 @@ def alg_bytes(kernel, T, U, dt):
     activations in/out). U = distinct experts routed in that step."""
     gu_rb = D if dt == 2 else D // 2
     d_rb = F if dt == 2 else F // 2
-    kernel = kernel.replace("mma_", "").replace("down_ep", "down").replace("ep_combine", "combine")
+    kernel = (kernel.replace("mma_", "").replace("down_ep", "down").replace("ep_combine", "combine")
+              .replace("route_dispatch", "route"))
     if kernel == "gateup":
         return U * (2 * F * gu_rb + 2 * F * 4)
     if kernel == "down":
@@ -170,9 +171,10 @@ class Runner:
     each rank receives its own tokens' slots (exactly one rank contributes each
     slot, so the sum is exact), then the k-ordered combine + residual.
     With MOE_EP_EXCHANGE=fused (the default when every rank has its own GPU)
-    the reduce-scatter is replaced by moe_ffn_ep: the down GEMM's epilogue
-    stores each slot row into the owning rank's receive buffer over NVLink
-    and the combine waits on the ranks' flags.
+    the step is one moe_ffn_ep call and no collective: the routing kernel
+    sends this rank's tokens and top-k to every rank, the down GEMM's
+    epilogue stores each slot row into the owning rank's buffer over NVLink,
+    and kernels synchronise on flags in peer memory.
     """
 
     def __init__(self, torch, mc, dist, world, rank, T, nl, pool):
@@ -203,8 +205,7 @@ class Runner:
         if self.world == 1:
             self.mc.moe_ffn_dev(layer, x, o, topk_idx, None, stream=self.stream)
         elif self.fused and topk_idx is None:
-            self.dist.all_gather_into_tensor(self.x_all, x)
-            self.mc.moe_ffn_ep(layer, self.x_all, o, stream=self.stream)
+            self.mc.moe_ffn_ep(layer, x, o, stream=self.stream)
         else:
             self.dist.all_gather_into_tensor(self.x_all, x)
             self.mc.moe_ffn_partial(layer, self.x_all, self.y_all, topk_idx, self.p_all, stream=self.stream)

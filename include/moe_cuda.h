@@ -187,31 +187,39 @@ int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots,
 int moe_ffn_combine(const float* y_slots, const float* topk_p, float* x_inout,
                     int T, int D, int top_k, void* stream);
 
-/* ---- expert parallelism with the exchange fused into the down GEMM ------
- * The same split as moe_ffn_partial + reduce + moe_ffn_combine, without the
- * reduce: the down projection's epilogue stores each slot's output row into
- * the receive buffer of the rank that owns the slot's token (peer stores over
- * NVLink), a one-warp kernel raises this rank's flag at every peer, and the
- * combine waits (bounded; MOE_ERR_CUDA with a timeout message afterwards via
- * moe_cuda_check_status) on all ranks' flags before the k-ordered combine.
- * The reference runs the whole MoE block on one CPU (test_model_trace.c:
- * 463-517); this is the multi-GPU form of that block and has no counterpart
- * there. One GPU per rank (moe_cuda_init with ep_world > 1).
- *   moe_cuda_ep_setup: allocate the receive buffer for max_tokens_local tokens
- *     of width D with top_k slots each; write this rank's 64-byte CUDA IPC
- *     handle to ipc_handle_out. Collective in the caller's sense: every rank
- *     calls it, then exchanges the handles (e.g. an all-gather).
- *   moe_cuda_ep_connect: ipc_handles = ep_world handles of 64 bytes, in rank
- *     order; opens the peers' buffers.
- *   moe_ffn_ep: x_norm2_all = the normalised tokens of ALL ranks, [T_local *
- *     ep_world][D], rank-major (identical on every rank); x_inout = this
- *     rank's residual stream [T_local][D] (rows rank*T_local ...), updated in
- *     place. Every rank must call it with the same T_local. Tensor-core path
- *     only (Q8/Q4 layers, D and F multiples of 128), else
- *     MOE_ERR_UNSUPPORTED. Device pointers, async on `stream`. */
+/* ---- expert parallelism with both exchanges fused into the kernels --------
+ * The multi-GPU form of the MoE block (the reference runs it on one CPU,
+ * test_model_trace.c:463-517; no counterpart there). Rank r owns experts
+ * [r*E/W, (r+1)*E/W) (moe_cuda_init's ep_world/ep_rank) and T_local tokens.
+ * Per call, with no collective library involved:
+ *   routing kernel  routes this rank's tokens, stores their truncated
+ *                   activations and top-k into every rank's exchange buffer
+ *                   (peer stores over NVLink), raises this rank's dispatch
+ *                   flag at every rank, waits (bounded) for all ranks' flags
+ *                   and builds the routing lists of its own experts over all
+ *                   ranks' tokens;
+ *   expert GEMMs    as in moe_ffn; the down projection's epilogue stores each
+ *                   slot row into the exchange buffer of the rank owning the
+ *                   slot's token, and its last CTA raises the combine flag;
+ *   combine         waits (bounded) for all ranks' combine flags, then the
+ *                   k-ordered combine + residual of this rank's tokens.
+ * A wait that runs out reports a timeout through moe_cuda_check_status
+ * instead of hanging. Needs one GPU per rank.
+ *   moe_cuda_ep_setup: allocate this rank's exchange buffers for up to
+ *     max_tokens_local tokens per rank of width D with top_k slots each and
+ *     write its 64-byte CUDA IPC handle to ipc_handle_out. Every rank calls
+ *     it, then the ranks exchange the handles (e.g. an all-gather).
+ *   moe_cuda_ep_connect: ipc_handles = ep_world handles of 64 bytes in rank
+ *     order; maps the peers' buffers.
+ *   moe_ffn_ep: x_norm2 = this rank's normalised tokens [T_local][D];
+ *     x_inout = its residual stream [T_local][D], updated in place. Every
+ *     rank calls it with the same layer and T_local. Tensor-core path only
+ *     (Q8/Q4 layers, D and F multiples of 128) and at most 2048 routed slots
+ *     (T_local * ep_world * top_k) per call, else MOE_ERR_UNSUPPORTED.
+ *     Device pointers, async on `stream`. */
 int moe_cuda_ep_setup(int max_tokens_local, int D, int top_k, void* ipc_handle_out);
 int moe_cuda_ep_connect(const void* ipc_handles);
-int moe_ffn_ep(int layer, const float* x_norm2_all, int T_local, float* x_inout,
+int moe_ffn_ep(int layer, const float* x_norm2, int T_local, float* x_inout,
                void* stream);
 
 /* ---- profiling -------------------------------------------------------------

@@ -45,6 +45,30 @@ struct Workspace {
   float* xo = nullptr;        // [T][D]
 };
 
+// Expert-parallel exchange buffers. Every rank allocates the same layout
+// (CUDA IPC-shared): at offset 0 the dispatch flags [kEpMaxRanks] u64 and the
+// combine flags [kEpMaxRanks] u64 (rank r raises entry r; values are call
+// sequence numbers, so they only grow), then an int arrival counter of the
+// down kernel (local, kept zero); then two parities of data, alternate calls
+// using alternate parities:
+//   xact [world*T_local][2*D] u8   truncated activations of every rank's tokens
+//   xsum [world*T_local] int       their Σ (Q4 zero point)
+//   idx, p [world*T_local*K]       every rank's top-k choice and weight
+//   y [T_local*K][D] f32           this rank's slot rows, stored by the owners
+//                                  of the slots' experts
+// base[] holds the peers' mappings (own buffer at base[rank]); the *_off
+// fields point into this call's parity.
+constexpr int kEpMaxRanks = 64;
+constexpr size_t kEpDispatchFlags = 0, kEpCombineFlags = 8 * kEpMaxRanks, kEpCounter = 16 * kEpMaxRanks;
+constexpr size_t kEpHeader = 16 * kEpMaxRanks + 256;
+struct EpView {
+  uint8_t* const* base = nullptr;   // device array [world]
+  uint8_t* base_local = nullptr;    // == base[rank]
+  int world = 0, rank = 0, T_local = 0;
+  unsigned long long seq = 0;
+  size_t xact_off = 0, xsum_off = 0, idx_off = 0, p_off = 0, y_off = 0;
+};
+
 struct RouteView {
   int* n_active; int* active; int* exp_off; int* slot_list;
 };
@@ -116,12 +140,11 @@ bool mma_supported(const LayerDev& L);
 int mma_tile_n(int T, int dtype);
 void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream_t st);
 bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st);
-// ep_y (device array of per-rank receive buffers) != null: expert-parallel
-// mode, each slot row is stored into the buffer of the rank owning its token
-// (ep_T tokens per rank)
+// ep != null: expert-parallel mode, each slot row is stored into the y buffer
+// of the rank owning its token, and the last CTA raises this rank's combine
+// flag at every peer
 bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, float* ys, bool fuse,
-                     const float* xres, float* out, int* err, cudaStream_t st,
-                     float* const* ep_y = nullptr, int ep_T = 0);
+                     const float* xres, float* out, int* err, cudaStream_t st, const EpView* ep = nullptr);
 void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
                            const float* xres, float* out, int T, int D, int K, cudaStream_t st);
 void launch_unsort_rows(const LayerDev& L, const Workspace& ws, int T, float* y_slots, cudaStream_t st);
@@ -130,15 +153,16 @@ void launch_unsort_rows(const LayerDev& L, const Workspace& ws, int T, float* y_
 namespace moe {
 // router.cu: decode routing prologue in one launch
 bool decode_route_supported(const LayerDev& L, int T, const float* x);
+// ep != null: T = this rank's tokens; their activations and top-k go to every
+// rank's buffers, and the routing lists cover all ranks' tokens (after a
+// bounded wait on the dispatch flags)
 void launch_decode_route(const LayerDev& L, const Workspace& ws, const float* x, int T, int nt,
-                         int* counter, int* err, cudaStream_t st);
+                         int* counter, int* err, cudaStream_t st, const EpView* ep = nullptr);
 }  // namespace moe
 
 namespace moe {
-// ep.cu: cross-rank completion signal and the waiting combine
-void launch_ep_signal(unsigned long long* const* peer_flags, int rank, int world, unsigned long long seq,
-                      cudaStream_t st);
-void launch_ep_combine(const unsigned long long* flags, int world, unsigned long long seq, const float* y,
-                       const float* p, const int* idx, const float* xres, float* out, int T, int D, int K,
-                       int* err, cudaStream_t st);
+// ep.cu: the combine of the expert-parallel exchange (waits on the ranks'
+// combine flags, then the k-ordered combine of this rank's tokens)
+void launch_ep_combine(const EpView& ep, const float* xres, float* out, int D, int K, int* err,
+                       cudaStream_t st);
 }  // namespace moe

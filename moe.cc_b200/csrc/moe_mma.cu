@@ -58,7 +58,7 @@ struct Args {
   int* cnt; const int* slot_pos; const float* topk_p; const int* topk_idx;
   const int* xsum; int* hsum;                // Q4 zero-point sums (token / slot)
   int tokb;                                  // GATEUP: B = all T token rows (decode, T <= NT)
-  float* const* ep_y; int ep_T;              // DOWN, expert parallel: owners' receive buffers, tokens per rank
+  int ep_on; EpView ep;                      // DOWN, expert parallel: slot rows go to their owners' y buffers
   const float* xres; float* out;
   int* err;
 };
@@ -282,13 +282,15 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
           }
         } else {
           const float yv = fmul(fdiv(__int2float_rn(dot[0]), S), sc0);
-          if (a.ep_y) {
+          if (a.ep_on) {
             // expert parallel: the row goes straight to the rank owning the
-            // slot's token, into its receive buffer, over NVLink
+            // slot's token, into its y buffer, over NVLink
             const int sl = __ldg(a.route + 2 + 2 * a.E_local + j);
-            const int owner = sl / (a.topk * a.ep_T);
-            const int sloc = sl - owner * a.topk * a.ep_T;
-            a.ep_y[owner][(size_t)sloc * a.rows + n] = yv;
+            const int per = a.topk * a.ep.T_local;
+            const int owner = sl / per;
+            float* yo = reinterpret_cast<float*>(__ldg(reinterpret_cast<const unsigned long long*>(a.ep.base) + owner) +
+                                                 a.ep.y_off);
+            yo[(size_t)(sl - owner * per) * a.rows + n] = yv;
           } else {
             a.ys[(size_t)j * a.rows + n] = yv;
           }
@@ -359,8 +361,23 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
       }
     }
   }
-  if (MODE == DOWN && a.ep_y) __threadfence_system();   // peer stores before the ranks' signal
   __syncthreads();
+  if (MODE == DOWN && a.ep_on && threadIdx.x == 0) {
+    // The barrier orders the CTA's peer stores before this thread's system
+    // fence; the last CTA to arrive then raises this rank's combine flag at
+    // every rank (release), so a rank that sees the flag sees the rows.
+    __threadfence_system();
+    int* counter = reinterpret_cast<int*>(a.ep.base_local + kEpCounter);
+    if (atomicAdd(counter, 1) == (int)gridDim.x - 1) {
+      __threadfence_system();
+      for (int i = 0; i < a.ep.world; ++i) {
+        const int p = (a.ep.rank + i) % a.ep.world;
+        uint8_t* pb = reinterpret_cast<uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(a.ep.base) + p));
+        st_release_sys(reinterpret_cast<unsigned long long*>(pb + kEpCombineFlags) + a.ep.rank, a.ep.seq);
+      }
+      *counter = 0;
+    }
+  }
   if (threadIdx.x == 0 && s_abort) {
     // let the tensor copies still in flight land before the CTA's smem goes away
     for (int it = max(0, s_issued - a.stages); it < s_issued; ++it)
@@ -565,7 +582,7 @@ bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, in
 }
 
 bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, float* ys, bool fuse,
-                     const float* xres, float* out, int* err, cudaStream_t st, float* const* ep_y, int ep_T) {
+                     const float* xres, float* out, int* err, cudaStream_t st, const EpView* ep) {
   const int E_local = L.e_end - L.e_begin, TK = T * L.topk, cap = ws.cap_T * ws.cap_K;
   mm::TMap a0, b0, b1;
   if (!mm::map_weights(a0, L, L.dq_off, L.F, L.D) || !mm::map_rows(b0, ws.hs0, L.F, cap, nt) ||
@@ -578,7 +595,8 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
   a.ys = ys; a.fuse = fuse ? 1 : 0; a.T = T; a.topk = L.topk;
   a.cnt = ws.cnt; a.slot_pos = ws.slot_pos; a.topk_p = ws.topk_p; a.topk_idx = ws.topk_idx;
   a.xres = xres; a.out = out; a.err = err;
-  a.xsum = ws.xsum; a.hsum = ws.hsum; a.ep_y = ep_y; a.ep_T = ep_T;
+  a.xsum = ws.xsum; a.hsum = ws.hsum; a.ep_on = ep != nullptr;
+  if (ep) a.ep = *ep;
   const int units = a.max_tiles * a.n_mblk, gc = mm::grid_ctas(L.dtype == 2 ? 8 : 4);
   const int grid = units < gc ? units : gc;
   bool ok = false;

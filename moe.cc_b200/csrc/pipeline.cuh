@@ -60,4 +60,26 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 // copy latency (microseconds) yet ends in well under a second.
 constexpr uint32_t kWaitBudget = 1u << 24;
 
+// ---- cross-GPU flags (expert-parallel exchange over peer memory) ----------
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// One thread: wait until flags[0..world) all reached seq. Bounded: a rank
+// that never arrives makes this return false after ~kWaitBudget polls per
+// flag instead of hanging the GPU.
+__device__ __forceinline__ bool wait_flags_sys(const unsigned long long* flags, int world,
+                                               unsigned long long seq) {
+  for (int src = 0; src < world; ++src) {
+    uint32_t i = 0;
+    while (ld_acquire_sys(flags + src) < seq)
+      if (++i >= kWaitBudget) return false;
+  }
+  return true;
+}
+
 }  // namespace moe

@@ -32,7 +32,12 @@ struct Args {
   int* route; int e_begin, E_local; int* hsum; int nt, max_tiles; int* slot_pos;
   uint8_t* xact; int* xsum; int q4_mma;
   int* counter; int* err;
+  int ep_on; EpView ep;    // expert parallel: dispatch this rank's tokens, route all ranks' tokens
 };
+
+__device__ __forceinline__ uint8_t* peer_base(const EpView& ep, int p) {
+  return reinterpret_cast<uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(ep.base) + p));
+}
 
 template <int DT>
 __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
@@ -108,7 +113,17 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
     const int q0 = tid - kChainThreads, nq = kThreads - kChainThreads;
     for (int c = 0; c < kChunks; ++c)
       if (!mbar_wait(&bar[c], 0, kWaitBudget)) { ok = false; break; }
-    if (ok) {
+    // expert parallel: the activations go to every rank's xact (rows of this
+    // rank's tokens), starting with the next rank so the links share the load
+    const int ndst = a.ep_on ? a.ep.world : 1;
+    for (int di = 0; ok && di < ndst; ++di) {
+      uint8_t* xact = a.xact;
+      int* xsum = a.xsum;
+      if (a.ep_on) {
+        uint8_t* pb = peer_base(a.ep, (a.ep.rank + 1 + di) % a.ep.world);
+        xact = pb + a.ep.xact_off + (size_t)a.ep.rank * a.ep.T_local * 2 * a.D;
+        xsum = reinterpret_cast<int*>(pb + a.ep.xsum_off) + a.ep.rank * a.ep.T_local;
+      }
       const int c0 = (int)((long)a.D * blockIdx.x / gridDim.x);
       const int c1 = (int)((long)a.D * (blockIdx.x + 1) / gridDim.x);
       const int w = c1 - c0;
@@ -116,7 +131,7 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
       for (int q = q0; q < nt * w; q += nq) {
         const int t = q / w, k = c0 + q % w;
         const int v = trunc_scale(sx[t * pitch + k], DT == 8 ? 127.0f : 7.0f);
-        uint8_t* ar = a.xact + (size_t)(t0 + t) * 2 * a.D;
+        uint8_t* ar = xact + (size_t)(t0 + t) * 2 * a.D;
         if (DT == 8) {
           bad |= (v < -32768 || v > 32767);
           ar[k] = (uint8_t)(v & 0xFF);
@@ -132,7 +147,7 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
           int sacc = 0;
           for (int k = q0 % 32; k < a.D; k += 32) sacc += trunc_scale(sx[t * pitch + k], 7.0f);
           sacc = warp_sum(sacc);
-          if ((q0 & 31) == 0) a.xsum[t0 + t] = sacc;
+          if ((q0 & 31) == 0) xsum[t0 + t] = sacc;
         }
       }
     }
@@ -140,8 +155,14 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
   if (!ok && (tid & 31) == 0) atomicOr(a.err, kErrTimeout);
 
   // ---- last CTA: top-k, softmax, routing ----
-  __threadfence();
-  __syncthreads();
+  if (a.ep_on) {
+    // the barrier orders the CTA's peer stores before thread 0's system fence
+    __syncthreads();
+    if (tid == 0) __threadfence_system();
+  } else {
+    __threadfence();
+    __syncthreads();
+  }
   if (tid == 0) s_last = atomicAdd(a.counter, 1) == (int)(gridDim.x * gridDim.y) - 1;
   __syncthreads();
   if (!s_last) return;
@@ -151,7 +172,7 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
   __shared__ int cnt[kMaxE], start[kMaxE], s_tab[1 + 3 * kMaxTiles];
   __shared__ int s_route[2 + 2 * kMaxE + kMaxTK];
   const int lane = tid & 31, warp = tid >> 5;
-  const int TK = a.T * a.K;
+  int TK = a.T * a.K;
   for (int i = tid; i < a.E_local; i += kThreads) cnt[i] = 0;
   // top-k per token: one warp per token, K rounds; each round is two warp
   // reductions (redux.sync): the largest order-preserving key, then the lowest
@@ -200,12 +221,41 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
     for (int i = 0; i < a.K; ++i) sum = fadd(sum, __shfl_sync(0xffffffffu, ev, i));
     const float inv = fdiv(1.0f, fadd(sum, 1e-9f));
     if (lane < a.K) {
+      const float pv = fmul(ev, inv);
       a.idx[t * a.K + lane] = myi;
-      a.p[t * a.K + lane] = fmul(ev, inv);
+      a.p[t * a.K + lane] = pv;
       sidx[t * a.K + lane] = myi;
+      if (a.ep_on)
+        for (int di = 0; di < a.ep.world; ++di) {
+          uint8_t* pb = peer_base(a.ep, (a.ep.rank + 1 + di) % a.ep.world);
+          const size_t s = (size_t)a.ep.rank * a.ep.T_local * a.K + t * a.K + lane;
+          reinterpret_cast<int*>(pb + a.ep.idx_off)[s] = myi;
+          reinterpret_cast<float*>(pb + a.ep.p_off)[s] = pv;
+        }
     }
   }
   __syncthreads();
+  if (a.ep_on) {
+    // dispatch: raise this rank's flag at every rank, wait for every rank's,
+    // then route the slots of all ranks' tokens (slot = global token * K + k)
+    __shared__ int s_ok;
+    if (tid == 0) {
+      __threadfence_system();
+      for (int di = 0; di < a.ep.world; ++di) {
+        const int p = (a.ep.rank + 1 + di) % a.ep.world;
+        st_release_sys(reinterpret_cast<unsigned long long*>(peer_base(a.ep, p) + kEpDispatchFlags) + a.ep.rank,
+                       a.ep.seq);
+      }
+      s_ok = wait_flags_sys(reinterpret_cast<const unsigned long long*>(a.ep.base_local + kEpDispatchFlags),
+                            a.ep.world, a.ep.seq);
+      if (!s_ok) atomicOr(a.err, kErrTimeout);
+    }
+    __syncthreads();
+    TK = s_ok ? a.ep.world * a.ep.T_local * a.K : 0;   // a failed wait routes nothing
+    const int* all = reinterpret_cast<const int*>(a.ep.base_local + a.ep.idx_off);
+    for (int s = tid; s < TK; s += kThreads) sidx[s] = __ldcg(all + s);
+    __syncthreads();
+  }
   for (int s = tid; s < TK; s += kThreads) {
     const int el = sidx[s] - a.e_begin;
     if (el >= 0 && el < a.E_local) atomicAdd(&cnt[el], 1);
@@ -309,15 +359,18 @@ bool decode_route_supported(const LayerDev& L, int T, const float* x) {
 }
 
 void launch_decode_route(const LayerDev& L, const Workspace& ws, const float* x, int T, int nt,
-                         int* counter, int* err, cudaStream_t st) {
+                         int* counter, int* err, cudaStream_t st, const EpView* ep) {
   rt::Args a{};
   a.x = x; a.W = L.router_w; a.b = L.router_b; a.T = T; a.E = L.E; a.D = L.D; a.K = L.topk;
   a.logits = ws.logits; a.idx = ws.topk_idx; a.p = ws.topk_p;
   a.route = ws.route; a.e_begin = L.e_begin; a.E_local = L.e_end - L.e_begin;
   a.hsum = L.dtype == 3 ? ws.hsum : nullptr;
-  a.nt = nt; a.max_tiles = nt > 0 ? route_max_tiles(T * L.topk, a.E_local, nt) : 0;
+  const int T_route = ep ? ep->world * ep->T_local : T;     // tokens whose slots are routed here
+  a.nt = nt; a.max_tiles = nt > 0 ? route_max_tiles(T_route * L.topk, a.E_local, nt) : 0;
   a.slot_pos = nt > 0 ? ws.slot_pos : nullptr;
   a.xact = ws.xact; a.xsum = ws.xsum; a.q4_mma = nt > 0; a.counter = counter; a.err = err;
+  a.ep_on = ep != nullptr;
+  if (ep) a.ep = *ep;
   const size_t smem = (size_t)(rt::kE + rt::kT) * (L.D + 4) * 4;
   dim3 grid((L.E + rt::kE - 1) / rt::kE, (T + rt::kT - 1) / rt::kT);
   if (L.dtype == 2) {

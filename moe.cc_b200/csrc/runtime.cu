@@ -764,34 +764,31 @@ int moe_cuda_profile_read(int max_kernels, char* names, int name_len, double* to
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
-// expert parallelism with the slot exchange fused into the down GEMM
+// expert parallelism: dispatch fused into the routing kernel, exchange of the
+// slot rows fused into the down GEMM (buffer layout: EpView in kernels.cuh)
 // ---------------------------------------------------------------------------
 namespace moe {
-constexpr int kMaxEpRanks = 64;
 struct EpCtx {
   bool ready = false, connected = false;
-  int cap_tokens = 0, D = 0, K = 0;
-  // [flags: kMaxEpRanks u64][receive rows, call parity 0][receive rows, parity 1]
+  int cap_tokens = 0, D = 0, K = 0, world = 0;
   uint8_t* buf = nullptr;
-  size_t recv_bytes = 0;                     // one parity's receive rows
-  void* peer_base[kMaxEpRanks] = {};
-  float** d_peer_y = nullptr;                // device arrays of peer pointers, [2][world]
-  unsigned long long** d_peer_flags = nullptr;
+  size_t xact_off = 0, xsum_off = 0, idx_off = 0, p_off = 0, y_off = 0, parity_bytes = 0;
+  void* peer_base[kEpMaxRanks] = {};
+  uint8_t** d_base = nullptr;                // device array of the peers' bases
   unsigned long long seq = 0;
 };
 static EpCtx g_ep;
-constexpr size_t kEpFlagBytes = 8 * kMaxEpRanks;
-static void ep_release();
-static void ep_shutdown_hook() { ep_release(); }
 
 static void ep_release() {
-  for (int p = 0; p < kMaxEpRanks; ++p)
+  for (int p = 0; p < kEpMaxRanks; ++p)
     if (g_ep.peer_base[p] && g_ep.peer_base[p] != g_ep.buf) cudaIpcCloseMemHandle(g_ep.peer_base[p]);
   if (g_ep.buf) cudaFree(g_ep.buf);
-  if (g_ep.d_peer_y) cudaFree(g_ep.d_peer_y);
-  if (g_ep.d_peer_flags) cudaFree(g_ep.d_peer_flags);
+  if (g_ep.d_base) cudaFree(g_ep.d_base);
   g_ep = EpCtx{};
 }
+static void ep_shutdown_hook() { ep_release(); }
+
+static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 }  // namespace moe
 
 extern "C" {
@@ -800,23 +797,28 @@ int moe_cuda_ep_setup(int max_tokens_local, int D, int top_k, void* ipc_handle_o
   std::lock_guard<std::recursive_mutex> lk(g.mu);
   int rc = ensure_init();
   if (rc) return rc;
-  if (g.ep_world < 2) return set_err(MOE_ERR_INVALID, "moe_cuda_ep_setup needs an expert-parallel group (ep_world > 1)");
-  if (g.ep_world > kMaxEpRanks) return set_err(MOE_ERR_UNSUPPORTED, "at most %d ranks", kMaxEpRanks);
+  const int W = g.ep_world;
+  if (W < 2) return set_err(MOE_ERR_INVALID, "moe_cuda_ep_setup needs an expert-parallel group (ep_world > 1)");
+  if (W > kEpMaxRanks) return set_err(MOE_ERR_UNSUPPORTED, "at most %d ranks", kEpMaxRanks);
   if (max_tokens_local <= 0 || D <= 0 || top_k <= 0 || !ipc_handle_out)
     return set_err(MOE_ERR_INVALID, "moe_cuda_ep_setup: bad arguments");
   ep_release();
-  // two receive buffers, used by alternate calls: a peer can store into the
-  // parity of call n+2 only after this rank signalled call n+1, which it does
-  // after its combine of call n has consumed that parity.
-  g_ep.recv_bytes = sizeof(float) * (size_t)max_tokens_local * top_k * D;
-  const size_t bytes = kEpFlagBytes + 2 * g_ep.recv_bytes;
+  const size_t TA = (size_t)W * max_tokens_local;          // tokens of all ranks
+  size_t o = 0;
+  g_ep.xact_off = o;  o = align256(o + TA * 2 * D);
+  g_ep.xsum_off = o;  o = align256(o + TA * 4);
+  g_ep.idx_off = o;   o = align256(o + TA * top_k * 4);
+  g_ep.p_off = o;     o = align256(o + TA * top_k * 4);
+  g_ep.y_off = o;     o = align256(o + (size_t)max_tokens_local * top_k * D * 4);
+  g_ep.parity_bytes = o;
+  const size_t bytes = kEpHeader + 2 * o;
   if (cudaMalloc((void**)&g_ep.buf, bytes) != cudaSuccess)
-    return set_err(MOE_ERR_NOMEM, "expert-parallel receive buffer (%zu bytes)", bytes);
-  CU(cudaMemset(g_ep.buf, 0, kEpFlagBytes));
+    return set_err(MOE_ERR_NOMEM, "expert-parallel buffers (%zu bytes)", bytes);
+  CU(cudaMemset(g_ep.buf, 0, bytes));
   cudaIpcMemHandle_t h;
   CU(cudaIpcGetMemHandle(&h, g_ep.buf));
   memcpy(ipc_handle_out, &h, sizeof(h));
-  g_ep.cap_tokens = max_tokens_local; g_ep.D = D; g_ep.K = top_k;
+  g_ep.cap_tokens = max_tokens_local; g_ep.D = D; g_ep.K = top_k; g_ep.world = W;
   g_ep.ready = true;
   return MOE_OK;
 }
@@ -824,10 +826,10 @@ int moe_cuda_ep_setup(int max_tokens_local, int D, int top_k, void* ipc_handle_o
 int moe_cuda_ep_connect(const void* ipc_handles) {
   std::lock_guard<std::recursive_mutex> lk(g.mu);
   if (!g_ep.ready) return set_err(MOE_ERR_NOT_INIT, "moe_cuda_ep_setup has not been called");
-  const int W = g.ep_world;
+  if (!ipc_handles) return set_err(MOE_ERR_INVALID, "moe_cuda_ep_connect: null handles");
+  const int W = g_ep.world;
   const cudaIpcMemHandle_t* hs = (const cudaIpcMemHandle_t*)ipc_handles;
-  std::vector<float*> py(2 * W);
-  std::vector<unsigned long long*> pf(W);
+  std::vector<uint8_t*> base(W);
   for (int p = 0; p < W; ++p) {
     if (p == g.ep_rank) {
       g_ep.peer_base[p] = g_ep.buf;
@@ -836,19 +838,15 @@ int moe_cuda_ep_connect(const void* ipc_handles) {
       CU(cudaIpcOpenMemHandle(&ptr, hs[p], cudaIpcMemLazyEnablePeerAccess));
       g_ep.peer_base[p] = ptr;
     }
-    pf[p] = (unsigned long long*)g_ep.peer_base[p];
-    py[p] = (float*)((uint8_t*)g_ep.peer_base[p] + kEpFlagBytes);
-    py[W + p] = (float*)((uint8_t*)g_ep.peer_base[p] + kEpFlagBytes + g_ep.recv_bytes);
+    base[p] = (uint8_t*)g_ep.peer_base[p];
   }
-  CU(cudaMalloc((void**)&g_ep.d_peer_y, sizeof(float*) * 2 * W));
-  CU(cudaMalloc((void**)&g_ep.d_peer_flags, sizeof(void*) * W));
-  CU(cudaMemcpy(g_ep.d_peer_y, py.data(), sizeof(float*) * 2 * W, cudaMemcpyHostToDevice));
-  CU(cudaMemcpy(g_ep.d_peer_flags, pf.data(), sizeof(void*) * W, cudaMemcpyHostToDevice));
+  if (!g_ep.d_base) CU(cudaMalloc((void**)&g_ep.d_base, sizeof(uint8_t*) * W));
+  CU(cudaMemcpy(g_ep.d_base, base.data(), sizeof(uint8_t*) * W, cudaMemcpyHostToDevice));
   g_ep.connected = true;
   return MOE_OK;
 }
 
-int moe_ffn_ep(int layer, const float* x_all, int T_local, float* x_inout, void* stream) {
+int moe_ffn_ep(int layer, const float* x_norm2, int T_local, float* x_inout, void* stream) {
   std::lock_guard<std::recursive_mutex> lk(g.mu);
   const LayerDev* Lp;
   int rc = get_layer(layer, &Lp);
@@ -856,35 +854,46 @@ int moe_ffn_ep(int layer, const float* x_all, int T_local, float* x_inout, void*
   const LayerDev& L = *Lp;
   if (!g_ep.connected) return set_err(MOE_ERR_NOT_INIT, "moe_cuda_ep_connect has not been called");
   if (T_local < 0 || T_local > g_ep.cap_tokens || L.D != g_ep.D || L.topk != g_ep.K)
-    return set_err(MOE_ERR_INVALID, "moe_ffn_ep: T_local=%d exceeds the receive buffer (%d) or shape differs",
+    return set_err(MOE_ERR_INVALID, "moe_ffn_ep: T_local=%d exceeds the buffers (%d) or the layer shape differs",
                    T_local, g_ep.cap_tokens);
+  const int W = g_ep.world, T = T_local * W;
   if (!use_tensor_cores(L, 0))
     return set_err(MOE_ERR_UNSUPPORTED, "moe_ffn_ep needs the tensor-core path (Q8/Q4, D and F multiples of 128)");
   if (T_local == 0) return MOE_OK;
-  const int W = g.ep_world, T = T_local * W;
+  if (!decode_route_supported(L, T, x_norm2))
+    return set_err(MOE_ERR_UNSUPPORTED,
+                   "moe_ffn_ep: %d routed slots per step over all ranks (at most 2048), or unaligned input",
+                   T * L.topk);
   if ((rc = ensure_workspace(T, L.E, L.D, L.F, L.topk))) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  const Workspace& w = g.ws;
+  const unsigned long long seq = ++g_ep.seq;
+  const size_t par = (seq & 1) ? g_ep.parity_bytes : 0;
+  EpView ep;
+  ep.base = g_ep.d_base; ep.base_local = g_ep.buf;
+  ep.world = W; ep.rank = g.ep_rank; ep.T_local = T_local; ep.seq = seq;
+  ep.xact_off = kEpHeader + par + g_ep.xact_off; ep.xsum_off = kEpHeader + par + g_ep.xsum_off;
+  ep.idx_off = kEpHeader + par + g_ep.idx_off;   ep.p_off = kEpHeader + par + g_ep.p_off;
+  ep.y_off = kEpHeader + par + g_ep.y_off;
+  // the expert kernels read all ranks' tokens from the exchange buffers
+  Workspace w = g.ws;
+  w.xact = g_ep.buf + ep.xact_off;
+  w.xsum = (int*)(g_ep.buf + ep.xsum_off);
+  w.topk_idx = (int*)(g_ep.buf + ep.idx_off);
+  w.topk_p = (float*)(g_ep.buf + ep.p_off);
+  w.cap_T = std::min(g.ws.cap_T, W * g_ep.cap_tokens);     // rows the tensor maps may cover
   const int nt = mma_tile_n(T, L.dtype);
-  route_tokens(L, x_all, T, nt, st);
+  timed("route_dispatch", st, [&] {
+    launch_decode_route(L, g.ws, x_norm2, T_local, nt, g.ws.route_counter, g.d_err, st, &ep);
+  });
   if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
-  const unsigned long long seq = g_ep.seq + 1;
-  const int par = (int)(seq & 1);
   bool ok = true;
   timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
   if (ok)
     timed("mma_down_ep", st, [&] {
-      ok = launch_mma_down(L, w, T, nt, w.y, false, nullptr, nullptr, g.d_err, st, g_ep.d_peer_y + par * W, T_local);
+      ok = launch_mma_down(L, w, T, nt, w.y, false, nullptr, nullptr, g.d_err, st, &ep);
     });
   if (!ok) return set_err(MOE_ERR_CUDA, "tensor-core launch failed (tensor map or shared memory)");
-  g_ep.seq = seq;
-  timed("ep_signal", st, [&] { launch_ep_signal(g_ep.d_peer_flags, g.ep_rank, W, seq, st); });
-  const size_t off = (size_t)g.ep_rank * T_local * L.topk;
-  timed("ep_combine", st, [&] {
-    launch_ep_combine((const unsigned long long*)g_ep.buf, W, seq,
-                      (const float*)(g_ep.buf + kEpFlagBytes + par * g_ep.recv_bytes), w.topk_p + off, w.topk_idx + off, x_inout,
-                      x_inout, T_local, L.D, L.topk, g.d_err, st);
-  });
+  timed("ep_combine", st, [&] { launch_ep_combine(ep, x_inout, x_inout, L.D, L.topk, g.d_err, st); });
   CU(cudaGetLastError());
   return MOE_OK;
 }

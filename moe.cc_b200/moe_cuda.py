@@ -256,9 +256,10 @@ def ep_connect(handles):
     check(lib().moe_cuda_ep_connect(C.c_char_p(buf)))
 
 
-def moe_ffn_ep(layer, x_norm2_all, x_inout, stream=None):
-    """Fused expert-parallel MoE block (include/moe_cuda.h: moe_ffn_ep)."""
-    check(lib().moe_ffn_ep(layer, _p(x_norm2_all), x_inout.shape[0], _p(x_inout), _stream(stream)))
+def moe_ffn_ep(layer, x_norm2, x_inout, stream=None):
+    """Expert-parallel MoE block over this rank's tokens, exchanges fused into
+    the kernels (include/moe_cuda.h: moe_ffn_ep)."""
+    check(lib().moe_ffn_ep(layer, _p(x_norm2), x_inout.shape[0], _p(x_inout), _stream(stream)))
 
 
 def profile(enable):

@@ -32,7 +32,7 @@ def fused_exchange(rank, world, T, xn, xa):
     outs = []
     for _ in range(3):
         x = mine.clone()
-        mc.moe_ffn_ep(0, xn, x)
+        mc.moe_ffn_ep(0, xn[rank * Tl:(rank + 1) * Tl], x)
         outs.append(x)
     torch.cuda.synchronize()
     mc.check_status()
