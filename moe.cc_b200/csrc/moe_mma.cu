@@ -58,6 +58,7 @@ struct Args {
   int* cnt; const int* slot_pos; const float* topk_p; const int* topk_idx;
   const int* xsum; int* hsum;                // Q4 zero-point sums (token / slot)
   int tokb;                                  // GATEUP: B = all T token rows (decode, T <= NT)
+  int w_once;                                // T <= NT: one token tile per expert, weights read once
   int ep_on; EpView ep;                      // DOWN, expert parallel: slot rows go to their owners' y buffers
   const float* xres; float* out;
   int* err;
@@ -123,6 +124,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
     // ------------------------- TMA producer -------------------------
     if (lane == 0) {
       const uint32_t bytes = (DT == 4 ? NM * kPackedBytes : NM * A_BYTES) + NL * B_BYTES;
+      const uint64_t wpol = tc::policy_evict_first();
       int it = 0;
       for (int u = u0; u < n_units && !*abort_flag; u += ustep) {
         const int tile = u / a.n_mblk, mb = u % a.n_mblk;
@@ -134,12 +136,16 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
           }
           uint8_t* sb = smem + (size_t)st * a.stage_bytes;
           mbar_arrive_expect_tx(&full[st], bytes);
-          if (DT == 8) {
-            tc::tma_load_3d(sb, &tmA0.m, kc * 128, mb * 128, e, &full[st]);
-            if (NM == 2) tc::tma_load_3d(sb + A_BYTES, &tmA1.m, kc * 128, mb * 128, e, &full[st]);
-          } else {   // packed nibbles; the expanders build the A tiles from them
-            tc::tma_load_3d(sb, &tmA0.m, kc * 64, mb * 128, e, &full[st]);
-            if (NM == 2) tc::tma_load_3d(sb + kPackedBytes, &tmA1.m, kc * 64, mb * 128, e, &full[st]);
+          // weights: when every expert has a single token tile (a.w_once) each
+          // weight tile is read exactly once, so it is loaded evict-first
+          const int kx = DT == 8 ? kc * 128 : kc * 64;
+          const int a1 = DT == 8 ? A_BYTES : kPackedBytes;
+          if (a.w_once) {
+            tc::tma_load_3d_hint(sb, &tmA0.m, kx, mb * 128, e, &full[st], wpol);
+            if (NM == 2) tc::tma_load_3d_hint(sb + a1, &tmA1.m, kx, mb * 128, e, &full[st], wpol);
+          } else {   // Q4: packed nibbles; the expanders build the A tiles from them
+            tc::tma_load_3d(sb, &tmA0.m, kx, mb * 128, e, &full[st]);
+            if (NM == 2) tc::tma_load_3d(sb + a1, &tmA1.m, kx, mb * 128, e, &full[st]);
           }
           const int by = a.tokb ? 0 : j0;   // decode: all token rows from row 0
           tc::tma_load_2d(sb + (DT == 4 ? NM * kPackedBytes : NM * A_BYTES), &tmB0.m, kc * 128, by, &full[st]);
@@ -491,6 +497,13 @@ static int sms() {
 // with the whole shared-memory budget.
 static int ctas_for(int dt) { return dt == 4 ? 1 : ctas_per_sm(); }
 static int grid_ctas(int dt) { return sms() * ctas_for(dt); }
+// weights read once per call are loaded evict-first (MOE_NO_EVICT_FIRST=1
+// turns it off, for measurements)
+static bool evict_first_on() {
+  static int v = -1;
+  if (v < 0) v = getenv("MOE_NO_EVICT_FIRST") ? 0 : 1;
+  return v == 1;
+}
 
 template <int DT, int MODE, int NT>
 static bool launch_kernel(const TMap& a0, const TMap& a1, const TMap& b0, const TMap& b1, Args a, int grid,
@@ -572,7 +585,7 @@ bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, in
   a.route = ws.route; a.E_local = E_local; a.TK = TK; a.max_tiles = route_max_tiles(TK, E_local, nt);
   a.slab = L.slab; a.stride = L.expert_stride; a.s0_off = L.gs_off; a.s1_off = L.us_off;
   a.F = L.F; a.hs0 = ws.hs0; a.hs1 = ws.hs1; a.err = err;
-  a.xsum = ws.xsum; a.hsum = ws.hsum; a.topk = L.topk; a.tokb = tokb;
+  a.xsum = ws.xsum; a.hsum = ws.hsum; a.topk = L.topk; a.tokb = tokb; a.w_once = T <= nt && mm::evict_first_on();
   const int units = a.max_tiles * a.n_mblk, gc = mm::grid_ctas(L.dtype == 2 ? 8 : 4);
   const int grid = units < gc ? units : gc;
   bool ok = false;
@@ -596,6 +609,7 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
   a.cnt = ws.cnt; a.slot_pos = ws.slot_pos; a.topk_p = ws.topk_p; a.topk_idx = ws.topk_idx;
   a.xres = xres; a.out = out; a.err = err;
   a.xsum = ws.xsum; a.hsum = ws.hsum; a.ep_on = ep != nullptr;
+  a.w_once = T <= nt && mm::evict_first_on();
   if (ep) a.ep = *ep;
   const int units = a.max_tiles * a.n_mblk, gc = mm::grid_ctas(L.dtype == 2 ? 8 : 4);
   const int grid = units < gc ? units : gc;

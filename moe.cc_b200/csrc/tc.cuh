@@ -26,6 +26,23 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, 
       : "memory");
 }
 
+// Same with an L2 cache policy (createpolicy result): weights streamed once
+// per call are loaded evict-first so they do not push the kernels' code and
+// the small per-call tables out of L2.
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
