@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <utility>
 
 namespace moe {
 
@@ -104,6 +105,31 @@ __host__ __device__ __forceinline__ int q4_act_pos(int k) {
 // low-nibble bytes followed by 16 high-nibble bytes.
 __host__ __device__ __forceinline__ int q4_mma_pos(int k) {
   return (k & ~31) + ((k & 1) << 4) + ((k & 31) >> 1);
+}
+
+// ---- programmatic dependent launch ----------------------------------------
+// The kernels of one MoE call are launched with programmatic stream
+// serialization: a kernel may start while its predecessor in the stream still
+// runs. Each kernel runs pdl_wait() before it touches anything the
+// predecessor writes or reads, and signals pdl_launch() only after its own
+// pdl_wait(), so when a kernel starts, everything two launches back is
+// complete. Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch with programmatic stream serialization (MOE_PDL=0 turns it off).
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid; cfg.blockDim = block; cfg.dynamicSmemBytes = smem; cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Error flag bits written by kernels (read by the host).

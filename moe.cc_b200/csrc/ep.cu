@@ -21,6 +21,8 @@ namespace moe {
 __global__ void __launch_bounds__(256) ep_combine_kernel(const EpView ep, const float* xres, float* out,
                                                          int D, int K, int* err) {
   __shared__ int s_ok;
+  pdl_wait();
+  pdl_launch();
   const uint8_t* mine = ep.base_local;
   if (threadIdx.x == 0) {
     const int ok = wait_flags_sys(reinterpret_cast<const unsigned long long*>(mine + kEpCombineFlags),
@@ -49,7 +51,7 @@ void launch_ep_combine(const EpView& ep, const float* xres, float* out, int D, i
                        cudaStream_t st) {
   const long total = (long)ep.T_local * D;
   if (total <= 0) return;
-  ep_combine_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(ep, xres, out, D, K, err);
+  launch_pdl(ep_combine_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, ep, xres, out, D, K, err);
 }
 
 }  // namespace moe

@@ -1003,6 +1003,8 @@ void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y, bool f
 // k-ordered combine + residual as a separate pass (prefill, expert parallel)
 __global__ void combine_kernel(const float* __restrict__ y, const float* __restrict__ p,
                                const float* xres, float* out, int T, int D, int K) {
+  pdl_wait();
+  pdl_launch();
   const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= (long)T * D) return;
   const int t = (int)(q / D), n = (int)(q % D);
@@ -1018,7 +1020,7 @@ void launch_combine(const float* y, const float* p, const float* xres, float* ou
                     int K, cudaStream_t st) {
   const long total = (long)T * D;
   if (total <= 0) return;
-  combine_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(y, p, xres, out, T, D, K);
+  launch_pdl(combine_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, y, p, xres, out, T, D, K);
 }
 
 // --------------------------------------------------------------------------

@@ -113,6 +113,12 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = s_tmem;
+  // Dependent launch: gate/up reads the routing tables of the kernel right
+  // before it, so it waits here. The down projection needs the gate/up output
+  // only for its B operand: its routing tables are two launches old (complete),
+  // so its producer first streams the weights of the first stages and waits
+  // only before the first B load; the other warps wait here.
+  if (MODE == GATEUP || threadIdx.x != 0) { pdl_wait(); pdl_launch(); }
 
   // units are dealt round-robin: tiles of heavily loaded experts (full slot
   // columns, the costliest epilogues) sit next to each other in the tile table
@@ -125,34 +131,71 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
     if (lane == 0) {
       const uint32_t bytes = (DT == 4 ? NM * kPackedBytes : NM * A_BYTES) + NL * B_BYTES;
       const uint64_t wpol = tc::policy_evict_first();
-      int it = 0;
-      for (int u = u0; u < n_units && !*abort_flag; u += ustep) {
-        const int tile = u / a.n_mblk, mb = u % a.n_mblk;
-        const int e = active[tv.u[tile]], j0 = tv.j0[tile];
-        for (int kc = 0; kc < a.kchunks; ++kc, ++it) {
-          const int st = it % a.stages;
-          if (it >= a.stages && !mbar_wait(&empty[st], ((it / a.stages) - 1) & 1, kWaitBudget)) {
-            atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
-          }
-          uint8_t* sb = smem + (size_t)st * a.stage_bytes;
-          mbar_arrive_expect_tx(&full[st], bytes);
-          // weights: when every expert has a single token tile (a.w_once) each
-          // weight tile is read exactly once, so it is loaded evict-first
-          const int kx = DT == 8 ? kc * 128 : kc * 64;
-          const int a1 = DT == 8 ? A_BYTES : kPackedBytes;
-          if (a.w_once) {
-            tc::tma_load_3d_hint(sb, &tmA0.m, kx, mb * 128, e, &full[st], wpol);
-            if (NM == 2) tc::tma_load_3d_hint(sb + a1, &tmA1.m, kx, mb * 128, e, &full[st], wpol);
-          } else {   // Q4: packed nibbles; the expanders build the A tiles from them
-            tc::tma_load_3d(sb, &tmA0.m, kx, mb * 128, e, &full[st]);
-            if (NM == 2) tc::tma_load_3d(sb + a1, &tmA1.m, kx, mb * 128, e, &full[st]);
-          }
-          const int by = a.tokb ? 0 : j0;   // decode: all token rows from row 0
-          tc::tma_load_2d(sb + (DT == 4 ? NM * kPackedBytes : NM * A_BYTES), &tmB0.m, kc * 128, by, &full[st]);
-          if (NL == 2) tc::tma_load_2d(sb + NM * A_BYTES + B_BYTES, &tmB1.m, kc * 128, by, &full[st]);
-          s_issued = it + 1;
+      // f(unit, kc, it) over this CTA's k-chunk iterations, until it returns
+      // false; the unit's expert, row block and first slot are read once
+      struct Unit { int e, mb, j0; };
+      auto for_iters = [&](auto&& f) {
+        int it = 0;
+        for (int u = u0; u < n_units; u += ustep) {
+          const int tile = u / a.n_mblk;
+          const Unit un{active[tv.u[tile]], u % a.n_mblk, tv.j0[tile]};
+          for (int kc = 0; kc < a.kchunks; ++kc, ++it)
+            if (!f(un, kc, it)) return;
         }
+      };
+      auto load_a = [&](const Unit& un, int kc, int it) {
+        const int mb = un.mb, e = un.e, st = it % a.stages;
+        uint8_t* sb = smem + (size_t)st * a.stage_bytes;
+        // weights: when every expert has a single token tile (a.w_once) each
+        // weight tile is read exactly once, so it is loaded evict-first
+        const int kx = DT == 8 ? kc * 128 : kc * 64;
+        const int a1 = DT == 8 ? A_BYTES : kPackedBytes;
+        if (a.w_once) {
+          tc::tma_load_3d_hint(sb, &tmA0.m, kx, mb * 128, e, &full[st], wpol);
+          if (NM == 2) tc::tma_load_3d_hint(sb + a1, &tmA1.m, kx, mb * 128, e, &full[st], wpol);
+        } else {   // Q4: packed nibbles; the expanders build the A tiles from them
+          tc::tma_load_3d(sb, &tmA0.m, kx, mb * 128, e, &full[st]);
+          if (NM == 2) tc::tma_load_3d(sb + a1, &tmA1.m, kx, mb * 128, e, &full[st]);
+        }
+      };
+      auto load_b = [&](const Unit& un, int kc, int it) {
+        const int st = it % a.stages;
+        uint8_t* sb = smem + (size_t)st * a.stage_bytes;
+        const int by = a.tokb ? 0 : un.j0;   // decode: all token rows from row 0
+        tc::tma_load_2d(sb + (DT == 4 ? NM * kPackedBytes : NM * A_BYTES), &tmB0.m, kc * 128, by, &full[st]);
+        if (NL == 2) tc::tma_load_2d(sb + NM * A_BYTES + B_BYTES, &tmB1.m, kc * 128, by, &full[st]);
+      };
+      int pre = 0;   // iterations whose weights went out before the dependency wait
+      if (MODE == DOWN) {
+        for_iters([&](const Unit& un, int kc, int it) {
+          if (it >= a.stages) return false;
+          mbar_arrive_expect_tx(&full[it], bytes);
+          load_a(un, kc, it);
+          pre = it + 1;
+          return true;
+        });
+        pdl_wait();
+        pdl_launch();
+        for_iters([&](const Unit& un, int kc, int it) {
+          if (it >= pre) return false;
+          load_b(un, kc, it);
+          return true;
+        });
+        s_issued = pre;
       }
+      for_iters([&](const Unit& un, int kc, int it) {
+        if (*abort_flag) return false;
+        if (it < pre) return true;
+        const int st = it % a.stages;
+        if (it >= a.stages && !mbar_wait(&empty[st], ((it / a.stages) - 1) & 1, kWaitBudget)) {
+          atomicOr(a.err, kErrTimeout); *abort_flag = 1; return false;
+        }
+        mbar_arrive_expect_tx(&full[st], bytes);
+        load_a(un, kc, it);
+        load_b(un, kc, it);
+        s_issued = it + 1;
+        return true;
+      });
     }
   } else if (warp == 1) {
     // ------------------------- MMA issuer ---------------------------
@@ -411,6 +454,8 @@ __global__ void gather_rows_kernel(const uint8_t* __restrict__ xact, int act_str
                                    const int* __restrict__ route, int E_local, int topk,
                                    uint8_t* __restrict__ xs0, uint8_t* __restrict__ xs1) {
   const int j = blockIdx.x;
+  pdl_wait();
+  pdl_launch();
   const RouteView r = route_view(const_cast<int*>(route), E_local);
   if (j >= r.exp_off[*r.n_active]) return;
   const int t = r.slot_list[j] / topk;
@@ -523,8 +568,7 @@ static bool launch_kernel(const TMap& a0, const TMap& a1, const TMap& b0, const 
       return false;
     attr = smem;
   }
-  k<<<grid, cta_threads(DT, NT), smem, st>>>(a0, a1, b0, b1, a);
-  return true;
+  return launch_pdl(k, dim3(grid), dim3(cta_threads(DT, NT)), smem, st, a0, a1, b0, b1, a) == cudaSuccess;
 }
 
 }  // namespace mm
@@ -547,7 +591,7 @@ bool mma_supported(const LayerDev& L) {
 void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream_t st) {
   if (T <= mma_tile_n(T, L.dtype)) return;   // decode: the GEMM reads the token rows directly
   const int E_local = L.e_end - L.e_begin, TK = T * L.topk;
-  mm::gather_rows_kernel<<<TK, 128, 0, st>>>(ws.xact, 2 * L.D, L.D, L.dtype == 2 ? 2 : 1, ws.route, E_local,
+  launch_pdl(mm::gather_rows_kernel, dim3(TK), dim3(128), 0, st, ws.xact, 2 * L.D, L.D, L.dtype == 2 ? 2 : 1, ws.route, E_local,
                                              L.topk, ws.xs0, ws.xs1);
 }
 
@@ -623,6 +667,8 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
 __global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* __restrict__ slot_pos,
                                       const float* __restrict__ p, const int* __restrict__ idx,
                                       const float* xres, float* out, int T, int D, int K) {
+  pdl_wait();
+  pdl_launch();
   const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= (long)T * D) return;
   const int t = (int)(q / D), n = (int)(q % D);
@@ -639,7 +685,8 @@ void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p,
                            const float* xres, float* out, int T, int D, int K, cudaStream_t st) {
   const long total = (long)T * D;
   if (total <= 0) return;
-  combine_sorted_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(ys, slot_pos, p, idx, xres, out, T, D, K);
+  launch_pdl(combine_sorted_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, ys, slot_pos, p, idx, xres,
+             out, T, D, K);
 }
 
 // Expert-parallel output: slot-ordered rows of this rank's slots, zeros for
@@ -648,6 +695,8 @@ __global__ void unsort_rows_kernel(const float* __restrict__ ys, const int* __re
                                    const int* __restrict__ idx, int e_begin, int e_end,
                                    float* __restrict__ y_slots, int D) {
   const int s = blockIdx.x;
+  pdl_wait();
+  pdl_launch();
   const int e = idx[s];
   float4* dst = reinterpret_cast<float4*>(y_slots + (size_t)s * D);
   if (e < e_begin || e >= e_end) {
@@ -659,8 +708,8 @@ __global__ void unsort_rows_kernel(const float* __restrict__ ys, const int* __re
 }
 
 void launch_unsort_rows(const LayerDev& L, const Workspace& ws, int T, float* y_slots, cudaStream_t st) {
-  unsort_rows_kernel<<<T * L.topk, 128, 0, st>>>(ws.y, ws.slot_pos, ws.topk_idx, L.e_begin, L.e_end,
-                                                 y_slots, L.D);
+  launch_pdl(unsort_rows_kernel, dim3(T * L.topk), dim3(128), 0, st, ws.y, ws.slot_pos, ws.topk_idx, L.e_begin,
+             L.e_end, y_slots, L.D);
 }
 
 }  // namespace moe

@@ -57,14 +57,20 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
   if (tid == 0) {
     for (int c = 0; c < kChunks; ++c) mbar_init(&bar[c], 1);
     fence_mbar_init();
+    // the router rows are constant: they go out before the wait for the
+    // previous kernel (dependent launch); the token rows after it
     for (int c = 0; c < kChunks; ++c) {
       mbar_arrive_expect_tx(&bar[c], (uint32_t)((ne + nt) * dc * 4));
       for (int i = 0; i < ne; ++i)
         bulk_g2s(sw + i * pitch + c * dc, a.W + (size_t)(e0 + i) * a.D + c * dc, dc * 4, &bar[c]);
+    }
+    pdl_wait();
+    for (int c = 0; c < kChunks; ++c)
       for (int i = 0; i < nt; ++i)
         bulk_g2s(sx + i * pitch + c * dc, a.x + (size_t)(t0 + i) * a.D + c * dc, dc * 4, &bar[c]);
-    }
   }
+  pdl_wait();
+  pdl_launch();
   __syncthreads();
   // A timed-out copy flags the call as failed; the CTA still reports its
   // arrival below so the arrival counter stays consistent for later calls.
@@ -379,14 +385,14 @@ void launch_decode_route(const LayerDev& L, const Workspace& ws, const float* x,
       cudaFuncSetAttribute(rt::decode_route_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       attr = smem;
     }
-    rt::decode_route_kernel<8><<<grid, rt::kThreads, smem, st>>>(a);
+    launch_pdl(rt::decode_route_kernel<8>, grid, dim3(rt::kThreads), smem, st, a);
   } else {
     static size_t attr = 0;
     if (smem > attr) {
       cudaFuncSetAttribute(rt::decode_route_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       attr = smem;
     }
-    rt::decode_route_kernel<4><<<grid, rt::kThreads, smem, st>>>(a);
+    launch_pdl(rt::decode_route_kernel<4>, grid, dim3(rt::kThreads), smem, st, a);
   }
 }
 

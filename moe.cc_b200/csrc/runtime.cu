@@ -58,6 +58,12 @@ int set_error_message(int code, const char* msg) { return set_err(code, "%s", ms
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) { const char* e = getenv("MOE_PDL"); v = e ? atoi(e) != 0 : 1; }
+  return v == 1;
+}
+
 static int ensure_init() {
   if (!g.init) return set_err(MOE_ERR_NOT_INIT, "moe_cuda_init() has not been called");
   return MOE_OK;
