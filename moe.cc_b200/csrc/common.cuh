@@ -132,6 +132,40 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// ---- optional step timeline (build with -DMOE_TIMELINE) ---------------------
+// Each hooked kernel records the globaltimer of its first CTA start and last
+// CTA end (ns) in a device table, read by moe_debug_timeline(). Without the
+// macro the hooks compile to nothing.
+enum : int { kTlRoute = 0, kTlGather, kTlGateup, kTlDown, kTlCombine, kTlCount };
+#ifdef MOE_TIMELINE
+// one table per translation unit (no relocatable device code); each file
+// that launches hooked kernels ends with MOE_TL_IO(name), and the runtime
+// merges the tables
+static __device__ unsigned long long g_timeline[kTlCount][2];
+#define MOE_TL_IO(name)                                                              \
+  void tl_io_##name(unsigned long long* out, int reset) {                           \
+    unsigned long long t[kTlCount][2];                                              \
+    cudaMemcpyFromSymbol(t, g_timeline, sizeof(t));                                 \
+    for (int i = 0; i < kTlCount; ++i) {                                            \
+      if (t[i][0] < out[2 * i]) out[2 * i] = t[i][0];                               \
+      if (t[i][1] > out[2 * i + 1]) out[2 * i + 1] = t[i][1];                       \
+      t[i][0] = ~0ull; t[i][1] = 0;                                                 \
+    }                                                                               \
+    if (reset) cudaMemcpyToSymbol(g_timeline, t, sizeof(t));                        \
+  }
+__device__ __forceinline__ unsigned long long tl_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+#define MOE_TL_START(id) do { if (threadIdx.x == 0) atomicMin(&::moe::g_timeline[id][0], ::moe::tl_now()); } while (0)
+#define MOE_TL_END(id) do { if (threadIdx.x == 0) atomicMax(&::moe::g_timeline[id][1], ::moe::tl_now()); } while (0)
+#else
+#define MOE_TL_IO(name)
+#define MOE_TL_START(id) do { } while (0)
+#define MOE_TL_END(id) do { } while (0)
+#endif
+
 // Error flag bits written by kernels (read by the host).
 enum : int { kErrRange = 1, kErrTimeout = 2 };
 

@@ -21,6 +21,7 @@ namespace moe {
 __global__ void __launch_bounds__(256) ep_combine_kernel(const EpView ep, const float* xres, float* out,
                                                          int D, int K, int* err) {
   __shared__ int s_ok;
+  MOE_TL_START(kTlCombine);
   pdl_wait();
   pdl_launch();
   const uint8_t* mine = ep.base_local;
@@ -45,6 +46,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const EpView ep, const 
     acc = fadd(acc, fmul(__ldcg(p + s), __ldcg(y + (size_t)s * D + n)));
   }
   out[q] = fadd(xres[q], acc);
+  MOE_TL_END(kTlCombine);
 }
 
 void launch_ep_combine(const EpView& ep, const float* xres, float* out, int D, int K, int* err,
@@ -53,5 +55,7 @@ void launch_ep_combine(const EpView& ep, const float* xres, float* out, int D, i
   if (total <= 0) return;
   launch_pdl(ep_combine_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, ep, xres, out, D, K, err);
 }
+
+MOE_TL_IO(ep)
 
 }  // namespace moe

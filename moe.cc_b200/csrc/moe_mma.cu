@@ -93,6 +93,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_issued;
 
+  MOE_TL_START(MODE == GATEUP ? kTlGateup : kTlDown);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const TileView tv = tile_view(a.route, a.E_local, a.TK, a.max_tiles);
   const int* active = a.route + 1;
@@ -437,6 +438,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, TCOLS);
   }
+  MOE_TL_END(MODE == GATEUP ? kTlGateup : kTlDown);
 }
 
 }  // namespace mm
@@ -454,6 +456,8 @@ __global__ void gather_rows_kernel(const uint8_t* __restrict__ xact, int act_str
                                    const int* __restrict__ route, int E_local, int topk,
                                    uint8_t* __restrict__ xs0, uint8_t* __restrict__ xs1) {
   const int j = blockIdx.x;
+  MOE_TL_START(kTlGather);
+  MOE_TL_END(kTlGather);
   pdl_wait();
   pdl_launch();
   const RouteView r = route_view(const_cast<int*>(route), E_local);
@@ -667,6 +671,7 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
 __global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* __restrict__ slot_pos,
                                       const float* __restrict__ p, const int* __restrict__ idx,
                                       const float* xres, float* out, int T, int D, int K) {
+  MOE_TL_START(kTlCombine);
   pdl_wait();
   pdl_launch();
   const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -679,6 +684,7 @@ __global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* _
     acc = fadd(acc, fmul(p[s], ys[(size_t)slot_pos[s] * D + n]));
   }
   out[q] = fadd(xres[q], acc);
+  MOE_TL_END(kTlCombine);
 }
 
 void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
@@ -711,5 +717,7 @@ void launch_unsort_rows(const LayerDev& L, const Workspace& ws, int T, float* y_
   launch_pdl(unsort_rows_kernel, dim3(T * L.topk), dim3(128), 0, st, ws.y, ws.slot_pos, ws.topk_idx, L.e_begin,
              L.e_end, y_slots, L.D);
 }
+
+MOE_TL_IO(moe_mma)
 
 }  // namespace moe

@@ -20,7 +20,7 @@
 namespace moe {
 namespace rt {
 
-constexpr int kE = 8, kT = 16, kThreads = 256, kChainThreads = kE * kT, kChunks = 4;
+constexpr int kE = 8, kT = 16, kThreads = 512, kChainThreads = kE * kT, kChunks = 4;
 constexpr int kMaxTK = 2048;    // T*K handled by the last CTA (decode and EP-gathered sizes)
 constexpr int kMaxE = 256;
 constexpr int kMaxTiles = kMaxTK / 16 + kMaxE + 1;
@@ -51,6 +51,7 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
   const int ne = min(kE, a.E - e0), nt = min(kT, a.T - t0);
   const int tid = threadIdx.x;
   const int dc = a.D / kChunks;                                // columns per chunk
+  MOE_TL_START(kTlRoute);
 
   // the rows arrive in kChunks column chunks, each on its own barrier, so the
   // chains start on chunk 0 while the rest is still in flight
@@ -117,7 +118,12 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
   } else {
     // ---- truncated activations: this CTA's column slice of its tokens ----
     const int q0 = tid - kChainThreads, nq = kThreads - kChainThreads;
-    for (int c = 0; c < kChunks; ++c)
+    // wait only for the chunks holding this CTA's column slice (the Q4 Σa of
+    // CTA 0 needs every column), so these warps do not poll beside the chains
+    const int cs0 = (int)((long)a.D * blockIdx.x / gridDim.x), cs1 = (int)((long)a.D * (blockIdx.x + 1) / gridDim.x);
+    const bool all = DT == 4 && blockIdx.x == 0;
+    const int cf = all ? 0 : cs0 / dc, cl = all ? kChunks - 1 : (cs1 - 1) / dc;
+    for (int c = cf; c <= cl && cs1 > cs0; ++c)
       if (!mbar_wait(&bar[c], 0, kWaitBudget)) { ok = false; break; }
     // expert parallel: the activations go to every rank's xact (rows of this
     // rank's tokens), starting with the next rank so the links share the load
@@ -269,52 +275,46 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
   if (a.hsum)
     for (int s = tid; s < TK; s += kThreads) a.hsum[s] = 0;
   __syncthreads();
-  // one warp: exclusive scans over experts of (slots, active flag, tiles)
+  // exclusive scans over experts of (slots, active flag, tiles): one thread
+  // per expert, warp shuffles, then the warp totals through shared memory
+  static_assert(kMaxE <= kThreads, "one thread per expert");
   int* r_active = s_route + 1;
   int* r_off = s_route + 1 + a.E_local;
   const int mt = a.max_tiles;
-  if (warp == 0) {
-    constexpr int PER = kMaxE / 32;
-    int c[PER], sl = 0, sa = 0, stl = 0;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int el = lane * PER + i;
-      c[i] = el < a.E_local ? cnt[el] : 0;
-      sl += c[i];
-      sa += c[i] > 0;
-      stl += a.nt > 0 ? (c[i] + a.nt - 1) / a.nt : 0;
-    }
-    int xl = sl, xa = sa, xt = stl;
+  {
+    __shared__ int s_wsum[3][kThreads / 32];
+    const int el = tid;
+    const int c = el < a.E_local ? cnt[el] : 0, act = c > 0;
+    const int til = a.nt > 0 ? (c + a.nt - 1) / a.nt : 0;
+    int xl = c, xa = act, xt = til;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int yl = __shfl_up_sync(0xffffffffu, xl, o), ya = __shfl_up_sync(0xffffffffu, xa, o),
                 yt = __shfl_up_sync(0xffffffffu, xt, o);
       if (lane >= o) { xl += yl; xa += ya; xt += yt; }
     }
-    int off = xl - sl, na = xa - sa, ntl = xt - stl;      // exclusive prefixes
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int el = lane * PER + i;
-      if (el >= a.E_local) break;
+    if (lane == 31) { s_wsum[0][warp] = xl; s_wsum[1][warp] = xa; s_wsum[2][warp] = xt; }
+    __syncthreads();
+    for (int w = 0; w < warp; ++w) { xl += s_wsum[0][w]; xa += s_wsum[1][w]; xt += s_wsum[2][w]; }
+    const int off = xl - c, na = xa - act, ntl = xt - til;      // exclusive prefixes
+    if (el < a.E_local) {
       start[el] = off;
-      if (c[i] > 0) {
+      if (c > 0) {
         r_active[na] = el;
         r_off[na] = off;
-        if (a.nt > 0)
-          for (int j0 = off; j0 < off + c[i] && ntl < mt; j0 += a.nt, ++ntl) {
-            s_tab[1 + ntl] = na;
-            s_tab[1 + mt + ntl] = j0;
-            s_tab[1 + 2 * mt + ntl] = min(a.nt, off + c[i] - j0);
-          }
-        ++na;
+        for (int j0 = off, k = ntl; a.nt > 0 && j0 < off + c && k < mt; j0 += a.nt, ++k) {
+          s_tab[1 + k] = na;
+          s_tab[1 + mt + k] = j0;
+          s_tab[1 + 2 * mt + k] = min(a.nt, off + c - j0);
+        }
       }
-      off += c[i];
+      if (el == a.E_local - 1) {      // totals
+        r_off[xa] = xl;
+        s_route[0] = xa;
+        s_tab[0] = xt < mt ? xt : mt;
+      }
     }
-    if (lane == 31) {
-      r_off[na] = off;
-      s_route[0] = na;
-      s_tab[0] = ntl < mt ? ntl : mt;
-    }
+    if (a.E_local == 0 && tid == 0) { r_off[0] = 0; s_route[0] = 0; s_tab[0] = 0; }
   }
   __syncthreads();
   // slot lists: placed with shared-memory atomics, then each expert's list is
@@ -353,6 +353,7 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
     for (int i = tid; i < 1 + 3 * mt; i += kThreads) tab[i] = s_tab[i];
   }
   if (tid == 0) *a.counter = 0;
+  MOE_TL_END(kTlRoute);
 }
 
 }  // namespace rt
@@ -395,5 +396,7 @@ void launch_decode_route(const LayerDev& L, const Workspace& ws, const float* x,
     launch_pdl(rt::decode_route_kernel<4>, grid, dim3(rt::kThreads), smem, st, a);
   }
 }
+
+MOE_TL_IO(router)
 
 }  // namespace moe

@@ -29,6 +29,7 @@ struct State {
   std::unordered_map<const void*, Alias> alias;  // host q/s pointer -> device copy
   Workspace ws;
   int* d_err = nullptr;                          // kernel-flagged errors
+  int* h_err = nullptr;                          // pinned host copy of d_err
   std::string last_error;
   std::recursive_mutex mu;
 };
@@ -57,6 +58,12 @@ int set_error_message(int code, const char* msg) { return set_err(code, "%s", ms
   } while (0)
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+#ifdef MOE_TIMELINE
+void tl_io_router(unsigned long long*, int);
+void tl_io_moe_mma(unsigned long long*, int);
+void tl_io_ep(unsigned long long*, int);
+#endif
 
 bool pdl_enabled() {
   static int v = -1;
@@ -120,12 +127,8 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
 }
 
 // Read (and clear) the kernel error flag. Synchronises the device.
-static int consume_device_error() {
-  int h = 0;
-  CU(cudaDeviceSynchronize());
-  CU(cudaMemcpy(&h, g.d_err, sizeof(int), cudaMemcpyDeviceToHost));
+static int error_status(int h) {
   if (h) {
-    CU(cudaMemset(g.d_err, 0, sizeof(int)));
     if (h & kErrRange)
       return set_err(MOE_ERR_RANGE,
                      "an activation was NaN/inf or outside the integer range of the "
@@ -134,6 +137,29 @@ static int consume_device_error() {
       return set_err(MOE_ERR_CUDA, "a pipelined kernel gave up waiting on a copy (bounded wait)");
   }
   return MOE_OK;
+}
+
+static int consume_device_error() {
+  int h = 0;
+  CU(cudaDeviceSynchronize());
+  CU(cudaMemcpy(&h, g.d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h) CU(cudaMemset(g.d_err, 0, sizeof(int)));
+  return error_status(h);
+}
+
+// The error flag as of the work queued on `st`: an async copy into pinned
+// host memory and one stream synchronisation (no device-wide sync), for the
+// synchronous host-pointer entry points.
+static int consume_stream_error(cudaStream_t st) {
+  CU(cudaMemcpyAsync(g.h_err, g.d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  CU(cudaStreamSynchronize(st));
+  const int h = *g.h_err;
+  if (h) {
+    *g.h_err = 0;
+    CU(cudaMemsetAsync(g.d_err, 0, sizeof(int), st));
+    CU(cudaStreamSynchronize(st));
+  }
+  return error_status(h);
 }
 
 }  // namespace moe
@@ -216,7 +242,7 @@ static int matmul_q_host(int dtype, const float* A, const void* Bq, const float*
     return rc;
   CU(cudaMemcpy(s_A.p, A, sizeof(float) * (size_t)M * K, cudaMemcpyHostToDevice));
   if ((rc = matmul_q_dev(dtype, (const float*)s_A.p, dq, ds, (float*)s_C.p, M, N, K, 0))) return rc;
-  rc = consume_device_error();
+  rc = consume_stream_error(0);
   if (rc == MOE_ERR_RANGE) {
     // Large activations: rerun on the exact int32 kernel (any magnitude).
     launch_gemv_generic(dtype, (const float*)s_A.p, (const uint8_t*)dq, ds, (float*)s_C.p, M, N, K, 0);
@@ -251,6 +277,8 @@ int moe_cuda_init(int device, int ep_world, int ep_rank, const void* nccl_uid) {
   CU(cudaDeviceGetAttribute(&g.sm_count, cudaDevAttrMultiProcessorCount, device));
   CU(cudaMalloc((void**)&g.d_err, sizeof(int)));
   CU(cudaMemset(g.d_err, 0, sizeof(int)));
+  CU(cudaHostAlloc((void**)&g.h_err, sizeof(int), cudaHostAllocDefault));
+  *g.h_err = 0;
   g.device = device; g.ep_world = ep_world; g.ep_rank = ep_rank;
   g.init = true;
   return MOE_OK;
@@ -275,6 +303,8 @@ int moe_cuda_shutdown(void) {
   Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum};
   for (Buf* b : bufs) { if (b->p) cudaFree(b->p); *b = Buf{}; }
   cudaFree(g.d_err); g.d_err = nullptr;
+  if (g.h_err) cudaFreeHost(g.h_err);
+  g.h_err = nullptr;
   g.init = false;
   return MOE_OK;
 }
@@ -665,8 +695,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
   if (topk_p_out) CU(cudaMemcpyAsync(topk_p_out, w.topk_p, kb, out_kind, st));
   if (host) {
     CU(cudaMemcpyAsync(x_inout, xo, xb, cudaMemcpyDeviceToHost, st));
-    CU(cudaStreamSynchronize(st));
-    return consume_device_error();
+    return consume_stream_error(st);
   }
   return MOE_OK;
 }
@@ -798,6 +827,21 @@ static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 }  // namespace moe
 
 extern "C" {
+
+#ifdef MOE_TIMELINE
+// Timeline build only: copy out (and optionally reset) the per-kernel
+// [first start, last end] globaltimer table, kTlCount x 2 values.
+int moe_debug_timeline(unsigned long long* out, int reset) {
+  CU(cudaDeviceSynchronize());
+  unsigned long long t[2 * kTlCount];
+  for (int i = 0; i < kTlCount; ++i) { t[2 * i] = ~0ull; t[2 * i + 1] = 0; }
+  moe::tl_io_router(t, reset);
+  moe::tl_io_moe_mma(t, reset);
+  moe::tl_io_ep(t, reset);
+  if (out) memcpy(out, t, sizeof(t));
+  return MOE_OK;
+}
+#endif
 
 int moe_cuda_ep_setup(int max_tokens_local, int D, int top_k, void* ipc_handle_out) {
   std::lock_guard<std::recursive_mutex> lk(g.mu);
