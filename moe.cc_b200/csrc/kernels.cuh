@@ -43,6 +43,7 @@ struct Workspace {
   int* slot_pos = nullptr;    // [T*K] slot -> expert-sorted row
   float* xn = nullptr;        // staging for host-pointer calls [T][D]
   float* xo = nullptr;        // [T][D]
+  int* fused_ctr = nullptr;   // fused decode kernel: work, arrival, per-tile completion (kept zero)
 };
 
 // Expert-parallel exchange buffers. Every rank allocates the same layout
@@ -145,6 +146,11 @@ bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, in
 // flag at every peer
 bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, float* ys, bool fuse,
                      const float* xres, float* out, int* err, cudaStream_t st, const EpView* ep = nullptr);
+// moe_fused.cu: Q8 decode gate/up + down in one persistent kernel
+constexpr int kFusedMaxTiles = 256;
+bool fused_supported(const LayerDev& L, int T, int nt);
+bool launch_mma_fused(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st,
+                      const EpView* ep = nullptr);
 void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
                            const float* xres, float* out, int T, int D, int K, cudaStream_t st);
 void launch_unsort_rows(const LayerDev& L, const Workspace& ws, int T, float* y_slots, cudaStream_t st);

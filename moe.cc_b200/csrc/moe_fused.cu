@@ -1,0 +1,463 @@
+// moe_fused.cu — decode expert FFN (Q8) as ONE persistent tcgen05 kernel:
+// gate/up and down projections of all routed experts, with the dependency
+// between them tracked per expert instead of per kernel.
+//
+// Units. A gate/up unit is (expert tile, 128-row block of F): 16 k-chunks of
+// 128 bytes over D, gate and up weights, B = the T token rows (decode: every
+// expert has one tile of at most NT slots, and the token rows are read as
+// they are). A down unit is (expert tile, 128-row block of D): 6 k-chunks over
+// F, B = the expert's slot rows of h written by its gate/up units.
+//
+// Schedule. One global work counter hands out unit ids; ids [0, NG) are the
+// gate/up units, [NG, NG+ND) the down units, so every gate/up unit is claimed
+// before any down unit. A gate/up unit's epilogue warps each bump the
+// expert's completion counter after storing their rows of h; the warp that
+// completes it appends the expert to a ready list (release store). Down unit
+// c takes 128-row block c % (D/128) of the (c / (D/128))-th expert to become
+// ready, so the down units follow the order in which experts finish; its
+// producer waits (bounded) only until that list entry is published. Gate/up
+// units never wait and a unit is only claimed by a running CTA, so the waits
+// cannot form a cycle.
+// With the dependency per expert, the down weights of experts whose gate/up
+// is done stream while other experts' gate/up still run: no kernel boundary,
+// no drain and refill between the two projections.
+//
+// Shared memory: a ring of slots, each = one 128x128 weight tile (16 KB,
+// 128B-swizzled, TMA) + one B pair (low / high activation limb, NT x 128 B
+// each). A gate/up k-chunk takes two slots (gate tile + B, up tile); a down
+// k-chunk one. TMEM: two accumulator buffers of 4*NT columns (gate lo/hi, up
+// lo/hi; down uses the first 2*NT). Arithmetic is that of moe_mma.cu
+// (kernels.c:51-93 Q8 dot products, exact int32, then the fp32 epilogues of
+// test_model_trace.c:499-510), so results are bit-identical to it.
+//
+// Roles: warp 0 lane 0 = work claiming + TMA producer, warp 1 lane 0 = MMA
+// issuer, warps 2..9 = epilogue (tcgen05.ld, one weight row per thread).
+// Every wait is bounded (kWaitBudget polls): on expiry the CTA flags
+// kErrTimeout and leaves, after waiting (bounded) for its own copies.
+#include <cuda.h>
+#include "common.cuh"
+#include "kernels.cuh"
+#include "pipeline.cuh"
+#include "tc.cuh"
+#include "tmap.cuh"
+
+namespace moe {
+namespace fz {
+#ifdef MOE_TIMELINE
+// per-CTA trace of the timeline build: [start, first claim, gate/up units,
+// down units, ns stalled on expert dependencies, producer done, end]
+__device__ unsigned long long g_fz_trace[512][8];
+#define FZ_T(i, v) do { if (blockIdx.x < 512) g_fz_trace[blockIdx.x][i] = (v); } while (0)
+#else
+#define FZ_T(i, v) do { } while (0)
+#endif
+
+using mm::TMap;
+
+constexpr int kEpiWarps = 8, kThreads = (2 + kEpiWarps) * 32;
+constexpr int kUnitRing = 8;           // claimed unit ids published to the MMA / epilogue warps
+constexpr int kA = 128 * 128;          // one weight tile
+
+struct Args {
+  const int* route; int E_local, TK, max_tiles, topk;
+  const uint8_t* slab; size_t stride, gs_off, us_off, ds_off;
+  int D, F;                            // hidden, intermediate
+  uint8_t* hs0; uint8_t* hs1;          // h planes [J][F] (expert-sorted slots)
+  float* ys;                           // [J][D] y rows (expert-sorted slots)
+  int nslots, slot_bytes, w_once;
+  int* ctr;                            // [0] work, [1] arrivals, [2] ready count, then per-tile
+                                       // completion [kFusedMaxTiles] and the ready list [kFusedMaxTiles]
+  int ep_on; EpView ep;
+  int* err;
+};
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 2)
+    moe_fused_kernel(const __grid_constant__ TMap tG, const __grid_constant__ TMap tU,
+                     const __grid_constant__ TMap tX0, const __grid_constant__ TMap tX1,
+                     const __grid_constant__ TMap tDn, const __grid_constant__ TMap tH0,
+                     const __grid_constant__ TMap tH1, const Args a) {
+  constexpr int B = NT * 128;                       // one activation limb tile
+  constexpr int ACC = 4 * NT;                       // accumulator columns per buffer
+  constexpr uint32_t TCOLS = 2 * ACC <= 128 ? 128 : 256;
+  constexpr float S = 127.0f;
+  MOE_TL_START(kTlGateup);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)a.nslots * a.slot_bytes);
+  uint64_t* empty = full + a.nslots;
+  __shared__ uint64_t acc_full[2], acc_empty[2], unit_rdy[kUnitRing];
+  __shared__ int s_unit[kUnitRing], s_utile[kUnitRing];
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort, s_issued, s_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    s_abort = 0; s_issued = 0;
+    for (int s = 0; s < a.nslots; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiWarps); }
+    for (int i = 0; i < kUnitRing; ++i) mbar_init(&unit_rdy[i], 1);
+    fence_mbar_init();
+    tc::prefetch_tmap(&tG.m); tc::prefetch_tmap(&tU.m); tc::prefetch_tmap(&tX0.m);
+    tc::prefetch_tmap(&tX1.m); tc::prefetch_tmap(&tDn.m); tc::prefetch_tmap(&tH0.m);
+    tc::prefetch_tmap(&tH1.m);
+  }
+  if (warp == 1) tc::tmem_alloc(&s_tmem, TCOLS);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = s_tmem;
+  pdl_wait();          // the routing tables and token activations come from the kernels before
+  pdl_launch();
+
+  const TileView tv = tile_view(a.route, a.E_local, a.TK, a.max_tiles);
+  const int* active = a.route + 1;
+  const int* slots = a.route + 2 + 2 * a.E_local;
+  const int nmg = a.F / 128, nmd = a.D / 128, kcg = a.D / 128, kcd = a.F / 128;
+  const int ntiles = *tv.n;
+  const int NG = ntiles * nmg, NTOT = NG + ntiles * nmd;
+  const int done_target = nmg * kEpiWarps;          // epilogue-warp signals per expert tile
+  int* work = a.ctr;
+  int* rcount = a.ctr + 2;
+  int* done = a.ctr + 3;
+  int* ready = a.ctr + 3 + kFusedMaxTiles;
+  volatile int* abort_flag = &s_abort;
+
+  if (warp == 0) {
+    // ------------------- work claiming + TMA producer -------------------
+    if (lane == 0) {
+#ifdef MOE_TIMELINE
+      unsigned long long n_gu = 0, n_dn = 0, stall = 0;
+      FZ_T(0, tl_now());
+#endif
+      const uint64_t wpol = tc::policy_evict_first();
+      auto load_w = [&](const TMap& m, int kc, int mb, int e, uint8_t* dst, uint64_t* bar) {
+        if (a.w_once) tc::tma_load_3d_hint(dst, &m.m, kc * 128, mb * 128, e, bar, wpol);
+        else tc::tma_load_3d(dst, &m.m, kc * 128, mb * 128, e, bar);
+      };
+      int it = 0, ul = 0;                    // slot items issued, units claimed
+      int nxt = atomicAdd(work, 1);
+      for (;; ++ul) {
+        const int g = nxt;
+        const int ri = ul % kUnitRing;
+        bool stop = g >= NTOT || *abort_flag;
+        int tile = 0;
+        if (!stop && g >= NG) {
+          // down unit: its expert is the ((g - NG) / (D/128))-th to finish gate/up
+          const int pos = (g - NG) / nmd;
+          uint32_t i = 0;
+#ifdef MOE_TIMELINE
+          const unsigned long long w0 = tl_now();
+#endif
+          int v;
+          while ((v = ld_acquire_gpu(ready + pos)) == 0)
+            if (++i >= kWaitBudget) break;
+#ifdef MOE_TIMELINE
+          stall += tl_now() - w0;
+#endif
+          if (v == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; stop = true; }
+          tile = v - 1;
+          fence_proxy_async_global();        // generic stores of h -> the tensor copies below
+        }
+        s_unit[ri] = stop ? -1 : g;
+        s_utile[ri] = tile;
+        mbar_arrive(&unit_rdy[ri]);          // release: the id is visible to the consumers
+        if (stop) break;
+#ifdef MOE_TIMELINE
+        if (ul == 0) FZ_T(1, tl_now());
+        if (g < NG) ++n_gu; else ++n_dn;
+#endif
+        nxt = atomicAdd(work, 1);            // next claim in flight while this unit streams
+        // one slot item: wait the slot free, expect its bytes
+        auto take = [&](uint32_t bytes) -> int {
+          const int st = it % a.nslots;
+          if (it >= a.nslots && !mbar_wait(&empty[st], ((it / a.nslots) - 1) & 1, kWaitBudget)) {
+            atomicOr(a.err, kErrTimeout); *abort_flag = 1; return -1;
+          }
+          mbar_arrive_expect_tx(&full[st], bytes);
+          ++it;
+          s_issued = it;
+          return st;
+        };
+        if (g < NG) {
+          const int tile = g / nmg, mb = g % nmg, e = active[tv.u[tile]];
+          for (int kc = 0; kc < kcg && !*abort_flag; ++kc) {
+            const int s0 = take(kA + 2 * B);
+            if (s0 < 0) break;
+            uint8_t* p0 = smem + (size_t)s0 * a.slot_bytes;
+            load_w(tG, kc, mb, e, p0, &full[s0]);
+            tc::tma_load_2d(p0 + kA, &tX0.m, kc * 128, 0, &full[s0]);       // decode: token rows 0..
+            tc::tma_load_2d(p0 + kA + B, &tX1.m, kc * 128, 0, &full[s0]);
+            const int s1 = take(kA);
+            if (s1 < 0) break;
+            load_w(tU, kc, mb, e, smem + (size_t)s1 * a.slot_bytes, &full[s1]);
+          }
+        } else {
+          const int mb = (g - NG) % nmd, e = active[tv.u[tile]], j0 = tv.j0[tile];
+          for (int kc = 0; kc < kcd && !*abort_flag; ++kc) {
+            const int s0 = take(kA + 2 * B);
+            if (s0 < 0) break;
+            uint8_t* p0 = smem + (size_t)s0 * a.slot_bytes;
+            load_w(tDn, kc, mb, e, p0, &full[s0]);
+            tc::tma_load_2d(p0 + kA, &tH0.m, kc * 128, j0, &full[s0]);
+            tc::tma_load_2d(p0 + kA + B, &tH1.m, kc * 128, j0, &full[s0]);
+          }
+        }
+      }
+#ifdef MOE_TIMELINE
+      FZ_T(2, n_gu); FZ_T(3, n_dn); FZ_T(4, stall); FZ_T(5, tl_now());
+#endif
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      const uint32_t idesc_lo = tc::idesc_i8(128, NT, true, false);   // s8 weights x u8 low limb
+      const uint32_t idesc_hi = tc::idesc_i8(128, NT, true, true);    // s8 weights x s8 high limb
+      int it = 0;
+      for (int ul = 0;; ++ul) {
+        const int ri = ul % kUnitRing;
+        if (!mbar_wait(&unit_rdy[ri], (ul / kUnitRing) & 1, kWaitBudget)) {
+          atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
+        }
+        const int g = s_unit[ri];
+        if (g < 0) break;
+        const int buf = ul & 1;
+        if (ul >= 2 && !mbar_wait(&acc_empty[buf], ((ul >> 1) - 1) & 1, kWaitBudget)) {
+          atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
+        }
+        tc::fence_after_sync();
+        const uint32_t dbase = tmem + buf * ACC;
+        const bool gu = g < NG;
+        const int kcs = gu ? kcg : kcd;
+        bool bad = false;
+        for (int kc = 0; kc < kcs && !bad; ++kc) {
+          const int s0 = it % a.nslots;
+          if (!mbar_wait(&full[s0], (it / a.nslots) & 1, kWaitBudget)) { bad = true; break; }
+          ++it;
+          const uint8_t* p0 = smem + (size_t)s0 * a.slot_bytes;
+          int s1 = -1;
+          if (gu) {
+            s1 = it % a.nslots;
+            if (!mbar_wait(&full[s1], (it / a.nslots) & 1, kWaitBudget)) { bad = true; break; }
+            ++it;
+          }
+          tc::fence_after_sync();
+          const uint64_t db0 = tc::sw128_desc(p0 + kA), db1 = tc::sw128_desc(p0 + kA + B);
+          const uint64_t da0 = tc::sw128_desc(p0);
+          const uint64_t da1 = gu ? tc::sw128_desc(smem + (size_t)s1 * a.slot_bytes) : 0;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t acc = (kc | kk) != 0;
+            tc::mma_i8(dbase + 0 * NT, da0 + 2 * kk, db0 + 2 * kk, idesc_lo, acc);
+            tc::mma_i8(dbase + 1 * NT, da0 + 2 * kk, db1 + 2 * kk, idesc_hi, acc);
+            if (gu) {
+              tc::mma_i8(dbase + 2 * NT, da1 + 2 * kk, db0 + 2 * kk, idesc_lo, acc);
+              tc::mma_i8(dbase + 3 * NT, da1 + 2 * kk, db1 + 2 * kk, idesc_hi, acc);
+            }
+          }
+          tc::mma_commit(&empty[s0]);
+          if (gu) tc::mma_commit(&empty[s1]);
+        }
+        if (bad) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; break; }
+        tc::mma_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    // ------------------------------- epilogue -------------------------------
+    const int q = warp & 3, half = (warp - 2) >> 2, r = q * 32 + lane;
+    for (int ul = 0;; ++ul) {
+      const int ri = ul % kUnitRing;
+      if (!mbar_wait(&unit_rdy[ri], (ul / kUnitRing) & 1, kWaitBudget)) {
+        if (lane == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; }
+        break;
+      }
+      const int g = s_unit[ri], dtile = s_utile[ri];
+      if (g < 0) break;
+      const int buf = ul & 1;
+      if (!mbar_wait(&acc_full[buf], (ul >> 1) & 1, kWaitBudget)) {
+        if (lane == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; }
+        break;
+      }
+      tc::fence_after_sync();
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * ACC;
+      if (g < NG) {
+        const int tile = g / nmg, mb = g % nmg, e = active[tv.u[tile]];
+        const int j0 = tv.j0[tile], nt = tv.cnt[tile], n = mb * 128 + r;
+        const uint8_t* ex = a.slab + (size_t)e * a.stride;
+        const float sg = __ldg(reinterpret_cast<const float*>(ex + a.gs_off) + n);
+        const float su = __ldg(reinterpret_cast<const float*>(ex + a.us_off) + n);
+        // accumulator column t is token t; each routed slot reads its token's column
+        for (int jj = half; jj < nt; jj += kEpiWarps / 4) {
+          const int j = j0 + jj, t = __ldg(slots + j) / a.topk;       // warp-uniform
+          uint32_t v[4][8], raw[4];
+#pragma unroll
+          for (int x = 0; x < 4; ++x) tc::tmem_ld8(tbase + x * NT + (t & ~7), v[x]);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            raw[x] = v[x][0];
+#pragma unroll
+            for (int c = 1; c < 8; ++c) if ((t & 7) == c) raw[x] = v[x][c];
+          }
+          const int dg = (int)(raw[0] + (raw[1] << 8)), du = (int)(raw[2] + (raw[3] << 8));
+          const float gv = fmul(fdiv(__int2float_rn(dg), S), sg);
+          const float uv = fmul(fdiv(__int2float_rn(du), S), su);
+          const int ha = trunc_scale(fmul(silu_ref(gv), uv), S);
+          if (ha < -32768 || ha > 32767) atomicOr(a.err, kErrRange);
+          a.hs0[(size_t)j * a.F + n] = (uint8_t)(ha & 0xFF);
+          a.hs1[(size_t)j * a.F + n] = (uint8_t)((ha >> 8) & 0xFF);
+        }
+        // this warp's rows of h are stored: count it toward the expert's completion
+        __threadfence();
+        __syncwarp();
+        if (lane == 0 && atomicAdd(done + tile, 1) == done_target - 1) {
+          // the expert's h is complete: publish it on the ready list
+          const int pos = atomicAdd(rcount, 1);
+          st_release_gpu(ready + pos, tile + 1);
+        }
+      } else {
+        const int tile = dtile, mb = (g - NG) % nmd, e = active[tv.u[tile]];
+        const int j0 = tv.j0[tile], nt = tv.cnt[tile], n = mb * 128 + r;
+        const uint8_t* ex = a.slab + (size_t)e * a.stride;
+        const float sd = __ldg(reinterpret_cast<const float*>(ex + a.ds_off) + n);
+        for (int c0 = 8 * half; c0 < nt; c0 += 8 * (kEpiWarps / 4)) {
+          uint32_t v0[8], v1[8];
+          tc::tmem_ld8(tbase + c0, v0);
+          tc::tmem_ld8(tbase + NT + c0, v1);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (c0 + i >= nt) break;
+            const int j = j0 + c0 + i;
+            const float yv = fmul(fdiv(__int2float_rn((int)(v0[i] + (v1[i] << 8))), S), sd);
+            if (a.ep_on) {
+              const int sl = __ldg(slots + j), per = a.topk * a.ep.T_local, owner = sl / per;
+              float* yo = reinterpret_cast<float*>(
+                  __ldg(reinterpret_cast<const unsigned long long*>(a.ep.base) + owner) + a.ep.y_off);
+              yo[(size_t)(sl - owner * per) * a.D + n] = yv;
+            } else {
+              a.ys[(size_t)j * a.D + n] = yv;
+            }
+          }
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && s_abort) {
+    // let the tensor copies still in flight land before the CTA's smem goes away
+    for (int i = max(0, s_issued - a.nslots); i < s_issued; ++i)
+      mbar_wait(&full[i % a.nslots], (i / a.nslots) & 1, kWaitBudget);
+  }
+  // The last CTA out resets the work and completion counters for the next
+  // call and, expert-parallel, raises this rank's combine flag at every rank.
+  if (threadIdx.x == 0) {
+    if (a.ep_on) __threadfence_system(); else __threadfence();
+    s_last = atomicAdd(a.ctr + 1, 1) == (int)gridDim.x - 1;
+    if (s_last) {
+      __threadfence();
+      a.ctr[0] = 0;
+      a.ctr[1] = 0;
+      a.ctr[2] = 0;
+      for (int i = 0; i < ntiles; ++i) { done[i] = 0; ready[i] = 0; }
+      if (a.ep_on) {
+        __threadfence_system();
+        for (int i = 0; i < a.ep.world; ++i) {
+          const int p = (a.ep.rank + i) % a.ep.world;
+          uint8_t* pb = reinterpret_cast<uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(a.ep.base) + p));
+          st_release_sys(reinterpret_cast<unsigned long long*>(pb + kEpCombineFlags) + a.ep.rank, a.ep.seq);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, TCOLS);
+  }
+  MOE_TL_END(kTlGateup);
+#ifdef MOE_TIMELINE
+  if (threadIdx.x == 0) FZ_T(6, tl_now());
+#endif
+}
+
+}  // namespace fz
+
+#ifdef MOE_TIMELINE
+void fz_trace_read(unsigned long long* out) { cudaMemcpyFromSymbol(out, fz::g_fz_trace, sizeof(fz::g_fz_trace)); }
+#endif
+
+// Q8 decode only: every expert's slots fit one tile (T <= NT <= 32). Used
+// from 8 tokens up: below that there are fewer gate/up units than CTAs, every
+// expert completes at the same late moment and the down claims only wait
+// (measured, Qwen3-30B-A3B layer: T=1 50.1 vs 43.2 us two-kernel, T=4 57.7 vs
+// 54.8; T=8 75.6 vs 77.5, T=16 94.7 vs 96.0, T=24 108.7 vs 118.7, T=32 115.9
+// vs 125.7). MOE_FUSED=0 never uses it, MOE_FUSED=2 for every decode size.
+bool fused_supported(const LayerDev& L, int T, int nt) {
+  static int env = -1;
+  if (env < 0) { const char* e = getenv("MOE_FUSED"); env = e ? atoi(e) : 1; }
+  return env && (T >= 8 || env == 2) && L.dtype == 2 && T <= nt && (nt == 16 || nt == 32) &&
+         L.D % 128 == 0 && L.F % 128 == 0 && L.e_end - L.e_begin <= kFusedMaxTiles;
+}
+
+bool launch_mma_fused(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st,
+                      const EpView* ep) {
+  using namespace mm;
+  const int E_local = L.e_end - L.e_begin, TK = T * L.topk, cap = ws.cap_T * ws.cap_K;
+  TMap tG, tU, tX0, tX1, tDn, tH0, tH1;
+  if (!map_weights(tG, L, L.gq_off, L.D, L.F) || !map_weights(tU, L, L.uq_off, L.D, L.F) ||
+      !map_rows(tX0, ws.xact, L.D, ws.cap_T, nt, 2 * L.D) ||
+      !map_rows(tX1, ws.xact + L.D, L.D, ws.cap_T, nt, 2 * L.D) ||
+      !map_weights(tDn, L, L.dq_off, L.F, L.D) || !map_rows(tH0, ws.hs0, L.F, cap, nt) ||
+      !map_rows(tH1, ws.hs1, L.F, cap, nt))
+    return false;
+  fz::Args a{};
+  a.route = ws.route; a.E_local = E_local; a.TK = TK; a.max_tiles = route_max_tiles(TK, E_local, nt);
+  a.topk = L.topk;
+  a.slab = L.slab; a.stride = L.expert_stride; a.gs_off = L.gs_off; a.us_off = L.us_off; a.ds_off = L.ds_off;
+  a.D = L.D; a.F = L.F; a.hs0 = ws.hs0; a.hs1 = ws.hs1; a.ys = ws.y;
+  a.w_once = evict_first_on() ? 1 : 0;
+  a.ctr = ws.fused_ctr; a.err = err;
+  a.ep_on = ep != nullptr;
+  if (ep) a.ep = *ep;
+  a.slot_bytes = fz::kA + 2 * nt * 128;
+  const int budget = 220 * 1024 / 2;
+  a.nslots = (budget - 1024 - 256) / a.slot_bytes;
+  if (a.nslots > 8) a.nslots = 8;
+  if (a.nslots < 2) return false;
+  const size_t smem = (size_t)a.nslots * a.slot_bytes + 1024 + 16 * (size_t)a.nslots;
+  const int grid = 2 * sms();
+  auto run = [&](auto kern) -> bool {
+    static size_t attr[2] = {0, 0};
+    size_t& at = attr[nt == 16 ? 0 : 1];
+    if (smem > at) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return false;
+      at = smem;
+    }
+    return launch_pdl(kern, dim3(grid), dim3(fz::kThreads), smem, st, tG, tU, tX0, tX1, tDn, tH0, tH1, a) ==
+           cudaSuccess;
+  };
+  return nt == 16 ? run(fz::moe_fused_kernel<16>) : run(fz::moe_fused_kernel<32>);
+}
+
+MOE_TL_IO(moe_fused)
+
+}  // namespace moe

@@ -63,6 +63,8 @@ static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 void tl_io_router(unsigned long long*, int);
 void tl_io_moe_mma(unsigned long long*, int);
 void tl_io_ep(unsigned long long*, int);
+void tl_io_moe_fused(unsigned long long*, int);
+void fz_trace_read(unsigned long long*);
 #endif
 
 bool pdl_enabled() {
@@ -86,7 +88,8 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   const int nF = F > w.cap_F ? F : w.cap_F, nK = K > w.cap_K ? K : w.cap_K;
   CU(cudaDeviceSynchronize());
   void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum, w.hact, w.hsum,
-                  w.y, w.cnt, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter, w.route_tmp};
+                  w.y, w.cnt, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter, w.route_tmp,
+                  w.fused_ctr};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
   const size_t TK = (size_t)nT * nK;
@@ -118,7 +121,9 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   ALLOC(route_tmp, sizeof(int) * 3 * (size_t)nE);
   ALLOC(xn, sizeof(float) * (size_t)nT * nD);
   ALLOC(xo, sizeof(float) * (size_t)nT * nD);
+  ALLOC(fused_ctr, sizeof(int) * (3 + 2 * kFusedMaxTiles));
 #undef ALLOC
+  CU(cudaMemset(w.fused_ctr, 0, sizeof(int) * (3 + 2 * kFusedMaxTiles)));
   CU(cudaMemset(w.cnt, 0, sizeof(int) * (size_t)nD));
   CU(cudaMemset(w.route_counter, 0, sizeof(int)));
   CU(cudaMemset(w.route_tmp, 0, sizeof(int) * 3 * (size_t)nE));
@@ -297,7 +302,8 @@ int moe_cuda_shutdown(void) {
   g.alias.clear();
   Workspace& w = g.ws;
   void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum, w.hact, w.hsum,
-                  w.y, w.cnt, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter, w.route_tmp};
+                  w.y, w.cnt, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter, w.route_tmp,
+                  w.fused_ctr};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
   Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum};
@@ -674,8 +680,12 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
     route_tokens(L, xn, T, nt, st);
     if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
     bool ok = true;
-    timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
-    if (ok) timed("mma_down", st, [&] { ok = launch_mma_down(L, w, T, nt, w.y, fuse, xo, xo, g.d_err, st); });
+    if (!fuse && fused_supported(L, T, nt)) {
+      timed("mma_fused", st, [&] { ok = launch_mma_fused(L, w, T, nt, g.d_err, st); });
+    } else {
+      timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
+      if (ok) timed("mma_down", st, [&] { ok = launch_mma_down(L, w, T, nt, w.y, fuse, xo, xo, g.d_err, st); });
+    }
     if (!ok) return set_err(MOE_ERR_CUDA, "tensor-core launch failed (tensor map or shared memory)");
     if (!fuse)
       timed("combine", st, [&] {
@@ -831,6 +841,12 @@ extern "C" {
 #ifdef MOE_TIMELINE
 // Timeline build only: copy out (and optionally reset) the per-kernel
 // [first start, last end] globaltimer table, kTlCount x 2 values.
+int moe_debug_fused_trace(unsigned long long* out) {
+  CU(cudaDeviceSynchronize());
+  moe::fz_trace_read(out);
+  return MOE_OK;
+}
+
 int moe_debug_timeline(unsigned long long* out, int reset) {
   CU(cudaDeviceSynchronize());
   unsigned long long t[2 * kTlCount];
@@ -838,6 +854,7 @@ int moe_debug_timeline(unsigned long long* out, int reset) {
   moe::tl_io_router(t, reset);
   moe::tl_io_moe_mma(t, reset);
   moe::tl_io_ep(t, reset);
+  moe::tl_io_moe_fused(t, reset);
   if (out) memcpy(out, t, sizeof(t));
   return MOE_OK;
 }
@@ -937,11 +954,15 @@ int moe_ffn_ep(int layer, const float* x_norm2, int T_local, float* x_inout, voi
   });
   if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
   bool ok = true;
-  timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
-  if (ok)
-    timed("mma_down_ep", st, [&] {
-      ok = launch_mma_down(L, w, T, nt, w.y, false, nullptr, nullptr, g.d_err, st, &ep);
-    });
+  if (fused_supported(L, T, nt)) {
+    timed("mma_fused_ep", st, [&] { ok = launch_mma_fused(L, w, T, nt, g.d_err, st, &ep); });
+  } else {
+    timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
+    if (ok)
+      timed("mma_down_ep", st, [&] {
+        ok = launch_mma_down(L, w, T, nt, w.y, false, nullptr, nullptr, g.d_err, st, &ep);
+      });
+  }
   if (!ok) return set_err(MOE_ERR_CUDA, "tensor-core launch failed (tensor map or shared memory)");
   timed("ep_combine", st, [&] { launch_ep_combine(ep, x_inout, x_inout, L.D, L.topk, g.d_err, st); });
   CU(cudaGetLastError());

@@ -1,0 +1,99 @@
+// tmap.cuh — host helpers shared by the tensor-core kernels: TMA tensor maps
+// (built through the driver entry point, no libcuda link), the SM count and
+// the residency / cache-policy switches.
+#pragma once
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <stdlib.h>
+#include "kernels.cuh"
+
+namespace moe {
+namespace mm {
+
+struct __align__(64) TMap { CUtensorMap m; };
+
+static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// uint8 tensor map, 128-byte inner box with 128-byte swizzle.
+static bool map_u8(TMap& t, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                   const cuuint32_t* box, bool swizzle = true) {
+  auto fn = encoder();
+  if (!fn) return false;
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(&t.m, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// weights of one projection over all local experts: (row bytes, rows, expert).
+// Q8: 128-byte boxes, 128-byte swizzle (the MMA operand layout itself);
+// Q4: 64-byte boxes of packed nibbles, unswizzled (expanded in shared memory).
+static bool map_weights(TMap& t, const LayerDev& L, size_t off, int kelems, int rows) {
+  const bool q4 = L.dtype == 3;
+  const int rb = q4 ? kelems / 2 : kelems;
+  const cuuint64_t dims[3] = {(cuuint64_t)rb, (cuuint64_t)rows, (cuuint64_t)(L.e_end - L.e_begin)};
+  const cuuint64_t strides[2] = {(cuuint64_t)rb, (cuuint64_t)L.expert_stride};
+  const cuuint32_t box[3] = {q4 ? 64u : 128u, 128, 1};
+  return map_u8(t, L.slab + off, 3, dims, strides, box, !q4);
+}
+
+// activation rows: (K bytes, J rows, row pitch); J >= the box height
+static bool map_rows(TMap& t, const uint8_t* base, int kbytes, int J, int nt, int pitch = 0) {
+  const cuuint64_t dims[2] = {(cuuint64_t)kbytes, (cuuint64_t)J};
+  const cuuint64_t strides[1] = {(cuuint64_t)(pitch ? pitch : kbytes)};
+  const cuuint32_t box[2] = {128, (cuuint32_t)nt};
+  return map_u8(t, base, 2, dims, strides, box);
+}
+
+// Resident CTAs per SM. Two independent producer/MMA/epilogue pipelines per
+// SM measured faster than one with twice the stages (T=16 decode: gate/up 58
+// -> 51 us, down 39 -> 32 us); three leave too few stages. MOE_MMA_CTAS
+// overrides, for tuning runs.
+static int ctas_per_sm() {
+  static int c = 0;
+  if (!c) {
+    const char* e = getenv("MOE_MMA_CTAS");
+    c = e ? atoi(e) : 2;
+    if (c < 1 || c > 3) c = 2;
+  }
+  return c;
+}
+
+static int sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+// Q4 stages carry the packed staging tiles too, so Q4 runs one CTA per SM
+// with the whole shared-memory budget.
+static int ctas_for(int dt) { return dt == 4 ? 1 : ctas_per_sm(); }
+static int grid_ctas(int dt) { return sms() * ctas_for(dt); }
+// weights read once per call are loaded evict-first (MOE_NO_EVICT_FIRST=1
+// turns it off, for measurements)
+static bool evict_first_on() {
+  static int v = -1;
+  if (v < 0) v = getenv("MOE_NO_EVICT_FIRST") ? 0 : 1;
+  return v == 1;
+}
+
+}  // namespace mm
+}  // namespace moe
