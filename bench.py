@@ -154,7 +154,9 @@ def alg_bytes(kernel, T, U, dt):
     gu_rb = D if dt == 2 else D // 2
     d_rb = F if dt == 2 else F // 2
     kernel = (kernel.replace("mma_", "").replace("down_ep", "down").replace("ep_combine", "combine")
-              .replace("route_dispatch", "route"))
+              .replace("route_dispatch", "route").replace("fused_ep", "fused"))
+    if kernel == "fused":      # gate/up and down in one persistent kernel
+        return alg_bytes("gateup", T, U, dt) + alg_bytes("down", T, U, dt)
     if kernel == "gateup":
         return U * (2 * F * gu_rb + 2 * F * 4)
     if kernel == "down":
