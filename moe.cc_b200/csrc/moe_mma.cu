@@ -32,14 +32,53 @@
 
 namespace moe {
 namespace mm {
+#ifdef MOE_TIMELINE
+// timeline build: per-stage clock64 stamps of CTA 0 of the Q4 gate/up kernel
+// [stage][producer issued, expander saw data, expander done, MMA issued]
+__device__ long long g_q4_trace[64][4];
+#define Q4T(i, k) do { if (DT == 4 && MODE == GATEUP && blockIdx.x == 0 && (i) < 64) g_q4_trace[i][k] = clock64(); } while (0)
+#else
+#define Q4T(i, k) do { } while (0)
+#endif
 
 enum { GATEUP = 0, DOWN = 1 };
 // Epilogue warps: several per TMEM lane quarter, splitting the slot columns.
 // Wide (prefill) tiles need 16 to hide the epilogue's latency; decode tiles
 // (<= 32 slots) use 8, which keeps two CTAs resident per SM.
-__host__ __device__ constexpr int epi_warps(int nt) { return nt >= 64 ? 16 : 8; }
-__host__ __device__ constexpr int cta_threads(int dt, int nt) { return (2 + epi_warps(nt) + (dt == 4 ? 4 : 0)) * 32; }
-constexpr int kPackedBytes = 128 * 64;  // one packed Q4 tile: 128 rows x 128 nibbles
+// Q4 decode tiles keep the expanded weights in tensor memory (the MMA reads A
+// from TMEM): the expanders unpack each thread's packed row in registers and
+// store it with tcgen05.st, so neither the expanded tile's write nor the
+// MMA's read goes through shared memory (in shared memory the expansion made
+// the decode pipeline shared-memory-bandwidth bound).
+#ifndef MOE_Q4_TMEM
+#define MOE_Q4_TMEM 1
+#endif
+__host__ __device__ constexpr bool q4_a_in_tmem(int dt, int nt) { return MOE_Q4_TMEM && dt == 4 && nt <= 32; }
+// Epilogue warps: 16 for wide tiles, 8 for decode tiles, 4 for Q4 decode
+// (whose two CTAs per SM need the registers; decode tiles have few slots).
+__host__ __device__ constexpr int epi_warps(int nt, int dt = 8) {
+  return nt >= 64 ? 16 : (dt == 4 && MOE_Q4_TMEM) ? 4 : 8;
+}
+// Q4 nibble-expander warps: the expansion paces the decode pipeline, so small
+// tiles get 8 (the wide prefill tiles keep 4 and their threads for the epilogue)
+#ifndef MOE_Q4_EXP_DECODE
+#define MOE_Q4_EXP_DECODE 8
+#endif
+__host__ __device__ constexpr int exp_warps(int dt, int nt) { return dt == 4 ? (nt <= 32 ? MOE_Q4_EXP_DECODE : 4) : 0; }
+__host__ __device__ constexpr int cta_threads(int dt, int nt) { return (2 + epi_warps(nt, dt) + exp_warps(dt, nt)) * 32; }
+// Q4 weights are loaded as 128-byte-wide, 128B-swizzled boxes: two k-chunks
+// (256 nibbles) per row and per pipeline stage. The tensor copy engine's cost
+// goes by row segment, so 64-byte boxes (one k-chunk) halved the achievable
+// weight stream per SM.
+constexpr int kQ4KPerStage = 2;
+// Depth of the Q4 expanded-tile ring: the expanders run this many k-chunks
+// ahead of the MMAs. Decode tiles are small, so the ring can be deep; the
+// wide prefill tiles need the shared memory for their B operands.
+#ifndef MOE_Q4_ARING
+#define MOE_Q4_ARING 2
+#endif
+__host__ __device__ constexpr int q4_aring_depth(int nt) { return nt <= 32 ? MOE_Q4_ARING : 2; }
+
 
 
 struct Args {
@@ -65,19 +104,25 @@ struct Args {
 };
 
 template <int DT, int MODE, int NT>
-__global__ void __launch_bounds__(cta_threads(DT, NT), 1)
+__global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM && NT <= 32) ? 2 : 1)
     moe_mma_kernel(const __grid_constant__ TMap tmA0, const __grid_constant__ TMap tmA1,
                    const __grid_constant__ TMap tmB0, const __grid_constant__ TMap tmB1, const Args a) {
-  constexpr int kEpiWarps = epi_warps(NT), kEpiPerQ = kEpiWarps / 4, kExpWarp0 = 2 + kEpiWarps;
+  constexpr int kEpiWarps = epi_warps(NT, DT), kEpiPerQ = kEpiWarps / 4, kExpWarp0 = 2 + kEpiWarps;
+  constexpr int kExpWarps = exp_warps(DT, NT), kExpThreads = kExpWarps * 32;
   constexpr int NM = MODE == GATEUP ? 2 : 1;     // weight matrices per tile
   constexpr int NL = DT == 8 ? 2 : 1;            // activation limbs
   constexpr int ACC = NM * NL * NT;              // accumulator columns per buffer
-  constexpr uint32_t TCOLS = ACC * 2 <= 32 ? 32 : ACC * 2 <= 64 ? 64 : ACC * 2 <= 128 ? 128
-                             : ACC * 2 <= 256 ? 256 : 512;
-  static_assert(ACC * 2 <= 512, "accumulators exceed TMEM");
+  constexpr bool ATM = q4_a_in_tmem(DT, NT);
+  constexpr int ACOL = 2 * ACC;                  // ATM: first TMEM column of the expanded-A ring
+  constexpr int TNEED = 2 * ACC + (ATM ? q4_aring_depth(NT) * NM * 32 : 0);
+  constexpr uint32_t TCOLS = TNEED <= 32 ? 32 : TNEED <= 64 ? 64 : TNEED <= 128 ? 128
+                             : TNEED <= 256 ? 256 : 512;
+  static_assert(TNEED <= 512, "accumulators exceed TMEM");
+  static_assert(!ATM || exp_warps(DT, NT) == 8, "TMEM expansion: one warp per (lane quarter, matrix or half)");
   constexpr float S = DT == 8 ? 127.0f : 7.0f;
-  constexpr int A_BYTES = 128 * 128;
-  constexpr int B_BYTES = NT * 128;
+  constexpr int A_BYTES = 128 * 128;              // one weight tile (Q4: two packed k-chunks)
+  constexpr int B_BYTES = NT * 128;               // one activation limb tile of one k-chunk
+  constexpr int KPS = DT == 4 ? kQ4KPerStage : 1;  // k-chunks per pipeline stage
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -85,11 +130,13 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
   uint64_t* empty = full + a.stages;
   uint64_t* acc_full = empty + a.stages;     // [2]
   uint64_t* acc_empty = acc_full + 2;        // [2]
-  uint64_t* afull = acc_empty + 2;           // [2] Q4: expanded A tiles written
-  uint64_t* aempty = afull + 2;              // [2] Q4: expanded A tiles consumed by the MMAs
+  constexpr int AR = q4_aring_depth(NT);
+  uint64_t* afull = acc_empty + 2;           // [AR] Q4: expanded A tiles written
+  uint64_t* aempty = afull + AR;             // [AR] Q4: expanded A tiles consumed by the MMAs
   // Q4: the stage ring holds [packed tiles | B]; the expanded A tiles live in
-  // their own 2-deep ring after the barriers (1024-aligned)
-  uint8_t* aring = smem + (((size_t)a.stages * a.stage_bytes + 16 * (size_t)a.stages + 64 + 1023) & ~(size_t)1023);
+  // their own AR-deep ring after the barriers (1024-aligned)
+  uint8_t* aring = smem + (((size_t)a.stages * a.stage_bytes + 16 * (size_t)a.stages + 32 + 16 * AR + 1023) &
+                           ~(size_t)1023);
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_issued;
 
@@ -103,7 +150,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
     for (int s = 0; s < a.stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiWarps); }
     if (DT == 4)
-      for (int b = 0; b < 2; ++b) { mbar_init(&afull[b], 4); mbar_init(&aempty[b], 1); }
+      for (int b = 0; b < AR; ++b) { mbar_init(&afull[b], kExpWarps); mbar_init(&aempty[b], 1); }
     fence_mbar_init();
     tc::prefetch_tmap(&tmA0.m); tc::prefetch_tmap(&tmB0.m);
     if (NM == 2) tc::prefetch_tmap(&tmA1.m);
@@ -130,7 +177,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
   if (warp == 0) {
     // ------------------------- TMA producer -------------------------
     if (lane == 0) {
-      const uint32_t bytes = (DT == 4 ? NM * kPackedBytes : NM * A_BYTES) + NL * B_BYTES;
+      const uint32_t bytes = NM * A_BYTES + KPS * NL * B_BYTES;
       const uint64_t wpol = tc::policy_evict_first();
       // f(unit, kc, it) over this CTA's k-chunk iterations, until it returns
       // false; the unit's expert, row block and first slot are read once
@@ -140,7 +187,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
         for (int u = u0; u < n_units; u += ustep) {
           const int tile = u / a.n_mblk;
           const Unit un{active[tv.u[tile]], u % a.n_mblk, tv.j0[tile]};
-          for (int kc = 0; kc < a.kchunks; ++kc, ++it)
+          for (int kc = 0; kc < a.kchunks; kc += KPS, ++it)   // one stage per KPS k-chunks
             if (!f(un, kc, it)) return;
         }
       };
@@ -149,22 +196,26 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
         uint8_t* sb = smem + (size_t)st * a.stage_bytes;
         // weights: when every expert has a single token tile (a.w_once) each
         // weight tile is read exactly once, so it is loaded evict-first
+        // (Q4: packed nibbles of k-chunks kc, kc+1; the expanders build the A tiles)
         const int kx = DT == 8 ? kc * 128 : kc * 64;
-        const int a1 = DT == 8 ? A_BYTES : kPackedBytes;
         if (a.w_once) {
           tc::tma_load_3d_hint(sb, &tmA0.m, kx, mb * 128, e, &full[st], wpol);
-          if (NM == 2) tc::tma_load_3d_hint(sb + a1, &tmA1.m, kx, mb * 128, e, &full[st], wpol);
-        } else {   // Q4: packed nibbles; the expanders build the A tiles from them
+          if (NM == 2) tc::tma_load_3d_hint(sb + A_BYTES, &tmA1.m, kx, mb * 128, e, &full[st], wpol);
+        } else {
           tc::tma_load_3d(sb, &tmA0.m, kx, mb * 128, e, &full[st]);
-          if (NM == 2) tc::tma_load_3d(sb + a1, &tmA1.m, kx, mb * 128, e, &full[st]);
+          if (NM == 2) tc::tma_load_3d(sb + A_BYTES, &tmA1.m, kx, mb * 128, e, &full[st]);
         }
       };
       auto load_b = [&](const Unit& un, int kc, int it) {
         const int st = it % a.stages;
         uint8_t* sb = smem + (size_t)st * a.stage_bytes;
         const int by = a.tokb ? 0 : un.j0;   // decode: all token rows from row 0
-        tc::tma_load_2d(sb + (DT == 4 ? NM * kPackedBytes : NM * A_BYTES), &tmB0.m, kc * 128, by, &full[st]);
-        if (NL == 2) tc::tma_load_2d(sb + NM * A_BYTES + B_BYTES, &tmB1.m, kc * 128, by, &full[st]);
+#pragma unroll
+        for (int q = 0; q < KPS; ++q) {
+          uint8_t* bb = sb + NM * A_BYTES + q * NL * B_BYTES;
+          tc::tma_load_2d(bb, &tmB0.m, (kc + q) * 128, by, &full[st]);
+          if (NL == 2) tc::tma_load_2d(bb + B_BYTES, &tmB1.m, (kc + q) * 128, by, &full[st]);
+        }
       };
       int pre = 0;   // iterations whose weights went out before the dependency wait
       if (MODE == DOWN) {
@@ -194,6 +245,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
         mbar_arrive_expect_tx(&full[st], bytes);
         load_a(un, kc, it);
         load_b(un, kc, it);
+        Q4T(it, 0);
         s_issued = it + 1;
         return true;
       });
@@ -206,7 +258,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
       uint32_t idesc[2];
       idesc[0] = tc::idesc_i8(128, NT, DT == 8, DT != 8);
       idesc[1] = tc::idesc_i8(128, NT, true, true);
-      int it = 0, ul = 0;
+      int ik = 0, ul = 0;                      // k-chunks consumed, units
       for (int u = u0; u < n_units && !*abort_flag; u += ustep, ++ul) {
         const int buf = ul & 1;
         if (ul >= 2 && !mbar_wait(&acc_empty[buf], ((ul >> 1) - 1) & 1, kWaitBudget)) {
@@ -214,20 +266,21 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
         }
         tc::fence_after_sync();
         const uint32_t dbase = tmem + buf * ACC;
-        for (int kc = 0; kc < a.kchunks; ++kc, ++it) {
-          const int st = it % a.stages;
-          const int ab = it & 1;
-          if (!mbar_wait(DT == 4 ? &afull[ab] : &full[st], DT == 4 ? (it >> 1) & 1 : (it / a.stages) & 1,
+        for (int kc = 0; kc < a.kchunks; ++kc, ++ik) {
+          const int it = ik / KPS, st = it % a.stages, q = ik % KPS;   // stage and k-chunk within it
+          const int ab = ik % AR;
+          if (!mbar_wait(DT == 4 ? &afull[ab] : &full[st], DT == 4 ? (ik / AR) & 1 : (it / a.stages) & 1,
                          kWaitBudget)) {
             atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
           }
           tc::fence_after_sync();
+          if (threadIdx.x == 32 && q == 0) Q4T(it, 3);
           const uint8_t* sb = smem + (size_t)st * a.stage_bytes;
           const uint8_t* atile = DT == 4 ? aring + (size_t)ab * NM * A_BYTES : sb;
-          const uint8_t* btile = sb + (DT == 4 ? NM * kPackedBytes : NM * A_BYTES);
+          const uint8_t* btile = sb + NM * A_BYTES + q * NL * B_BYTES;
           uint64_t da[NM], db[NL];
 #pragma unroll
-          for (int m = 0; m < NM; ++m) da[m] = tc::sw128_desc(atile + m * A_BYTES);
+          for (int m = 0; m < NM; ++m) da[m] = ATM ? 0 : tc::sw128_desc(atile + m * A_BYTES);
 #pragma unroll
           for (int l = 0; l < NL; ++l) db[l] = tc::sw128_desc(btile + l * B_BYTES);
 #pragma unroll
@@ -235,11 +288,16 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
 #pragma unroll
             for (int m = 0; m < NM; ++m)
 #pragma unroll
-              for (int l = 0; l < NL; ++l)
-                tc::mma_i8(dbase + (m * NL + l) * NT, da[m] + 2 * kk, db[l] + 2 * kk, idesc[l],
-                           (kc | kk) != 0);
-          tc::mma_commit(&empty[st]);               // stage free once these MMAs finish
-          if (DT == 4) tc::mma_commit(&aempty[ab]);  // and the expanded A tiles
+              for (int l = 0; l < NL; ++l) {
+                if (ATM)   // A: 32 TMEM columns per tile, 8 per 32-byte K step
+                  tc::mma_i8_ts(dbase + (m * NL + l) * NT, tmem + ACOL + (ab * NM + m) * 32 + kk * 8,
+                                db[l] + 2 * kk, idesc[l], (kc | kk) != 0);
+                else
+                  tc::mma_i8(dbase + (m * NL + l) * NT, da[m] + 2 * kk, db[l] + 2 * kk, idesc[l],
+                             (kc | kk) != 0);
+              }
+          if (q == KPS - 1) tc::mma_commit(&empty[st]);   // stage free once its MMAs finish
+          if (DT == 4) tc::mma_commit(&aempty[ab]);      // and the expanded A tiles
         }
         if (*abort_flag) break;
         tc::mma_commit(&acc_full[buf]);             // accumulator of this tile complete
@@ -247,29 +305,67 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
     }
   } else if (DT == 4 && warp >= kExpWarp0) {
     // ------------------- Q4 nibble expanders ------------------------
-    // row r of each packed tile (64 bytes = 128 nibbles) becomes 128 bytes of
-    // the 128B-swizzled u8 A tile: packed 16-byte chunk c -> chunk 2c holds its
-    // 16 low nibbles, chunk 2c+1 its 16 high nibbles (the activations use the
-    // same k order, q4_mma_pos). 16-byte chunk h of row r sits at h ^ (r & 7).
-    const int r = (warp - kExpWarp0) * 32 + lane;
-    int it = 0;
+    // A stage holds, per matrix, 128 packed rows of 128 bytes (k-chunks kc and
+    // kc+1, 128B-swizzled by the tensor copy: 16-byte chunk h of row r at
+    // h ^ (r & 7)). For k-chunk q of the stage, packed 16-byte chunk c of row r
+    // (= row bytes 64q + 16c) becomes two 16-byte chunks of the 128B-swizzled
+    // u8 A tile: chunk 2c holds its 16 low nibbles, chunk 2c+1 its 16 high
+    // nibbles (the activations use the same k order, q4_mma_pos). Thread ti
+    // takes items ti + kExpThreads*i = (row, chunk): a warp covers 8 rows,
+    // spread over all banks by the swizzle.
+    const int ti = (warp - kExpWarp0) * 32 + lane;
+    int ik = 0;
     for (int u = u0; u < n_units && !*abort_flag; u += ustep) {
-      for (int kc = 0; kc < a.kchunks; ++kc, ++it) {
-        const int st = it % a.stages, ab = it & 1;
+      for (int kc = 0; kc < a.kchunks; ++kc, ++ik) {
+        const int it = ik / KPS, st = it % a.stages, qk = ik % KPS, ab = ik % AR;
         if (!mbar_wait(&full[st], (it / a.stages) & 1, kWaitBudget) ||
-            (it >= 2 && !mbar_wait(&aempty[ab], ((it >> 1) - 1) & 1, kWaitBudget))) {
+            (ik >= AR && !mbar_wait(&aempty[ab], ((ik / AR) - 1) & 1, kWaitBudget))) {
           if (lane == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; }
           break;
         }
+        if (ti == 0 && qk == 0) Q4T(it, 1);
         const uint8_t* stg = smem + (size_t)st * a.stage_bytes;
+        if (ATM) {
+          // warp = (lane quarter, part): part = matrix (gate/up) or column half
+          // (down); row r's packed 64 bytes of this k-chunk -> 128 bytes = 32
+          // TMEM columns (chunk 2c = columns 8c..8c+3, chunk 2c+1 = 8c+4..8c+7)
+          const int quarter = warp & 3, part = (warp - kExpWarp0) >> 2, r = quarter * 32 + lane;
+          const int m = NM == 2 ? part : 0;
+          const uint8_t* prow = stg + m * A_BYTES + r * 128;
+          const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + ACOL + (ab * NM + m) * 32;
+          auto unpack = [&](int c, uint32_t* o) {
+            const uint4 w = *reinterpret_cast<const uint4*>(prow + ((((qk << 2) + c) ^ (r & 7)) << 4));
+            o[0] = w.x & 0x0F0F0F0Fu; o[1] = w.y & 0x0F0F0F0Fu; o[2] = w.z & 0x0F0F0F0Fu; o[3] = w.w & 0x0F0F0F0Fu;
+            o[4] = (w.x >> 4) & 0x0F0F0F0Fu; o[5] = (w.y >> 4) & 0x0F0F0F0Fu;
+            o[6] = (w.z >> 4) & 0x0F0F0F0Fu; o[7] = (w.w >> 4) & 0x0F0F0F0Fu;
+          };
+          if (NM == 2) {
+            uint32_t o[32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) unpack(c, o + 8 * c);
+            tc::tmem_st32(trow, o);
+          } else {
+            uint32_t o[16];
+#pragma unroll
+            for (int c = 0; c < 2; ++c) unpack(2 * part + c, o + 8 * c);
+            tc::tmem_st16(trow + 16 * part, o);
+          }
+          tc::tmem_wait_st();
+          tc::fence_before_sync();          // TMEM stores -> the MMA thread after the barrier
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&afull[ab]);
+          if (ti == 0 && qk == KPS - 1) Q4T(it, 2);
+          continue;
+        }
         uint8_t* at = aring + (size_t)ab * NM * A_BYTES;
 #pragma unroll
         for (int m = 0; m < NM; ++m) {
-          const uint4* src = reinterpret_cast<const uint4*>(stg + m * kPackedBytes + r * 64);
-          uint8_t* dst = at + m * A_BYTES + r * 128;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 w = src[c];
+          for (int i = 0; i < 512 / (kExpWarps > 0 ? kExpThreads : 128); ++i) {
+            const int item = ti + kExpThreads * i, r = item >> 2, c = item & 3;
+            const uint4 w = *reinterpret_cast<const uint4*>(stg + m * A_BYTES + r * 128 +
+                                                            ((((qk << 2) + c) ^ (r & 7)) << 4));
+            uint8_t* dst = at + m * A_BYTES + r * 128;
             const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
             const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu,
                                         (w.z >> 4) & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
@@ -280,6 +376,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), 1)
         tc::fence_proxy_async_smem();     // generic-proxy writes -> visible to the MMA
         __syncwarp();
         if (lane == 0) mbar_arrive(&afull[ab]);
+        if (ti == 0 && qk == KPS - 1) Q4T(it, 2);
       }
     }
   } else {
@@ -476,13 +573,14 @@ template <int DT, int MODE, int NT>
 static bool launch_kernel(const TMap& a0, const TMap& a1, const TMap& b0, const TMap& b1, Args a, int grid,
                           cudaStream_t st) {
   constexpr int NM = MODE == GATEUP ? 2 : 1, NL = DT == 8 ? 2 : 1;
-  a.stage_bytes = (DT == 4 ? NM * kPackedBytes : NM * 128 * 128) + NL * NT * 128;
-  const int aring = DT == 4 ? 2 * NM * 128 * 128 + 1024 : 0;   // Q4 expanded-A ring
-  const int budget = 220 * 1024 / ctas_for(DT) - aring;
+  a.stage_bytes = NM * 128 * 128 + (DT == 4 ? kQ4KPerStage : 1) * NL * NT * 128;
+  const int aring = (DT == 4 && !q4_a_in_tmem(DT, NT)) ? q4_aring_depth(NT) * NM * 128 * 128 + 1024 : 0;
+  const int budget = 220 * 1024 / ctas_for(DT, NT) - aring;
   a.stages = (budget - 1024 - 256) / a.stage_bytes;
   if (a.stages > 8) a.stages = 8;
   if (a.stages < 2) return false;
-  const size_t smem = (size_t)a.stages * a.stage_bytes + 1024 + 16 * (size_t)a.stages + 64 + aring;
+  const size_t smem = (size_t)a.stages * a.stage_bytes + 1024 + 16 * (size_t)a.stages + 32 +
+                      16 * (DT == 4 ? q4_aring_depth(NT) : 2) + aring;
   auto k = moe_mma_kernel<DT, MODE, NT>;
   static size_t attr = 0;
   if (smem > attr) {
@@ -506,8 +604,11 @@ int mma_tile_n(int T, int dtype) {
   return dtype == 3 && T > 256 ? 128 : 64;
 }
 
+// Q8: K dimensions in 128-element chunks; Q4: two chunks per pipeline stage.
 bool mma_supported(const LayerDev& L) {
-  return (L.dtype == 2 || L.dtype == 3) && L.D % 128 == 0 && L.F % 128 == 0 && mm::encoder() != nullptr;
+  const int kq = L.dtype == 3 ? 128 * mm::kQ4KPerStage : 128;
+  return (L.dtype == 2 || L.dtype == 3) && L.D % kq == 0 && L.F % kq == 0 && L.D % 128 == 0 &&
+         L.F % 128 == 0 && mm::encoder() != nullptr;
 }
 
 void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream_t st) {
@@ -552,7 +653,7 @@ bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, in
   a.slab = L.slab; a.stride = L.expert_stride; a.s0_off = L.gs_off; a.s1_off = L.us_off;
   a.F = L.F; a.hs0 = ws.hs0; a.hs1 = ws.hs1; a.err = err;
   a.xsum = ws.xsum; a.hsum = ws.hsum; a.topk = L.topk; a.tokb = tokb; a.w_once = T <= nt && mm::evict_first_on();
-  const int units = a.max_tiles * a.n_mblk, gc = mm::grid_ctas(L.dtype == 2 ? 8 : 4);
+  const int units = a.max_tiles * a.n_mblk, gc = mm::grid_ctas(L.dtype == 2 ? 8 : 4, nt);
   const int grid = units < gc ? units : gc;
   bool ok = false;
   if (L.dtype == 2) { NT_SWITCH(nt, (ok = mm::launch_kernel<8, mm::GATEUP, NT>(a0, a1, b0, b1, a, grid, st))); }
@@ -577,7 +678,7 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
   a.xsum = ws.xsum; a.hsum = ws.hsum; a.ep_on = ep != nullptr;
   a.w_once = T <= nt && mm::evict_first_on();
   if (ep) a.ep = *ep;
-  const int units = a.max_tiles * a.n_mblk, gc = mm::grid_ctas(L.dtype == 2 ? 8 : 4);
+  const int units = a.max_tiles * a.n_mblk, gc = mm::grid_ctas(L.dtype == 2 ? 8 : 4, nt);
   const int grid = units < gc ? units : gc;
   bool ok = false;
   if (L.dtype == 2) { NT_SWITCH(nt, (ok = mm::launch_kernel<8, mm::DOWN, NT>(a0, a0, b0, b1, a, grid, st))); }
@@ -636,6 +737,9 @@ void launch_unsort_rows(const LayerDev& L, const Workspace& ws, int T, float* y_
              L.e_end, y_slots, L.D);
 }
 
+#ifdef MOE_TIMELINE
+void q4_trace_read(long long* out) { cudaMemcpyFromSymbol(out, mm::g_q4_trace, sizeof(mm::g_q4_trace)); }
+#endif
 MOE_TL_IO(moe_mma)
 
 }  // namespace moe

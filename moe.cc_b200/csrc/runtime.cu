@@ -65,6 +65,7 @@ void tl_io_moe_mma(unsigned long long*, int);
 void tl_io_ep(unsigned long long*, int);
 void tl_io_moe_fused(unsigned long long*, int);
 void fz_trace_read(unsigned long long*);
+void q4_trace_read(long long*);
 #endif
 
 bool pdl_enabled() {
@@ -841,6 +842,12 @@ extern "C" {
 #ifdef MOE_TIMELINE
 // Timeline build only: copy out (and optionally reset) the per-kernel
 // [first start, last end] globaltimer table, kTlCount x 2 values.
+int moe_debug_q4_trace(long long* out) {
+  CU(cudaDeviceSynchronize());
+  moe::q4_trace_read(out);
+  return MOE_OK;
+}
+
 int moe_debug_fused_trace(unsigned long long* out) {
   CU(cudaDeviceSynchronize());
   moe::fz_trace_read(out);

@@ -8,6 +8,11 @@
 #include <stdlib.h>
 #include "kernels.cuh"
 
+// Q4 decode keeps the expanded weights in tensor memory (moe_mma.cu)
+#ifndef MOE_Q4_TMEM
+#define MOE_Q4_TMEM 1
+#endif
+
 namespace moe {
 namespace mm {
 
@@ -39,16 +44,16 @@ static bool map_u8(TMap& t, const void* base, int rank, const cuuint64_t* dims, 
   return r == CUDA_SUCCESS;
 }
 
-// weights of one projection over all local experts: (row bytes, rows, expert).
-// Q8: 128-byte boxes, 128-byte swizzle (the MMA operand layout itself);
-// Q4: 64-byte boxes of packed nibbles, unswizzled (expanded in shared memory).
+// weights of one projection over all local experts: (row bytes, rows, expert),
+// 128-byte boxes with 128-byte swizzle. Q8: the MMA operand layout itself;
+// Q4: 256 packed nibbles per row (two k-chunks), expanded in shared memory.
 static bool map_weights(TMap& t, const LayerDev& L, size_t off, int kelems, int rows) {
   const bool q4 = L.dtype == 3;
   const int rb = q4 ? kelems / 2 : kelems;
   const cuuint64_t dims[3] = {(cuuint64_t)rb, (cuuint64_t)rows, (cuuint64_t)(L.e_end - L.e_begin)};
   const cuuint64_t strides[2] = {(cuuint64_t)rb, (cuuint64_t)L.expert_stride};
-  const cuuint32_t box[3] = {q4 ? 64u : 128u, 128, 1};
-  return map_u8(t, L.slab + off, 3, dims, strides, box, !q4);
+  const cuuint32_t box[3] = {128u, 128, 1};
+  return map_u8(t, L.slab + off, 3, dims, strides, box, true);
 }
 
 // activation rows: (K bytes, J rows, row pitch); J >= the box height
@@ -85,8 +90,13 @@ static int sms() {
 
 // Q4 stages carry the packed staging tiles too, so Q4 runs one CTA per SM
 // with the whole shared-memory budget.
-static int ctas_for(int dt) { return dt == 4 ? 1 : ctas_per_sm(); }
-static int grid_ctas(int dt) { return sms() * ctas_for(dt); }
+// Q4 decode tiles (expanded weights in TMEM, no shared-memory ring) run two
+// CTAs per SM like Q8: two MMA issuers per SM.
+static int ctas_for(int dt, int nt = 0) {
+  const bool q4_two = MOE_Q4_TMEM && nt > 0 && nt <= 32;
+  return dt == 4 ? (q4_two ? 2 : 1) : ctas_per_sm();
+}
+static int grid_ctas(int dt, int nt = 0) { return sms() * ctas_for(dt, nt); }
 // weights read once per call are loaded evict-first (MOE_NO_EVICT_FIRST=1
 // turns it off, for measurements)
 static bool evict_first_on() {
