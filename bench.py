@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-t", default="512,2048",
                     help="configs[2] Q4 prefill sizes reported beside the headline ('' to skip)")
+    ap.add_argument("--q4-batch", type=int, default=32,
+                    help="configs[4]: Q4 batched decode of this many tokens per step over all GPUs "
+                         "(strong scaling; 0 to skip)")
     return ap.parse_args()
 
 
@@ -172,10 +175,10 @@ def layer_bytes_step(T, U, dt):
     return sum(alg_bytes(k, T, U, dt) for k in ("route", "gateup", "down", "combine"))
 
 
-def build_layers(torch, mc, sy, nl, dt):
+def build_layers(torch, mc, sy, nl, dt, base=0):
     for l in range(nl):
         Ld = sy.make_layer_dev(torch, 1, l, E, D, F, dt, bias=False)
-        mc.upload_layer(l, Ld, device_arrays=True)
+        mc.upload_layer(base + l, Ld, device_arrays=True)
         del Ld
     torch.cuda.synchronize()
     mc.check_status()
@@ -208,9 +211,9 @@ class Runner:
     and kernels synchronise on flags in peer memory.
     """
 
-    def __init__(self, torch, mc, dist, world, rank, T, nl, pool):
+    def __init__(self, torch, mc, dist, world, rank, T, nl, pool, base=0, ep_ready=False):
         self.torch, self.mc, self.dist, self.world, self.rank = torch, mc, dist, world, rank
-        self.T, self.nl = T, nl
+        self.T, self.nl, self.base = T, nl, base
         self.xs, self.xa = make_inputs(torch, mc, T, pool, seed=T * 131 + rank)
         self.out = [x.clone() for x in self.xa]
         self.stream = torch.cuda.current_stream()
@@ -222,7 +225,7 @@ class Runner:
             self.y_loc = torch.empty(T * TOPK, D, device="cuda")
             own_gpu = torch.cuda.device_count() >= world
             self.fused = os.environ.get("MOE_EP_EXCHANGE", "fused" if own_gpu else "nccl") == "fused"
-            if self.fused:
+            if self.fused and not ep_ready:
                 handles = [None] * world
                 dist.all_gather_object(handles, mc.ep_setup(T, D, TOPK))
                 mc.ep_connect(handles)
@@ -230,7 +233,7 @@ class Runner:
 
     def step(self, i, topk_idx=None, x_in=None, out=None):
         j = i % len(self.xs)
-        layer = i % self.nl
+        layer = self.base + i % self.nl
         x = self.xs[j] if x_in is None else x_in
         o = self.out[j] if out is None else out
         if self.world == 1:
@@ -552,6 +555,20 @@ def run_ours(args):
         e2e = {"value": TN * steps / (ms_h / 1e3), "unit": "tok/s",
                "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4,
                "ms_per_step": ms_h / steps, "note": "per rank: tokens in from pinned host, result out"}
+    # Q4 experts, batched decode of q4_batch sequences per step, the
+    # experts sharded over the ranks (strong scaling: q4_batch / N tokens per rank)
+    q4b = None
+    if args.q4_batch and args.q4_batch % world == 0 and (world == 1 or args.q4_batch // world <= T):
+        nlq = 8
+        build_layers(torch, mc, sy, nlq, 3, base=1000)
+        r4 = Runner(torch, mc, dist, world, rank, args.q4_batch // world, nlq, 16, base=1000, ep_ready=True)
+        ms4 = r4.timed(steps, warmup)
+        q4b = {"workload": f"configs[4]: Q4 experts, batched decode of {args.q4_batch} tokens per step, "
+                           f"experts sharded over {world} GPU(s)",
+               "tokens_per_step": args.q4_batch, "tokens_per_gpu": args.q4_batch // world,
+               "tok_s": args.q4_batch * steps / (ms4 / 1e3), "us_per_step": ms4 * 1e3 / steps,
+               "scaling": "strong", "resident_layers": nlq,
+               "exchange": None if world == 1 else ("fused peer stores" if r4.fused else "nccl")}
     prefill = None
     if world == 1 and args.prefill_t:
         prefill = prefill_bench(torch, mc, sy, 30, 3, [int(v) for v in args.prefill_t.split(",") if v])
@@ -577,7 +594,7 @@ def run_ours(args):
                 "kernels": kern, "gpu_launches": int(round(launches_per_step * steps)),
                 "gpu_launches_per_step": launches_per_step,
                 "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu, "extra": extra,
-                "prefill_q4": prefill}
+                "prefill_q4": prefill, "q4_batch32": q4b}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
