@@ -560,9 +560,13 @@ def run_ours(args):
     q4b = None
     if args.q4_batch and args.q4_batch % world == 0 and (world == 1 or args.q4_batch // world <= T):
         nlq = 8
-        build_layers(torch, mc, sy, nlq, 3, base=1000)
-        r4 = Runner(torch, mc, dist, world, rank, args.q4_batch // world, nlq, 16, base=1000, ep_ready=True)
-        ms4 = r4.timed(steps, warmup)
+        try:
+            build_layers(torch, mc, sy, nlq, 3, base=1000)
+            r4 = Runner(torch, mc, dist, world, rank, args.q4_batch // world, nlq, 16, base=1000, ep_ready=True)
+            ms4 = r4.timed(steps, warmup)
+        except Exception as exc:       # the headline line must still be printed
+            ms4, q4b = None, {"error": str(exc)[:300]}
+    if q4b is None and args.q4_batch and args.q4_batch % world == 0 and (world == 1 or args.q4_batch // world <= T):
         q4b = {"workload": f"configs[4]: Q4 experts, batched decode of {args.q4_batch} tokens per step, "
                            f"experts sharded over {world} GPU(s)",
                "tokens_per_step": args.q4_batch, "tokens_per_gpu": args.q4_batch // world,
