@@ -139,7 +139,7 @@ namespace moe {
 // moe_mma.cu: tcgen05 grouped GEMMs over the routed experts
 bool mma_supported(const LayerDev& L);
 int mma_tile_n(int T, int dtype);
-void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream_t st);
+void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, int nt, cudaStream_t st);
 bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st);
 // ep != null: expert-parallel mode, each slot row is stored into the y buffer
 // of the rank owning its token, and the last CTA raises this rank's combine
@@ -148,7 +148,8 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
                      const float* xres, float* out, int* err, cudaStream_t st, const EpView* ep = nullptr);
 // moe_fused.cu: Q8 decode gate/up + down in one persistent kernel
 constexpr int kFusedMaxTiles = 256;
-bool fused_supported(const LayerDev& L, int T, int nt);
+// tile width the fused kernel would use for T tokens (16 or 32), 0 = not used
+int fused_tile_n(const LayerDev& L, int T);
 bool launch_mma_fused(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st,
                       const EpView* ep = nullptr);
 void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,

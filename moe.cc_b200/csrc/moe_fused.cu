@@ -65,6 +65,8 @@ struct Args {
   uint8_t* hs0; uint8_t* hs1;          // h planes [J][F] (expert-sorted slots)
   float* ys;                           // [J][D] y rows (expert-sorted slots)
   int nslots, slot_bytes, w_once;
+  int tokb;                            // 1: B of gate/up = the token rows (T <= NT); 0: the
+                                       // expert-sorted gathered rows (tile j0...)
   int* ctr;                            // [0] work, [1] arrivals, [2] ready count, then per-tile
                                        // completion [kFusedMaxTiles] and the ready list [kFusedMaxTiles]
   int ep_on; EpView ep;
@@ -199,8 +201,9 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (s0 < 0) break;
             uint8_t* p0 = smem + (size_t)s0 * a.slot_bytes;
             load_w(tG, kc, mb, e, p0, &full[s0]);
-            tc::tma_load_2d(p0 + kA, &tX0.m, kc * 128, 0, &full[s0]);       // decode: token rows 0..
-            tc::tma_load_2d(p0 + kA + B, &tX1.m, kc * 128, 0, &full[s0]);
+            const int by = a.tokb ? 0 : tv.j0[tile];   // token rows, or this tile's gathered rows
+            tc::tma_load_2d(p0 + kA, &tX0.m, kc * 128, by, &full[s0]);
+            tc::tma_load_2d(p0 + kA + B, &tX1.m, kc * 128, by, &full[s0]);
             const int s1 = take(kA);
             if (s1 < 0) break;
             load_w(tU, kc, mb, e, smem + (size_t)s1 * a.slot_bytes, &full[s1]);
@@ -299,9 +302,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint8_t* ex = a.slab + (size_t)e * a.stride;
         const float sg = __ldg(reinterpret_cast<const float*>(ex + a.gs_off) + n);
         const float su = __ldg(reinterpret_cast<const float*>(ex + a.us_off) + n);
-        // accumulator column t is token t; each routed slot reads its token's column
+        // token rows: accumulator column t is token t, each routed slot reads its
+        // token's column; gathered rows: column jj is the tile's slot jj
         for (int jj = half; jj < nt; jj += kEpiWarps / 4) {
-          const int j = j0 + jj, t = __ldg(slots + j) / a.topk;       // warp-uniform
+          const int j = j0 + jj;
+          const int t = a.tokb ? __ldg(slots + j) / a.topk : jj;      // warp-uniform column
           uint32_t v[4][8], raw[4];
 #pragma unroll
           for (int x = 0; x < 4; ++x) tc::tmem_ld8(tbase + x * NT + (t & ~7), v[x]);
@@ -404,27 +409,35 @@ __global__ void __launch_bounds__(kThreads, 2)
 void fz_trace_read(unsigned long long* out) { cudaMemcpyFromSymbol(out, fz::g_fz_trace, sizeof(fz::g_fz_trace)); }
 #endif
 
-// Q8 decode only: every expert's slots fit one tile (T <= NT <= 32). Used
-// from 8 tokens up: below that there are fewer gate/up units than CTAs, every
-// expert completes at the same late moment and the down claims only wait
-// (measured, Qwen3-30B-A3B layer: T=1 50.1 vs 43.2 us two-kernel, T=4 57.7 vs
-// 54.8; T=8 75.6 vs 77.5, T=16 94.7 vs 96.0, T=24 108.7 vs 118.7, T=32 115.9
-// vs 125.7). MOE_FUSED=0 never uses it, MOE_FUSED=2 for every decode size.
-bool fused_supported(const LayerDev& L, int T, int nt) {
-  static int env = -1;
+// Q8 only. Up to 32 tokens the gate/up B operand is the token rows (every
+// expert's slots fit one tile); above, 32-slot tiles of the expert-sorted
+// gathered rows (an expert with more slots has several tiles, each with its
+// own completion count). Used from 8 tokens up: below that there are fewer
+// gate/up units than CTAs, every expert completes at the same late moment and
+// the down claims only wait (measured, Qwen3-30B-A3B layer: T=1 50.1 vs 43.2
+// us two-kernel, T=4 57.7 vs 54.8; T=8 75.6 vs 77.5, T=16 94.7 vs 96.0, T=24
+// 108.7 vs 118.7, T=32 115.9 vs 125.7). MOE_FUSED=0 never uses it, 2 for
+// every decode size; MOE_FUSED_MAX_T bounds the gathered sizes.
+int fused_tile_n(const LayerDev& L, int T) {
+  static int env = -1, tmax = -1;
   if (env < 0) { const char* e = getenv("MOE_FUSED"); env = e ? atoi(e) : 1; }
-  return env && (T >= 8 || env == 2) && L.dtype == 2 && T <= nt && (nt == 16 || nt == 32) &&
-         L.D % 128 == 0 && L.F % 128 == 0 && L.e_end - L.e_begin <= kFusedMaxTiles;
+  if (tmax < 0) { const char* e = getenv("MOE_FUSED_MAX_T"); tmax = e ? atoi(e) : 256; }
+  if (!env || (T < 8 && env != 2) || T > tmax || L.dtype != 2 || L.D % 128 || L.F % 128) return 0;
+  const int nt = T <= 16 ? 16 : 32;
+  if (route_max_tiles(T * L.topk, L.e_end - L.e_begin, nt) > kFusedMaxTiles) return 0;
+  return nt;
 }
 
 bool launch_mma_fused(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st,
                       const EpView* ep) {
   using namespace mm;
   const int E_local = L.e_end - L.e_begin, TK = T * L.topk, cap = ws.cap_T * ws.cap_K;
+  const bool tokb = T <= nt;
   TMap tG, tU, tX0, tX1, tDn, tH0, tH1;
-  if (!map_weights(tG, L, L.gq_off, L.D, L.F) || !map_weights(tU, L, L.uq_off, L.D, L.F) ||
-      !map_rows(tX0, ws.xact, L.D, ws.cap_T, nt, 2 * L.D) ||
-      !map_rows(tX1, ws.xact + L.D, L.D, ws.cap_T, nt, 2 * L.D) ||
+  const bool xmap = tokb ? (map_rows(tX0, ws.xact, L.D, ws.cap_T, nt, 2 * L.D) &&
+                            map_rows(tX1, ws.xact + L.D, L.D, ws.cap_T, nt, 2 * L.D))
+                         : (map_rows(tX0, ws.xs0, L.D, cap, nt) && map_rows(tX1, ws.xs1, L.D, cap, nt));
+  if (!xmap || !map_weights(tG, L, L.gq_off, L.D, L.F) || !map_weights(tU, L, L.uq_off, L.D, L.F) ||
       !map_weights(tDn, L, L.dq_off, L.F, L.D) || !map_rows(tH0, ws.hs0, L.F, cap, nt) ||
       !map_rows(tH1, ws.hs1, L.F, cap, nt))
     return false;
@@ -433,7 +446,8 @@ bool launch_mma_fused(const LayerDev& L, const Workspace& ws, int T, int nt, int
   a.topk = L.topk;
   a.slab = L.slab; a.stride = L.expert_stride; a.gs_off = L.gs_off; a.us_off = L.us_off; a.ds_off = L.ds_off;
   a.D = L.D; a.F = L.F; a.hs0 = ws.hs0; a.hs1 = ws.hs1; a.ys = ws.y;
-  a.w_once = evict_first_on() ? 1 : 0;
+  a.w_once = tokb && evict_first_on() ? 1 : 0;   // gathered: an expert may have several tiles
+  a.tokb = tokb ? 1 : 0;
   a.ctr = ws.fused_ctr; a.err = err;
   a.ep_on = ep != nullptr;
   if (ep) a.ep = *ep;

@@ -611,8 +611,8 @@ bool mma_supported(const LayerDev& L) {
          L.F % 128 == 0 && mm::encoder() != nullptr;
 }
 
-void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, cudaStream_t st) {
-  if (T <= mma_tile_n(T, L.dtype)) return;   // decode: the GEMM reads the token rows directly
+void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, int nt, cudaStream_t st) {
+  if (T <= nt) return;   // decode: the GEMM reads the token rows directly
   const int E_local = L.e_end - L.e_begin, TK = T * L.topk;
   launch_pdl(mm::gather_rows_kernel, dim3(TK), dim3(128), 0, st, ws.xact, 2 * L.D, L.D, L.dtype == 2 ? 2 : 1, ws.route, E_local,
                                              L.topk, ws.xs0, ws.xs1);

@@ -668,7 +668,8 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
     xn = w.xn; xo = w.xo;
   }
   if (use_tensor_cores(L, flags)) {
-    const int nt = mma_tile_n(T, L.dtype);
+    const int fnt = fused_tile_n(L, T);                 // fused gate/up + down kernel, if used
+    const int nt = fnt ? fnt : mma_tile_n(T, L.dtype);
     // The combine runs as its own kernel: fused into the down epilogue it left
     // the last warp through each row block with T*K dependent loads at the
     // end of the kernel (measured 90 us vs 39 + 6 us). MOE_MMA_FUSE=1 restores it.
@@ -679,9 +680,9 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
     }
     const bool fuse = fuse_env && T <= kFuseCombineMaxT;
     route_tokens(L, xn, T, nt, st);
-    if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
+    if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, nt, st); });
     bool ok = true;
-    if (!fuse && fused_supported(L, T, nt)) {
+    if (!fuse && fnt) {
       timed("mma_fused", st, [&] { ok = launch_mma_fused(L, w, T, nt, g.d_err, st); });
     } else {
       timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
@@ -727,7 +728,7 @@ int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots, int*
   if (use_tensor_cores(L, 0)) {
     const int nt = mma_tile_n(T, L.dtype);
     route_tokens(L, x_norm2, T, nt, st);
-    if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
+    if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, nt, st); });
     bool ok = true;
     timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
     if (ok)
@@ -955,13 +956,14 @@ int moe_ffn_ep(int layer, const float* x_norm2, int T_local, float* x_inout, voi
   w.topk_idx = (int*)(g_ep.buf + ep.idx_off);
   w.topk_p = (float*)(g_ep.buf + ep.p_off);
   w.cap_T = std::min(g.ws.cap_T, W * g_ep.cap_tokens);     // rows the tensor maps may cover
-  const int nt = mma_tile_n(T, L.dtype);
+  const int fnt = fused_tile_n(L, T);
+  const int nt = fnt ? fnt : mma_tile_n(T, L.dtype);
   timed("route_dispatch", st, [&] {
     launch_decode_route(L, g.ws, x_norm2, T_local, nt, g.ws.route_counter, g.d_err, st, &ep);
   });
-  if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, st); });
+  if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, nt, st); });
   bool ok = true;
-  if (fused_supported(L, T, nt)) {
+  if (fnt) {
     timed("mma_fused_ep", st, [&] { ok = launch_mma_fused(L, w, T, nt, g.d_err, st, &ep); });
   } else {
     timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });

@@ -10,7 +10,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
-TS = "1,4,8,16,24,32"
+TS = "1,4,8,16,24,32,40,64,128"
 
 
 def run(tmp_path, mode):
