@@ -3,10 +3,12 @@
 // between them tracked per expert instead of per kernel.
 //
 // Units. A gate/up unit is (expert tile, 128-row block of F): 16 k-chunks of
-// 128 bytes over D, gate and up weights, B = the T token rows (decode: every
-// expert has one tile of at most NT slots, and the token rows are read as
-// they are). A down unit is (expert tile, 128-row block of D): 6 k-chunks over
-// F, B = the expert's slot rows of h written by its gate/up units.
+// 128 bytes over D, gate and up weights. Its B operand is either the T token
+// rows as they are (T <= NT: every expert has one tile of at most NT slots,
+// the epilogue reads each slot's token column), or NT-slot tiles of the
+// expert-sorted gathered rows (larger T: an expert may have several tiles).
+// A down unit is (expert tile, 128-row block of D): 6 k-chunks over F, B =
+// the tile's slot rows of h written by its gate/up units.
 //
 // Schedule. One global work counter hands out unit ids; ids [0, NG) are the
 // gate/up units, [NG, NG+ND) the down units, so every gate/up unit is claimed

@@ -67,13 +67,13 @@ __host__ __device__ constexpr int epi_warps(int nt, int dt = 8) {
 __host__ __device__ constexpr int exp_warps(int dt, int nt) { return dt == 4 ? (nt <= 32 ? MOE_Q4_EXP_DECODE : 4) : 0; }
 __host__ __device__ constexpr int cta_threads(int dt, int nt) { return (2 + epi_warps(nt, dt) + exp_warps(dt, nt)) * 32; }
 // Q4 weights are loaded as 128-byte-wide, 128B-swizzled boxes: two k-chunks
-// (256 nibbles) per row and per pipeline stage. The tensor copy engine's cost
-// goes by row segment, so 64-byte boxes (one k-chunk) halved the achievable
-// weight stream per SM.
+// (256 nibbles) per row and per pipeline stage, so one tensor copy per matrix
+// feeds two expansions and the swizzle spreads the expanders' row reads over
+// all shared-memory banks.
 constexpr int kQ4KPerStage = 2;
 // Depth of the Q4 expanded-tile ring: the expanders run this many k-chunks
-// ahead of the MMAs. Decode tiles are small, so the ring can be deep; the
-// wide prefill tiles need the shared memory for their B operands.
+// ahead of the MMAs (2 and 4 measured the same for decode; the wide prefill
+// tiles need the shared memory for their B operands).
 #ifndef MOE_Q4_ARING
 #define MOE_Q4_ARING 2
 #endif
