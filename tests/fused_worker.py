@@ -18,8 +18,9 @@ import synth as sy  # noqa: E402
 
 def main():
     out, ts = sys.argv[1], [int(v) for v in sys.argv[2].split(",")]
+    dt = int(sys.argv[3]) if len(sys.argv) > 3 else 2
     mc.init(0)
-    Ld = sy.make_layer_dev(torch, 1, 0, 128, 2048, 768, 2)
+    Ld = sy.make_layer_dev(torch, 1, 0, 128, 2048, 768, dt)
     mc.upload_layer(0, Ld, device_arrays=True)
     res = {}
     for T in ts:

@@ -1,6 +1,6 @@
 """GPU: the fused decode kernel (gate/up + down in one persistent kernel,
 per-expert dependencies, moe_fused.cu) gives the same bits as the two-kernel
-path, for every decode size it can take, and matches the oracle."""
+path, Q8 and Q4, for every decode size it can take, and matches the oracle."""
 import os
 import subprocess
 import sys
@@ -13,17 +13,18 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 TS = "1,4,8,16,24,32,40,64,128"
 
 
-def run(tmp_path, mode):
-    out = str(tmp_path / f"fused_{mode}.npz")
+def run(tmp_path, mode, dt=2):
+    out = str(tmp_path / f"fused_{mode}_{dt}.npz")
     env = dict(os.environ, MOE_FUSED=mode)
-    r = subprocess.run([sys.executable, os.path.join(HERE, "fused_worker.py"), out, TS],
+    r = subprocess.run([sys.executable, os.path.join(HERE, "fused_worker.py"), out, TS, str(dt)],
                        capture_output=True, text=True, timeout=600, env=env)
     assert r.returncode == 0, r.stderr[-3000:]
     return np.load(out)
 
 
-def test_fused_kernel_equals_two_kernel_path(tmp_path):
-    fused, split = run(tmp_path, "2"), run(tmp_path, "0")
+@pytest.mark.parametrize("dt", [2, 3])
+def test_fused_kernel_equals_two_kernel_path(tmp_path, dt):
+    fused, split = run(tmp_path, "2", dt), run(tmp_path, "0", dt)
     for T in TS.split(","):
         assert np.array_equal(fused[f"idx_{T}"], split[f"idx_{T}"]), f"T={T}: top-k differs"
         assert np.array_equal(fused[f"out_{T}"], split[f"out_{T}"]), f"T={T}: outputs differ"
