@@ -6,6 +6,9 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdlib.h>
+#include <string.h>
+#include <mutex>
+#include <unordered_map>
 #include "kernels.cuh"
 
 // Q4 decode keeps the expanded weights in tensor memory (moe_mma.cu)
@@ -32,16 +35,46 @@ static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   return fn;
 }
 
-// uint8 tensor map, 128-byte inner box with 128-byte swizzle.
+// uint8 tensor map, 128-byte inner box with 128-byte swizzle. The encoding
+// is a pure function of its arguments, and the same few maps (resident
+// weight slabs, workspace planes) recur on every call, so encodings are
+// memoised: a host call then costs no driver encode calls.
+struct MapKey {
+  const void* base; int rank, swizzle;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3];
+  bool operator==(const MapKey& o) const { return memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    const unsigned char* p = reinterpret_cast<const unsigned char*>(&k);
+    size_t h = 1469598103934665603ull;                 // FNV-1a over the key bytes
+    for (size_t i = 0; i < sizeof(MapKey); ++i) h = (h ^ p[i]) * 1099511628211ull;
+    return h;
+  }
+};
 static bool map_u8(TMap& t, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
                    const cuuint32_t* box, bool swizzle = true) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, TMap, MapKeyHash> cache;
+  MapKey k;
+  memset(&k, 0, sizeof(k));
+  k.base = base; k.rank = rank; k.swizzle = swizzle ? 1 : 0;
+  for (int i = 0; i < rank; ++i) { k.dims[i] = dims[i]; k.box[i] = box[i]; }
+  for (int i = 0; i + 1 < rank; ++i) k.strides[i] = strides[i];
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(k);
+  if (it != cache.end()) { t = it->second; return true; }
   auto fn = encoder();
   if (!fn) return false;
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = fn(&t.m, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), dims, strides, box, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  if (r != CUDA_SUCCESS) return false;
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(k, t);
+  return true;
 }
 
 // weights of one projection over all local experts: (row bytes, rows, expert),
