@@ -697,10 +697,34 @@ __global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* _
   if (q >= (long)T * D) return;
   const int t = (int)(q / D), n = (int)(q % D);
   float acc = 0.0f;
-  for (int k = 0; k < K; ++k) {
-    const int s = t * K + k;
-    if (idx[s] < 0) continue;
-    acc = fadd(acc, fmul(p[s], ys[(size_t)slot_pos[s] * D + n]));
+  constexpr int KF = 8;
+  if (K <= KF) {
+    // all slots' routing words first, then all their y values: two dependent
+    // load rounds instead of 2K; the sum keeps the k order
+    int js[KF];
+    float ps[KF], yv[KF];
+#pragma unroll
+    for (int k = 0; k < KF; ++k) {
+      js[k] = -1;
+      if (k < K) {
+        const int s = t * K + k;
+        const int e = __ldg(idx + s), j = __ldg(slot_pos + s);
+        ps[k] = __ldg(p + s);
+        js[k] = e < 0 ? -1 : j;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < KF; ++k)
+      if (js[k] >= 0) yv[k] = __ldg(ys + (size_t)js[k] * D + n);
+#pragma unroll
+    for (int k = 0; k < KF; ++k)
+      if (js[k] >= 0) acc = fadd(acc, fmul(ps[k], yv[k]));
+  } else {
+    for (int k = 0; k < K; ++k) {
+      const int s = t * K + k;
+      if (idx[s] < 0) continue;
+      acc = fadd(acc, fmul(p[s], ys[(size_t)slot_pos[s] * D + n]));
+    }
   }
   out[q] = fadd(xres[q], acc);
   MOE_TL_END(kTlCombine);
