@@ -23,6 +23,21 @@ __device__ __forceinline__ float silu_ref(float v) {
   return fdiv(v, fadd(1.0f, exp_f32(-v)));
 }
 
+// (float)d / S, IEEE round-to-nearest, for an int32 d and the quantisation
+// divisors S = 127 (Q8) and 7 (Q4), as the reference's ((float)dot / 127f)
+// (kernels.c:71 / :126). Markstein's correction of the reciprocal product: with
+// r = RN(1/S), q0 = RN(x r), the remainder x - q0 S is exact under FMA and
+// RN(q0 + rem r) is the correctly rounded quotient. Checked against IEEE
+// division for every one of the 2^32 inputs and both divisors
+// (tests/divide_check.c). One multiply and two FMAs instead of a divide.
+__device__ __forceinline__ float div_qscale(int d, bool q8) {
+  const float S = q8 ? 127.0f : 7.0f;
+  const float r = q8 ? 0x1.020408p-7f : 0x1.24924ap-3f;   // RN(1/127), RN(1/7)
+  const float x = __int2float_rn(d);
+  const float q0 = __fmul_rn(x, r);
+  return __fmaf_rn(__fmaf_rn(-q0, S, x), r, q0);
+}
+
 // (int32_t)(a * scale) — kernels.c:66 / :113, truncation toward zero.
 // Returns INT32_MIN for NaN (x86 cvttss2si gives the same "indefinite" value).
 __device__ __forceinline__ int trunc_scale(float a, float scale) {

@@ -72,9 +72,8 @@ __device__ __forceinline__ int group_sum(int v) {
 // ((float)dot / S) * s — kernels.c:71 / :126
 template <int DT>
 __device__ __forceinline__ float dequant_out(int dot, int asum, float s) {
-  constexpr float S = DT == 8 ? 127.0f : 7.0f;
   if (DT == 4) dot = (int)((unsigned)dot - 8u * (unsigned)asum);
-  return fmul(fdiv(__int2float_rn(dot), S), s);
+  return fmul(div_qscale(dot, DT == 8), s);
 }
 
 // --------------------------------------------------------------------------
@@ -731,7 +730,7 @@ __global__ void gemv_generic_kernel(const float* __restrict__ A, const uint8_t* 
   if (DT == 8) {
     const int8_t* w = reinterpret_cast<const int8_t*>(Wq) + (size_t)n * K;
     for (int k = 0; k < K; ++k) acc += (unsigned)(trunc_scale(__ldg(a + k), 127.0f) * (int)w[k]);
-    C[c] = fmul(fdiv(__int2float_rn((int)acc), 127.0f), __ldg(Ws + n));
+    C[c] = fmul(div_qscale((int)acc, true), __ldg(Ws + n));
   } else {
     const uint8_t* w = Wq + (size_t)n * (K / 2);
     for (int k = 0; k < K; k += 2) {
@@ -739,7 +738,7 @@ __global__ void gemv_generic_kernel(const float* __restrict__ A, const uint8_t* 
       acc += (unsigned)(trunc_scale(__ldg(a + k), 7.0f) * ((int)(b & 0xF) - 8));
       acc += (unsigned)(trunc_scale(__ldg(a + k + 1), 7.0f) * ((int)(b >> 4) - 8));
     }
-    C[c] = fmul(fdiv(__int2float_rn((int)acc), 7.0f), __ldg(Ws + n));
+    C[c] = fmul(div_qscale((int)acc, false), __ldg(Ws + n));
   }
 }
 

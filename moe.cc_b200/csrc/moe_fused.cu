@@ -437,8 +437,8 @@ __global__ void __launch_bounds__(threads(DT), 2)
             dg = (int)(raw[0] + (raw[1] << 8));
             du = (int)(raw[2] + (raw[3] << 8));
           }
-          const float gv = fmul(fdiv(__int2float_rn(dg), S), sg);
-          const float uv = fmul(fdiv(__int2float_rn(du), S), su);
+          const float gv = fmul(div_qscale(dg, !Q4), sg);
+          const float uv = fmul(div_qscale(du, !Q4), su);
           const int ha = trunc_scale(fmul(silu_ref(gv), uv), S);
           if (Q4) {
             if (ha < -128 || ha > 127) atomicOr(a.err, kErrRange);
@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(threads(DT), 2)
             // Q4: the down nibbles are stored +8: subtract 8 * Σ h of the slot
             // (complete: all the tile's gate/up units finished before this claim)
             const int dot = Q4 ? (int)(v0[i] - 8u * (unsigned)__ldcg(a.hsum + j)) : (int)(v0[i] + (v1[i] << 8));
-            const float yv = fmul(fdiv(__int2float_rn(dot), S), sd);
+            const float yv = fmul(div_qscale(dot, !Q4), sd);
             if (a.ep_on) {
               const int sl = __ldg(slots + j), per = a.topk * a.ep.T_local, owner = sl / per;
               float* yo = reinterpret_cast<float*>(

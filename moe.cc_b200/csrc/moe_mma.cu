@@ -412,8 +412,8 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
           for (int m = 0; m < NM; ++m) dot[m] = (int)((unsigned)dot[m] - 8u * (unsigned)as);
         }
         if (MODE == GATEUP) {
-          const float g = fmul(fdiv(__int2float_rn(dot[0]), S), sc0);
-          const float uu = fmul(fdiv(__int2float_rn(dot[NM - 1]), S), sc1);
+          const float g = fmul(div_qscale(dot[0], DT == 8), sc0);
+          const float uu = fmul(div_qscale(dot[NM - 1], DT == 8), sc1);
           const float h = fmul(silu_ref(g), uu);
           const int ha = trunc_scale(h, S);
           if (DT == 8) {
@@ -428,7 +428,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
             if (lane == 0) atomicAdd(a.hsum + j, ws);
           }
         } else {
-          const float yv = fmul(fdiv(__int2float_rn(dot[0]), S), sc0);
+          const float yv = fmul(div_qscale(dot[0], DT == 8), sc0);
           if (a.ep_on) {
             // expert parallel: the row goes straight to the rank owning the
             // slot's token, into its y buffer, over NVLink

@@ -59,7 +59,7 @@ __global__ void exact_fixup_kernel(const int* __restrict__ flag, const float* __
   if (DT == 8) {
     const int8_t* w = reinterpret_cast<const int8_t*>(Wq) + (size_t)n * K;
     for (int k = 0; k < K; ++k) acc += (unsigned)(trunc_scale(a[k], 127.0f) * (int)w[k]);
-    C[c] = fmul(fdiv(__int2float_rn((int)acc), 127.0f), Ws[n]);
+    C[c] = fmul(div_qscale((int)acc, true), Ws[n]);
   } else {
     const uint8_t* w = Wq + (size_t)n * (K / 2);
     for (int k = 0; k < K; k += 2) {
@@ -67,7 +67,7 @@ __global__ void exact_fixup_kernel(const int* __restrict__ flag, const float* __
       acc += (unsigned)(trunc_scale(a[k], 7.0f) * ((int)(b & 0xF) - 8));
       acc += (unsigned)(trunc_scale(a[k + 1], 7.0f) * ((int)(b >> 4) - 8));
     }
-    C[c] = fmul(fdiv(__int2float_rn((int)acc), 7.0f), Ws[n]);
+    C[c] = fmul(div_qscale((int)acc, false), Ws[n]);
   }
 }
 
