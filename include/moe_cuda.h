@@ -159,6 +159,30 @@ int moe_cuda_free_layer(int layer);
 /* Bytes of device memory the layer's expert slabs occupy on this rank. */
 size_t moe_cuda_layer_bytes(int layer);
 
+/* ---- weight files -------------------------------------------------------------
+ * The reference's .bin weight file (export.py _save_tensor, :8-21; read by
+ * io.c:193-285 and model.h:212-305): magic "QW3W\0\1", a u32 count, then
+ * records (u32 name length, name, u32 dtype, u32 ndim, u32 shape[ndim], data).
+ *
+ * moe_bin_layer_info: the MoE shape of layer src_layer of the file (E experts,
+ * hidden D, expert width F, dtype 2 = Q8 / 3 = Q4, has_bias 1 when an f32
+ * model.layers.L.mlp.gate.bias is present). Host only: needs no GPU and no
+ * moe_cuda_init. Any output pointer may be NULL.
+ *
+ * moe_cuda_load_bin_layer: reads layer src_layer's router (and bias) and this
+ * rank's experts from the file and makes them resident as `layer`, as
+ * moe_cuda_upload_layer does (replaces load_model_weights' per-layer MoE part,
+ * model.h:212-305, for a caller that hands the layer to moe_ffn). Only the
+ * record headers of the rest of the file are read. No host pointers are
+ * registered for the matmul_* drop-ins.
+ *
+ * Both return MOE_ERR_INVALID for a malformed or truncated file, a missing
+ * tensor or a shape/dtype mismatch (the reference exits the process),
+ * MOE_ERR_UNSUPPORTED for unquantised (f32) experts. */
+int moe_bin_layer_info(const char* path, int src_layer, int* E, int* D, int* F,
+                       int* dtype, int* has_bias);
+int moe_cuda_load_bin_layer(const char* path, int src_layer, int layer);
+
 /* ---- fused MoE block --------------------------------------------------------
  * Replaces test_model_trace.c:463-517 (router matmul + bias, topk_desc,
  * top-k softmax, per-(token,k) gate/up/SiLU·up/down, k-ordered weighted

@@ -438,6 +438,9 @@ namespace moe {
 static int validate_layer(const QuantizedWeight* Wg, const QuantizedWeight* Wu,
                           const QuantizedWeight* Wd, int E, int* D, int* F, int* dtype) {
   if (E <= 0 || !Wg || !Wu || !Wd) return set_err(MOE_ERR_INVALID, "empty layer (E=%d)", E);
+  // the router keeps the top 8 (test_model_trace.c:475-478, top_k fixed at 8
+  // by model.h:160)
+  if (E < 8) return set_err(MOE_ERR_UNSUPPORTED, "top-8 routing needs at least 8 experts (E=%d)", E);
   *dtype = Wg[0].dtype; *F = Wg[0].rows; *D = Wg[0].cols;
   if (*dtype != MOE_DTYPE_Q8 && *dtype != MOE_DTYPE_Q4)
     return set_err(MOE_ERR_UNSUPPORTED, "expert dtype %d (only Q8=2 / Q4=3)", *dtype);
@@ -456,9 +459,11 @@ static int validate_layer(const QuantizedWeight* Wg, const QuantizedWeight* Wu,
   return MOE_OK;
 }
 
+// register_alias: remember the host q/s pointers for the matmul_* drop-ins
+// (not for staging memory the caller frees right after the upload)
 static int upload_layer(int layer, const QuantizedWeight* Wg, const QuantizedWeight* Wu,
                         const QuantizedWeight* Wd, const float* router_w, const float* router_b,
-                        int E, cudaMemcpyKind kind) {
+                        int E, cudaMemcpyKind kind, bool register_alias = true) {
   int rc = ensure_init();
   if (rc) return rc;
   int D, F, dtype;
@@ -502,10 +507,11 @@ static int upload_layer(int layer, const QuantizedWeight* Wg, const QuantizedWei
         {Wd[e].s, L.ds_off, sizeof(float) * D}};
     for (const Part& p : parts) {
       CU(cudaMemcpy(base + p.off, p.src, p.bytes, kind));
-      if (kind == cudaMemcpyHostToDevice) g.alias[p.src] = Alias{base + p.off, p.bytes};
+      if (kind == cudaMemcpyHostToDevice && register_alias) g.alias[p.src] = Alias{base + p.off, p.bytes};
     }
   }
-  if (kind == cudaMemcpyHostToDevice) g.alias[router_w] = Alias{L.router_w, sizeof(float) * (size_t)E * D};
+  if (kind == cudaMemcpyHostToDevice && register_alias)
+    g.alias[router_w] = Alias{L.router_w, sizeof(float) * (size_t)E * D};
   return MOE_OK;
 }
 
@@ -601,6 +607,22 @@ static bool use_tensor_cores(const LayerDev& L, int flags) {
 
 // Tokens at or below this count use the fused down+combine epilogue.
 constexpr int kFuseCombineMaxT = 64;
+
+// Experts [*begin, *end) of E that this rank holds (all of them without
+// expert parallelism).
+void local_expert_range(int E, int* begin, int* end) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  *begin = (int)((long)E * g.ep_rank / g.ep_world);
+  *end = (int)((long)E * (g.ep_rank + 1) / g.ep_world);
+}
+
+// Upload from host staging memory the caller frees right after (the .bin
+// loader): no host-pointer aliases are registered for it.
+int upload_layer_staged(int layer, const QuantizedWeight* Wg, const QuantizedWeight* Wu,
+                        const QuantizedWeight* Wd, const float* router_w, const float* router_b, int E) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  return upload_layer(layer, Wg, Wu, Wd, router_w, router_b, E, cudaMemcpyHostToDevice, false);
+}
 
 }  // namespace moe
 

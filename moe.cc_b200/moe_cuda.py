@@ -34,6 +34,7 @@ EXPORTS = (
     "moe_synth_normal_host", "moe_synth_normal_dev",
     "moe_cuda_profile", "moe_cuda_profile_read", "moe_matmul_q_dev_noalloc",
     "moe_cuda_ep_setup", "moe_cuda_ep_connect", "moe_ffn_ep",
+    "moe_bin_layer_info", "moe_cuda_load_bin_layer",
 )
 
 
@@ -86,6 +87,8 @@ def lib():
             "moe_cuda_ep_setup": ([i, i, i, vp], i),
             "moe_cuda_ep_connect": ([vp], i),
             "moe_ffn_ep": ([i, vp, i, vp, vp], i),
+            "moe_bin_layer_info": ([C.c_char_p, i, vp, vp, vp, vp, vp], i),
+            "moe_cuda_load_bin_layer": ([C.c_char_p, i, i], i),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -206,6 +209,18 @@ def upload_layer(layer, L, device_arrays=False):
     fn = lib().moe_cuda_upload_layer_dev if device_arrays else lib().moe_cuda_upload_layer
     check(fn(layer, C.addressof(g), C.addressof(u), C.addressof(d), _p(L["router_w"]),
              _p(L.get("router_b")), E))
+
+
+def bin_layer_info(path, src_layer):
+    """(E, D, F, dtype, has_bias) of one layer of a .bin weight file."""
+    v = [C.c_int(0) for _ in range(5)]
+    check(lib().moe_bin_layer_info(os.fsencode(path), src_layer, *[C.byref(x) for x in v]))
+    return tuple(x.value for x in v)
+
+
+def load_bin_layer(path, src_layer, layer):
+    """Makes layer `src_layer` of a .bin weight file resident as `layer`."""
+    check(lib().moe_cuda_load_bin_layer(os.fsencode(path), src_layer, layer))
 
 
 def free_layer(layer):

@@ -12,6 +12,12 @@ Run in a container where the reference sources are present (default
   small ragged shapes.
 * moe_small.npz — the reference's layer_forward_f32 MoE block
   (test_model_trace.c:463-517, via oracle/ref_shim.c) on a small seeded layer.
+* layer_ref.bin — a tiny weight file written by the reference's own writer
+  (export.MAGIC, export._save_tensor, export._rowwise_q8/_q4): two MoE
+  layers (Q8 at index 1, Q4 with a router bias at index 3, router under the
+  mlp.router.gate.weight name), a norm weight and a repeated name. Pins the
+  tests' .bin writer (byte for byte) and the loader's parse.
+  `python tests/golden/make_golden.py bin` writes only this file.
 
 Inputs come from the counter-based normal stream moe_synth_normal_host of
 libmoe_cuda.so (host code, no GPU needed), so tests can rebuild them.
@@ -48,6 +54,10 @@ def main():
     sys.path.insert(0, REF_DIR)
     import torch
     import export  # the reference's exporter (its quantisers)
+    bin_fixture(torch, export)
+    if sys.argv[1:] == ["bin"]:
+        print("layer_ref.bin written to", OUT)
+        return
     from oracle.oracle import Ref
 
     ref = Ref()
@@ -87,6 +97,34 @@ def main():
                   f"idx_{dt}": idx, f"p_{dt}": p})
     np.savez(os.path.join(OUT, "moe_small.npz"), **m)
     print("golden fixtures written to", OUT)
+
+
+def bin_fixture(torch, export):
+    """layer_ref.bin through the reference's writer (export.py:188-206)."""
+    import struct
+    recs = [("model.norm.weight", torch.from_numpy(synth(60, 32, 1.0)))]
+    for layer, dt, fn, bias, rname in ((1, 2, export._rowwise_q8, False, "mlp.gate.weight"),
+                                        (3, 3, export._rowwise_q4, True, "mlp.router.gate.weight")):
+        E, D, F = 3, 32, 16
+        pre = f"model.layers.{layer}."
+        recs.append((pre + rname, torch.from_numpy(synth(61 + layer, E * D, 0.02).reshape(E, D))))
+        if bias:
+            recs.append((pre + "mlp.gate.bias", torch.from_numpy(synth(62 + layer, E, 1.0))))
+        q = "q8" if dt == 2 else "q4"
+        for e in range(E):
+            for j, (proj, rows, cols) in enumerate((("gate_proj", F, D), ("up_proj", F, D),
+                                                    ("down_proj", D, F))):
+                w = torch.from_numpy(synth(700 + 10 * layer + 3 * e + j, rows * cols, 0.02).reshape(rows, cols))
+                s, qq = fn(w)
+                base = f"{pre}mlp.experts.{e}.{proj}.weight"
+                recs += [(base + ".scale", s), (base + "." + q, qq)]
+    # a repeated name: the reader keeps the first record (io.c:333-338)
+    recs.append(("model.norm.weight", torch.zeros(32)))
+    with open(os.path.join(OUT, "layer_ref.bin"), "wb") as f:
+        f.write(export.MAGIC)
+        f.write(struct.pack("<I", len(recs)))
+        for name, t in recs:
+            export._save_tensor(f, name, t)
 
 
 def small_layer(E, D, F, dt, bias, quant, torch=None):

@@ -48,3 +48,42 @@ def layer_to_numpy(Ld):
     for k, v in Ld.items():
         out[k] = v.cpu().numpy() if hasattr(v, "cpu") else v
     return out
+
+
+# ---- the reference's .bin weight file (export.py _save_tensor, :8-21) ----
+BIN_MAGIC = b"QW3W\x00\x01"
+_BIN_DTYPE = {np.dtype(np.float32): 0, np.dtype(np.float16): 1,
+              np.dtype(np.int8): 2, np.dtype(np.uint8): 3}
+
+
+def write_bin(path, tensors, count=None):
+    """Writes (name, ndarray) records in the .bin layout; pinned byte for byte
+    to the reference's writer by tests/golden/layer_ref.bin."""
+    import struct
+    with open(path, "wb") as f:
+        f.write(BIN_MAGIC)
+        f.write(struct.pack("<I", len(tensors) if count is None else count))
+        for name, a in tensors:
+            a = np.ascontiguousarray(a)
+            nb = name.encode()
+            f.write(struct.pack("<I", len(nb)) + nb)
+            f.write(struct.pack("<II", _BIN_DTYPE[a.dtype], a.ndim))
+            f.write(struct.pack("<" + "I" * a.ndim, *a.shape))
+            f.write(a.tobytes())
+
+
+def layer_records(L, layer, router_name="mlp.gate.weight"):
+    """One quantised MoE layer as .bin records, in the exporter's order
+    (router, bias, then per projection .scale before .q8/.q4, export.py:197-206)."""
+    q = "q8" if L["dtype"] == 2 else "q4"
+    pre = f"model.layers.{layer}."
+    recs = [(pre + router_name, np.asarray(L["router_w"], np.float32))]
+    if L.get("router_b") is not None:
+        recs.append((pre + "mlp.gate.bias", np.asarray(L["router_b"], np.float32)))
+    E = L["router_w"].shape[0]
+    for e in range(E):
+        for nm, proj in (("g", "gate_proj"), ("u", "up_proj"), ("d", "down_proj")):
+            base = f"{pre}mlp.experts.{e}.{proj}.weight"
+            recs.append((base + ".scale", np.asarray(L[nm + "s"][e], np.float32)))
+            recs.append((base + "." + q, L[nm + "q"][e]))
+    return recs

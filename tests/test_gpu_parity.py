@@ -244,3 +244,47 @@ def test_moe_ffn_empty_and_errors(gpu):
     gpu.check(gpu.lib().moe_ffn(lid, x.ctypes.data, x.ctypes.data, 0, None, None, gpu.HOST_PTRS, None))
     with pytest.raises(gpu.MoeError):
         gpu.moe_ffn_host(9999, np.zeros((1, 2048), np.float32), np.zeros((1, 2048), np.float32))
+
+
+# ---- .bin weight file straight into residency (model.h:212-305) -----------------
+
+@pytest.mark.parametrize("dt", [2, 3])
+def test_load_bin_layer_matches_reference_golden(gpu, dt, tmp_path):
+    """The golden layer written as a .bin (the writer is pinned to export.py's
+    bytes), loaded by moe_cuda_load_bin_layer: same output as the reference's
+    layer_forward_f32, and as the same layer through moe_cuda_upload_layer."""
+    from helpers import layer_records, write_bin
+    g = np.load(os.path.join(GOLDEN, "moe_small.npz"))
+    L = small_layer(16, 256, 64, dt, bias=(dt == 3))
+    decoy = small_layer(16, 256, 64, dt, bias=False, seed_base=5)
+    path = str(tmp_path / "w.bin")
+    write_bin(path, layer_records(decoy, 6) + layer_records(L, 7) + layer_records(decoy, 8))
+    assert gpu.bin_layer_info(path, 7) == (16, 256, 64, dt, int(dt == 3))
+    gpu.load_bin_layer(path, 7, 200 + dt)
+    xo, idx, p = gpu.moe_ffn_host(200 + dt, g[f"xn_{dt}"], g[f"x_{dt}"])
+    assert np.array_equal(idx, g[f"idx_{dt}"])
+    assert np.array_equal(xo, g[f"xo_{dt}"])
+    assert np.array_equal(p, g[f"p_{dt}"])
+    gpu.upload_layer(300 + dt, L)
+    assert gpu.layer_bytes(200 + dt) == gpu.layer_bytes(300 + dt)
+    x = synth(77, 24 * 256, 1.0).reshape(24, 256)
+    xa = synth(78, 24 * 256, 1.0).reshape(24, 256)
+    a = gpu.moe_ffn_host(200 + dt, x, xa)
+    b = gpu.moe_ffn_host(300 + dt, x, xa)
+    for u, v in zip(a, b):
+        assert np.array_equal(u, v)
+    gpu.free_layer(200 + dt)
+    gpu.free_layer(300 + dt)
+
+
+def test_load_bin_layer_errors(gpu):
+    ref = os.path.join(GOLDEN, "layer_ref.bin")
+    with pytest.raises(gpu.MoeError) as ei:
+        gpu.load_bin_layer(ref, 0, 210)                  # no such layer in the file
+    assert ei.value.code == gpu.MOE_ERR_INVALID
+    with pytest.raises(gpu.MoeError) as ei:
+        gpu.load_bin_layer(ref, 3, 210)                  # 3 experts (and Q4 rows of 8 bytes)
+    assert ei.value.code == gpu.MOE_ERR_UNSUPPORTED
+    with pytest.raises(gpu.MoeError) as ei:
+        gpu.load_bin_layer(ref, 1, 211)                  # 3 experts: fewer than the top 8
+    assert ei.value.code == gpu.MOE_ERR_UNSUPPORTED
