@@ -20,7 +20,8 @@
 // Unlike the reference's loader, which mallocs and reads every tensor of the
 // file, this one walks the record headers once (seeking past the data) into a
 // name index, then reads only the requested layer's router and this rank's
-// experts into one staging buffer, uploads it and frees it. Malformed files
+// experts, each straight into a pinned slab image whose host-to-device copy
+// overlaps the read of the next expert. Malformed files
 // and missing tensors return MOE_ERR_INVALID with a message where the
 // reference exits the process.
 #include <stdarg.h>
@@ -35,13 +36,13 @@
 #include <vector>
 
 #include "../../include/moe_cuda.h"
+#include "kernels.cuh"
 
 namespace moe {
 int set_error_message(int code, const char* msg);                       // runtime.cu
-void local_expert_range(int E, int* begin, int* end);                    // runtime.cu
-int upload_layer_staged(int layer, const QuantizedWeight* Wg, const QuantizedWeight* Wu,
-                        const QuantizedWeight* Wd, const float* router_w, const float* router_b,
-                        int E);                                          // runtime.cu
+int upload_layer_streamed(int layer, const QuantizedWeight* Wg, const QuantizedWeight* Wu,
+                          const QuantizedWeight* Wd, const float* router_w, const float* router_b, int E,
+                          const ExpertReader& reader);                    // runtime.cu
 
 namespace {
 
@@ -224,59 +225,48 @@ int moe_bin_layer_info(const char* path, int src_layer, int* E, int* D, int* F, 
 }
 
 int moe_cuda_load_bin_layer(const char* path, int src_layer, int layer) {
-  FILE* f = nullptr;
-  BinIndex ix;
-  LayerRecs lr;
-  int rc = open_and_resolve(path, src_layer, &f, ix, lr);
+  struct Ctx {
+    FILE* f = nullptr;
+    BinIndex ix;
+    LayerRecs lr;
+    const char* path = nullptr;
+    ~Ctx() { if (f) fclose(f); }
+  } c;
+  c.path = path;
+  int rc = open_and_resolve(path, src_layer, &c.f, c.ix, c.lr);
   if (rc) return rc;
-  int eb = 0, ee = 0;
-  local_expert_range(lr.E, &eb, &ee);
-  // staging: router, bias, then this rank's experts (q and s of each projection)
-  size_t total = lr.router->bytes + (lr.bias ? lr.bias->bytes : 0);
-  for (int e = eb; e < ee; ++e)
-    for (int p = 0; p < 3; ++p) total += lr.q[p][e]->bytes + lr.s[p][e]->bytes;
-  std::vector<unsigned char> stage;
-  try { stage.resize(total); } catch (...) {
-    fclose(f);
-    return fail(MOE_ERR_NOMEM, "%s: %zu bytes of host staging", path, total);
-  }
-  unsigned char* cur = stage.data();
-  auto take = [&](const Rec* r) -> void* {
-    if (!read_at(f, r, cur)) return nullptr;
-    void* p = cur;
-    cur += r->bytes;
-    return p;
-  };
-  const float* router_w = (const float*)take(lr.router);
-  const float* router_b = lr.bias ? (const float*)take(lr.bias) : nullptr;
-  if (!router_w || (lr.bias && !router_b)) {
-    fclose(f);
+  const LayerRecs& lr = c.lr;
+  std::vector<unsigned char> router(lr.router->bytes + (lr.bias ? lr.bias->bytes : 0));
+  if (!read_at(c.f, lr.router, router.data()) || (lr.bias && !read_at(c.f, lr.bias, router.data() + lr.router->bytes)))
     return fail(MOE_ERR_INVALID, "%s: read of the layer %d router failed", path, src_layer);
-  }
-  // experts outside [eb, ee) are never copied; their entries carry the
-  // shapes with a placeholder pointer
+  // the experts' q/s pointers are placeholders (shapes only): the slab
+  // images come from `fill`, read straight into pinned staging
   static const float placeholder[1] = {0.0f};
   std::vector<QuantizedWeight> W[3];
   for (int p = 0; p < 3; ++p) {
     W[p].resize(lr.E);
-    for (int e = 0; e < lr.E; ++e) {
-      QuantizedWeight& w = W[p][e];
+    for (QuantizedWeight& w : W[p]) {
       w.rows = p < 2 ? lr.F : lr.D;
       w.cols = p < 2 ? lr.D : lr.F;
       w.dtype = lr.dtype;
       w.q = (const int8_t*)placeholder;
       w.s = placeholder;
-      if (e < eb || e >= ee) continue;
-      w.q = (const int8_t*)take(lr.q[p][e]);
-      w.s = (const float*)take(lr.s[p][e]);
-      if (!w.q || !w.s) {
-        fclose(f);
-        return fail(MOE_ERR_INVALID, "%s: read of expert %d failed", path, e);
-      }
     }
   }
-  fclose(f);
-  return upload_layer_staged(layer, W[0].data(), W[1].data(), W[2].data(), router_w, router_b, lr.E);
+  ExpertReader rd;
+  rd.ctx = &c;
+  rd.fill = [](void* ctx, int e, const LayerDev& L, uint8_t* img) -> bool {
+    Ctx& c = *static_cast<Ctx*>(ctx);
+    const size_t qoff[3] = {L.gq_off, L.uq_off, L.dq_off}, soff[3] = {L.gs_off, L.us_off, L.ds_off};
+    for (int p = 0; p < 3; ++p)
+      if (!read_at(c.f, c.lr.q[p][e], img + qoff[p]) || !read_at(c.f, c.lr.s[p][e], img + soff[p])) {
+        fail(MOE_ERR_INVALID, "%s: read of expert %d failed", c.path, e);
+        return false;
+      }
+    return true;
+  };
+  return upload_layer_streamed(layer, W[0].data(), W[1].data(), W[2].data(), (const float*)router.data(),
+                               lr.bias ? (const float*)(router.data() + lr.router->bytes) : nullptr, lr.E, rd);
 }
 
 }  // extern "C"

@@ -21,6 +21,15 @@ struct LayerDev {
   size_t bytes = 0;
 };
 
+// Source of one local expert's slab image for a streamed upload: fill writes
+// the six parts at the LayerDev offsets (gq_off .. ds_off) into `img`
+// (expert_stride bytes of host memory) and returns false on a read error,
+// after setting the library's error message.
+struct ExpertReader {
+  bool (*fill)(void* ctx, int e, const LayerDev& L, uint8_t* img);
+  void* ctx;
+};
+
 // Per-call scratch of moe_ffn (capacity for up to cap_T tokens).
 struct Workspace {
   int cap_T = 0, cap_D = 0, cap_E = 0, cap_F = 0, cap_K = 0;

@@ -459,11 +459,31 @@ static int validate_layer(const QuantizedWeight* Wg, const QuantizedWeight* Wu,
   return MOE_OK;
 }
 
+// Pinned staging for streamed uploads: two expert-slab images, filled on the
+// host while the other one's copy runs; released after the stream drains.
+struct PinnedRing {
+  uint8_t* buf[2] = {nullptr, nullptr};
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  cudaStream_t st = nullptr;
+  ~PinnedRing() {
+    if (st) cudaStreamSynchronize(st);
+    for (int i = 0; i < 2; ++i) {
+      if (buf[i]) cudaFreeHost(buf[i]);
+      if (ev[i]) cudaEventDestroy(ev[i]);
+    }
+    if (st) cudaStreamDestroy(st);
+  }
+};
+
 // register_alias: remember the host q/s pointers for the matmul_* drop-ins
-// (not for staging memory the caller frees right after the upload)
+// (not for staging memory the caller frees right after the upload).
+// reader: when set, the experts' q/s pointers are placeholders and each local
+// expert's slab image is produced by reader->fill into pinned memory instead,
+// double-buffered against its host-to-device copy.
 static int upload_layer(int layer, const QuantizedWeight* Wg, const QuantizedWeight* Wu,
                         const QuantizedWeight* Wd, const float* router_w, const float* router_b,
-                        int E, cudaMemcpyKind kind, bool register_alias = true) {
+                        int E, cudaMemcpyKind kind, bool register_alias = true,
+                        const ExpertReader* reader = nullptr) {
   int rc = ensure_init();
   if (rc) return rc;
   int D, F, dtype;
@@ -499,6 +519,29 @@ static int upload_layer(int layer, const QuantizedWeight* Wg, const QuantizedWei
   g.layers[layer] = L;  // registered before the copies so free_layer cleans up on error
   CU(cudaMemcpy(L.router_w, router_w, sizeof(float) * (size_t)E * D, kind));
   if (router_b) CU(cudaMemcpy(L.router_b, router_b, sizeof(float) * E, kind));
+  if (reader) {
+    PinnedRing ring;
+    CU(cudaStreamCreateWithFlags(&ring.st, cudaStreamNonBlocking));
+    for (int i = 0; i < 2 && i < El; ++i) {
+      CU(cudaHostAlloc((void**)&ring.buf[i], L.expert_stride, cudaHostAllocDefault));
+      memset(ring.buf[i], 0, L.expert_stride);     // alignment padding stays zero
+      CU(cudaEventCreateWithFlags(&ring.ev[i], cudaEventDisableTiming));
+    }
+    for (int e = L.e_begin; e < L.e_end; ++e) {
+      const int i = (e - L.e_begin) & 1;
+      if (e - L.e_begin >= 2) CU(cudaEventSynchronize(ring.ev[i]));
+      if (!reader->fill(reader->ctx, e, L, ring.buf[i])) {
+        cudaStreamSynchronize(ring.st);
+        moe_cuda_free_layer(layer);
+        return MOE_ERR_INVALID;                      // the reader set the message
+      }
+      CU(cudaMemcpyAsync(L.slab + (size_t)(e - L.e_begin) * L.expert_stride, ring.buf[i], L.expert_stride,
+                         cudaMemcpyHostToDevice, ring.st));
+      CU(cudaEventRecord(ring.ev[i], ring.st));
+    }
+    CU(cudaStreamSynchronize(ring.st));
+    return MOE_OK;
+  }
   for (int e = L.e_begin; e < L.e_end; ++e) {
     uint8_t* base = L.slab + (size_t)(e - L.e_begin) * L.expert_stride;
     struct Part { const void* src; size_t off, bytes; } parts[6] = {
@@ -608,20 +651,14 @@ static bool use_tensor_cores(const LayerDev& L, int flags) {
 // Tokens at or below this count use the fused down+combine epilogue.
 constexpr int kFuseCombineMaxT = 64;
 
-// Experts [*begin, *end) of E that this rank holds (all of them without
-// expert parallelism).
-void local_expert_range(int E, int* begin, int* end) {
+// Upload whose experts come from a reader (the .bin loader); router_w and
+// router_b are host memory the caller frees right after, so no host-pointer
+// aliases are registered.
+int upload_layer_streamed(int layer, const QuantizedWeight* Wg, const QuantizedWeight* Wu,
+                          const QuantizedWeight* Wd, const float* router_w, const float* router_b, int E,
+                          const ExpertReader& reader) {
   std::lock_guard<std::recursive_mutex> lk(g.mu);
-  *begin = (int)((long)E * g.ep_rank / g.ep_world);
-  *end = (int)((long)E * (g.ep_rank + 1) / g.ep_world);
-}
-
-// Upload from host staging memory the caller frees right after (the .bin
-// loader): no host-pointer aliases are registered for it.
-int upload_layer_staged(int layer, const QuantizedWeight* Wg, const QuantizedWeight* Wu,
-                        const QuantizedWeight* Wd, const float* router_w, const float* router_b, int E) {
-  std::lock_guard<std::recursive_mutex> lk(g.mu);
-  return upload_layer(layer, Wg, Wu, Wd, router_w, router_b, E, cudaMemcpyHostToDevice, false);
+  return upload_layer(layer, Wg, Wu, Wd, router_w, router_b, E, cudaMemcpyHostToDevice, false, &reader);
 }
 
 }  // namespace moe

@@ -288,3 +288,30 @@ def test_load_bin_layer_errors(gpu):
     with pytest.raises(gpu.MoeError) as ei:
         gpu.load_bin_layer(ref, 1, 211)                  # 3 experts: fewer than the top 8
     assert ei.value.code == gpu.MOE_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("dt", [2, 3])
+def test_load_bin_layer_qwen_shape(gpu, dt, tmp_path):
+    """A Qwen3-shaped layer (D=2048, F=768, 32 experts) streamed from a .bin:
+    resident bytes and moe_ffn outputs (tensor-core / fused paths, T=16 and
+    T=96) identical to the same layer through moe_cuda_upload_layer."""
+    import time
+    from helpers import layer_records, write_bin
+    L = small_layer(32, 2048, 768, dt, bias=True, seed_base=3)
+    path = str(tmp_path / "q.bin")
+    write_bin(path, layer_records(L, 0))
+    t0 = time.perf_counter()
+    gpu.load_bin_layer(path, 0, 220 + dt)
+    dt_s = time.perf_counter() - t0
+    print(f"load_bin_layer dtype {dt}: {os.path.getsize(path) / dt_s / 1e9:.2f} GB/s of file")
+    gpu.upload_layer(320 + dt, L)
+    assert gpu.layer_bytes(220 + dt) == gpu.layer_bytes(320 + dt)
+    for T in (16, 96):
+        x = synth(80 + T, T * 2048, 1.0).reshape(T, 2048)
+        xa = synth(81 + T, T * 2048, 1.0).reshape(T, 2048)
+        a = gpu.moe_ffn_host(220 + dt, x, xa)
+        b = gpu.moe_ffn_host(320 + dt, x, xa)
+        for u, v in zip(a, b):
+            assert np.array_equal(u, v)
+    gpu.free_layer(220 + dt)
+    gpu.free_layer(320 + dt)
