@@ -183,6 +183,23 @@ int moe_bin_layer_info(const char* path, int src_layer, int* E, int* D, int* F,
                        int* dtype, int* has_bias);
 int moe_cuda_load_bin_layer(const char* path, int src_layer, int layer);
 
+/* The same over an open file, indexed once (bin_load / bin_find, io.h:20-22,
+ * without reading the data). moe_bin_open returns NULL on error (message in
+ * moe_cuda_last_error). moe_bin_find gives a record's dtype (0 f32, 1 f16,
+ * 2 i8, 3 packed i4), ndim, shape (up to 8 entries) and data bytes;
+ * moe_bin_read copies its data into dst (nbytes must equal the record's).
+ * A repeated name resolves to its first record. A handle may be shared by
+ * threads (reads are serialised). */
+typedef struct MoeBin MoeBin;
+MoeBin* moe_bin_open(const char* path);
+void moe_bin_close(MoeBin* bin);
+int moe_bin_find(MoeBin* bin, const char* name, int* dtype, int* ndim, int* shape,
+                 size_t* nbytes);
+int moe_bin_read(MoeBin* bin, const char* name, void* dst, size_t nbytes);
+int moe_bin_layer_info_h(MoeBin* bin, int src_layer, int* E, int* D, int* F,
+                         int* dtype, int* has_bias);
+int moe_cuda_load_bin_layer_h(MoeBin* bin, int src_layer, int layer);
+
 /* ---- fused MoE block --------------------------------------------------------
  * Replaces test_model_trace.c:463-517 (router matmul + bias, topk_desc,
  * top-k softmax, per-(token,k) gate/up/SiLU·up/down, k-ordered weighted

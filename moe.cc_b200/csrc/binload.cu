@@ -31,6 +31,7 @@
 #include <string.h>
 #include <sys/stat.h>
 
+#include <mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -48,7 +49,7 @@ namespace {
 
 struct Rec {
   int dtype = 0, ndim = 0;
-  uint32_t shape[4] = {0, 0, 0, 0};
+  uint32_t shape[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   uint64_t off = 0, bytes = 0;   // data position in the file and its size
 };
 
@@ -101,7 +102,7 @@ int index_file(const char* path, FILE* f, BinIndex& ix) {
     for (uint32_t d = 0; d < nd; ++d) {
       uint32_t v;
       if (!rd_u32(f, &v)) return fail(MOE_ERR_INVALID, "%s: truncated shape of %s", path, name.c_str());
-      if (d < 4) r.shape[d] = v;
+      r.shape[d] = v;
       elems *= v;
       if (elems > fsize) return fail(MOE_ERR_INVALID, "%s: %s is larger than the file", path, name.c_str());
     }
@@ -187,35 +188,69 @@ int resolve_layer(const char* path, const BinIndex& ix, int L, LayerRecs& lr) {
   return MOE_OK;
 }
 
-int open_and_resolve(const char* path, int src_layer, FILE** fp, BinIndex& ix, LayerRecs& lr) {
-  if (!path) return fail(MOE_ERR_INVALID, "path is NULL");
-  FILE* f = fopen(path, "rb");
-  if (!f) return fail(MOE_ERR_INVALID, "%s: cannot open", path);
-  int rc = index_file(path, f, ix);
-  if (!rc) rc = resolve_layer(path, ix, src_layer, lr);
-  if (rc) { fclose(f); return rc; }
-  *fp = f;
-  return MOE_OK;
-}
-
 bool read_at(FILE* f, const Rec* r, void* dst) {
   return fseeko(f, (off_t)r->off, SEEK_SET) == 0 && fread(dst, 1, r->bytes, f) == r->bytes;
 }
 
 }  // namespace
+
+// An open weight file: the FILE and its name index (bin_load + bin_find of
+// io.c:193-338, without reading the data).
+struct BinHandle {
+  FILE* f = nullptr;
+  std::string path;
+  BinIndex ix;
+  std::mutex mu;   // one reader at a time on the FILE position
+  ~BinHandle() { if (f) fclose(f); }
+};
+
 }  // namespace moe
 
 using namespace moe;
+struct MoeBin : BinHandle {};
 
 extern "C" {
 
-int moe_bin_layer_info(const char* path, int src_layer, int* E, int* D, int* F, int* dtype, int* has_bias) {
-  FILE* f = nullptr;
-  BinIndex ix;
+MoeBin* moe_bin_open(const char* path) {
+  if (!path) { fail(MOE_ERR_INVALID, "path is NULL"); return nullptr; }
+  MoeBin* h = new MoeBin;
+  h->path = path;
+  h->f = fopen(path, "rb");
+  if (!h->f) { fail(MOE_ERR_INVALID, "%s: cannot open", path); delete h; return nullptr; }
+  if (index_file(path, h->f, h->ix)) { delete h; return nullptr; }
+  return h;
+}
+
+void moe_bin_close(MoeBin* h) { delete h; }
+
+int moe_bin_find(MoeBin* h, const char* name, int* dtype, int* ndim, int* shape, size_t* nbytes) {
+  if (!h || !name) return fail(MOE_ERR_INVALID, "moe_bin_find: NULL handle or name");
+  const Rec* r = h->ix.find(name);
+  if (!r) return fail(MOE_ERR_INVALID, "%s: missing %s", h->path.c_str(), name);
+  if (dtype) *dtype = r->dtype;
+  if (ndim) *ndim = r->ndim;
+  if (shape) for (int d = 0; d < r->ndim; ++d) shape[d] = (int)r->shape[d];
+  if (nbytes) *nbytes = (size_t)r->bytes;
+  return MOE_OK;
+}
+
+int moe_bin_read(MoeBin* h, const char* name, void* dst, size_t nbytes) {
+  if (!h || !name || !dst) return fail(MOE_ERR_INVALID, "moe_bin_read: NULL argument");
+  const Rec* r = h->ix.find(name);
+  if (!r) return fail(MOE_ERR_INVALID, "%s: missing %s", h->path.c_str(), name);
+  if (r->bytes != nbytes)
+    return fail(MOE_ERR_INVALID, "%s: %s holds %llu bytes, not %zu", h->path.c_str(), name,
+                (unsigned long long)r->bytes, nbytes);
+  std::lock_guard<std::mutex> lk(h->mu);
+  if (!read_at(h->f, r, dst)) return fail(MOE_ERR_INVALID, "%s: read of %s failed", h->path.c_str(), name);
+  return MOE_OK;
+}
+
+int moe_bin_layer_info_h(MoeBin* h, int src_layer, int* E, int* D, int* F, int* dtype, int* has_bias) {
+  if (!h) return fail(MOE_ERR_INVALID, "moe_bin_layer_info_h: NULL handle");
   LayerRecs lr;
-  const int rc = open_and_resolve(path, src_layer, &f, ix, lr);
+  const int rc = resolve_layer(h->path.c_str(), h->ix, src_layer, lr);
   if (rc) return rc;
-  fclose(f);
   if (E) *E = lr.E;
   if (D) *D = lr.D;
   if (F) *F = lr.F;
@@ -224,21 +259,28 @@ int moe_bin_layer_info(const char* path, int src_layer, int* E, int* D, int* F, 
   return MOE_OK;
 }
 
-int moe_cuda_load_bin_layer(const char* path, int src_layer, int layer) {
+int moe_bin_layer_info(const char* path, int src_layer, int* E, int* D, int* F, int* dtype, int* has_bias) {
+  MoeBin* h = moe_bin_open(path);
+  if (!h) return MOE_ERR_INVALID;
+  const int rc = moe_bin_layer_info_h(h, src_layer, E, D, F, dtype, has_bias);
+  moe_bin_close(h);
+  return rc;
+}
+
+int moe_cuda_load_bin_layer_h(MoeBin* h, int src_layer, int layer) {
+  if (!h) return fail(MOE_ERR_INVALID, "moe_cuda_load_bin_layer_h: NULL handle");
   struct Ctx {
-    FILE* f = nullptr;
-    BinIndex ix;
+    BinHandle* h;
     LayerRecs lr;
-    const char* path = nullptr;
-    ~Ctx() { if (f) fclose(f); }
   } c;
-  c.path = path;
-  int rc = open_and_resolve(path, src_layer, &c.f, c.ix, c.lr);
+  c.h = h;
+  int rc = resolve_layer(h->path.c_str(), h->ix, src_layer, c.lr);
   if (rc) return rc;
+  std::lock_guard<std::mutex> lk(h->mu);
   const LayerRecs& lr = c.lr;
   std::vector<unsigned char> router(lr.router->bytes + (lr.bias ? lr.bias->bytes : 0));
-  if (!read_at(c.f, lr.router, router.data()) || (lr.bias && !read_at(c.f, lr.bias, router.data() + lr.router->bytes)))
-    return fail(MOE_ERR_INVALID, "%s: read of the layer %d router failed", path, src_layer);
+  if (!read_at(h->f, lr.router, router.data()) || (lr.bias && !read_at(h->f, lr.bias, router.data() + lr.router->bytes)))
+    return fail(MOE_ERR_INVALID, "%s: read of the layer %d router failed", h->path.c_str(), src_layer);
   // the experts' q/s pointers are placeholders (shapes only): the slab
   // images come from `fill`, read straight into pinned staging
   static const float placeholder[1] = {0.0f};
@@ -259,14 +301,22 @@ int moe_cuda_load_bin_layer(const char* path, int src_layer, int layer) {
     Ctx& c = *static_cast<Ctx*>(ctx);
     const size_t qoff[3] = {L.gq_off, L.uq_off, L.dq_off}, soff[3] = {L.gs_off, L.us_off, L.ds_off};
     for (int p = 0; p < 3; ++p)
-      if (!read_at(c.f, c.lr.q[p][e], img + qoff[p]) || !read_at(c.f, c.lr.s[p][e], img + soff[p])) {
-        fail(MOE_ERR_INVALID, "%s: read of expert %d failed", c.path, e);
+      if (!read_at(c.h->f, c.lr.q[p][e], img + qoff[p]) || !read_at(c.h->f, c.lr.s[p][e], img + soff[p])) {
+        fail(MOE_ERR_INVALID, "%s: read of expert %d failed", c.h->path.c_str(), e);
         return false;
       }
     return true;
   };
   return upload_layer_streamed(layer, W[0].data(), W[1].data(), W[2].data(), (const float*)router.data(),
                                lr.bias ? (const float*)(router.data() + lr.router->bytes) : nullptr, lr.E, rd);
+}
+
+int moe_cuda_load_bin_layer(const char* path, int src_layer, int layer) {
+  MoeBin* h = moe_bin_open(path);
+  if (!h) return MOE_ERR_INVALID;
+  const int rc = moe_cuda_load_bin_layer_h(h, src_layer, layer);
+  moe_bin_close(h);
+  return rc;
 }
 
 }  // extern "C"

@@ -35,6 +35,8 @@ EXPORTS = (
     "moe_cuda_profile", "moe_cuda_profile_read", "moe_matmul_q_dev_noalloc",
     "moe_cuda_ep_setup", "moe_cuda_ep_connect", "moe_ffn_ep",
     "moe_bin_layer_info", "moe_cuda_load_bin_layer",
+    "moe_bin_open", "moe_bin_close", "moe_bin_find", "moe_bin_read",
+    "moe_bin_layer_info_h", "moe_cuda_load_bin_layer_h",
 )
 
 
@@ -89,6 +91,11 @@ def lib():
             "moe_ffn_ep": ([i, vp, i, vp, vp], i),
             "moe_bin_layer_info": ([C.c_char_p, i, vp, vp, vp, vp, vp], i),
             "moe_cuda_load_bin_layer": ([C.c_char_p, i, i], i),
+            "moe_bin_open": ([C.c_char_p], vp), "moe_bin_close": ([vp], None),
+            "moe_bin_find": ([vp, C.c_char_p, vp, vp, vp, vp], i),
+            "moe_bin_read": ([vp, C.c_char_p, vp, sz], i),
+            "moe_bin_layer_info_h": ([vp, i, vp, vp, vp, vp, vp], i),
+            "moe_cuda_load_bin_layer_h": ([vp, i, i], i),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -216,6 +223,48 @@ def bin_layer_info(path, src_layer):
     v = [C.c_int(0) for _ in range(5)]
     check(lib().moe_bin_layer_info(os.fsencode(path), src_layer, *[C.byref(x) for x in v]))
     return tuple(x.value for x in v)
+
+
+class BinFile:
+    """An open .bin weight file (moe_bin_open): find(name) -> (dtype, shape,
+    nbytes), read(name) -> numpy array."""
+    _NP = {0: np.float32, 1: np.float16, 2: np.int8, 3: np.uint8}
+
+    def __init__(self, path):
+        self.h = lib().moe_bin_open(os.fsencode(path))
+        if not self.h:
+            raise MoeError(MOE_ERR_INVALID, lib().moe_cuda_last_error().decode())
+
+    def close(self):
+        if self.h:
+            lib().moe_bin_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def find(self, name):
+        dt, nd, nb = C.c_int(0), C.c_int(0), C.c_size_t(0)
+        shape = (C.c_int * 8)()
+        check(lib().moe_bin_find(self.h, name.encode(), C.byref(dt), C.byref(nd), shape, C.byref(nb)))
+        return dt.value, tuple(shape[:nd.value]), nb.value
+
+    def read(self, name):
+        dt, shape, nb = self.find(name)
+        out = np.empty(shape, self._NP[dt])
+        check(lib().moe_bin_read(self.h, name.encode(), out.ctypes.data, nb))
+        return out
+
+    def layer_info(self, src_layer):
+        v = [C.c_int(0) for _ in range(5)]
+        check(lib().moe_bin_layer_info_h(self.h, src_layer, *[C.byref(x) for x in v]))
+        return tuple(x.value for x in v)
+
+    def load_layer(self, src_layer, layer):
+        check(lib().moe_cuda_load_bin_layer_h(self.h, src_layer, layer))
 
 
 def load_bin_layer(path, src_layer, layer):

@@ -126,3 +126,21 @@ def test_expert_count_and_shape_checks(tmp_path):
         with pytest.raises(mc.MoeError) as ei:
             mc.bin_layer_info(str(p), 2)
         assert ei.value.code == mc.MOE_ERR_INVALID
+
+
+def test_open_handle_find_read():
+    with mc.BinFile(REF_BIN) as b:
+        # the repeated name resolves to its first record (io.c:333-338)
+        assert np.array_equal(b.read("model.norm.weight"), synth(60, 32, 1.0))
+        assert b.find("model.layers.3.mlp.experts.2.down_proj.weight.q4") == (3, (32, 8), 256)
+        assert b.find("model.layers.3.mlp.router.gate.weight") == (0, (3, 32), 384)
+        recs = dict(ref_records()[:4])
+        for name, a in recs.items():
+            assert np.array_equal(b.read(name), a)
+        assert b.layer_info(3) == (3, 32, 16, mc.Q4, 1)
+        with pytest.raises(mc.MoeError):
+            b.find("model.layers.9.mlp.gate.weight")
+        buf = np.empty(31, np.float32)
+        assert mc.lib().moe_bin_read(b.h, b"model.norm.weight", buf.ctypes.data, buf.nbytes) == mc.MOE_ERR_INVALID
+    with pytest.raises(mc.MoeError):
+        mc.BinFile(os.path.join(GOLDEN, "absent.bin"))
