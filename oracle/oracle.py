@@ -113,6 +113,37 @@ class Ref:
         self.lib.ref_moe_layer.restype = i
         self.lib.ref_matmul.argtypes = [vp, vp, vp, vp, vp, i, i, i, i]
 
+    def model_forward(self, ids, cfg, g, attn, moe):
+        """The reference's model_forward_f32 (test_model_trace.c:526-596):
+        logits of the last of ids. cfg: TINY-style dict; g/attn/moe as built
+        by tests/helpers.tiny_model."""
+        names = ("Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo", "q_norm", "k_norm", "rms1_w", "rms2_w")
+        keep = []
+
+        def ptr(a):
+            if a is None:
+                return None
+            a = np.ascontiguousarray(a)
+            keep.append(a)
+            return a.ctypes.data
+        L = cfg["n_layers"]
+        ap = (C.c_void_p * (12 * L))(*[ptr(attn[l].get(n)) for l in range(L) for n in names])
+        rp = (C.c_void_p * (2 * L))(*[ptr(moe[l][k]) for l in range(L) for k in ("router_w", "router_b")])
+        ep = (C.c_void_p * (6 * L))(*[ptr(moe[l][k]) for l in range(L)
+                                      for k in ("gq", "gs", "uq", "us", "dq", "ds")])
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty(cfg["vocab_size"], np.float32)
+        f = self.lib.ref_model_forward
+        f.argtypes = [C.c_void_p] + [C.c_int] * 9 + [C.c_float] * 2 + [C.c_void_p] * 5 + [C.c_int, C.c_void_p,
+                                                                                           C.c_void_p]
+        f.restype = C.c_int
+        r = f(ids.ctypes.data, len(ids), cfg["d_model"], L, cfg["head_dim"], cfg["n_q"], cfg["n_kv"],
+              cfg["d_ff"], cfg["n_experts"], cfg["vocab_size"], cfg["rope_theta"], cfg["rms_eps"],
+              ptr(g["tok_emb"]), ptr(g["final_norm_w"]), ptr(g.get("lm_head")), ap, rp, moe[0]["dtype"], ep,
+              out.ctypes.data)
+        assert r == 0
+        return out
+
     def matmul(self, A, q, s, N, K, dtype):
         A = np.ascontiguousarray(A, np.float32)
         M = A.shape[0]

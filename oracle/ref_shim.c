@@ -117,3 +117,59 @@ int ref_matmul(const float* A, const void* Wq, const float* Ws, const float* Wf,
   matmul_adaptive(A, Wf, dtype == 0 ? NULL : &w, C, M, N, K);
   return 0;
 }
+
+/*
+ * The reference's whole model_forward_f32 (test_model_trace.c:526-596) on
+ * caller-provided weights: logits of the last of T tokens.
+ *   attn: n_layers x 12 pointers (Wq, bq, Wk, bk, Wv, bv, Wo, bo, q_norm,
+ *         k_norm, rms1_w, rms2_w; biases and q/k norms may be NULL)
+ *   router: n_layers x 2 (router_w, router_b or NULL)
+ *   experts: n_layers x 6 (gq, gs, uq, us, dq, ds, contiguous per projection
+ *            as in ref_moe_layer)
+ * top_k 8, causal (model.h:159-161).
+ */
+int ref_model_forward(const int* ids, int T, int D, int n_layers, int head_dim, int n_q, int n_kv,
+                      int F, int E, int V, float rope_theta, float rms_eps,
+                      const float* tok_emb, const float* final_norm_w, const float* lm_head,
+                      const float* const* attn, const float* const* router, int dtype,
+                      const void* const* experts, float* out_last) {
+  if (dtype != 2 && dtype != 3) return -1;
+  QwenConfig cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.d_model = D; cfg.n_layers = n_layers; cfg.head_dim = head_dim; cfg.n_q = n_q; cfg.n_kv = n_kv;
+  cfg.d_ff = F; cfg.n_experts = E; cfg.top_k = 8; cfg.vocab_size = V; cfg.causal = 1;
+  cfg.rope_theta = rope_theta; cfg.rms_eps = rms_eps;
+  QwenWeights w;
+  memset(&w, 0, sizeof(w));
+  w.tok_emb = tok_emb; w.final_norm_w = final_norm_w; w.lm_head = lm_head;
+  w.layers = (QwenLayerWeights*)calloc((size_t)n_layers, sizeof(QwenLayerWeights));
+  QuantizedWeight* qw = (QuantizedWeight*)calloc((size_t)n_layers * 3 * E, sizeof(QuantizedWeight));
+  const size_t gu_row = dtype == 2 ? (size_t)D : (size_t)D / 2;
+  const size_t d_row = dtype == 2 ? (size_t)F : (size_t)F / 2;
+  for (int l = 0; l < n_layers; ++l) {
+    QwenLayerWeights* lw = &w.layers[l];
+    const float* const* a = attn + 12 * l;
+    lw->Wq = a[0]; lw->bq = a[1]; lw->Wk = a[2]; lw->bk = a[3]; lw->Wv = a[4]; lw->bv = a[5];
+    lw->Wo = a[6]; lw->bo = a[7]; lw->q_norm = a[8]; lw->k_norm = a[9]; lw->rms1_w = a[10]; lw->rms2_w = a[11];
+    lw->router_w = router[2 * l]; lw->router_b = router[2 * l + 1];
+    const void* const* x = experts + 6 * l;
+    QuantizedWeight* g = qw + (size_t)l * 3 * E;
+    QuantizedWeight* u = g + E;
+    QuantizedWeight* d = u + E;
+    for (int e = 0; e < E; ++e) {
+      g[e].q = (const int8_t*)x[0] + (size_t)e * F * gu_row; g[e].s = (const float*)x[1] + (size_t)e * F;
+      u[e].q = (const int8_t*)x[2] + (size_t)e * F * gu_row; u[e].s = (const float*)x[3] + (size_t)e * F;
+      d[e].q = (const int8_t*)x[4] + (size_t)e * D * d_row;  d[e].s = (const float*)x[5] + (size_t)e * D;
+      g[e].rows = u[e].rows = F; g[e].cols = u[e].cols = D;
+      d[e].rows = D; d[e].cols = F;
+      g[e].dtype = u[e].dtype = d[e].dtype = dtype;
+    }
+    lw->Wg_q = g; lw->Wu_q = u; lw->Wd_q = d;
+    lw->experts_quantized = 1;
+  }
+  model_forward_f32(ids, T, &cfg, &w, /*apply_softmax=*/0, out_last);
+  free(w.layers);
+  free(qw);
+  ref_prof_clear();
+  return 0;
+}

@@ -12,6 +12,11 @@ Run in a container where the reference sources are present (default
   small ragged shapes.
 * moe_small.npz — the reference's layer_forward_f32 MoE block
   (test_model_trace.c:463-517, via oracle/ref_shim.c) on a small seeded layer.
+* host_tiny.npz — the reference's model_forward_f32 (test_model_trace.c:526-596)
+  on tests/helpers.tiny_model weights (Q8 and Q4), two sequences: a 6-token
+  prompt then greedy decode, the logits of every step, recomputed over the
+  whole prefix as the reference does. `python tests/golden/make_golden.py
+  host` writes only this file.
 * layer_ref.bin — a tiny weight file written by the reference's own writer
   (export.MAGIC, export._save_tensor, export._rowwise_q8/_q4): two MoE
   layers (Q8 at index 1, Q4 with a router bias at index 3, router under the
@@ -54,6 +59,10 @@ def main():
     sys.path.insert(0, REF_DIR)
     import torch
     import export  # the reference's exporter (its quantisers)
+    if sys.argv[1:] == ["host"]:
+        host_fixture()
+        print("host_tiny.npz written to", OUT)
+        return
     bin_fixture(torch, export)
     if sys.argv[1:] == ["bin"]:
         print("layer_ref.bin written to", OUT)
@@ -125,6 +134,34 @@ def bin_fixture(torch, export):
         f.write(struct.pack("<I", len(recs)))
         for name, t in recs:
             export._save_tensor(f, name, t)
+
+
+def host_fixture():
+    """host_tiny.npz: greedy decode of two sequences through the reference."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from helpers import TINY, tiny_model
+    from oracle.oracle import Ref
+    ref = Ref()
+    out = {}
+    B, P, steps = 2, 6, 6
+    for dt in (2, 3):
+        g, attn, moe = tiny_model(dt, seed=1)
+        rng = np.random.default_rng(100 + dt)
+        seqs = [list(map(int, rng.integers(0, TINY["vocab_size"], P))) for _ in range(B)]
+        out[f"prompt_{dt}"] = np.array(seqs, np.int32)
+        logits = np.empty((steps, B, TINY["vocab_size"]), np.float32)
+        for s in range(steps):
+            for b in range(B):
+                lg = ref.model_forward(seqs[b], TINY, g, attn, moe)
+                logits[s, b] = lg
+                # greedy: the first maximum of softmax(logits) (test_model_trace.c:723-731);
+                # with the top two logits this far apart it is the logits' argmax
+                top = np.sort(lg)[-2:]
+                assert top[1] - top[0] > 1e-3
+                seqs[b].append(int(np.argmax(lg)))
+        out[f"logits_{dt}"] = logits
+        out[f"tokens_{dt}"] = np.array([sq[P:] for sq in seqs], np.int32)
+    np.savez(os.path.join(OUT, "host_tiny.npz"), **out)
 
 
 def small_layer(E, D, F, dt, bias, quant, torch=None):

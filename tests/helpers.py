@@ -87,3 +87,67 @@ def layer_records(L, layer, router_name="mlp.gate.weight"):
             recs.append((base + ".scale", np.asarray(L[nm + "s"][e], np.float32)))
             recs.append((base + "." + q, L[nm + "q"][e]))
     return recs
+
+
+# ---- a tiny full model (host driver tests) -----------------------------------
+TINY = dict(d_model=64, n_layers=2, head_dim=16, n_q=4, n_kv=2, d_ff=32, n_experts=8,
+            vocab_size=97, rope_theta=1e7, rms_eps=1e-6)   # theta and eps of model.h:119-120
+
+
+def tiny_model(dt, seed=0, attn_bias=False, qk_norm=True, tied=False, router_bias=False):
+    """Seeded weights of a TINY-shaped Qwen3-MoE model: globals (tok_emb,
+    final_norm_w, lm_head or None), per-layer attention dicts (MhLayerWeights
+    field names) and per-layer MoE dicts in the upload layout."""
+    c = TINY
+    D, hd, nq, nkv, E, F, V = (c[k] for k in ("d_model", "head_dim", "n_q", "n_kv", "n_experts",
+                                              "d_ff", "vocab_size"))
+    s = 5000 + 100 * seed
+
+    def n(k, shape, std, mean=0.0):
+        return (synth(s + k, int(np.prod(shape)), std).reshape(shape) + np.float32(mean)).astype(np.float32)
+
+    g = {"tok_emb": n(0, (V, D), 1.0), "final_norm_w": n(1, (D,), 0.1, 1.0),
+         "lm_head": None if tied else n(2, (V, D), 0.1)}
+    attn, moe = [], []
+    for l in range(c["n_layers"]):
+        b = 10 + 40 * l
+        a = {"Wq": n(b, (nq * hd, D), 0.15), "Wk": n(b + 1, (nkv * hd, D), 0.15),
+             "Wv": n(b + 2, (nkv * hd, D), 0.15), "Wo": n(b + 3, (D, nq * hd), 0.1),
+             "rms1_w": n(b + 4, (D,), 0.1, 1.0), "rms2_w": n(b + 5, (D,), 0.1, 1.0)}
+        if qk_norm:
+            a["q_norm"] = n(b + 6, (hd,), 0.1, 1.0)
+            a["k_norm"] = n(b + 7, (hd,), 0.1, 1.0)
+        if attn_bias:
+            a["bq"], a["bk"] = n(b + 8, (nq * hd,), 0.1), n(b + 9, (nkv * hd,), 0.1)
+            a["bv"], a["bo"] = n(b + 10, (nkv * hd,), 0.1), n(b + 11, (D,), 0.1)
+        attn.append(a)
+        L = {"dtype": dt, "topk": 8, "router_w": n(b + 12, (E, D), 0.5),
+             "router_b": n(b + 13, (E,), 0.5) if router_bias else None}
+        for j, (nm, rows, cols) in enumerate((("g", F, D), ("u", F, D), ("d", D, F))):
+            ss, qs = [], []
+            for e in range(E):
+                sc, q = quant(dt)(n(b + 14 + 3 * e + j, (rows, cols), 0.3))
+                ss.append(sc); qs.append(q)
+            L[nm + "s"] = np.ascontiguousarray(np.stack(ss))
+            L[nm + "q"] = np.ascontiguousarray(np.stack(qs))
+        moe.append(L)
+    return g, attn, moe
+
+
+def model_records(g, attn, moe):
+    """A whole tiny model as .bin records, with the tensor names the reference's
+    loader reads (model.h:162-210)."""
+    recs = [("model.embed_tokens.weight", g["tok_emb"]), ("model.norm.weight", g["final_norm_w"])]
+    if g.get("lm_head") is not None:
+        recs.append(("lm_head.weight", g["lm_head"]))
+    names = {"Wq": "self_attn.q_proj.weight", "Wk": "self_attn.k_proj.weight", "Wv": "self_attn.v_proj.weight",
+             "Wo": "self_attn.o_proj.weight", "bq": "self_attn.q_proj.bias", "bk": "self_attn.k_proj.bias",
+             "bv": "self_attn.v_proj.bias", "bo": "self_attn.o_proj.bias", "q_norm": "self_attn.q_norm.weight",
+             "k_norm": "self_attn.k_norm.weight", "rms1_w": "input_layernorm.weight",
+             "rms2_w": "post_attention_layernorm.weight"}
+    for l, a in enumerate(attn):
+        for k, nm in names.items():
+            if a.get(k) is not None:
+                recs.append((f"model.layers.{l}.{nm}", a[k]))
+        recs += layer_records(moe[l], l)
+    return recs

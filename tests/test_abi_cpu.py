@@ -1,5 +1,5 @@
-"""CPU: the C-ABI library loads and exports every symbol include/moe_cuda.h
-declares; host-side error paths (no GPU here)."""
+"""CPU: the C-ABI libraries load and export every symbol include/moe_cuda.h
+and include/moe_host.h declare; host-side error paths (no GPU here)."""
 import os
 import re
 
@@ -10,8 +10,8 @@ import moe_cuda as mc
 HDR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "moe_cuda.h")
 
 
-def declared():
-    src = open(HDR).read()
+def declared(hdr=HDR):
+    src = open(hdr).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
     names = re.findall(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b([a-z_][a-z0-9_]*)\s*\(", src, flags=re.M)
     return sorted(set(n for n in names if n not in ("if", "typedef")))
@@ -24,6 +24,15 @@ def test_header_lists_expected_entry_points():
 def test_library_exports_every_declared_symbol():
     lib = mc.lib()
     for name in declared():
+        assert hasattr(lib, name), name
+
+
+def test_host_driver_exports_every_declared_symbol():
+    import moe_host as mh
+    names = declared(os.path.join(os.path.dirname(HDR), "moe_host.h"))
+    assert set(names) == set(mh.EXPORTS)
+    lib = mh.lib()
+    for name in names:
         assert hasattr(lib, name), name
 
 

@@ -1,0 +1,112 @@
+"""The C host driver (include/moe_host.h) on the CPU: its KV-cached attention
+and head, composed with the oracle's MoE block, against the reference's own
+model_forward_f32 (test_model_trace.c:526-596, compiled from source into
+oracle/_ref), which recomputes the whole prefix at every step. Bar: logits
+bit for bit at every prefill and decode step."""
+import numpy as np
+import pytest
+
+import moe_cuda as mc
+from helpers import TINY, tiny_model
+
+mh = pytest.importorskip("moe_host")
+from oracle.oracle import Port, Ref  # noqa: E402
+
+needs_ref = pytest.mark.skipif(not Ref.available(), reason="oracle/_ref (the reference's own code) not built")
+
+
+def load(model, g, attn):
+    model.set_globals(g["tok_emb"], g["final_norm_w"], g["lm_head"])
+    for l, a in enumerate(attn):
+        model.set_layer(l, a)
+
+
+def cpu_step(model, port, moe, ids):
+    """One driver step with the MoE block from the oracle instead of the GPU."""
+    ids = np.asarray(ids, np.int32).reshape(model.batch, -1)
+    T = ids.shape[1]
+    x = model.embed(ids)
+    for l in range(TINY["n_layers"]):
+        xa, xn = model.attention(l, x, T)
+        x = port.moe_block(xn, xa, moe[l])[0]
+    logits = model.head(x, T)
+    model.advance(T)
+    return logits
+
+
+@needs_ref
+@pytest.mark.parametrize("dt,variant", [(2, {}), (3, {}), (2, {"attn_bias": True, "tied": True}),
+                                        (3, {"qk_norm": False, "router_bias": True})])
+def test_cached_decode_matches_reference_full_recompute(dt, variant):
+    g, attn, moe = tiny_model(dt, seed=1, **variant)
+    ref, port = Ref(), Port()
+    B, P, steps = 2, 6, 5
+    rng = np.random.default_rng(dt)
+    seqs = [list(rng.integers(0, TINY["vocab_size"], P)) for _ in range(B)]
+    model = mh.HostModel(TINY, batch=B, max_ctx=32)
+    load(model, g, attn)
+    logits = cpu_step(model, port, moe, np.array(seqs))
+    for s in range(steps):
+        for b in range(B):
+            want = ref.model_forward(seqs[b], TINY, g, attn, moe)
+            assert np.array_equal(logits[b], want), f"step {s} sequence {b}"
+        nxt = model.pick_greedy(logits)
+        for b in range(B):
+            seqs[b].append(int(nxt[b]))
+        logits = cpu_step(model, port, moe, nxt)
+    assert model.pos() == P + steps
+
+
+@needs_ref
+def test_chunked_prefill_matches():
+    """Prompt fed in chunks of 3, 1 and 4 tokens: same logits as one pass."""
+    g, attn, moe = tiny_model(2, seed=2)
+    ref, port = Ref(), Port()
+    ids = list(np.random.default_rng(9).integers(0, TINY["vocab_size"], 8))
+    model = mh.HostModel(TINY, batch=1, max_ctx=16)
+    load(model, g, attn)
+    pos = 0
+    for n in (3, 1, 4):
+        logits = cpu_step(model, port, moe, ids[pos:pos + n])
+        pos += n
+        assert np.array_equal(logits[0], ref.model_forward(ids[:pos], TINY, g, attn, moe))
+
+
+def test_pick_greedy_first_maximum():
+    model = mh.HostModel(TINY, batch=2, max_ctx=4)
+    lg = np.zeros((2, TINY["vocab_size"]), np.float32)
+    lg[0, 5] = lg[0, 9] = 3.0
+    lg[1, -1] = 1.0
+    assert list(model.pick_greedy(lg)) == [5, TINY["vocab_size"] - 1]
+
+
+def test_errors_without_gpu_or_weights():
+    model = mh.HostModel(TINY, batch=1, max_ctx=4)
+    with pytest.raises(mc.MoeError):
+        model.embed([1])                       # no embedding set
+    g, attn, moe = tiny_model(2)
+    load(model, g, attn)
+    with pytest.raises(mc.MoeError):
+        model.embed([TINY["vocab_size"]])      # id out of range
+    x = model.embed([1])
+    with pytest.raises(mc.MoeError):
+        model.attention(0, np.vstack([x] * 5), 5)   # past max_ctx
+    xa, xn = model.attention(0, x, 1)
+    with pytest.raises(mc.MoeError):
+        model.moe(0, xn, xa, 1)                # the MoE block needs the GPU library initialised
+    bad = dict(TINY, n_q=3)
+    with pytest.raises(mc.MoeError):
+        mh.HostModel(bad)                      # n_q not a multiple of n_kv
+
+
+def test_config_from_bin(tmp_path):
+    from helpers import model_records, write_bin
+    g, attn, moe = tiny_model(3, seed=1)
+    p = str(tmp_path / "m.bin")
+    write_bin(p, model_records(g, attn, moe))
+    got = mh.config_from_bin(p)
+    assert got == {k: (float(np.float32(v)) if isinstance(v, float) else v) for k, v in TINY.items()}
+    # without q_norm the head size is inferred as rows/32 (model.h:113-115)
+    g2, attn2, moe2 = tiny_model(3, seed=1, qk_norm=False)
+    write_bin(p, model_records(g2, attn2, moe2))
+    assert mh.config_from_bin(p)["head_dim"] == TINY["n_q"] * TINY["head_dim"] // 32
