@@ -94,10 +94,12 @@ TINY = dict(d_model=64, n_layers=2, head_dim=16, n_q=4, n_kv=2, d_ff=32, n_exper
             vocab_size=97, rope_theta=1e7, rms_eps=1e-6)   # theta and eps of model.h:119-120
 
 
-def tiny_model(dt, seed=0, attn_bias=False, qk_norm=True, tied=False, router_bias=False):
+def tiny_model(dt, seed=0, attn_bias=False, qk_norm=True, tied=False, router_bias=False, expert_std=0.1):
     """Seeded weights of a TINY-shaped Qwen3-MoE model: globals (tok_emb,
     final_norm_w, lm_head or None), per-layer attention dicts (MhLayerWeights
-    field names) and per-layer MoE dicts in the upload layout."""
+    field names) and per-layer MoE dicts in the upload layout. expert_std keeps
+    the expert activations inside the GPU kernels' Q4 range (trunc(7h) in
+    [-128, 127], h = silu(gate x) * up x), which wider weights leave."""
     c = TINY
     D, hd, nq, nkv, E, F, V = (c[k] for k in ("d_model", "head_dim", "n_q", "n_kv", "n_experts",
                                               "d_ff", "vocab_size"))
@@ -126,7 +128,7 @@ def tiny_model(dt, seed=0, attn_bias=False, qk_norm=True, tied=False, router_bia
         for j, (nm, rows, cols) in enumerate((("g", F, D), ("u", F, D), ("d", D, F))):
             ss, qs = [], []
             for e in range(E):
-                sc, q = quant(dt)(n(b + 14 + 3 * e + j, (rows, cols), 0.3))
+                sc, q = quant(dt)(n(b + 14 + 3 * e + j, (rows, cols), expert_std))
                 ss.append(sc); qs.append(q)
             L[nm + "s"] = np.ascontiguousarray(np.stack(ss))
             L[nm + "q"] = np.ascontiguousarray(np.stack(qs))
