@@ -200,6 +200,22 @@ int moe_bin_layer_info_h(MoeBin* bin, int src_layer, int* E, int* D, int* F,
                          int* dtype, int* has_bias);
 int moe_cuda_load_bin_layer_h(MoeBin* bin, int src_layer, int layer);
 
+/* Writing the format: moe_bin_create writes the magic and `count`, then
+ * moe_bin_put appends one record per call (dtype 0 f32, 1 f16, 2 i8, 3
+ * packed i4; data of prod(shape) x 4/2/1/1 bytes) and moe_bin_finish closes
+ * the file. export.py and merge_dir.py (:34-43) write the number of original
+ * tensors as the count, while a quantised tensor contributes two records,
+ * .scale then .q8/.q4 (export.py:197-206); readers go to end of file. */
+typedef struct MoeBinWriter MoeBinWriter;
+MoeBinWriter* moe_bin_create(const char* path, uint32_t count);
+int moe_bin_put(MoeBinWriter* w, const char* name, int dtype, int ndim,
+                const int* shape, const void* data);
+int moe_bin_finish(MoeBinWriter* w);
+
+/* The quantisers above on host memory (same results bit for bit). */
+int moe_quantize_rowwise_q8_host(const float* W, int rows, int cols, int8_t* q, float* s);
+int moe_quantize_rowwise_q4_host(const float* W, int rows, int cols, uint8_t* q, float* s);
+
 /* ---- fused MoE block --------------------------------------------------------
  * Replaces test_model_trace.c:463-517 (router matmul + bias, topk_desc,
  * top-k softmax, per-(token,k) gate/up/SiLU·up/down, k-ordered weighted

@@ -37,6 +37,8 @@ EXPORTS = (
     "moe_bin_layer_info", "moe_cuda_load_bin_layer",
     "moe_bin_open", "moe_bin_close", "moe_bin_find", "moe_bin_read",
     "moe_bin_layer_info_h", "moe_cuda_load_bin_layer_h",
+    "moe_bin_create", "moe_bin_put", "moe_bin_finish",
+    "moe_quantize_rowwise_q8_host", "moe_quantize_rowwise_q4_host",
 )
 
 
@@ -96,6 +98,10 @@ def lib():
             "moe_bin_read": ([vp, C.c_char_p, vp, sz], i),
             "moe_bin_layer_info_h": ([vp, i, vp, vp, vp, vp, vp], i),
             "moe_cuda_load_bin_layer_h": ([vp, i, i], i),
+            "moe_bin_create": ([C.c_char_p, C.c_uint32], vp), "moe_bin_put": ([vp, C.c_char_p, i, i, vp, vp], i),
+            "moe_bin_finish": ([vp], i),
+            "moe_quantize_rowwise_q8_host": ([vp, i, i, vp, vp], i),
+            "moe_quantize_rowwise_q4_host": ([vp, i, i, vp, vp], i),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -265,6 +271,39 @@ class BinFile:
 
     def load_layer(self, src_layer, layer):
         check(lib().moe_cuda_load_bin_layer_h(self.h, src_layer, layer))
+
+
+def quantize_rowwise_host(W, dtype):
+    """(s, q) of export._rowwise_q8 / _q4 on the host (moe_quantize_rowwise_*_host)."""
+    W = np.ascontiguousarray(W, np.float32)
+    rows, cols = W.shape
+    s = np.empty(rows, np.float32)
+    if dtype == Q8:
+        q = np.empty((rows, cols), np.int8)
+        check(lib().moe_quantize_rowwise_q8_host(W.ctypes.data, rows, cols, q.ctypes.data, s.ctypes.data))
+    else:
+        q = np.empty((rows, cols // 2), np.uint8)
+        check(lib().moe_quantize_rowwise_q4_host(W.ctypes.data, rows, cols, q.ctypes.data, s.ctypes.data))
+    return s, q
+
+
+class BinWriter:
+    """moe_bin_create / moe_bin_put / moe_bin_finish."""
+    _DT = {np.dtype(np.float32): 0, np.dtype(np.float16): 1, np.dtype(np.int8): 2, np.dtype(np.uint8): 3}
+
+    def __init__(self, path, count):
+        self.h = lib().moe_bin_create(os.fsencode(path), count)
+        if not self.h:
+            raise MoeError(MOE_ERR_INVALID, lib().moe_cuda_last_error().decode())
+
+    def put(self, name, a):
+        a = np.ascontiguousarray(a)
+        shape = (C.c_int * max(1, a.ndim))(*a.shape)
+        check(lib().moe_bin_put(self.h, name.encode(), self._DT[a.dtype], a.ndim, shape, a.ctypes.data))
+
+    def finish(self):
+        h, self.h = self.h, None
+        check(lib().moe_bin_finish(h))
 
 
 def load_bin_layer(path, src_layer, layer):

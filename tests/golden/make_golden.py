@@ -17,6 +17,11 @@ Run in a container where the reference sources are present (default
   prompt then greedy decode, the logits of every step, recomputed over the
   whole prefix as the reference does. `python tests/golden/make_golden.py
   host` writes only this file.
+* mkbin_ref.bin — a tiny random-init model (2 layers, D=64, 8 experts, Q4)
+  dumped per tensor as export.py --outdir does (export._save_tensor,
+  export._rowwise_q4, export.py:130-178) and merged by the reference's own
+  merge_dir.py. moe_mkbin must write these bytes for the same arguments.
+  `python tests/golden/make_golden.py mkbin` writes only this file.
 * layer_ref.bin — a tiny weight file written by the reference's own writer
   (export.MAGIC, export._save_tensor, export._rowwise_q8/_q4): two MoE
   layers (Q8 at index 1, Q4 with a router bias at index 3, router under the
@@ -59,6 +64,9 @@ def main():
     sys.path.insert(0, REF_DIR)
     import torch
     import export  # the reference's exporter (its quantisers)
+    if sys.argv[1:] == ["mkbin"]:
+        mkbin_fixture(torch, export)
+        return
     if sys.argv[1:] == ["host"]:
         host_fixture()
         print("host_tiny.npz written to", OUT)
@@ -134,6 +142,66 @@ def bin_fixture(torch, export):
         f.write(struct.pack("<I", len(recs)))
         for name, t in recs:
             export._save_tensor(f, name, t)
+
+
+MKBIN_ARGS = dict(layers=2, d_model=64, n_q=4, n_kv=2, head_dim=16, d_ff=32, experts=8, vocab=97,
+                  seed=3, quant="q4")
+
+
+def mkbin_fixture(torch, export):
+    """mkbin_ref.bin: export --outdir layout merged by merge_dir.py."""
+    import json
+    import shutil
+    import struct
+    import tempfile
+    a = MKBIN_ARGS
+    D, hd, nq, nkv, F, E, V = (a[k] for k in ("d_model", "head_dim", "n_q", "n_kv", "d_ff", "experts", "vocab"))
+
+    def t(layer, tid, shape):
+        sd = (a["seed"] * 1000003 + layer * 1009 + tid) & ((1 << 64) - 1)
+        return torch.from_numpy(synth(sd, int(np.prod(shape)), 0.02).reshape(shape))
+    tensors = [("model.embed_tokens.weight", t(65535, 0, (V, D)))]
+    for L in range(a["layers"]):
+        pre = f"model.layers.{L}."
+        for j, (nm, shp) in enumerate((("q_proj", (nq * hd, D)), ("k_proj", (nkv * hd, D)),
+                                        ("v_proj", (nkv * hd, D)), ("o_proj", (D, nq * hd)))):
+            tensors.append((pre + f"self_attn.{nm}.weight", t(L, 100000 + j, shp)))
+        tensors.append((pre + "self_attn.q_norm.weight", t(L, 100004, (hd,))))
+        tensors.append((pre + "self_attn.k_norm.weight", t(L, 100005, (hd,))))
+        tensors.append((pre + "mlp.gate.weight", t(L, 0, (E, D))))
+        for e in range(E):
+            for j, (nm, shp) in enumerate((("gate_proj", (F, D)), ("up_proj", (F, D)), ("down_proj", (D, F)))):
+                tensors.append((pre + f"mlp.experts.{e}.{nm}.weight", t(L, 2 + 3 * e + j, shp)))
+        tensors.append((pre + "input_layernorm.weight", t(L, 100006, (D,))))
+        tensors.append((pre + "post_attention_layernorm.weight", t(L, 100007, (D,))))
+    tensors.append(("model.norm.weight", t(65535, 1, (D,))))
+    tensors.append(("lm_head.weight", t(65535, 2, (V, D))))
+    tmp = tempfile.mkdtemp()
+    try:
+        manifest = {"tensors": []}
+        for name, w in tensors:
+            fn = export._sanitize(name) + ".bin"
+            with open(os.path.join(tmp, fn), "wb") as f:      # export.py:143-170
+                f.write(export.MAGIC)
+                f.write(struct.pack("<I", 1))
+                if export._is_expert_weight(name) and w.dim() == 2:
+                    sc, q = export._rowwise_q4(w)
+                    export._save_tensor(f, name + ".scale", sc)
+                    export._save_tensor(f, name + ".q4", q)
+                else:
+                    export._save_tensor(f, name, w.float())
+            manifest["tensors"].append({"name": name, "file": fn})
+        with open(os.path.join(tmp, "manifest.json"), "w") as f:
+            json.dump(manifest, f)
+        import merge_dir                                        # the reference's merger
+        argv = sys.argv
+        sys.argv = ["merge_dir.py", os.path.join(OUT, "mkbin_ref.bin"), tmp]
+        try:
+            merge_dir.main()
+        finally:
+            sys.argv = argv
+    finally:
+        shutil.rmtree(tmp)
 
 
 def host_fixture():

@@ -144,3 +144,38 @@ def test_open_handle_find_read():
         assert mc.lib().moe_bin_read(b.h, b"model.norm.weight", buf.ctypes.data, buf.nbytes) == mc.MOE_ERR_INVALID
     with pytest.raises(mc.MoeError):
         mc.BinFile(os.path.join(GOLDEN, "absent.bin"))
+
+
+def test_host_quantisers_match_exporter():
+    """moe_quantize_rowwise_*_host against export._rowwise_q8/_q4 outputs."""
+    z = np.load(os.path.join(GOLDEN, "quant.npz"))
+    s8, q8 = mc.quantize_rowwise_host(z["W"], mc.Q8)
+    s4, q4 = mc.quantize_rowwise_host(z["W"], mc.Q4)
+    assert np.array_equal(s8, z["s8"]) and np.array_equal(q8, z["q8"])
+    assert np.array_equal(s4, z["s4"]) and np.array_equal(q4, z["q4"])
+
+
+def test_writer_reproduces_reference_file(tmp_path):
+    p = str(tmp_path / "w.bin")
+    recs = ref_records()
+    w = mc.BinWriter(p, len(recs))
+    for name, a in recs:
+        w.put(name, a)
+    w.finish()
+    assert open(p, "rb").read() == open(REF_BIN, "rb").read()
+
+
+def test_mkbin_matches_reference_export_and_merge(tmp_path):
+    """moe_mkbin writes what export.py --outdir + merge_dir.py write for the
+    same tensors (tests/golden/mkbin_ref.bin, made by the reference's code)."""
+    import subprocess
+    tool = os.path.join(os.path.dirname(mc.LIB_PATH), "moe_mkbin")
+    p = str(tmp_path / "m.bin")
+    subprocess.check_call([tool, "--out", p, "--layers", "2", "--d-model", "64", "--n-q", "4", "--n-kv", "2",
+                           "--head-dim", "16", "--d-ff", "32", "--experts", "8", "--vocab", "97", "--seed", "3",
+                           "--quant", "q4"])
+    assert open(p, "rb").read() == open(os.path.join(GOLDEN, "mkbin_ref.bin"), "rb").read()
+    with mc.BinFile(p) as b:
+        assert b.layer_info(1) == (8, 64, 32, mc.Q4, 0)
+        # header count = original tensors (merge_dir.py:37-39), records beyond it
+        assert open(p, "rb").read()[6:10] == (1 + 2 * (9 + 24) + 2).to_bytes(4, "little")
