@@ -7,7 +7,8 @@
  * is a separately rounded IEEE operation in the order shown):
  *   matmul_f32 (test_model_trace.c:213-227): each output is one sequential
  *     chain acc = 0; acc += a[k]*w[k] for k = 0..K-1. Parallelism is over
- *     outputs only; four outputs share a pass over the activation row.
+ *     outputs only: 16 outputs per pass in 8-wide AVX2 lanes where the CPU
+ *     has AVX2, else four scalar chains per pass.
  *   rmsnorm_forward_f32 (:241-255): msq sequential, msq /= D,
  *     inv = 1/sqrtf(msq + eps), y = (x*inv)*w.
  *   per-head Q/K RMSNorm (:371-392): inv = 1/sqrtf(msq/hd + eps),
@@ -30,6 +31,7 @@
 #include <time.h>
 
 #include <cuda_runtime.h>
+#include <immintrin.h>
 #include <omp.h>
 
 #include "../../include/moe_cuda.h"
@@ -94,8 +96,78 @@ static float* own(MhModel* m, size_t n) {
 
 /* ---- CPU arithmetic (bit-compatible with the reference) ------------------- */
 
+/* AVX2 form of the same chains: 16 outputs per pass, two 8-lane
+   accumulators. Each 8x8 tile of weights (8 rows x 8 consecutive k) is
+   transposed in registers so that lane j of column i holds w[n0+j][k+i];
+   the lanes then add a[k+i]*w in k order, one separately rounded multiply
+   and add at a time, exactly the scalar chain of each output. */
+__attribute__((target("avx2"))) static inline void transpose8(__m256 r[8]) {
+  const __m256 t0 = _mm256_unpacklo_ps(r[0], r[1]), t1 = _mm256_unpackhi_ps(r[0], r[1]);
+  const __m256 t2 = _mm256_unpacklo_ps(r[2], r[3]), t3 = _mm256_unpackhi_ps(r[2], r[3]);
+  const __m256 t4 = _mm256_unpacklo_ps(r[4], r[5]), t5 = _mm256_unpackhi_ps(r[4], r[5]);
+  const __m256 t6 = _mm256_unpacklo_ps(r[6], r[7]), t7 = _mm256_unpackhi_ps(r[6], r[7]);
+  const __m256 s0 = _mm256_shuffle_ps(t0, t2, 0x44), s1 = _mm256_shuffle_ps(t0, t2, 0xEE);
+  const __m256 s2 = _mm256_shuffle_ps(t1, t3, 0x44), s3 = _mm256_shuffle_ps(t1, t3, 0xEE);
+  const __m256 s4 = _mm256_shuffle_ps(t4, t6, 0x44), s5 = _mm256_shuffle_ps(t4, t6, 0xEE);
+  const __m256 s6 = _mm256_shuffle_ps(t5, t7, 0x44), s7 = _mm256_shuffle_ps(t5, t7, 0xEE);
+  r[0] = _mm256_permute2f128_ps(s0, s4, 0x20); r[1] = _mm256_permute2f128_ps(s1, s5, 0x20);
+  r[2] = _mm256_permute2f128_ps(s2, s6, 0x20); r[3] = _mm256_permute2f128_ps(s3, s7, 0x20);
+  r[4] = _mm256_permute2f128_ps(s0, s4, 0x31); r[5] = _mm256_permute2f128_ps(s1, s5, 0x31);
+  r[6] = _mm256_permute2f128_ps(s2, s6, 0x31); r[7] = _mm256_permute2f128_ps(s3, s7, 0x31);
+}
+
+/* outputs n0..n0+15 of row a (all 16 rows exist) */
+__attribute__((target("avx2"))) static void dot16_avx2(const float* a, const float* w, float* c, int K) {
+  __m256 acc0 = _mm256_setzero_ps(), acc1 = _mm256_setzero_ps();
+  const int K8 = K & ~7;
+  for (int k = 0; k < K8; k += 8) {
+    __m256 r[8], q[8];
+    for (int j = 0; j < 8; ++j) {
+      r[j] = _mm256_loadu_ps(w + (size_t)j * K + k);
+      q[j] = _mm256_loadu_ps(w + (size_t)(j + 8) * K + k);
+    }
+    transpose8(r);
+    transpose8(q);
+    for (int i = 0; i < 8; ++i) {
+      const __m256 av = _mm256_set1_ps(a[k + i]);
+      acc0 = _mm256_add_ps(acc0, _mm256_mul_ps(av, r[i]));
+      acc1 = _mm256_add_ps(acc1, _mm256_mul_ps(av, q[i]));
+    }
+  }
+  float acc[16];
+  _mm256_storeu_ps(acc, acc0);
+  _mm256_storeu_ps(acc + 8, acc1);
+  for (int k = K8; k < K; ++k)
+    for (int j = 0; j < 16; ++j) acc[j] += a[k] * w[(size_t)j * K + k];
+  memcpy(c, acc, sizeof(acc));
+}
+
+/* MOE_HOST_SCALAR=1 keeps the portable path (for tests and comparisons) */
+static int use_avx2(void) {
+  static int v = -1;
+  if (v < 0) v = !getenv("MOE_HOST_SCALAR") && __builtin_cpu_supports("avx2");
+  return v;
+}
+
 /* C[M][N] = A[M][K] . W[N][K]^T, each output one sequential chain. */
 static void mm_f32(const float* A, const float* W, float* C, int M, int N, int K) {
+  if (use_avx2() && N >= 16) {
+    const int nb = N / 16;
+#pragma omp parallel for schedule(static)
+    for (int b = 0; b < nb; ++b)
+      for (int m = 0; m < M; ++m)
+        dot16_avx2(A + (size_t)m * K, W + (size_t)16 * b * K, C + (size_t)m * N + 16 * b, K);
+    const int n_done = nb * 16;
+    for (int m = 0; m < M; ++m)
+      for (int n = n_done; n < N; ++n) {
+        const float* a = A + (size_t)m * K;
+        const float* w = W + (size_t)n * K;
+        float acc = 0.f;
+        for (int k = 0; k < K; ++k) acc += a[k] * w[k];
+        C[(size_t)m * N + n] = acc;
+      }
+    return;
+  }
   const int nb = (N + 3) / 4;
 #pragma omp parallel for schedule(static)
   for (int b = 0; b < nb; ++b) {

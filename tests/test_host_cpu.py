@@ -110,3 +110,44 @@ def test_config_from_bin(tmp_path):
     g2, attn2, moe2 = tiny_model(3, seed=1, qk_norm=False)
     write_bin(p, model_records(g2, attn2, moe2))
     assert mh.config_from_bin(p)["head_dim"] == TINY["n_q"] * TINY["head_dim"] // 32
+
+
+@pytest.mark.parametrize("D", [60, 64, 72])
+def test_head_is_the_reference_chain(D):
+    """mh_head = rmsnorm_forward_f32 then matmul_f32 (test_model_trace.c:213-255),
+    restated as scalar float32 loops, for row lengths with and without a
+    remainder of 8 (the vector path's tail)."""
+    cfg = dict(TINY, d_model=D, vocab_size=37)
+    rng = np.random.default_rng(D)
+    emb = rng.standard_normal((37, D), dtype=np.float32)
+    head = rng.standard_normal((37, D), dtype=np.float32)
+    fn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    x = rng.standard_normal((1, D), dtype=np.float32)
+    model = mh.HostModel(cfg, batch=1, max_ctx=4)
+    model.set_globals(emb, fn, head)
+    got = model.head(x, 1)[0]
+    f = np.float32
+    msq = f(0)
+    for v in x[0]:
+        msq = f(msq + f(v * v))
+    msq = f(msq / f(D))
+    inv = f(f(1) / f(np.sqrt(f(msq + f(TINY["rms_eps"])))))
+    y = [f(f(v * inv) * w) for v, w in zip(x[0], fn)]
+    want = np.empty(37, np.float32)
+    for n in range(37):
+        acc = f(0)
+        for k in range(D):
+            acc = f(acc + f(y[k] * head[n, k]))
+        want[n] = acc
+    assert np.array_equal(got, want)
+
+
+def test_scalar_path_too():
+    """The portable matmul path (MOE_HOST_SCALAR=1, read once per process)."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, MOE_HOST_SCALAR="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider", __file__,
+                        "-k", "head_is or cached_decode"], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:]
