@@ -145,7 +145,10 @@ __attribute__((target("avx2"))) static void dot16_avx2(const float* a, const flo
 /* MOE_HOST_SCALAR=1 keeps the portable path (for tests and comparisons) */
 static int use_avx2(void) {
   static int v = -1;
-  if (v < 0) v = !getenv("MOE_HOST_SCALAR") && __builtin_cpu_supports("avx2");
+  if (v < 0) {
+    __builtin_cpu_init();
+    v = !getenv("MOE_HOST_SCALAR") && __builtin_cpu_supports("avx2");
+  }
   return v;
 }
 
