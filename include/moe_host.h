@@ -18,7 +18,7 @@
  * (batch x new tokens rows), which is what batched decode buys on the GPU.
  *
  * Errors: status codes (MOE_OK / MOE_ERR_* of moe_cuda.h), message in
- * mh_last_error(). No function exits the process.
+ * mh_last_error() (per calling thread). No function exits the process.
  */
 #ifndef MOE_HOST_H
 #define MOE_HOST_H

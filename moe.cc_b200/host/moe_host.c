@@ -62,7 +62,7 @@ struct MhModel {
   int moe_uploaded;
 };
 
-static char g_err[512];
+static _Thread_local char g_err[512];   /* per calling thread */
 
 static int fail(int code, const char* fmt, ...) {
   va_list ap;
