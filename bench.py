@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=16)
     ap.add_argument("--extra-t", default="1,4", help="other T values reported beside the headline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemv-c1", action="store_true", help="skip the configs[0] batched GEMV line")
     ap.add_argument("--prefill-t", default="512,2048",
                     help="configs[2] Q4 prefill sizes reported beside the headline ('' to skip)")
     ap.add_argument("--q4-batch", type=int, default=32,
@@ -441,6 +442,56 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def gemv_c1(torch, mc, sy, peak, reps=50, warmup=5):
+    """BASELINE configs[0] (the reference's own CPU kernel path, one Q8/Q4
+    768x2048 matvec), in the batched form that can fill the GPU: all 128
+    experts' gate matrices against one x[2048] in one moe_matmul_batched_dev
+    call (201 MB Q8, 101 MB Q4). Two such sets alternate, so each call reads
+    its matrices from HBM. A call is two launches: the activation
+    quantisation and the GEMV. Algorithmic bytes: weights + scales + x + C."""
+    N, K, nm = 768, 2048, 128
+    st = torch.cuda.current_stream()
+    out = {}
+    for dt, name in ((mc.Q8, "q8"), (mc.Q4, "q4")):
+        rb = K if dt == mc.Q8 else K // 2
+        tmp = torch.empty(N, K, dtype=torch.float32, device="cuda")
+        sets = []
+        for s in range(2):
+            q = torch.empty(nm, N, rb, dtype=torch.int8 if dt == mc.Q8 else torch.uint8, device="cuda")
+            sc = torch.empty(nm, N, dtype=torch.float32, device="cuda")
+            for e in range(nm):
+                mc.synth_normal_dev(sy.stream_seed(1, s, 2 + 3 * e), tmp, 0.02, stream=st)
+                mc.quantize_rowwise_dev(tmp, q[e], sc[e], dt, stream=st)
+            qp = torch.tensor([q[e].data_ptr() for e in range(nm)], dtype=torch.int64, device="cuda")
+            sp = torch.tensor([sc[e].data_ptr() for e in range(nm)], dtype=torch.int64, device="cuda")
+            sets.append((q, sc, qp, sp))
+        x = torch.empty(1, K, dtype=torch.float32, device="cuda")
+        mc.synth_normal_dev(sy.stream_seed(2, 0, 0), x, 1.0, stream=st)
+        C = torch.empty(nm, N, dtype=torch.float32, device="cuda")
+
+        def call(i):
+            _, _, qp, sp = sets[i % 2]
+            mc.check(mc.lib().moe_matmul_batched_dev(x.data_ptr(), qp.data_ptr(), sp.data_ptr(), C.data_ptr(),
+                                                     nm, N, K, dt, st.cuda_stream))
+        for i in range(warmup):
+            call(i)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        for i in range(reps):
+            call(i)
+        b.record(st)
+        torch.cuda.synchronize()
+        mc.check_status()
+        us = a.elapsed_time(b) * 1e3 / reps
+        byts = nm * (N * rb + 4 * N) + 4 * K + 4 * nm * N
+        out[name] = {"matrices": nm, "N": N, "K": K, "us_per_call": us, "alg_bytes": byts,
+                     "gb_s": byts / (us * 1e-6) / 1e9, "frac_hbm": byts / (us * 1e-6) / 1e9 / peak,
+                     "launches_per_call": 2}
+        del sets, tmp, C
+    return out
+
+
 def prefill_bench(torch, mc, sy, steps, warmup, ts):
     """the same layer with Q4 experts, prefill of T tokens,
     router logits skewed by a seeded per-expert bias ~ N(0,1) (ragged expert
@@ -576,6 +627,12 @@ def run_ours(args):
     prefill = None
     if world == 1 and args.prefill_t:
         prefill = prefill_bench(torch, mc, sy, 30, 3, [int(v) for v in args.prefill_t.split(",") if v])
+    c1 = None
+    if world == 1 and not args.no_gemv_c1:
+        try:
+            c1 = gemv_c1(torch, mc, sy, peak)
+        except Exception as exc:       # the headline line must still be printed
+            c1 = {"error": str(exc)[:300]}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(mc, host_layer_from_device(torch, mc, sy, dt), T)
@@ -598,7 +655,7 @@ def run_ours(args):
                 "kernels": kern, "gpu_launches": int(round(launches_per_step * steps)),
                 "gpu_launches_per_step": launches_per_step,
                 "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu, "extra": extra,
-                "prefill_q4": prefill, "q4_batch32": q4b}
+                "prefill_q4": prefill, "q4_batch32": q4b, "gemv_c1": c1}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
