@@ -151,3 +151,17 @@ def test_scalar_path_too():
     r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider", __file__,
                         "-k", "head_is or cached_decode"], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:]
+
+
+def test_generate_program_fails_loudly_without_gpu():
+    """moe_generate needs the GPU for the MoE block: without one it exits
+    non-zero with the library's message, and runs no CPU substitute."""
+    import os
+    import subprocess
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    tool = os.path.join(os.path.dirname(mh.LIB_PATH), "moe_generate")
+    r = subprocess.run([tool, "--layers", "1", "--steps", "2", "--prompt", "2"], capture_output=True, text=True,
+                       timeout=120)
+    assert r.returncode != 0 and "moe_cuda_init" in r.stderr and not r.stdout
