@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--extra-t", default="1,4", help="other T values reported beside the headline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv-c1", action="store_true", help="skip the configs[0] batched GEMV line")
+    ap.add_argument("--no-full-model", action="store_true",
+                    help="skip the configs[3] 48-layer decode through the C host driver")
     ap.add_argument("--prefill-t", default="512,2048",
                     help="configs[2] Q4 prefill sizes reported beside the headline ('' to skip)")
     ap.add_argument("--q4-batch", type=int, default=32,
@@ -538,6 +540,26 @@ def gemv_c1(torch, mc, sy, peak, reps=50, warmup=5):
     return out
 
 
+def full_model_c4(layers=48, prompt=64, steps=16, timeout_s=300):
+    """BASELINE configs[3] through the C host driver (moe.cc_b200/moe_generate):
+    the 48-layer Qwen3-30B-A3B-shaped model with random-init weights and Q8
+    experts, a 64-token prompt, then greedy decode. Attention, norms and the
+    head run on the host (fp32), the MoE block of every layer on the GPU; the
+    figure of interest is the MoE wall time per layer call (host pointers,
+    copies included). Decodes `steps` of configs[3]'s 256 tokens to bound the
+    run time. Runs as its own process."""
+    import subprocess
+    tool = os.path.join(ROOT, "moe.cc_b200", "moe_generate")
+    r = subprocess.run([tool, "--layers", str(layers), "--prompt", str(prompt), "--steps", str(steps),
+                        "--dtype", "q8"], capture_output=True, text=True, timeout=timeout_s)
+    if r.returncode != 0:
+        return {"error": (r.stderr or r.stdout)[-300:]}
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    out["workload"] = (f"configs[3]: 48-layer decoder, Q8 experts, batch 1, {prompt}-token prompt, "
+                       f"{steps} of the 256 greedy tokens")
+    return out
+
+
 def prefill_bench(torch, mc, sy, steps, warmup, ts):
     """the same layer with Q4 experts, prefill of T tokens,
     router logits skewed by a seeded per-expert bias ~ N(0,1) (ragged expert
@@ -679,6 +701,12 @@ def run_ours(args):
             c1 = gemv_c1(torch, mc, sy, peak)
         except Exception as exc:       # the headline line must still be printed
             c1 = {"error": str(exc)[:300]}
+    c4 = None
+    if world == 1 and not args.no_full_model:
+        try:
+            c4 = full_model_c4()
+        except Exception as exc:       # the headline line must still be printed
+            c4 = {"error": str(exc)[:300]}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(mc, host_layer_from_device(torch, mc, sy, dt), T)
@@ -701,7 +729,7 @@ def run_ours(args):
                 "kernels": kern, "gpu_launches": int(round(launches_per_step * steps)),
                 "gpu_launches_per_step": launches_per_step,
                 "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu, "extra": extra,
-                "prefill_q4": prefill, "q4_batch32": q4b, "gemv_c1": c1}
+                "prefill_q4": prefill, "q4_batch32": q4b, "gemv_c1": c1, "full_model_q8": c4}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
