@@ -1,7 +1,7 @@
 """Generate tests/golden/*.npz from the REFERENCE itself.
 
-Run in a container where the reference sources are present (default
-/root/reference, override with MOE_REF_DIR) after `make -C oracle`:
+Run where the reference sources are present (the directory REF_DIR below,
+overridable with MOE_REF_DIR) after `make -C oracle`:
 
     python tests/golden/make_golden.py
 
