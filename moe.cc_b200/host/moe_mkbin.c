@@ -8,8 +8,11 @@
  *   moe_mkbin --out FILE [--layers 48] [--quant q8|q4|none] [--seed 1]
  *             [--std 0.02] [--d-model 2048] [--n-q 32] [--n-kv 4]
  *             [--head-dim 128] [--d-ff 768] [--experts 128] [--vocab 151936]
- *             [--tied]
+ *             [--tied] [--count tensors|records]
  *
+ * --count records writes the number of records as the header count instead:
+ * merge_bins.py (merge_bins.py:14-37) reads exactly that many records from
+ * each input, so only files counted this way pass through it whole.
  * Tensor order follows the model's state dict: embed_tokens; per layer
  * q/k/v/o_proj, q_norm, k_norm, mlp.gate, experts e = 0..E-1 gate/up/down,
  * input_layernorm, post_attention_layernorm; model.norm; lm_head (absent
@@ -67,7 +70,7 @@ static int put_expert(Ctx* c, const char* name, uint64_t layer, uint64_t tid, in
 
 int main(int argc, char** argv) {
   const char* out = NULL;
-  int layers = 48, D = 2048, nq = 32, nkv = 4, hd = 128, F = 768, E = 128, V = 151936, tied = 0;
+  int layers = 48, D = 2048, nq = 32, nkv = 4, hd = 128, F = 768, E = 128, V = 151936, tied = 0, by_records = 0;
   Ctx c = {0};
   c.seed = 1; c.std = 0.02f; c.quant = MOE_DTYPE_Q8;
   for (int i = 1; i < argc; ++i) {
@@ -87,6 +90,7 @@ int main(int argc, char** argv) {
     else if (!strcmp(a, "--d-ff")) F = atoi(v);
     else if (!strcmp(a, "--experts")) E = atoi(v);
     else if (!strcmp(a, "--vocab")) V = atoi(v);
+    else if (!strcmp(a, "--count")) by_records = !strcmp(v, "records");
     else { fprintf(stderr, "unknown option %s\n", a); return 2; }
   }
   if (!out || layers < 1 || D < 2 || nq < 1 || nkv < 1 || hd < 2 || F < 2 || E < 1 || V < 1) {
@@ -100,7 +104,9 @@ int main(int argc, char** argv) {
   c.qbuf = malloc((size_t)F * D);   /* the largest expert projection, as int8 */
   c.sbuf = (float*)malloc(sizeof(float) * (size_t)(F > D ? F : D));
   if (!c.buf || !c.qbuf || !c.sbuf) { fprintf(stderr, "out of host memory\n"); return 1; }
-  const uint32_t count = 1 + (uint32_t)layers * (9 + 3 * (uint32_t)E) + 1 + (tied ? 0 : 1);
+  const uint32_t per_expert = c.quant ? 2 : 1;   /* records per expert projection */
+  const uint32_t count = 1 + (uint32_t)layers * (9 + 3 * (uint32_t)E * (by_records ? per_expert : 1)) + 1 +
+                         (tied ? 0 : 1);
   c.w = moe_bin_create(out, count);
   if (!c.w) { fprintf(stderr, "%s\n", moe_cuda_last_error()); return 1; }
   int rc = 0;

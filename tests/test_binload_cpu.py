@@ -179,3 +179,25 @@ def test_mkbin_matches_reference_export_and_merge(tmp_path):
         assert b.layer_info(1) == (8, 64, 32, mc.Q4, 0)
         # header count = original tensors (merge_dir.py:37-39), records beyond it
         assert open(p, "rb").read()[6:10] == (1 + 2 * (9 + 24) + 2).to_bytes(4, "little")
+
+
+def test_mkbin_record_count_passes_merge_bins(tmp_path):
+    """merge_bins.py (the reference's merger of .bin files) reads exactly
+    `count` records per input: a file counted by records (--count records)
+    passes through it byte for byte, one counted by original tensors (the
+    merge_dir.py layout) loses its extra quantised records there."""
+    import subprocess
+    import sys
+    sys.path.insert(0, GOLDEN)
+    from make_golden import REF_DIR
+    script = os.path.join(REF_DIR, "merge_bins.py")
+    if not os.path.exists(script):
+        pytest.skip("the reference's merge_bins.py is not present")
+    tool = os.path.join(os.path.dirname(mc.LIB_PATH), "moe_mkbin")
+    args = ["--layers", "2", "--d-model", "64", "--n-q", "4", "--n-kv", "2", "--head-dim", "16", "--d-ff", "32",
+            "--experts", "8", "--vocab", "97", "--seed", "3", "--quant", "q4"]
+    for count, whole in (("records", True), ("tensors", False)):
+        src, dst = str(tmp_path / f"{count}.bin"), str(tmp_path / f"{count}_merged.bin")
+        subprocess.check_call([tool, "--out", src, "--count", count] + args)
+        subprocess.check_call([sys.executable, script, dst, src], stdout=subprocess.DEVNULL)
+        assert (open(dst, "rb").read() == open(src, "rb").read()) == whole
