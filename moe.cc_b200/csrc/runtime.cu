@@ -9,6 +9,7 @@
 #include <string.h>
 
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -79,10 +80,43 @@ static int ensure_init() {
   return MOE_OK;
 }
 
+// ---- graph replay of host-pointer moe_ffn calls (MOE_E2E_GRAPH=1) ----------
+// A host-pointer call is: two host-to-device copies, the kernels, two or
+// three device-to-host copies and the error-word readback. With the switch
+// on, each (layer, T, flags, outputs) key is captured once into a CUDA graph
+// (kernels as a child graph between explicit memcpy nodes) and replayed with
+// one launch; only the memcpy nodes' host pointers change between calls.
+// The graphs hold workspace and layer pointers, so every event that moves
+// them (workspace growth, upload, free, shutdown) drops the cache.
+struct HostGraph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  cudaGraphNode_t in_xn = nullptr, in_xo = nullptr, out_xo = nullptr, out_idx = nullptr, out_p = nullptr;
+  int eager_calls = 0;     // calls made eagerly before the capture (sets kernel attributes)
+  bool failed = false;     // capture or instantiation refused: this key stays eager
+};
+static std::map<std::tuple<int, int, int, bool, bool>, HostGraph> g_host_graphs;
+static cudaStream_t g_host_stream = nullptr;
+
+static void host_graphs_reset() {
+  for (auto& kv : g_host_graphs) {
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
+  }
+  g_host_graphs.clear();
+}
+
+static bool e2e_graph_on() {
+  static int v = -1;
+  if (v < 0) { const char* e = getenv("MOE_E2E_GRAPH"); v = e && atoi(e) != 0; }
+  return v == 1;
+}
+
 // Grow the workspace to hold T tokens for a layer of shape (E, D, F, K).
 static int ensure_workspace(int T, int E, int D, int F, int K) {
   Workspace& w = g.ws;
   if (T <= w.cap_T && E <= w.cap_E && D <= w.cap_D && F <= w.cap_F && K <= w.cap_K) return MOE_OK;
+  host_graphs_reset();
   int nT = T > w.cap_T ? (T > 2 * w.cap_T ? T : 2 * w.cap_T) : w.cap_T;
   if (nT < 32) nT = 32;  // >= the widest decode tile: token rows are read as a tile
   const int nE = E > w.cap_E ? E : w.cap_E, nD = D > w.cap_D ? D : w.cap_D;
@@ -294,6 +328,8 @@ int moe_cuda_shutdown(void) {
   std::lock_guard<std::recursive_mutex> lk(g.mu);
   if (!g.init) return MOE_OK;
   cudaDeviceSynchronize();
+  host_graphs_reset();
+  if (g_host_stream) { cudaStreamDestroy(g_host_stream); g_host_stream = nullptr; }
   ep_shutdown_hook();
   for (auto& kv : g.layers) {
     cudaFree(kv.second.slab); cudaFree(kv.second.router_w);
@@ -489,6 +525,7 @@ static int upload_layer(int layer, const QuantizedWeight* Wg, const QuantizedWei
   int D, F, dtype;
   if ((rc = validate_layer(Wg, Wu, Wd, E, &D, &F, &dtype))) return rc;
   if (!router_w) return set_err(MOE_ERR_INVALID, "router_w is NULL");
+  host_graphs_reset();
   if (g.layers.count(layer)) moe_cuda_free_layer(layer);
   LayerDev L;
   L.E = E; L.D = D; L.F = F; L.dtype = dtype; L.topk = 8;
@@ -651,6 +688,108 @@ static bool use_tensor_cores(const LayerDev& L, int flags) {
 // Tokens at or below this count use the fused down+combine epilogue.
 constexpr int kFuseCombineMaxT = 64;
 
+// Captures the kernels of one host-pointer call into hg (between explicit
+// memcpy nodes for the inputs, outputs and error word). False, with nothing
+// kept, when the runtime refuses any step.
+template <class Enqueue>
+static bool build_host_graph(HostGraph& hg, cudaStream_t st, const float* x_norm2, float* x_inout, int* idx_out,
+                             float* p_out, size_t xb, size_t kb, Enqueue& enqueue) {
+  const Workspace& w = g.ws;
+  cudaGraph_t kg = nullptr, gr = nullptr;
+  if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return false;
+  const int rc = enqueue(w.xn, w.xo, st);
+  const cudaError_t ce = cudaStreamEndCapture(st, &kg);
+  if (rc || ce != cudaSuccess || !kg) {
+    if (kg) cudaGraphDestroy(kg);
+    cudaGetLastError();
+    return false;
+  }
+  const cudaMemcpyKind h2d = cudaMemcpyHostToDevice, d2h = cudaMemcpyDeviceToHost;
+  cudaGraphNode_t child = nullptr, err = nullptr;
+  bool ok = cudaGraphCreate(&gr, 0) == cudaSuccess;
+  ok = ok && cudaGraphAddMemcpyNode1D(&hg.in_xn, gr, nullptr, 0, w.xn, x_norm2, xb, h2d) == cudaSuccess;
+  ok = ok && cudaGraphAddMemcpyNode1D(&hg.in_xo, gr, nullptr, 0, w.xo, x_inout, xb, h2d) == cudaSuccess;
+  cudaGraphNode_t ins[2] = {hg.in_xn, hg.in_xo};
+  ok = ok && cudaGraphAddChildGraphNode(&child, gr, ins, 2, kg) == cudaSuccess;
+  cudaGraphDestroy(kg);                          // the child node holds its own copy
+  ok = ok && cudaGraphAddMemcpyNode1D(&hg.out_xo, gr, &child, 1, x_inout, w.xo, xb, d2h) == cudaSuccess;
+  if (idx_out)
+    ok = ok && cudaGraphAddMemcpyNode1D(&hg.out_idx, gr, &child, 1, idx_out, w.topk_idx, kb, d2h) == cudaSuccess;
+  if (p_out)
+    ok = ok && cudaGraphAddMemcpyNode1D(&hg.out_p, gr, &child, 1, p_out, w.topk_p, kb, d2h) == cudaSuccess;
+  ok = ok && cudaGraphAddMemcpyNode1D(&err, gr, &child, 1, g.h_err, g.d_err, sizeof(int), d2h) == cudaSuccess;
+  ok = ok && cudaGraphInstantiate(&hg.exec, gr, 0) == cudaSuccess;
+  if (!ok) {
+    if (hg.exec) cudaGraphExecDestroy(hg.exec);
+    if (gr) cudaGraphDestroy(gr);
+    hg = HostGraph{};
+    cudaGetLastError();
+    return false;
+  }
+  hg.graph = gr;
+  return true;
+}
+
+// Host-pointer moe_ffn through a cached graph (MOE_E2E_GRAPH=1, stream NULL).
+// The library's own blocking stream keeps the order the legacy stream gives
+// the eager path. The first call of each key runs eagerly (it sets kernel
+// attributes and encodes tensor maps outside any capture); any key whose
+// capture, instantiation or node update the runtime refuses stays eager.
+template <class Enqueue>
+static int moe_ffn_host_graph(int layer, int T, int flags, const float* x_norm2, float* x_inout, int* idx_out,
+                              float* p_out, size_t xb, size_t kb, Enqueue& enqueue) {
+  const Workspace& w = g.ws;
+  if (!g_host_stream) CU(cudaStreamCreate(&g_host_stream));
+  cudaStream_t st = g_host_stream;
+  HostGraph& hg = g_host_graphs[std::make_tuple(layer, T, flags, idx_out != nullptr, p_out != nullptr)];
+  auto eager = [&]() -> int {
+    CU(cudaMemcpyAsync(w.xn, x_norm2, xb, cudaMemcpyHostToDevice, st));
+    CU(cudaMemcpyAsync(w.xo, x_inout, xb, cudaMemcpyHostToDevice, st));
+    const int rc = enqueue(w.xn, w.xo, st);
+    if (rc) return rc;
+    if (idx_out) CU(cudaMemcpyAsync(idx_out, w.topk_idx, kb, cudaMemcpyDeviceToHost, st));
+    if (p_out) CU(cudaMemcpyAsync(p_out, w.topk_p, kb, cudaMemcpyDeviceToHost, st));
+    CU(cudaMemcpyAsync(x_inout, w.xo, xb, cudaMemcpyDeviceToHost, st));
+    return consume_stream_error(st);
+  };
+  if (hg.failed || hg.eager_calls < 1) {
+    hg.eager_calls++;
+    return eager();
+  }
+  if (!hg.exec) {
+    if (!build_host_graph(hg, st, x_norm2, x_inout, idx_out, p_out, xb, kb, enqueue)) {
+      hg.failed = true;
+      return eager();
+    }
+  } else {
+    const cudaMemcpyKind h2d = cudaMemcpyHostToDevice, d2h = cudaMemcpyDeviceToHost;
+    bool ok = cudaGraphExecMemcpyNodeSetParams1D(hg.exec, hg.in_xn, w.xn, x_norm2, xb, h2d) == cudaSuccess &&
+              cudaGraphExecMemcpyNodeSetParams1D(hg.exec, hg.in_xo, w.xo, x_inout, xb, h2d) == cudaSuccess &&
+              cudaGraphExecMemcpyNodeSetParams1D(hg.exec, hg.out_xo, x_inout, w.xo, xb, d2h) == cudaSuccess;
+    if (ok && idx_out)
+      ok = cudaGraphExecMemcpyNodeSetParams1D(hg.exec, hg.out_idx, idx_out, w.topk_idx, kb, d2h) == cudaSuccess;
+    if (ok && p_out)
+      ok = cudaGraphExecMemcpyNodeSetParams1D(hg.exec, hg.out_p, p_out, w.topk_p, kb, d2h) == cudaSuccess;
+    if (!ok) {
+      cudaGetLastError();
+      cudaGraphExecDestroy(hg.exec);
+      cudaGraphDestroy(hg.graph);
+      hg = HostGraph{};
+      hg.failed = true;
+      return eager();
+    }
+  }
+  CU(cudaGraphLaunch(hg.exec, st));
+  CU(cudaStreamSynchronize(st));
+  const int h = *g.h_err;
+  if (h) {
+    *g.h_err = 0;
+    CU(cudaMemsetAsync(g.d_err, 0, sizeof(int), st));
+    CU(cudaStreamSynchronize(st));
+  }
+  return error_status(h);
+}
+
 // Upload whose experts come from a reader (the .bin loader); router_w and
 // router_b are host memory the caller frees right after, so no host-pointer
 // aliases are registered.
@@ -684,6 +823,7 @@ int moe_cuda_free_layer(int layer) {
   auto it = g.layers.find(layer);
   if (it == g.layers.end()) return set_err(MOE_ERR_NOT_INIT, "layer %d was not uploaded", layer);
   cudaDeviceSynchronize();
+  host_graphs_reset();
   LayerDev& L = it->second;
   for (auto a = g.alias.begin(); a != g.alias.end();) {
     const uint8_t* d = (const uint8_t*)a->second.dev;
@@ -719,6 +859,47 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
   const bool host = flags & MOE_FFN_HOST_PTRS;
   const Workspace& w = g.ws;
   const size_t xb = sizeof(float) * (size_t)T * L.D;
+  // The kernels of one call on stream s: read xn, update xo in place.
+  auto enqueue = [&](const float* xn, float* xo, cudaStream_t s) -> int {
+    if (use_tensor_cores(L, flags)) {
+      const int fnt = fused_tile_n(L, T);                 // fused gate/up + down kernel, if used
+      const int nt = fnt ? fnt : mma_tile_n(T, L.dtype);
+      // The combine runs as its own kernel: fused into the down epilogue it left
+      // the last warp through each row block with T*K dependent loads at the
+      // end of the kernel (measured 90 us vs 39 + 6 us). MOE_MMA_FUSE=1 restores it.
+      static int fuse_env = -1;
+      if (fuse_env < 0) {
+        const char* e = getenv("MOE_MMA_FUSE");
+        fuse_env = e ? atoi(e) : 0;
+      }
+      const bool fuse = fuse_env && T <= kFuseCombineMaxT;
+      route_tokens(L, xn, T, nt, s);
+      if (T > nt) timed("gather", s, [&] { launch_mma_gather(L, w, T, nt, s); });
+      bool ok = true;
+      if (!fuse && fnt) {
+        timed("mma_fused", s, [&] { ok = launch_mma_fused(L, w, T, nt, g.d_err, s); });
+      } else {
+        timed("mma_gateup", s, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, s); });
+        if (ok) timed("mma_down", s, [&] { ok = launch_mma_down(L, w, T, nt, w.y, fuse, xo, xo, g.d_err, s); });
+      }
+      if (!ok) return set_err(MOE_ERR_CUDA, "tensor-core launch failed (tensor map or shared memory)");
+      if (!fuse)
+        timed("combine", s, [&] {
+          launch_combine_sorted(w.y, w.slot_pos, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s);
+        });
+    } else {
+      const bool fuse = T <= kFuseCombineMaxT;
+      route_tokens(L, xn, T, 0, s);
+      timed("gateup", s, [&] { run_gateup(L, w, T, s); });
+      timed("down", s, [&] { run_down(L, w, T, w.y, fuse, xo, xo, s); });
+      if (!fuse) timed("combine", s, [&] { launch_combine(w.y, w.topk_p, xo, xo, T, L.D, L.topk, s); });
+    }
+    CU(cudaGetLastError());
+    return MOE_OK;
+  };
+  if (host && !st && !g_prof && e2e_graph_on())
+    return moe_ffn_host_graph(layer, T, flags, x_norm2, x_inout, topk_idx_out, topk_p_out, xb,
+                              sizeof(int) * (size_t)T * L.topk, enqueue);
   const float* xn = x_norm2;
   float* xo = x_inout;
   if (host) {
@@ -726,40 +907,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
     CU(cudaMemcpyAsync(w.xo, x_inout, xb, cudaMemcpyHostToDevice, st));
     xn = w.xn; xo = w.xo;
   }
-  if (use_tensor_cores(L, flags)) {
-    const int fnt = fused_tile_n(L, T);                 // fused gate/up + down kernel, if used
-    const int nt = fnt ? fnt : mma_tile_n(T, L.dtype);
-    // The combine runs as its own kernel: fused into the down epilogue it left
-    // the last warp through each row block with T*K dependent loads at the
-    // end of the kernel (measured 90 us vs 39 + 6 us). MOE_MMA_FUSE=1 restores it.
-    static int fuse_env = -1;
-    if (fuse_env < 0) {
-      const char* e = getenv("MOE_MMA_FUSE");
-      fuse_env = e ? atoi(e) : 0;
-    }
-    const bool fuse = fuse_env && T <= kFuseCombineMaxT;
-    route_tokens(L, xn, T, nt, st);
-    if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, nt, st); });
-    bool ok = true;
-    if (!fuse && fnt) {
-      timed("mma_fused", st, [&] { ok = launch_mma_fused(L, w, T, nt, g.d_err, st); });
-    } else {
-      timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
-      if (ok) timed("mma_down", st, [&] { ok = launch_mma_down(L, w, T, nt, w.y, fuse, xo, xo, g.d_err, st); });
-    }
-    if (!ok) return set_err(MOE_ERR_CUDA, "tensor-core launch failed (tensor map or shared memory)");
-    if (!fuse)
-      timed("combine", st, [&] {
-        launch_combine_sorted(w.y, w.slot_pos, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, st);
-      });
-  } else {
-    const bool fuse = T <= kFuseCombineMaxT;
-    route_tokens(L, xn, T, 0, st);
-    timed("gateup", st, [&] { run_gateup(L, w, T, st); });
-    timed("down", st, [&] { run_down(L, w, T, w.y, fuse, xo, xo, st); });
-    if (!fuse) timed("combine", st, [&] { launch_combine(w.y, w.topk_p, xo, xo, T, L.D, L.topk, st); });
-  }
-  CU(cudaGetLastError());
+  if ((rc = enqueue(xn, xo, st))) return rc;
   const size_t kb = sizeof(int) * (size_t)T * L.topk;
   const cudaMemcpyKind out_kind = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
   if (topk_idx_out) CU(cudaMemcpyAsync(topk_idx_out, w.topk_idx, kb, out_kind, st));
