@@ -116,15 +116,16 @@ __attribute__((target("avx2"))) static inline void transpose8(__m256 r[8]) {
   r[6] = _mm256_permute2f128_ps(s2, s6, 0x31); r[7] = _mm256_permute2f128_ps(s3, s7, 0x31);
 }
 
-/* outputs n0..n0+15 of row a (all 16 rows exist) */
-__attribute__((target("avx2"))) static void dot16_avx2(const float* a, const float* w, float* c, int K) {
+/* c[j] = chain(a . w[j]) for the 16 rows w + j*ldw, j = 0..15 */
+__attribute__((target("avx2"))) static void dot16_avx2(const float* a, const float* w, size_t ldw, float* c,
+                                                       int K) {
   __m256 acc0 = _mm256_setzero_ps(), acc1 = _mm256_setzero_ps();
   const int K8 = K & ~7;
   for (int k = 0; k < K8; k += 8) {
     __m256 r[8], q[8];
     for (int j = 0; j < 8; ++j) {
-      r[j] = _mm256_loadu_ps(w + (size_t)j * K + k);
-      q[j] = _mm256_loadu_ps(w + (size_t)(j + 8) * K + k);
+      r[j] = _mm256_loadu_ps(w + (size_t)j * ldw + k);
+      q[j] = _mm256_loadu_ps(w + (size_t)(j + 8) * ldw + k);
     }
     transpose8(r);
     transpose8(q);
@@ -138,7 +139,7 @@ __attribute__((target("avx2"))) static void dot16_avx2(const float* a, const flo
   _mm256_storeu_ps(acc, acc0);
   _mm256_storeu_ps(acc + 8, acc1);
   for (int k = K8; k < K; ++k)
-    for (int j = 0; j < 16; ++j) acc[j] += a[k] * w[(size_t)j * K + k];
+    for (int j = 0; j < 16; ++j) acc[j] += a[k] * w[(size_t)j * ldw + k];
   memcpy(c, acc, sizeof(acc));
 }
 
@@ -147,7 +148,8 @@ static int use_avx2(void) {
   static int v = -1;
   if (v < 0) {
     __builtin_cpu_init();
-    v = !getenv("MOE_HOST_SCALAR") && __builtin_cpu_supports("avx2");
+    const char* e = getenv("MOE_HOST_SCALAR");
+    v = !(e && atoi(e)) && __builtin_cpu_supports("avx2");
   }
   return v;
 }
@@ -159,7 +161,7 @@ static void mm_f32(const float* A, const float* W, float* C, int M, int N, int K
 #pragma omp parallel for schedule(static)
     for (int b = 0; b < nb; ++b)
       for (int m = 0; m < M; ++m)
-        dot16_avx2(A + (size_t)m * K, W + (size_t)16 * b * K, C + (size_t)m * N + 16 * b, K);
+        dot16_avx2(A + (size_t)m * K, W + (size_t)16 * b * K, (size_t)K, C + (size_t)m * N + 16 * b, K);
     const int n_done = nb * 16;
     for (int m = 0; m < M; ++m)
       for (int n = n_done; n < N; ++n) {
@@ -394,6 +396,7 @@ int mh_attention(MhModel* m, int layer, const float* x, int T, float* x_after, f
   /* one task per (sequence, KV head, new token): the group's query heads
      share each pass over the cached keys and values */
   const float scale = 1.0f / sqrtf((float)hd);
+  const int avx = use_avx2();
   const int tasks = m->batch * nkv * T;
 #pragma omp parallel for schedule(dynamic, 1)
   for (int task = 0; task < tasks; ++task) {
@@ -401,13 +404,21 @@ int mh_attention(MhModel* m, int layer, const float* x, int T, float* x_after, f
     const int P = m->pos + t;                           /* keys 0..P */
     float* S = m->scores + (size_t)omp_get_thread_num() * group * m->max_ctx;
     const float* qrow = m->q + ((size_t)b * T + t) * Dq;
-    for (int tk = 0; tk <= P; ++tk) {
-      const float* kv = kv_row(m, m->kc, layer, b, tk) + (size_t)kvh * hd;
-      for (int g = 0; g < group; ++g) {
-        const float* qv = qrow + (size_t)(kvh * group + g) * hd;
+    /* scores: keys are rows of stride Dkv, so 16 keys at a time take the
+       matmul's transposed-lane chains; the rest one chain each */
+    const int tk16 = avx ? (P + 1) & ~15 : 0;
+    for (int g = 0; g < group; ++g) {
+      const float* qv = qrow + (size_t)(kvh * group + g) * hd;
+      float* Sg = S + (size_t)g * m->max_ctx;
+      for (int tk = 0; tk < tk16; tk += 16) {
+        dot16_avx2(qv, kv_row(m, m->kc, layer, b, tk) + (size_t)kvh * hd, (size_t)Dkv, Sg + tk, hd);
+        for (int j = 0; j < 16; ++j) Sg[tk + j] = Sg[tk + j] * scale;
+      }
+      for (int tk = tk16; tk <= P; ++tk) {
+        const float* kv = kv_row(m, m->kc, layer, b, tk) + (size_t)kvh * hd;
         float dot = 0.f;
         for (int d = 0; d < hd; ++d) dot += qv[d] * kv[d];
-        S[(size_t)g * m->max_ctx + tk] = dot * scale;
+        Sg[tk] = dot * scale;
       }
     }
     for (int g = 0; g < group; ++g) {

@@ -149,7 +149,7 @@ def test_scalar_path_too():
     import sys
     env = dict(os.environ, MOE_HOST_SCALAR="1")
     r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider", __file__,
-                        "-k", "head_is or cached_decode"], env=env, capture_output=True, text=True, timeout=600)
+                        "-k", "head_is or cached_decode or long_prefix"], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:]
 
 
@@ -165,3 +165,24 @@ def test_generate_program_fails_loudly_without_gpu():
     r = subprocess.run([tool, "--layers", "1", "--steps", "2", "--prompt", "2"], capture_output=True, text=True,
                        timeout=120)
     assert r.returncode != 0 and "moe_cuda_init" in r.stderr and not r.stdout
+
+
+@needs_ref
+def test_long_prefix_matches_reference():
+    """A 21-token prompt then decode to 27 positions: key blocks of 16 plus
+    remainders in the attention scores, against the full recompute."""
+    g, attn, moe = tiny_model(2, seed=3)
+    ref, port = Ref(), Port()
+    B = 2
+    rng = np.random.default_rng(77)
+    seqs = [list(rng.integers(0, TINY["vocab_size"], 21)) for _ in range(B)]
+    model = mh.HostModel(TINY, batch=B, max_ctx=40)
+    load(model, g, attn)
+    logits = cpu_step(model, port, moe, np.array(seqs))
+    for s in range(6):
+        for b in range(B):
+            assert np.array_equal(logits[b], ref.model_forward(seqs[b], TINY, g, attn, moe)), f"step {s}"
+        nxt = model.pick_greedy(logits)
+        for b in range(B):
+            seqs[b].append(int(nxt[b]))
+        logits = cpu_step(model, port, moe, nxt)
