@@ -53,7 +53,7 @@ struct MhModel {
   /* per-step scratch, grown to the step's rows */
   int cap_rows;
   float *xn1, *q, *k, *v, *hcat, *ao, *x, *xa, *xn2, *xlast;
-  float* scores;                 /* per thread: group x max_ctx */
+  float* scores;                 /* per thread: max_ctx */
   int n_threads;
   float* inv_freq;               /* head_dim / 2 */
   double* moe_ms;
@@ -257,8 +257,7 @@ MhModel* mh_create(const MhConfig* cfg, int batch, int max_ctx, int moe_layer_ba
   m->kc = (float*)malloc(sizeof(float) * kv);
   m->vc = (float*)malloc(sizeof(float) * kv);
   m->n_threads = omp_get_max_threads();
-  const int group = cfg->n_q / cfg->n_kv;
-  m->scores = (float*)malloc(sizeof(float) * (size_t)m->n_threads * group * max_ctx);
+  m->scores = (float*)malloc(sizeof(float) * (size_t)m->n_threads * max_ctx);
   m->inv_freq = (float*)malloc(sizeof(float) * (size_t)(cfg->head_dim / 2));
   m->moe_ms = (double*)calloc((size_t)cfg->n_layers, sizeof(double));
   m->moe_calls = (long*)calloc((size_t)cfg->n_layers, sizeof(long));
@@ -393,52 +392,49 @@ int mh_attention(MhModel* m, int layer, const float* x, int T, float* x_after, f
     memcpy(kv_row(m, m->vc, layer, b, m->pos + t), m->v + (size_t)r * Dkv, sizeof(float) * (size_t)Dkv);
   }
 
-  /* one task per (sequence, KV head, new token): the group's query heads
-     share each pass over the cached keys and values */
+  /* one task per (sequence, query head, new token); one score row per thread */
   const float scale = 1.0f / sqrtf((float)hd);
   const int avx = use_avx2();
-  const int tasks = m->batch * nkv * T;
-#pragma omp parallel for schedule(dynamic, 1)
+  const int tasks = m->batch * nq * T;
+  const int nth = omp_get_max_threads();
+  if (nth > m->n_threads) {
+    float* sc = (float*)realloc(m->scores, sizeof(float) * (size_t)nth * m->max_ctx);
+    if (!sc) return fail(MOE_ERR_NOMEM, "attention score rows for %d threads", nth);
+    m->scores = sc;
+    m->n_threads = nth;
+  }
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nth)
   for (int task = 0; task < tasks; ++task) {
-    const int t = task % T, kvh = (task / T) % nkv, b = task / (T * nkv);
+    const int t = task % T, h = (task / T) % nq, b = task / (T * nq);
+    const int kvh = h / group;
     const int P = m->pos + t;                           /* keys 0..P */
-    float* S = m->scores + (size_t)omp_get_thread_num() * group * m->max_ctx;
-    const float* qrow = m->q + ((size_t)b * T + t) * Dq;
+    float* S = m->scores + (size_t)omp_get_thread_num() * m->max_ctx;
+    const float* qv = m->q + ((size_t)b * T + t) * Dq + (size_t)h * hd;
     /* scores: keys are rows of stride Dkv, so 16 keys at a time take the
        matmul's transposed-lane chains; the rest one chain each */
     const int tk16 = avx ? (P + 1) & ~15 : 0;
-    for (int g = 0; g < group; ++g) {
-      const float* qv = qrow + (size_t)(kvh * group + g) * hd;
-      float* Sg = S + (size_t)g * m->max_ctx;
-      for (int tk = 0; tk < tk16; tk += 16) {
-        dot16_avx2(qv, kv_row(m, m->kc, layer, b, tk) + (size_t)kvh * hd, (size_t)Dkv, Sg + tk, hd);
-        for (int j = 0; j < 16; ++j) Sg[tk + j] = Sg[tk + j] * scale;
-      }
-      for (int tk = tk16; tk <= P; ++tk) {
-        const float* kv = kv_row(m, m->kc, layer, b, tk) + (size_t)kvh * hd;
-        float dot = 0.f;
-        for (int d = 0; d < hd; ++d) dot += qv[d] * kv[d];
-        Sg[tk] = dot * scale;
-      }
+    for (int tk = 0; tk < tk16; tk += 16) {
+      dot16_avx2(qv, kv_row(m, m->kc, layer, b, tk) + (size_t)kvh * hd, (size_t)Dkv, S + tk, hd);
+      for (int j = 0; j < 16; ++j) S[tk + j] = S[tk + j] * scale;
     }
-    for (int g = 0; g < group; ++g) {
-      float* Sg = S + (size_t)g * m->max_ctx;
-      float mx = Sg[0];
-      for (int i = 1; i <= P; ++i) if (Sg[i] > mx) mx = Sg[i];
-      float ssum = 0.f;
-      for (int i = 0; i <= P; ++i) { const float e = expf(Sg[i] - mx); Sg[i] = e; ssum += e; }
-      const float inv = 1.f / (ssum + 1e-9f);
-      for (int i = 0; i <= P; ++i) Sg[i] *= inv;
-      float* out = m->hcat + ((size_t)b * T + t) * Dq + (size_t)(kvh * group + g) * hd;
-      for (int d = 0; d < hd; ++d) out[d] = 0.f;
+    for (int tk = tk16; tk <= P; ++tk) {
+      const float* kv = kv_row(m, m->kc, layer, b, tk) + (size_t)kvh * hd;
+      float dot = 0.f;
+      for (int d = 0; d < hd; ++d) dot += qv[d] * kv[d];
+      S[tk] = dot * scale;
     }
+    float mx = S[0];
+    for (int i = 1; i <= P; ++i) if (S[i] > mx) mx = S[i];
+    float ssum = 0.f;
+    for (int i = 0; i <= P; ++i) { const float e = expf(S[i] - mx); S[i] = e; ssum += e; }
+    const float inv = 1.f / (ssum + 1e-9f);
+    for (int i = 0; i <= P; ++i) S[i] *= inv;
+    float* out = m->hcat + ((size_t)b * T + t) * Dq + (size_t)h * hd;
+    for (int d = 0; d < hd; ++d) out[d] = 0.f;
     for (int tk = 0; tk <= P; ++tk) {
       const float* vv = kv_row(m, m->vc, layer, b, tk) + (size_t)kvh * hd;
-      for (int g = 0; g < group; ++g) {
-        const float pr = S[(size_t)g * m->max_ctx + tk];
-        float* out = m->hcat + ((size_t)b * T + t) * Dq + (size_t)(kvh * group + g) * hd;
-        for (int d = 0; d < hd; ++d) out[d] += pr * vv[d];
-      }
+      const float pr = S[tk];
+      for (int d = 0; d < hd; ++d) out[d] += pr * vv[d];
     }
   }
 
