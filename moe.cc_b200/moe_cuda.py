@@ -297,7 +297,7 @@ class BinWriter:
             raise MoeError(MOE_ERR_INVALID, lib().moe_cuda_last_error().decode())
 
     def put(self, name, a):
-        a = np.ascontiguousarray(a)
+        a = np.require(a, requirements="C")   # keeps 0-d arrays 0-d
         shape = (C.c_int * max(1, a.ndim))(*a.shape)
         check(lib().moe_bin_put(self.h, name.encode(), self._DT[a.dtype], a.ndim, shape, a.ctypes.data))
 

@@ -64,7 +64,7 @@ def write_bin(path, tensors, count=None):
         f.write(BIN_MAGIC)
         f.write(struct.pack("<I", len(tensors) if count is None else count))
         for name, a in tensors:
-            a = np.ascontiguousarray(a)
+            a = np.require(a, requirements="C")   # keeps 0-d arrays 0-d
             nb = name.encode()
             f.write(struct.pack("<I", len(nb)) + nb)
             f.write(struct.pack("<II", _BIN_DTYPE[a.dtype], a.ndim))

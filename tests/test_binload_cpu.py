@@ -201,3 +201,19 @@ def test_mkbin_record_count_passes_merge_bins(tmp_path):
         subprocess.check_call([tool, "--out", src, "--count", count] + args)
         subprocess.check_call([sys.executable, script, dst, src], stdout=subprocess.DEVNULL)
         assert (open(dst, "rb").read() == open(src, "rb").read()) == whole
+
+
+def test_writer_dtypes_and_errors(tmp_path):
+    p = str(tmp_path / "d.bin")
+    a16 = np.arange(12, dtype=np.float16).reshape(3, 4)
+    scalar = np.array(3.5, np.float32)                   # ndim 0: one element
+    w = mc.BinWriter(p, 2)
+    w.put("half", a16)
+    w.put("scalar", scalar)
+    with pytest.raises(mc.MoeError):
+        mc.check(mc.lib().moe_bin_put(w.h, b"bad", 7, 0, None, scalar.ctypes.data))   # unknown dtype
+    w.finish()
+    with mc.BinFile(p) as b:
+        assert b.find("half") == (1, (3, 4), 24) and np.array_equal(b.read("half"), a16)
+        assert b.find("scalar") == (0, (), 4) and b.read("scalar") == scalar
+    assert mc.lib().moe_bin_create(str(tmp_path / "no" / "dir.bin").encode(), 0) is None
