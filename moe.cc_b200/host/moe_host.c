@@ -143,6 +143,44 @@ __attribute__((target("avx2"))) static void dot16_avx2(const float* a, const flo
   memcpy(c, acc, sizeof(acc));
 }
 
+/* Rows m0..m0+nm-1 (nm <= 64) of A against the 16 rows w + j*ldw: each 16x8
+   weight tile is transposed once and applied to every row; the per-row
+   accumulators live in acc[nm][16] between tiles. Same chains as
+   dot16_avx2, row by row. */
+__attribute__((target("avx2"))) static void dot16_rows_avx2(const float* A, size_t lda, int nm, const float* w,
+                                                            size_t ldw, float* C, size_t ldc, int K) {
+  float acc[64 * 16] __attribute__((aligned(32)));
+  memset(acc, 0, sizeof(float) * 16 * (size_t)nm);
+  const int K8 = K & ~7;
+  for (int k = 0; k < K8; k += 8) {
+    __m256 r[8], q[8];
+    for (int j = 0; j < 8; ++j) {
+      r[j] = _mm256_loadu_ps(w + (size_t)j * ldw + k);
+      q[j] = _mm256_loadu_ps(w + (size_t)(j + 8) * ldw + k);
+    }
+    transpose8(r);
+    transpose8(q);
+    for (int m = 0; m < nm; ++m) {
+      const float* a = A + (size_t)m * lda + k;
+      __m256 acc0 = _mm256_load_ps(acc + 16 * m), acc1 = _mm256_load_ps(acc + 16 * m + 8);
+      for (int i = 0; i < 8; ++i) {
+        const __m256 av = _mm256_set1_ps(a[i]);
+        acc0 = _mm256_add_ps(acc0, _mm256_mul_ps(av, r[i]));
+        acc1 = _mm256_add_ps(acc1, _mm256_mul_ps(av, q[i]));
+      }
+      _mm256_store_ps(acc + 16 * m, acc0);
+      _mm256_store_ps(acc + 16 * m + 8, acc1);
+    }
+  }
+  for (int m = 0; m < nm; ++m) {
+    float* am = acc + 16 * m;
+    const float* a = A + (size_t)m * lda;
+    for (int k = K8; k < K; ++k)
+      for (int j = 0; j < 16; ++j) am[j] += a[k] * w[(size_t)j * ldw + k];
+    memcpy(C + (size_t)m * ldc, am, sizeof(float) * 16);
+  }
+}
+
 /* MOE_HOST_SCALAR=1 keeps the portable path (for tests and comparisons) */
 static int use_avx2(void) {
   static int v = -1;
@@ -159,9 +197,15 @@ static void mm_f32(const float* A, const float* W, float* C, int M, int N, int K
   if (use_avx2() && N >= 16) {
     const int nb = N / 16;
 #pragma omp parallel for schedule(static)
-    for (int b = 0; b < nb; ++b)
-      for (int m = 0; m < M; ++m)
-        dot16_avx2(A + (size_t)m * K, W + (size_t)16 * b * K, (size_t)K, C + (size_t)m * N + 16 * b, K);
+    for (int b = 0; b < nb; ++b) {
+      if (M == 1) {
+        dot16_avx2(A, W + (size_t)16 * b * K, (size_t)K, C + 16 * b, K);
+        continue;
+      }
+      for (int m0 = 0; m0 < M; m0 += 64)
+        dot16_rows_avx2(A + (size_t)m0 * K, (size_t)K, M - m0 < 64 ? M - m0 : 64, W + (size_t)16 * b * K,
+                        (size_t)K, C + (size_t)m0 * N + 16 * b, (size_t)N, K);
+    }
     const int n_done = nb * 16;
     for (int m = 0; m < M; ++m)
       for (int n = n_done; n < N; ++n) {
