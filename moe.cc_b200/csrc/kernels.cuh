@@ -134,6 +134,10 @@ void launch_gateup(const LayerDev& L, const Workspace& ws, int T, int* err,
 void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y,
                  bool fuse_combine, const float* xres, float* out,
                  cudaStream_t st);
+// Expert FFN of every routed slot with exact int32 activations of any
+// magnitude (exact.cu): h [T*K][F] scratch, y [T*K][D] for launch_combine.
+void launch_exact_experts(const LayerDev& L, const float* xn, const int* idx, int T, float* h, float* y,
+                          cudaStream_t st);
 void launch_combine(const float* y, const float* p, const float* xres,
                     float* out, int T, int D, int K, cudaStream_t st);
 void launch_quantize_rowwise(int dtype, const float* W, int rows, int cols,

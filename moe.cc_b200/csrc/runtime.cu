@@ -106,6 +106,12 @@ static void host_graphs_reset() {
   g_host_graphs.clear();
 }
 
+static bool range_rerun_on() {
+  static int v = -1;
+  if (v < 0) { const char* e = getenv("MOE_RANGE_RERUN"); v = e && atoi(e) != 0; }
+  return v == 1;
+}
+
 static bool e2e_graph_on() {
   static int v = -1;
   if (v < 0) { const char* e = getenv("MOE_E2E_GRAPH"); v = e && atoi(e) != 0; }
@@ -212,7 +218,7 @@ using namespace moe;
 namespace moe {
 static void ep_shutdown_hook();   // releases the expert-parallel buffers (defined below)
 struct Buf { void* p = nullptr; size_t cap = 0; };
-static Buf s_A, s_C, s_W, s_S, s_act, s_asum;
+static Buf s_A, s_C, s_W, s_S, s_act, s_asum, s_xres, s_xh;
 
 static int grow(Buf& b, size_t bytes) {
   if (bytes <= b.cap) return MOE_OK;
@@ -343,7 +349,7 @@ int moe_cuda_shutdown(void) {
                   w.fused_ctr};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
-  Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum};
+  Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum, &s_xres, &s_xh};
   for (Buf* b : bufs) { if (b->p) cudaFree(b->p); *b = Buf{}; }
   cudaFree(g.d_err); g.d_err = nullptr;
   if (g.h_err) cudaFreeHost(g.h_err);
@@ -902,6 +908,12 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
                               sizeof(int) * (size_t)T * L.topk, enqueue);
   const float* xn = x_norm2;
   float* xo = x_inout;
+  // MOE_RANGE_RERUN=1: host-pointer calls keep a device copy of x_inout so
+  // that a call the fast kernels refuse (MOE_ERR_RANGE) is recomputed with
+  // exact int32 activations of any magnitude, as the reference computes it.
+  const bool rerun = host && range_rerun_on();
+  if (rerun && (rc = grow(s_xres, xb))) return rc;
+  if (rerun) CU(cudaMemcpyAsync(s_xres.p, x_inout, xb, cudaMemcpyHostToDevice, st));
   if (host) {
     CU(cudaMemcpyAsync(w.xn, x_norm2, xb, cudaMemcpyHostToDevice, st));
     CU(cudaMemcpyAsync(w.xo, x_inout, xb, cudaMemcpyHostToDevice, st));
@@ -914,7 +926,17 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
   if (topk_p_out) CU(cudaMemcpyAsync(topk_p_out, w.topk_p, kb, out_kind, st));
   if (host) {
     CU(cudaMemcpyAsync(x_inout, xo, xb, cudaMemcpyDeviceToHost, st));
-    return consume_stream_error(st);
+    rc = consume_stream_error(st);
+    if (rc == MOE_ERR_RANGE && rerun) {
+      // same routing (fp32, unaffected); experts and combine recomputed
+      if ((rc = grow(s_xh, sizeof(float) * (size_t)T * L.topk * L.F))) return rc;
+      launch_exact_experts(L, w.xn, w.topk_idx, T, (float*)s_xh.p, w.y, st);
+      launch_combine(w.y, w.topk_p, (const float*)s_xres.p, w.xo, T, L.D, L.topk, st);
+      CU(cudaGetLastError());
+      CU(cudaMemcpyAsync(x_inout, w.xo, xb, cudaMemcpyDeviceToHost, st));
+      rc = consume_stream_error(st);
+    }
+    return rc;
   }
   return MOE_OK;
 }
