@@ -181,6 +181,16 @@ __attribute__((target("avx2"))) static void dot16_rows_avx2(const float* A, size
   }
 }
 
+/* out[d] += p * v[d] for d < n: independent lanes, one rounded multiply and
+   add each, in the caller's key order */
+__attribute__((target("avx2"))) static void axpy_avx2(float p, const float* v, float* out, int n) {
+  const __m256 pv = _mm256_set1_ps(p);
+  int d = 0;
+  for (; d + 8 <= n; d += 8)
+    _mm256_storeu_ps(out + d, _mm256_add_ps(_mm256_loadu_ps(out + d), _mm256_mul_ps(pv, _mm256_loadu_ps(v + d))));
+  for (; d < n; ++d) out[d] += p * v[d];
+}
+
 /* MOE_HOST_SCALAR=1 keeps the portable path (for tests and comparisons) */
 static int use_avx2(void) {
   static int v = -1;
@@ -478,7 +488,8 @@ int mh_attention(MhModel* m, int layer, const float* x, int T, float* x_after, f
     for (int tk = 0; tk <= P; ++tk) {
       const float* vv = kv_row(m, m->vc, layer, b, tk) + (size_t)kvh * hd;
       const float pr = S[tk];
-      for (int d = 0; d < hd; ++d) out[d] += pr * vv[d];
+      if (avx) axpy_avx2(pr, vv, out, hd);
+      else for (int d = 0; d < hd; ++d) out[d] += pr * vv[d];
     }
   }
 
