@@ -112,7 +112,7 @@ def lib():
 
 def check(rc):
     if rc != MOE_OK:
-        raise MoeError(rc, lib().moe_cuda_last_error().decode())
+        raise MoeError(rc, lib().moe_cuda_last_error().decode(errors="replace"))
     return rc
 
 
@@ -239,7 +239,7 @@ class BinFile:
     def __init__(self, path):
         self.h = lib().moe_bin_open(os.fsencode(path))
         if not self.h:
-            raise MoeError(MOE_ERR_INVALID, lib().moe_cuda_last_error().decode())
+            raise MoeError(MOE_ERR_INVALID, lib().moe_cuda_last_error().decode(errors="replace"))
 
     def close(self):
         if self.h:
@@ -294,7 +294,7 @@ class BinWriter:
     def __init__(self, path, count):
         self.h = lib().moe_bin_create(os.fsencode(path), count)
         if not self.h:
-            raise MoeError(MOE_ERR_INVALID, lib().moe_cuda_last_error().decode())
+            raise MoeError(MOE_ERR_INVALID, lib().moe_cuda_last_error().decode(errors="replace"))
 
     def put(self, name, a):
         a = np.require(a, requirements="C")   # keeps 0-d arrays 0-d

@@ -65,7 +65,7 @@ def lib():
 
 def check(rc):
     if rc != 0:
-        raise mc.MoeError(rc, lib().mh_last_error().decode())
+        raise mc.MoeError(rc, lib().mh_last_error().decode(errors="replace"))
 
 
 def _f32(a):
@@ -87,7 +87,7 @@ class HostModel:
         c = MhConfig(**{n: cfg[n] for n, _ in MhConfig._fields_})
         self.h = lib().mh_create(C.byref(c), batch, max_ctx, moe_base)
         if not self.h:
-            raise mc.MoeError(mc.MOE_ERR_INVALID, lib().mh_last_error().decode())
+            raise mc.MoeError(mc.MOE_ERR_INVALID, lib().mh_last_error().decode(errors="replace"))
         self._keep = []
 
     def close(self):

@@ -217,3 +217,26 @@ def test_writer_dtypes_and_errors(tmp_path):
         assert b.find("half") == (1, (3, 4), 24) and np.array_equal(b.read("half"), a16)
         assert b.find("scalar") == (0, (), 4) and b.read("scalar") == scalar
     assert mc.lib().moe_bin_create(str(tmp_path / "no" / "dir.bin").encode(), 0) is None
+
+
+def test_corrupted_files_never_crash(tmp_path):
+    """Random byte corruptions of the reference-written file (header fields,
+    lengths, shapes, data): every call returns a status, and a file that
+    still parses keeps the layer's shapes consistent."""
+    data = bytearray(open(REF_BIN, "rb").read())
+    rng = np.random.default_rng(11)
+    p = tmp_path / "fuzz.bin"
+    ok = 0
+    for trial in range(300):
+        d = bytearray(data)
+        for _ in range(int(rng.integers(1, 6))):
+            pos = int(rng.integers(6, len(d)))
+            d[pos] = int(rng.integers(0, 256))
+        p.write_bytes(bytes(d))
+        try:
+            info = mc.bin_layer_info(str(p), 3)
+            ok += 1
+            assert info[0] == 3 and info[3] == mc.Q4
+        except mc.MoeError as e:
+            assert e.code in (mc.MOE_ERR_INVALID, mc.MOE_ERR_UNSUPPORTED)
+    assert ok > 0
