@@ -13,15 +13,19 @@ exceed the 126 MB L2 between two visits of the same layer).
 Synthetic data: random-init weights of the real shapes (seeded, see
 moe.cc_b200/synth.py), hidden states ~ N(0,1).
 
-N>1 (torchrun): expert parallelism, rank r holds experts [16r/… ) — 128/N per
-GPU; every rank routes all T tokens (identical results), computes its own
-experts' slots, one NCCL all-reduce (sum) of the [T*8, 2048] slot outputs
-(exactly one rank contributes each slot, so the sum is exact), then the
-k-ordered combine. Total work is fixed as N grows: "strong" scaling.
+N>1 (torchrun): expert parallelism, rank r holds experts [r*128/N, (r+1)*128/N)
+and routes its own T tokens (weak scaling: T tokens per GPU). The default
+exchange is fused into the kernels (moe_ffn_ep): the routing kernel stores
+each rank's truncated activations and top-k into every peer's buffers, the
+down projection's epilogue stores each slot row straight into the owning
+rank's buffer, and a flag-synchronised combine finishes each rank's tokens.
+MOE_EP_EXCHANGE=nccl selects the NCCL decomposition instead (all-gather of
+the tokens, moe_ffn_partial, reduce-scatter of the slot rows, combine).
 
 --impl reference: the reference's own C (kernels.c + test_model_trace.c MoE
 block, compiled from source into oracle/_ref; else this repo's C port) on the
-host cores, same metric and config.
+host cores, same metric and config. That arm loads nothing of the product:
+its inputs come from the oracle's copy of the seeded input stream.
 """
 import argparse
 import json
@@ -358,25 +362,34 @@ def host_layer_from_device(torch, mc, sy, dt):
     return L
 
 
-def host_layer(mc, dt):
-    """Layer 0 built on the host (no GPU), same seeds as synth.make_layer_dev."""
+def host_layer(gen, dt):
+    """Layer 0 built on the host (no GPU), same seeds as synth.make_layer_dev.
+    gen(seed, n, std) draws the seeded normal stream: the product's
+    moe_synth_normal_host for the product arm's CPU baseline, the oracle's
+    restatement of it for the reference arm (which loads nothing of the
+    product). The streams are equal bit for bit (tests/test_oracle_cpu.py)."""
     import numpy as np
-    import synth as sy
     from oracle.oracle import Port
     port = Port()
     L = {"dtype": dt, "topk": TOPK, "router_b": None,
-         "router_w": mc.synth_normal_host(sy.stream_seed(1, 0, 0), E * D, 0.02).reshape(E, D)}
+         "router_w": gen(_stream_seed(1, 0, 0), E * D, 0.02).reshape(E, D)}
     shapes = {"g": (F, D), "u": (F, D), "d": (D, F)}
     for j, nm in enumerate("gud"):
         rows, cols = shapes[nm]
         qs, ss = [], []
         for e in range(E):
-            w = mc.synth_normal_host(sy.stream_seed(1, 0, 2 + 3 * e + j), rows * cols, 0.02)
+            w = gen(_stream_seed(1, 0, 2 + 3 * e + j), rows * cols, 0.02)
             q, s = port.quantize(w.reshape(rows, cols), dt)
             qs.append(q); ss.append(s)
         L[nm + "q"] = np.ascontiguousarray(np.stack(qs))
         L[nm + "s"] = np.ascontiguousarray(np.stack(ss))
     return L
+
+
+def _stream_seed(seed, layer, tid):
+    """synth.stream_seed, repeated here so the reference arm need not import
+    the product's Python package."""
+    return (seed * 1_000_003 + layer * 1009 + tid) & ((1 << 64) - 1)
 
 
 def cpu_engine():
@@ -394,14 +407,14 @@ def cpu_step(kind, eng, L, xn, xa):
         eng.moe_block(xn, xa, L)
 
 
-def cpu_baseline(mc, L, T, budget_s=12.0):
+def cpu_baseline(gen, L, T, budget_s=12.0):
     """The reference's own CPU path (oracle/_ref, single-threaded as shipped) on a
     bounded sample of the same workload: whole T-token steps until ~budget_s."""
     kind, eng = cpu_engine()
     n, t0 = 0, time.perf_counter()
     while True:
-        xn = mc.synth_normal_host(7000 + n, T * D, 1.0).reshape(T, D)
-        xa = mc.synth_normal_host(7500 + n, T * D, 1.0).reshape(T, D)
+        xn = gen(7000 + n, T * D, 1.0).reshape(T, D)
+        xa = gen(7500 + n, T * D, 1.0).reshape(T, D)
         cpu_step(kind, eng, L, xn, xa)
         n += 1
         if time.perf_counter() - t0 >= budget_s:
@@ -438,14 +451,14 @@ def run_reference(args, budget_s=150.0):
     if rank != 0:
         return
     import multiprocessing as mp
-    import synth  # noqa: F401  (seed helper)
-    import moe_cuda as mc
+    from oracle.oracle import Port
+    gen = Port().synth_normal        # the oracle's copy of the input stream
     dt = 2 if args.dtype == "q8" else 3
-    L = host_layer(mc, dt)
+    L = host_layer(gen, dt)
     kind, eng = cpu_engine()
     T = args.tokens
-    xs = [(mc.synth_normal_host(7000 + i, T * D, 1.0).reshape(T, D),
-           mc.synth_normal_host(7500 + i, T * D, 1.0).reshape(T, D)) for i in range(4)]
+    xs = [(gen(7000 + i, T * D, 1.0).reshape(T, D),
+           gen(7500 + i, T * D, 1.0).reshape(T, D)) for i in range(4)]
     for i in range(args.warmup):
         cpu_step(kind, eng, L, *xs[i % 4])
     try:
@@ -481,9 +494,9 @@ def run_reference(args, budget_s=150.0):
         sample += f"; capped at {budget_s:.0f} s of the {args.steps} requested"
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": done, "warmup": args.warmup, "ms_per_step": sec * 1e3 / max(done, 1),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int32-acc q8" if dt == 2 else "int32-acc q4", "data": "synthetic",
-            "config": {"workload": f"configs[1]: Qwen3-30B-A3B MoE layer decode, T={T}",
+            "config": {"workload": f"configs[1]: Qwen3-30B-A3B MoE layer decode, T={T} per GPU",
                        "tokens": T, "experts": E, "hidden": D, "moe_intermediate": F, "top_k": TOPK},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -709,7 +722,7 @@ def run_ours(args):
             c4 = {"error": str(exc)[:300]}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(mc, host_layer_from_device(torch, mc, sy, dt), T)
+        cpu = cpu_baseline(mc.synth_normal_host, host_layer_from_device(torch, mc, sy, dt), T)
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,

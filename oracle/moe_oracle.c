@@ -233,3 +233,28 @@ int orc_quantize_q4(const float* W, int rows, int cols, uint8_t* q, float* s) {
   }
   return 0;
 }
+
+/* Seeded N(0, std) stream used to make the benchmark's synthetic inputs:
+ * element i of stream `seed` is splitmix64 at counters 2i and 2i+1 -> two
+ * uniforms in [0,1) (53 bits) -> Box-Muller in double -> float. This is the
+ * same stream the product draws on the device and host, restated here so the
+ * reference arm of the benchmark builds its inputs without loading the
+ * product library. Not part of the reference's algorithm (its inputs are a
+ * checkpoint); pinned equal to the product's stream by tests/. */
+static uint64_t orc_splitmix_at(uint64_t seed, uint64_t i) {
+  uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+void orc_synth_normal(uint64_t seed, uint64_t offset, size_t n, float std, float* out) {
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < (long long)n; ++i) {
+    const uint64_t j = offset + (uint64_t)i;
+    const double u1 = (double)(orc_splitmix_at(seed, 2 * j) >> 11) * 0x1.0p-53;
+    const double u2 = (double)(orc_splitmix_at(seed, 2 * j + 1) >> 11) * 0x1.0p-53;
+    const double z = sqrt(-2.0 * log(1.0 - u1)) * cos(6.283185307179586 * u2);
+    out[i] = (float)(z * (double)std);
+  }
+}

@@ -52,6 +52,7 @@ class Port:
         self.lib.orc_quantize_q8.argtypes = [vp, i, i, vp, vp]
         self.lib.orc_quantize_q4.argtypes = [vp, i, i, vp, vp]
         self.lib.orc_quantize_q4.restype = i
+        self.lib.orc_synth_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_size_t, C.c_float, vp]
 
     def matmul(self, A, q, s, N, K, dtype):
         A = np.ascontiguousarray(A, np.float32)
@@ -84,6 +85,12 @@ class Port:
             _p(idx), _p(p), _p(logits))
         assert r == 0
         return out, idx, p, logits
+
+    def synth_normal(self, seed, n, std, offset=0):
+        """n values of the seeded N(0, std) stream (benchmark inputs)."""
+        out = np.empty(n, np.float32)
+        self.lib.orc_synth_normal(seed & ((1 << 64) - 1), offset, n, std, _p(out))
+        return out
 
     def quantize(self, W, dtype):
         W = np.ascontiguousarray(W, np.float32)

@@ -36,6 +36,14 @@ def test_synth_stream_is_pinned():
     assert np.all(np.isfinite(b)) and abs(float(synth(5, 100000, 1.0).std()) - 1.0) < 0.02
 
 
+def test_oracle_synth_stream_equals_product_stream(port):
+    # the benchmark's reference arm draws its inputs from the oracle's copy of
+    # the stream; it must be the product's stream bit for bit
+    import moe_cuda as mc
+    for seed, off, n, std in ((1, 0, 4096, 1.0), (7000, 0, 2048 * 16, 1.0), (123456789, 77, 3000, 0.02)):
+        assert np.array_equal(port.synth_normal(seed, n, std, off), mc.synth_normal_host(seed, n, std, off))
+
+
 @pytest.mark.parametrize("dt", [2, 3])
 def test_port_gemv_c1_matches_reference_golden(port, dt):
     g = np.load(os.path.join(GOLDEN, "gemv.npz"))
