@@ -39,10 +39,12 @@ __device__ __forceinline__ float div_qscale(int d, bool q8) {
 }
 
 // (int32_t)(a * scale) — kernels.c:66 / :113, truncation toward zero.
-// Returns INT32_MIN for NaN (x86 cvttss2si gives the same "indefinite" value).
+// Returns INT32_MIN for NaN, infinities and |v| >= 2^31: the reference's
+// x86-64 build converts with cvttss2si, which gives that "indefinite" value
+// for every input outside the int32 range (the GPU's conversion saturates).
 __device__ __forceinline__ int trunc_scale(float a, float scale) {
   float v = fmul(a, scale);
-  if (v != v) return INT32_MIN;
+  if (!(fabsf(v) < 2147483648.0f)) return INT32_MIN;
   return __float2int_rz(v);
 }
 
@@ -183,5 +185,15 @@ __device__ __forceinline__ unsigned long long tl_now() {
 
 // Error flag bits written by kernels (read by the host).
 enum : int { kErrRange = 1, kErrTimeout = 2 };
+
+// Records an activation of token t outside the fast kernels' integer range
+// (or NaN/inf). With per-call token flags (moe_ffn: flags[0] = any token,
+// flags[1] = arrival counter of the fix-up pass, flags[2 + t] = token t) the
+// exact fix-up pass recomputes that token's slots; without them the call's
+// error word gets kErrRange.
+__device__ __forceinline__ void range_fail(int* err, int* flags, int t) {
+  if (flags) { flags[2 + t] = 1; flags[0] = 1; }
+  else atomicOr(err, kErrRange);
+}
 
 }  // namespace moe

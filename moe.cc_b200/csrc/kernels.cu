@@ -83,7 +83,7 @@ template <int DT>
 __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restrict__ x, int K,
                                                            uint8_t* __restrict__ act, int act_stride,
                                                            int* __restrict__ asum, int* err,
-                                                           int mma_layout) {
+                                                           int mma_layout, int* flags) {
   const int m = blockIdx.x;
   const float* xr = x + (size_t)m * K;
   uint8_t* ar = act + (size_t)m * act_stride;
@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
       sum += a;
     }
   }
-  if (bad) atomicOr(err, kErrRange);
+  if (bad) range_fail(err, flags, m);
   if (DT == 4) {
     __shared__ int red[8];
     sum = warp_sum(sum);
@@ -115,12 +115,12 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
 }
 
 void launch_quantize_act(const float* x, int M, int K, int dtype, uint8_t* act, int act_stride,
-                         int* asum, int* err, cudaStream_t st, int mma_layout) {
+                         int* asum, int* err, cudaStream_t st, int mma_layout, int* flags) {
   if (M <= 0) return;
   if (dtype == 2)
-    quantize_act_kernel<8><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err, mma_layout);
+    quantize_act_kernel<8><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err, mma_layout, flags);
   else
-    quantize_act_kernel<4><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err, mma_layout);
+    quantize_act_kernel<4><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err, mma_layout, flags);
 }
 
 // --------------------------------------------------------------------------
@@ -768,6 +768,7 @@ struct GateUpArgs {
   uint8_t* hact; int hact_stride;
   int* hsum;
   int* err;
+  int* flags;        // per-token range flags (range_fail) or null
 };
 
 template <int DT, int LPR>
@@ -823,11 +824,11 @@ __global__ void __launch_bounds__(256) gateup_kernel(const GateUpArgs a) {
       const int ha = trunc_scale(h, S);             // down's activation truncation
       uint8_t* hr = a.hact + (size_t)s * a.hact_stride;
       if (DT == 8) {
-        if (ha < -32768 || ha > 32767) atomicOr(a.err, kErrRange);
+        if (ha < -32768 || ha > 32767) range_fail(a.err, a.flags, t);
         hr[n] = (uint8_t)(ha & 0xFF);
         hr[a.F + n] = (uint8_t)((ha >> 8) & 0xFF);
       } else {
-        if (ha < -128 || ha > 127) atomicOr(a.err, kErrRange);
+        if (ha < -128 || ha > 127) range_fail(a.err, a.flags, t);
         hr[q4_act_pos(n)] = (uint8_t)(ha & 0xFF);
         atomicAdd(a.hsum + s, ha);
       }
@@ -848,6 +849,7 @@ void launch_gateup(const LayerDev& L, const Workspace& ws, int T, int* err, cuda
   a.route = ws.route; a.E_local = E_local;
   a.xact = ws.xact; a.xact_stride = 2 * L.D; a.xsum = ws.xsum;
   a.hact = ws.hact; a.hact_stride = 2 * L.F; a.hsum = ws.hsum; a.err = err;
+  a.flags = ws.xbad;
   const int max_experts = E_local < T * L.topk ? E_local : T * L.topk;
   const long warps = (long)max_experts * a.items_per_expert;
   const unsigned grid = (unsigned)((warps + 7) / 8);
@@ -865,9 +867,8 @@ void launch_gateup(const LayerDev& L, const Workspace& ws, int T, int* err, cuda
 }
 
 // --------------------------------------------------------------------------
-// decode: down projection (test_model_trace.c:502-503) and, fused, the
-// k-ordered weighted combine + residual (:513, :517). The last warp to finish
-// a row block (an arrival counter per block reaches n_active) combines it.
+// decode: down projection (test_model_trace.c:502-503), slot rows y[s] for the
+// k-ordered combine
 // --------------------------------------------------------------------------
 struct DownArgs {
   const uint8_t* slab;
@@ -877,12 +878,6 @@ struct DownArgs {
   const uint8_t* hact; int hact_stride;
   const int* hsum;
   float* y;
-  int* cnt;
-  const int* topk_idx;
-  const float* topk_p;
-  const float* xres;
-  float* out;
-  int fuse;
 };
 
 template <int DT, int LPR, int RPG>
@@ -943,33 +938,9 @@ __global__ void __launch_bounds__(256) down_kernel(const DownArgs a) {
       if (lig == 0 && ok[j]) a.y[(size_t)s * a.D + n[j]] = dequant_out<DT>(v, as, sc[j]);
     }
   }
-  if (!a.fuse) return;
-  __threadfence();
-  __syncwarp();
-  int last = 0;
-  if (lane == 0) last = atomicAdd(a.cnt + item, 1) == na - 1;
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (!last) return;
-  __threadfence();
-  constexpr int ROWS = GPW * RPG;
-  const int row0 = item * ROWS;
-  for (int q = lane; q < a.T * ROWS; q += 32) {
-    const int t = q / ROWS, nn = row0 + q % ROWS;
-    if (nn >= a.D) continue;
-    float acc = 0.0f;
-    for (int k = 0; k < a.topk; ++k) {
-      const int s = t * a.topk + k;
-      if (__ldcg(a.topk_idx + s) < 0) continue;
-      acc = fadd(acc, fmul(__ldcg(a.topk_p + s), __ldcg(a.y + (size_t)s * a.D + nn)));
-    }
-    const size_t o = (size_t)t * a.D + nn;
-    a.out[o] = fadd(a.xres[o], acc);
-  }
-  if (lane == 0) atomicExch(a.cnt + item, 0);
 }
 
-void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y, bool fuse_combine,
-                 const float* xres, float* out, cudaStream_t st) {
+void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y, cudaStream_t st) {
   Geo g;
   pick_geo(L.d_rb, g);
   constexpr int RPG = 2;
@@ -981,8 +952,7 @@ void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y, bool f
   const int E_local = L.e_end - L.e_begin;
   a.route = ws.route; a.E_local = E_local;
   a.hact = ws.hact; a.hact_stride = 2 * L.F; a.hsum = ws.hsum;
-  a.y = y; a.cnt = ws.cnt; a.topk_idx = ws.topk_idx; a.topk_p = ws.topk_p;
-  a.xres = xres; a.out = out; a.fuse = fuse_combine ? 1 : 0;
+  a.y = y;
   const int max_experts = E_local < T * L.topk ? E_local : T * L.topk;
   const long warps = (long)max_experts * a.items_per_expert;
   const unsigned grid = (unsigned)((warps + 7) / 8);
@@ -1000,8 +970,14 @@ void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y, bool f
 }
 
 // k-ordered combine + residual as a separate pass (prefill, expert parallel)
+// out[t] = xres[t] + Σ_k p[t][k] y[t*K+k] in k order (test_model_trace.c:513,
+// :517). A slot with no expert (idx < 0: fewer than K logits that are neither
+// NaN nor -inf) adds p * 0: the reference reads an expert out of bounds
+// there, and its p is 0 (finite maximum) or NaN (no finite logit), which
+// gives 0 or NaN whatever that expert holds. idx may be null (every slot has
+// an expert).
 __global__ void combine_kernel(const float* __restrict__ y, const float* __restrict__ p,
-                               const float* xres, float* out, int T, int D, int K) {
+                               const int* __restrict__ idx, const float* xres, float* out, int T, int D, int K) {
   pdl_wait();
   pdl_launch();
   const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -1010,16 +986,18 @@ __global__ void combine_kernel(const float* __restrict__ y, const float* __restr
   float acc = 0.0f;
   for (int k = 0; k < K; ++k) {
     const int s = t * K + k;
-    acc = fadd(acc, fmul(p[s], y[(size_t)s * D + n]));
+    const float yv = (idx && idx[s] < 0) ? 0.0f : y[(size_t)s * D + n];
+    acc = fadd(acc, fmul(p[s], yv));
   }
   out[q] = fadd(xres[q], acc);
 }
 
-void launch_combine(const float* y, const float* p, const float* xres, float* out, int T, int D,
+void launch_combine(const float* y, const float* p, const int* idx, const float* xres, float* out, int T, int D,
                     int K, cudaStream_t st) {
   const long total = (long)T * D;
   if (total <= 0) return;
-  launch_pdl(combine_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, y, p, xres, out, T, D, K);
+  launch_pdl(combine_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, y, p, idx, xres, out, T, D,
+             K);
 }
 
 // --------------------------------------------------------------------------

@@ -42,7 +42,6 @@ struct Workspace {
   uint8_t* hact = nullptr;    // slot activations, 2*F bytes per slot
   int* hsum = nullptr;        // [T*K]
   float* y = nullptr;         // [T*K][D]
-  int* cnt = nullptr;         // [D] combine arrival counters (kept zero between calls)
   int* route_counter = nullptr;  // arrival counter of the fused routing kernel (kept zero)
   int* route_tmp = nullptr;   // [3][E] counts / starts / fill counters of the parallel route build
   uint8_t* xs0 = nullptr;     // expert-sorted token activations, plane 0 [T*K][D]
@@ -53,6 +52,11 @@ struct Workspace {
   float* xn = nullptr;        // staging for host-pointer calls [T][D]
   float* xo = nullptr;        // [T][D]
   int* fused_ctr = nullptr;   // fused decode kernel: work, arrival, per-tile completion (kept zero)
+  // Per-call range flags of the exact fix-up pass, [2 + cap_T] ints kept zero
+  // between calls: [0] any token flagged, [1] the pass's arrival counter,
+  // [2 + t] token t had an activation (x, or h of one of its slots) outside
+  // the fast kernels' integer range. Null: kernels report kErrRange instead.
+  int* xbad = nullptr;
 };
 
 // Expert-parallel exchange buffers. Every rank allocates the same layout
@@ -102,9 +106,10 @@ __host__ __device__ inline RouteView route_view(int* route, int E) {
 // xact planes from fp32 rows: Q8 -> [lo K][hi K] per row, Q4 -> permuted K
 // bytes per row + rowsum. Sets err bit kErrRange on out-of-range values.
 // mma_layout: Q4 activations in the tensor-core order (q4_mma_pos)
+// flags: per-token range flags (range_fail in common.cuh) instead of kErrRange
 void launch_quantize_act(const float* x, int M, int K, int dtype, uint8_t* act,
                          int act_stride, int* asum, int* err, cudaStream_t st,
-                         int mma_layout = 0);
+                         int mma_layout = 0, int* flags = nullptr);
 // C[m][n] = sequential fp32 Σ_k A[m][k] W[n][k] (+ b[n]).
 void launch_f32_seq_matmul(const float* A, const float* W, const float* b,
                            float* C, int M, int N, int K, cudaStream_t st);
@@ -130,15 +135,15 @@ void launch_gemv_generic(int dtype, const float* A, const uint8_t* Wq,
 bool fast_geometry_ok(int dtype, int K);
 void launch_gateup(const LayerDev& L, const Workspace& ws, int T, int* err,
                    cudaStream_t st);
-// down projection; if fuse_combine, also out[t] = xres[t] + Σ_k p y (k order)
-void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y,
-                 bool fuse_combine, const float* xres, float* out,
-                 cudaStream_t st);
-// Expert FFN of every routed slot with exact int32 activations of any
-// magnitude (exact.cu): h [T*K][F] scratch, y [T*K][D] for launch_combine.
-void launch_exact_experts(const LayerDev& L, const float* xn, const int* idx, int T, float* h, float* y,
-                          cudaStream_t st);
-void launch_combine(const float* y, const float* p, const float* xres,
+// down projection: slot rows y[s][D] for launch_combine
+void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y, cudaStream_t st);
+// Exact fix-up pass (exact.cu): when flags[0] is set, recomputes y of every
+// slot of each flagged token whose expert is local, with int32 activations
+// of any magnitude, into row slot_pos[s] (or s when slot_pos is null) of y;
+// the last CTA clears the flags. A no-op launch when nothing was flagged.
+void launch_exact_fixup(const LayerDev& L, const float* xn, const int* idx, const int* slot_pos, int T,
+                        float* y, int* flags, int sm_count, cudaStream_t st);
+void launch_combine(const float* y, const float* p, const int* idx, const float* xres,
                     float* out, int T, int D, int K, cudaStream_t st);
 void launch_quantize_rowwise(int dtype, const float* W, int rows, int cols,
                              void* q, float* s, cudaStream_t st);
@@ -157,8 +162,8 @@ bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, in
 // ep != null: expert-parallel mode, each slot row is stored into the y buffer
 // of the rank owning its token, and the last CTA raises this rank's combine
 // flag at every peer
-bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, float* ys, bool fuse,
-                     const float* xres, float* out, int* err, cudaStream_t st, const EpView* ep = nullptr);
+bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, float* ys, int* err, cudaStream_t st,
+                     const EpView* ep = nullptr);
 // moe_fused.cu: Q8 decode gate/up + down in one persistent kernel
 constexpr int kFusedMaxTiles = 256;
 // tile width the fused kernel would use for T tokens (16 or 32), 0 = not used

@@ -79,6 +79,7 @@ struct Args {
   int ep_on; EpView ep;
   const int* xsum; int* hsum;          // Q4 zero point: per-token Σa, per-slot Σh
   int* err;
+  int* flags;                          // per-token range flags (range_fail) or null
 };
 
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
@@ -441,13 +442,13 @@ __global__ void __launch_bounds__(threads(DT), 2)
           const float uv = fmul(div_qscale(du, !Q4), su);
           const int ha = trunc_scale(fmul(silu_ref(gv), uv), S);
           if (Q4) {
-            if (ha < -128 || ha > 127) atomicOr(a.err, kErrRange);
+            if (ha < -128 || ha > 127) range_fail(a.err, a.flags, __ldg(slots + j) / a.topk);
             a.hs0[(size_t)j * a.F + q4_mma_pos(n)] = (uint8_t)(ha & 0xFF);
             // Σ h of slot j for the down projection's zero-point correction
             const int hw = __reduce_add_sync(0xffffffffu, ha);
             if (lane == 0) atomicAdd(a.hsum + j, hw);
           } else {
-            if (ha < -32768 || ha > 32767) atomicOr(a.err, kErrRange);
+            if (ha < -32768 || ha > 32767) range_fail(a.err, a.flags, __ldg(slots + j) / a.topk);
             a.hs0[(size_t)j * a.F + n] = (uint8_t)(ha & 0xFF);
             a.hs1[(size_t)j * a.F + n] = (uint8_t)((ha >> 8) & 0xFF);
           }
@@ -581,7 +582,7 @@ bool launch_mma_fused(const LayerDev& L, const Workspace& ws, int T, int nt, int
   a.D = L.D; a.F = L.F; a.hs0 = ws.hs0; a.hs1 = ws.hs1; a.ys = ws.y;
   a.w_once = tokb && evict_first_on() ? 1 : 0;   // gathered: an expert may have several tiles
   a.tokb = tokb ? 1 : 0;
-  a.ctr = ws.fused_ctr; a.err = err;
+  a.ctr = ws.fused_ctr; a.err = err; a.flags = ws.xbad;
   a.xsum = ws.xsum; a.hsum = ws.hsum;
   a.ep_on = ep != nullptr;
   if (ep) a.ep = *ep;

@@ -15,8 +15,8 @@
 //               thread, every (row, slot) finished in parallel:
 //                 GATEUP: h = silu(g)*u, re-truncated for the down projection
 //                         (test_model_trace.c:496-501, kernels.c:66/:113)
-//                 DOWN:   y = dot/S*s; with `fuse`, the last tile to finish a
-//                         row block applies the k-ordered combine (:502-517)
+//                 DOWN:   y = dot/S*s (:502-503), rows for the separate
+//                         k-ordered combine (:513-517)
 // TMEM holds two accumulator buffers so the MMAs of tile i+1 overlap the
 // epilogue of tile i. Every wait is bounded (kWaitBudget polls); on expiry the
 // kernel flags kErrTimeout and leaves instead of hanging.
@@ -93,14 +93,13 @@ struct Args {
   int F;                                   // GATEUP: output plane row length
   uint8_t* hs0; uint8_t* hs1;              // GATEUP outputs (expert-sorted rows)
   float* ys;                               // DOWN output [J][D]
-  int fuse, T, topk;
-  int* cnt; const int* slot_pos; const float* topk_p; const int* topk_idx;
+  int T, topk;
   const int* xsum; int* hsum;                // Q4 zero-point sums (token / slot)
   int tokb;                                  // GATEUP: B = all T token rows (decode, T <= NT)
   int w_once;                                // T <= NT: one token tile per expert, weights read once
   int ep_on; EpView ep;                      // DOWN, expert parallel: slot rows go to their owners' y buffers
-  const float* xres; float* out;
   int* err;
+  int* flags;                                // GATEUP: per-token range flags (range_fail) or null
 };
 
 template <int DT, int MODE, int NT>
@@ -417,11 +416,13 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
           const float h = fmul(silu_ref(g), uu);
           const int ha = trunc_scale(h, S);
           if (DT == 8) {
-            if (ha < -32768 || ha > 32767) atomicOr(a.err, kErrRange);
+            if (ha < -32768 || ha > 32767)
+              range_fail(a.err, a.flags, __ldg(a.route + 2 + 2 * a.E_local + j) / a.topk);
             a.hs0[(size_t)j * a.F + n] = (uint8_t)(ha & 0xFF);
             a.hs1[(size_t)j * a.F + n] = (uint8_t)((ha >> 8) & 0xFF);
           } else {
-            if (ha < -128 || ha > 127) atomicOr(a.err, kErrRange);
+            if (ha < -128 || ha > 127)
+              range_fail(a.err, a.flags, __ldg(a.route + 2 + 2 * a.E_local + j) / a.topk);
             a.hs0[(size_t)j * a.F + q4_mma_pos(n)] = (uint8_t)(ha & 0xFF);
             // Σ h of slot j for the down projection's zero-point correction
             const int ws = __reduce_add_sync(0xffffffffu, ha);
@@ -481,31 +482,6 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
-
-      if (MODE == DOWN && a.fuse) {
-        // this warp's 32 rows of block mb are final once every tile has passed
-        // through them; the last warp to arrive applies the combine to them
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) last = atomicAdd(a.cnt + mb * 4 + q, 1) == kEpiPerQ * *tv.n - 1;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-          __threadfence();
-          for (int t = 0; t < a.T; ++t) {
-            float accf = 0.0f;
-            for (int k = 0; k < a.topk; ++k) {
-              const int s = t * a.topk + k;
-              if (__ldcg(a.topk_idx + s) < 0) continue;
-              const int j = __ldcg(a.slot_pos + s);
-              accf = fadd(accf, fmul(__ldcg(a.topk_p + s), __ldcg(a.ys + (size_t)j * a.rows + n)));
-            }
-            const size_t o = (size_t)t * a.rows + n;
-            a.out[o] = fadd(a.xres[o], accf);
-          }
-          if (lane == 0) atomicExch(a.cnt + mb * 4 + q, 0);
-        }
-      }
     }
   }
   __syncthreads();
@@ -651,7 +627,7 @@ bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, in
   a.rows = L.F; a.kchunks = L.D / 128; a.n_mblk = L.F / 128;
   a.route = ws.route; a.E_local = E_local; a.TK = TK; a.max_tiles = route_max_tiles(TK, E_local, nt);
   a.slab = L.slab; a.stride = L.expert_stride; a.s0_off = L.gs_off; a.s1_off = L.us_off;
-  a.F = L.F; a.hs0 = ws.hs0; a.hs1 = ws.hs1; a.err = err;
+  a.F = L.F; a.hs0 = ws.hs0; a.hs1 = ws.hs1; a.err = err; a.flags = ws.xbad;
   a.xsum = ws.xsum; a.hsum = ws.hsum; a.topk = L.topk; a.tokb = tokb; a.w_once = T <= nt && mm::evict_first_on();
   const int units = a.max_tiles * a.n_mblk, gc = mm::grid_ctas(L.dtype == 2 ? 8 : 4, nt);
   const int grid = units < gc ? units : gc;
@@ -661,8 +637,8 @@ bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, in
   return ok;
 }
 
-bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, float* ys, bool fuse,
-                     const float* xres, float* out, int* err, cudaStream_t st, const EpView* ep) {
+bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, float* ys, int* err, cudaStream_t st,
+                     const EpView* ep) {
   const int E_local = L.e_end - L.e_begin, TK = T * L.topk, cap = ws.cap_T * ws.cap_K;
   mm::TMap a0, b0, b1;
   if (!mm::map_weights(a0, L, L.dq_off, L.F, L.D) || !mm::map_rows(b0, ws.hs0, L.F, cap, nt) ||
@@ -672,9 +648,8 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
   a.rows = L.D; a.kchunks = L.F / 128; a.n_mblk = L.D / 128;
   a.route = ws.route; a.E_local = E_local; a.TK = TK; a.max_tiles = route_max_tiles(TK, E_local, nt);
   a.slab = L.slab; a.stride = L.expert_stride; a.s0_off = L.ds_off;
-  a.ys = ys; a.fuse = fuse ? 1 : 0; a.T = T; a.topk = L.topk;
-  a.cnt = ws.cnt; a.slot_pos = ws.slot_pos; a.topk_p = ws.topk_p; a.topk_idx = ws.topk_idx;
-  a.xres = xres; a.out = out; a.err = err;
+  a.ys = ys; a.T = T; a.topk = L.topk;
+  a.err = err;
   a.xsum = ws.xsum; a.hsum = ws.hsum; a.ep_on = ep != nullptr;
   a.w_once = T <= nt && mm::evict_first_on();
   if (ep) a.ep = *ep;
@@ -713,17 +688,16 @@ __global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* _
         js[k] = e < 0 ? -1 : j;
       }
     }
+    // a slot with no expert (idx < 0) adds p * 0, as combine_kernel
+#pragma unroll
+    for (int k = 0; k < KF; ++k) yv[k] = js[k] >= 0 ? __ldg(ys + (size_t)js[k] * D + n) : 0.0f;
 #pragma unroll
     for (int k = 0; k < KF; ++k)
-      if (js[k] >= 0) yv[k] = __ldg(ys + (size_t)js[k] * D + n);
-#pragma unroll
-    for (int k = 0; k < KF; ++k)
-      if (js[k] >= 0) acc = fadd(acc, fmul(ps[k], yv[k]));
+      if (k < K) acc = fadd(acc, fmul(ps[k], yv[k]));
   } else {
     for (int k = 0; k < K; ++k) {
       const int s = t * K + k;
-      if (idx[s] < 0) continue;
-      acc = fadd(acc, fmul(p[s], ys[(size_t)slot_pos[s] * D + n]));
+      acc = fadd(acc, fmul(p[s], idx[s] < 0 ? 0.0f : ys[(size_t)slot_pos[s] * D + n]));
     }
   }
   out[q] = fadd(xres[q], acc);

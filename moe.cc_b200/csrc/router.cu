@@ -32,6 +32,7 @@ struct Args {
   int* route; int e_begin, E_local; int* hsum; int nt, max_tiles; int* slot_pos;
   uint8_t* xact; int* xsum; int q4_mma;
   int* counter; int* err;
+  int* flags;              // per-token range flags (range_fail) or null
   int ep_on; EpView ep;    // expert parallel: dispatch this rank's tokens, route all ranks' tokens
 };
 
@@ -139,21 +140,21 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
       const int c0 = (int)((long)a.D * blockIdx.x / gridDim.x);
       const int c1 = (int)((long)a.D * (blockIdx.x + 1) / gridDim.x);
       const int w = c1 - c0;
-      int bad = 0;
       for (int q = q0; q < nt * w; q += nq) {
         const int t = q / w, k = c0 + q % w;
         const int v = trunc_scale(sx[t * pitch + k], DT == 8 ? 127.0f : 7.0f);
         uint8_t* ar = xact + (size_t)(t0 + t) * 2 * a.D;
+        bool bad;
         if (DT == 8) {
-          bad |= (v < -32768 || v > 32767);
+          bad = v < -32768 || v > 32767;
           ar[k] = (uint8_t)(v & 0xFF);
           ar[a.D + k] = (uint8_t)((v >> 8) & 0xFF);
         } else {
-          bad |= (v < -128 || v > 127);
+          bad = v < -128 || v > 127;
           ar[a.q4_mma ? q4_mma_pos(k) : q4_act_pos(k)] = (uint8_t)(v & 0xFF);
         }
+        if (bad && di == 0) range_fail(a.err, a.flags, t0 + t);
       }
-      if (bad) atomicOr(a.err, kErrRange);
       if (DT == 4 && blockIdx.x == 0) {       // Σ activation per token (Q4 zero point)
         for (int t = q0 / 32; t < nt; t += nq / 32) {
           int sacc = 0;
@@ -376,6 +377,7 @@ void launch_decode_route(const LayerDev& L, const Workspace& ws, const float* x,
   a.nt = nt; a.max_tiles = nt > 0 ? route_max_tiles(T_route * L.topk, a.E_local, nt) : 0;
   a.slot_pos = nt > 0 ? ws.slot_pos : nullptr;
   a.xact = ws.xact; a.xsum = ws.xsum; a.q4_mma = nt > 0; a.counter = counter; a.err = err;
+  a.flags = ep ? nullptr : ws.xbad;
   a.ep_on = ep != nullptr;
   if (ep) a.ep = *ep;
   const size_t smem = (size_t)(rt::kE + rt::kT) * (L.D + 4) * 4;

@@ -106,12 +106,6 @@ static void host_graphs_reset() {
   g_host_graphs.clear();
 }
 
-static bool range_rerun_on() {
-  static int v = -1;
-  if (v < 0) { const char* e = getenv("MOE_RANGE_RERUN"); v = e && atoi(e) != 0; }
-  return v == 1;
-}
-
 static bool e2e_graph_on() {
   static int v = -1;
   if (v < 0) { const char* e = getenv("MOE_E2E_GRAPH"); v = e && atoi(e) != 0; }
@@ -129,8 +123,8 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   const int nF = F > w.cap_F ? F : w.cap_F, nK = K > w.cap_K ? K : w.cap_K;
   CU(cudaDeviceSynchronize());
   void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum, w.hact, w.hsum,
-                  w.y, w.cnt, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter, w.route_tmp,
-                  w.fused_ctr};
+                  w.y, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter, w.route_tmp,
+                  w.fused_ctr, w.xbad};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
   const size_t TK = (size_t)nT * nK;
@@ -152,7 +146,6 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   ALLOC(hact, (size_t)2 * nF * TK);
   ALLOC(hsum, sizeof(int) * TK);
   ALLOC(y, sizeof(float) * TK * nD);
-  ALLOC(cnt, sizeof(int) * (size_t)nD);
   ALLOC(xs0, TK * nD);
   ALLOC(xs1, TK * nD);
   ALLOC(hs0, TK * nF);
@@ -163,9 +156,10 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   ALLOC(xn, sizeof(float) * (size_t)nT * nD);
   ALLOC(xo, sizeof(float) * (size_t)nT * nD);
   ALLOC(fused_ctr, sizeof(int) * (3 + 2 * kFusedMaxTiles));
+  ALLOC(xbad, sizeof(int) * (2 + (size_t)nT));
 #undef ALLOC
+  CU(cudaMemset(w.xbad, 0, sizeof(int) * (2 + (size_t)nT)));
   CU(cudaMemset(w.fused_ctr, 0, sizeof(int) * (3 + 2 * kFusedMaxTiles)));
-  CU(cudaMemset(w.cnt, 0, sizeof(int) * (size_t)nD));
   CU(cudaMemset(w.route_counter, 0, sizeof(int)));
   CU(cudaMemset(w.route_tmp, 0, sizeof(int) * 3 * (size_t)nE));
   w.cap_T = nT; w.cap_E = nE; w.cap_D = nD; w.cap_F = nF; w.cap_K = nK;
@@ -175,12 +169,13 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
 // Read (and clear) the kernel error flag. Synchronises the device.
 static int error_status(int h) {
   if (h) {
+    // a timeout is reported first: it means some kernel's results are missing
+    if (h & kErrTimeout)
+      return set_err(MOE_ERR_CUDA, "a pipelined kernel gave up waiting on a copy (bounded wait)");
     if (h & kErrRange)
       return set_err(MOE_ERR_RANGE,
                      "an activation was NaN/inf or outside the integer range of the "
                      "quantised kernels (Q8: |x| < 258, Q4: trunc(7x) in [-128,127])");
-    if (h & kErrTimeout)
-      return set_err(MOE_ERR_CUDA, "a pipelined kernel gave up waiting on a copy (bounded wait)");
   }
   return MOE_OK;
 }
@@ -218,7 +213,7 @@ using namespace moe;
 namespace moe {
 static void ep_shutdown_hook();   // releases the expert-parallel buffers (defined below)
 struct Buf { void* p = nullptr; size_t cap = 0; };
-static Buf s_A, s_C, s_W, s_S, s_act, s_asum, s_xres, s_xh;
+static Buf s_A, s_C, s_W, s_S, s_act, s_asum;
 
 static int grow(Buf& b, size_t bytes) {
   if (bytes <= b.cap) return MOE_OK;
@@ -345,11 +340,11 @@ int moe_cuda_shutdown(void) {
   g.alias.clear();
   Workspace& w = g.ws;
   void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum, w.hact, w.hsum,
-                  w.y, w.cnt, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter, w.route_tmp,
-                  w.fused_ctr};
+                  w.y, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter, w.route_tmp,
+                  w.fused_ctr, w.xbad};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
-  Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum, &s_xres, &s_xh};
+  Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum};
   for (Buf* b : bufs) { if (b->p) cudaFree(b->p); *b = Buf{}; }
   cudaFree(g.d_err); g.d_err = nullptr;
   if (g.h_err) cudaFreeHost(g.h_err);
@@ -641,7 +636,7 @@ static void route_tokens(const LayerDev& L, const float* xn, int T, int nt, cuda
   }
   const Workspace& w = g.ws;
   timed("quantize_act", st, [&] {
-    launch_quantize_act(xn, T, L.D, L.dtype, w.xact, 2 * L.D, w.xsum, g.d_err, st, nt > 0);
+    launch_quantize_act(xn, T, L.D, L.dtype, w.xact, 2 * L.D, w.xsum, g.d_err, st, nt > 0, w.xbad);
   });
   timed("router_logits", st, [&] {
     launch_f32_seq_matmul(xn, L.router_w, L.router_b, w.logits, T, L.E, L.D, st);
@@ -673,9 +668,8 @@ static void run_gateup(const LayerDev& L, const Workspace& w, int T, cudaStream_
   launch_gateup(L, w, T, g.d_err, st);
 }
 
-static void run_down(const LayerDev& L, const Workspace& w, int T, float* y, bool fuse,
-                     const float* xres, float* out, cudaStream_t st) {
-  launch_down(L, w, T, y, fuse, xres, out, st);
+static void run_down(const LayerDev& L, const Workspace& w, int T, float* y, cudaStream_t st) {
+  launch_down(L, w, T, y, st);
 }
 
 // Tensor-core (tcgen05) expert GEMMs unless the caller forces the CUDA-core
@@ -690,9 +684,6 @@ static bool use_tensor_cores(const LayerDev& L, int flags) {
   if (!env && !(flags & MOE_FFN_FORCE_GEMM)) return false;
   return mma_supported(L);
 }
-
-// Tokens at or below this count use the fused down+combine epilogue.
-constexpr int kFuseCombineMaxT = 64;
 
 // Captures the kernels of one host-pointer call into hg (between explicit
 // memcpy nodes for the inputs, outputs and error word). False, with nothing
@@ -866,39 +857,39 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
   const Workspace& w = g.ws;
   const size_t xb = sizeof(float) * (size_t)T * L.D;
   // The kernels of one call on stream s: read xn, update xo in place.
+  // The combine always runs as its own kernel, after the exact fix-up pass
+  // (exact.cu), which recomputes the slots of any token whose activations
+  // left the fast kernels' integer range. (Fused into the down epilogue the
+  // combine also left the last warp through each row block with T*K dependent
+  // loads at the end of the kernel: measured 90 us vs 39 + 6 us.)
   auto enqueue = [&](const float* xn, float* xo, cudaStream_t s) -> int {
     if (use_tensor_cores(L, flags)) {
       const int fnt = fused_tile_n(L, T);                 // fused gate/up + down kernel, if used
       const int nt = fnt ? fnt : mma_tile_n(T, L.dtype);
-      // The combine runs as its own kernel: fused into the down epilogue it left
-      // the last warp through each row block with T*K dependent loads at the
-      // end of the kernel (measured 90 us vs 39 + 6 us). MOE_MMA_FUSE=1 restores it.
-      static int fuse_env = -1;
-      if (fuse_env < 0) {
-        const char* e = getenv("MOE_MMA_FUSE");
-        fuse_env = e ? atoi(e) : 0;
-      }
-      const bool fuse = fuse_env && T <= kFuseCombineMaxT;
       route_tokens(L, xn, T, nt, s);
       if (T > nt) timed("gather", s, [&] { launch_mma_gather(L, w, T, nt, s); });
       bool ok = true;
-      if (!fuse && fnt) {
+      if (fnt) {
         timed("mma_fused", s, [&] { ok = launch_mma_fused(L, w, T, nt, g.d_err, s); });
       } else {
         timed("mma_gateup", s, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, s); });
-        if (ok) timed("mma_down", s, [&] { ok = launch_mma_down(L, w, T, nt, w.y, fuse, xo, xo, g.d_err, s); });
+        if (ok) timed("mma_down", s, [&] { ok = launch_mma_down(L, w, T, nt, w.y, g.d_err, s); });
       }
       if (!ok) return set_err(MOE_ERR_CUDA, "tensor-core launch failed (tensor map or shared memory)");
-      if (!fuse)
-        timed("combine", s, [&] {
-          launch_combine_sorted(w.y, w.slot_pos, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s);
-        });
+      timed("exact_fixup", s, [&] {
+        launch_exact_fixup(L, xn, w.topk_idx, w.slot_pos, T, w.y, w.xbad, g.sm_count, s);
+      });
+      timed("combine", s, [&] {
+        launch_combine_sorted(w.y, w.slot_pos, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s);
+      });
     } else {
-      const bool fuse = T <= kFuseCombineMaxT;
       route_tokens(L, xn, T, 0, s);
       timed("gateup", s, [&] { run_gateup(L, w, T, s); });
-      timed("down", s, [&] { run_down(L, w, T, w.y, fuse, xo, xo, s); });
-      if (!fuse) timed("combine", s, [&] { launch_combine(w.y, w.topk_p, xo, xo, T, L.D, L.topk, s); });
+      timed("down", s, [&] { run_down(L, w, T, w.y, s); });
+      timed("exact_fixup", s, [&] {
+        launch_exact_fixup(L, xn, w.topk_idx, nullptr, T, w.y, w.xbad, g.sm_count, s);
+      });
+      timed("combine", s, [&] { launch_combine(w.y, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s); });
     }
     CU(cudaGetLastError());
     return MOE_OK;
@@ -908,12 +899,6 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
                               sizeof(int) * (size_t)T * L.topk, enqueue);
   const float* xn = x_norm2;
   float* xo = x_inout;
-  // MOE_RANGE_RERUN=1: host-pointer calls keep a device copy of x_inout so
-  // that a call the fast kernels refuse (MOE_ERR_RANGE) is recomputed with
-  // exact int32 activations of any magnitude, as the reference computes it.
-  const bool rerun = host && range_rerun_on();
-  if (rerun && (rc = grow(s_xres, xb))) return rc;
-  if (rerun) CU(cudaMemcpyAsync(s_xres.p, x_inout, xb, cudaMemcpyHostToDevice, st));
   if (host) {
     CU(cudaMemcpyAsync(w.xn, x_norm2, xb, cudaMemcpyHostToDevice, st));
     CU(cudaMemcpyAsync(w.xo, x_inout, xb, cudaMemcpyHostToDevice, st));
@@ -926,17 +911,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
   if (topk_p_out) CU(cudaMemcpyAsync(topk_p_out, w.topk_p, kb, out_kind, st));
   if (host) {
     CU(cudaMemcpyAsync(x_inout, xo, xb, cudaMemcpyDeviceToHost, st));
-    rc = consume_stream_error(st);
-    if (rc == MOE_ERR_RANGE && rerun) {
-      // same routing (fp32, unaffected); experts and combine recomputed
-      if ((rc = grow(s_xh, sizeof(float) * (size_t)T * L.topk * L.F))) return rc;
-      launch_exact_experts(L, w.xn, w.topk_idx, T, (float*)s_xh.p, w.y, st);
-      launch_combine(w.y, w.topk_p, (const float*)s_xres.p, w.xo, T, L.D, L.topk, st);
-      CU(cudaGetLastError());
-      CU(cudaMemcpyAsync(x_inout, w.xo, xb, cudaMemcpyDeviceToHost, st));
-      rc = consume_stream_error(st);
-    }
-    return rc;
+    return consume_stream_error(st);
   }
   return MOE_OK;
 }
@@ -962,16 +937,22 @@ int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots, int*
     timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
     if (ok)
       timed("mma_down", st, [&] {
-        ok = launch_mma_down(L, w, T, nt, w.y, false, nullptr, nullptr, g.d_err, st);
+        ok = launch_mma_down(L, w, T, nt, w.y, g.d_err, st);
       });
     if (!ok) return set_err(MOE_ERR_CUDA, "tensor-core launch failed (tensor map or shared memory)");
     timed("unsort", st, [&] { launch_unsort_rows(L, w, T, y_slots, st); });
+    timed("exact_fixup", st, [&] {
+      launch_exact_fixup(L, x_norm2, w.topk_idx, nullptr, T, y_slots, w.xbad, g.sm_count, st);
+    });
   } else {
     CU(cudaMemsetAsync(y_slots, 0, sizeof(float) * TK * L.D, st));
     route_tokens(L, x_norm2, T, 0, st);
     if (L.e_end > L.e_begin) {
       timed("gateup", st, [&] { run_gateup(L, w, T, st); });
-      timed("down", st, [&] { run_down(L, w, T, y_slots, false, nullptr, nullptr, st); });
+      timed("down", st, [&] { run_down(L, w, T, y_slots, st); });
+      timed("exact_fixup", st, [&] {
+        launch_exact_fixup(L, x_norm2, w.topk_idx, nullptr, T, y_slots, w.xbad, g.sm_count, st);
+      });
     }
   }
   if (topk_idx_out) CU(cudaMemcpyAsync(topk_idx_out, w.topk_idx, sizeof(int) * TK, cudaMemcpyDeviceToDevice, st));
@@ -983,7 +964,7 @@ int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots, int*
 int moe_ffn_combine(const float* y_slots, const float* topk_p, float* x_inout, int T, int D,
                     int top_k, void* stream) {
   if (T < 0 || D <= 0 || top_k <= 0) return set_err(MOE_ERR_INVALID, "bad combine shape");
-  launch_combine(y_slots, topk_p, x_inout, x_inout, T, D, top_k, (cudaStream_t)stream);
+  launch_combine(y_slots, topk_p, nullptr, x_inout, x_inout, T, D, top_k, (cudaStream_t)stream);
   CU(cudaGetLastError());
   return MOE_OK;
 }
@@ -1185,6 +1166,9 @@ int moe_ffn_ep(int layer, const float* x_norm2, int T_local, float* x_inout, voi
   w.topk_idx = (int*)(g_ep.buf + ep.idx_off);
   w.topk_p = (float*)(g_ep.buf + ep.p_off);
   w.cap_T = std::min(g.ws.cap_T, W * g_ep.cap_tokens);     // rows the tensor maps may cover
+  // no exact fix-up across ranks: an out-of-range activation is reported as
+  // MOE_ERR_RANGE by moe_cuda_check_status
+  w.xbad = nullptr;
   const int fnt = fused_tile_n(L, T);
   const int nt = fnt ? fnt : mma_tile_n(T, L.dtype);
   timed("route_dispatch", st, [&] {
@@ -1198,7 +1182,7 @@ int moe_ffn_ep(int layer, const float* x_norm2, int T_local, float* x_inout, voi
     timed("mma_gateup", st, [&] { ok = launch_mma_gateup(L, w, T, nt, g.d_err, st); });
     if (ok)
       timed("mma_down_ep", st, [&] {
-        ok = launch_mma_down(L, w, T, nt, w.y, false, nullptr, nullptr, g.d_err, st, &ep);
+        ok = launch_mma_down(L, w, T, nt, w.y, g.d_err, st, &ep);
       });
   }
   if (!ok) return set_err(MOE_ERR_CUDA, "tensor-core launch failed (tensor map or shared memory)");

@@ -167,7 +167,14 @@ int orc_moe_block(const float* x_norm2, const float* x_after, float* x_out,
       for (int i = 0; i < topk; ++i) {
         const int e = idx[i];
         const float p = val[i];
-        if (e < 0) continue; /* fewer than topk finite logits (all NaN/-inf) */
+        if (e < 0) {
+          /* fewer than topk logits that are neither NaN nor -inf: the
+           * reference indexes expert -1 (out of bounds, undefined). Its p is
+           * then 0 (a finite maximum exists) or NaN (none does), so p * y is
+           * 0 or NaN whatever that memory holds; restated as p * 0. */
+          for (int q = 0; q < D; ++q) acc[q] += p * 0.0f;
+          continue;
+        }
         if (dtype == 2) {
           orc_matmul_q8(x, (const int8_t*)gq + (size_t)e * F * gu_row, gs + (size_t)e * F, g, 1, F, D);
         } else {

@@ -1,7 +1,8 @@
 """Generate tests/golden/*.npz from the REFERENCE itself.
 
-Run where the reference sources are present (the directory REF_DIR below,
-overridable with MOE_REF_DIR) after `make -C oracle`:
+Run where the reference sources are present (a checkout named `reference`
+beside this repository's, or the directory MOE_REF_DIR names) after
+`make -C oracle`:
 
     python tests/golden/make_golden.py
 
@@ -41,7 +42,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "moe.cc_b200"))
-REF_DIR = os.environ.get("MOE_REF_DIR", "/root/reference")
+# the reference checkout, by default beside this repository's checkout
+REF_DIR = os.environ.get("MOE_REF_DIR", os.path.join(os.path.dirname(ROOT), "reference"))
 OUT = os.path.dirname(os.path.abspath(__file__))
 
 

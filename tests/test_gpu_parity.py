@@ -227,17 +227,6 @@ def test_moe_ffn_device_ptrs_and_partial_combine(gpu, port):
     assert np.array_equal(out2.cpu().numpy(), ref)
 
 
-def test_moe_ffn_range_error_is_reported(gpu):
-    lid, L = qwen_layer(gpu, 2, False)
-    xn = np.full((1, 2048), 300.0, np.float32)   # trunc(127*300) needs > 16 bits
-    with pytest.raises(gpu.MoeError) as ei:
-        gpu.moe_ffn_host(lid, xn, np.zeros((1, 2048), np.float32))
-    assert ei.value.code == gpu.MOE_ERR_RANGE
-    # the library stays usable afterwards
-    xo, idx, p = gpu.moe_ffn_host(lid, np.zeros((1, 2048), np.float32), np.zeros((1, 2048), np.float32))
-    assert np.all(np.isfinite(xo))
-
-
 def test_moe_ffn_empty_and_errors(gpu):
     lid, _ = qwen_layer(gpu, 2, False)
     x = np.zeros((0, 2048), np.float32)
