@@ -8,8 +8,9 @@
 // ep_combine_kernel waits (bounded) until every rank's combine flag reached
 // this call's sequence number and applies the k-ordered combine + residual
 // (test_model_trace.c:513,517) to this rank's tokens. Exactly one rank writes
-// each slot row, so no reduction is involved. The wait gives up after
-// kWaitBudget polls per flag and reports kErrTimeout instead of hanging.
+// each slot row, so no reduction is involved. The wait gives up after the
+// group's time limit (EpView::wait_ns) and reports kErrTimeout instead of
+// hanging.
 // Requires one GPU per rank: a kernel waiting on another rank never shares a
 // GPU with that rank's kernels.
 #include "common.cuh"
@@ -27,7 +28,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const EpView ep, const 
   const uint8_t* mine = ep.base_local;
   if (threadIdx.x == 0) {
     const int ok = wait_flags_sys(reinterpret_cast<const unsigned long long*>(mine + kEpCombineFlags),
-                                  ep.world, ep.seq);
+                                  ep.world, ep.seq, ep.wait_ns);
     if (!ok) atomicOr(err, kErrTimeout);
     s_ok = ok;
   }

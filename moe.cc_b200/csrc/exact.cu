@@ -37,7 +37,12 @@ struct FixArgs {
   const int* slot_pos;    // slot -> y row, or null (row = slot)
   float* y;               // [rows][D]
   int* flags;             // [0] any, [1] arrival counter, [2 + t] token t
+  int ep_on; EpView ep;   // expert parallel (see launch_exact_fixup)
 };
+
+__device__ __forceinline__ uint8_t* ep_peer(const EpView& ep, int p) {
+  return reinterpret_cast<uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(ep.base) + p));
+}
 
 // Σ_k aq[k] * w[k] over one weight row, one warp, int32 with two's-complement
 // wrap (the reference's int32 accumulator; the sum is order-free). Q8: int8
@@ -78,8 +83,12 @@ __global__ void __launch_bounds__(kFixThreads) exact_fixup_kernel(const FixArgs 
   int* hq = fsm + a.D;           // [F] truncated h of the slot
   __shared__ int s_any, s_last;
   constexpr float S = DT == 8 ? 127.0f : 7.0f;
+  const int seq32 = (int)a.ep.seq;
   pdl_wait();
   pdl_launch();
+  // flags[0]: some token was marked, here or (expert parallel: copied by the
+  // routing kernel from every rank's xflag) by its home rank. Otherwise the
+  // expert kernels have raised the combine flags already.
   if (threadIdx.x == 0) s_any = *reinterpret_cast<volatile int*>(a.flags);
   __syncthreads();
   if (!s_any) return;            // nothing marked: every CTA leaves here
@@ -87,11 +96,21 @@ __global__ void __launch_bounds__(kFixThreads) exact_fixup_kernel(const FixArgs 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kFixThreads / 32;
   for (int s = blockIdx.x; s < a.T * a.K; s += gridDim.x) {
     const int t = s / a.K;
-    if (!a.flags[2 + t]) continue;
+    const float* x = a.xn + (size_t)t * a.D;
+    float* yr = a.y + (size_t)(a.slot_pos ? a.slot_pos[s] : s) * a.D;
+    bool marked = a.flags[2 + t] != 0;
+    if (a.ep_on) {
+      // token t lives on rank h as its local token tl
+      const int h = t / a.ep.T_local, tl = t - h * a.ep.T_local;
+      const uint8_t* hb = ep_peer(a.ep, h);
+      marked = marked || reinterpret_cast<const int*>(hb + a.ep.xflag_off)[2 + tl] == seq32;
+      x = reinterpret_cast<const float*>(hb + a.ep.xf_off) + (size_t)tl * a.D;
+      yr = reinterpret_cast<float*>(ep_peer(a.ep, h) + a.ep.y_off) + (size_t)(s - h * a.ep.T_local * a.K) * a.D;
+    }
+    if (!marked) continue;
     const int e = a.idx[s] - a.e_begin;
     if (e < 0 || e >= a.E_local) continue;     // another rank's expert, or no expert (all logits NaN/-inf)
     const uint8_t* ex = a.slab + (size_t)e * a.stride;
-    const float* x = a.xn + (size_t)t * a.D;
     for (int k = threadIdx.x; k < a.D; k += kFixThreads) xq[k] = trunc_scale(x[k], S);
     __syncthreads();
     const float* gs = reinterpret_cast<const float*>(ex + a.gs_off);
@@ -107,7 +126,6 @@ __global__ void __launch_bounds__(kFixThreads) exact_fixup_kernel(const FixArgs 
     }
     __syncthreads();
     const float* ds = reinterpret_cast<const float*>(ex + a.ds_off);
-    float* yr = a.y + (size_t)(a.slot_pos ? a.slot_pos[s] : s) * a.D;
     for (int d = warp; d < a.D; d += nw) {
       const int dd = warp_row_dot<DT>(hq, ex + a.dq_off + (size_t)d * a.d_rb, a.F, lane);
       if (lane == 0) yr[d] = fmul(div_qscale(dd, DT == 8), __ldg(ds + d));
@@ -115,24 +133,33 @@ __global__ void __launch_bounds__(kFixThreads) exact_fixup_kernel(const FixArgs 
     __syncthreads();             // xq / hq are rewritten by the next slot
   }
 
-  // the last CTA out clears the marks for the next call
+  // The last CTA out clears the local marks for the next call and,
+  // expert-parallel, raises this rank's combine flag at every rank (release
+  // after a system fence: a rank that sees the flag sees every y row this
+  // rank stored, from the expert kernels and from this pass; the expert
+  // kernels left the flags to this pass because a token was marked).
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
+    if (a.ep_on) __threadfence_system(); else __threadfence();
     s_last = atomicAdd(a.flags + 1, 1) == (int)gridDim.x - 1;
   }
   __syncthreads();
   if (s_last) {
     __threadfence();
     for (int i = 2 + threadIdx.x; i < 2 + a.T; i += kFixThreads) a.flags[i] = 0;
-    if (threadIdx.x == 0) { a.flags[0] = 0; a.flags[1] = 0; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      a.flags[0] = 0;
+      a.flags[1] = 0;
+      if (a.ep_on) ep_raise_combine(a.ep);
+    }
   }
 }
 
 }  // namespace
 
 void launch_exact_fixup(const LayerDev& L, const float* xn, const int* idx, const int* slot_pos, int T,
-                        float* y, int* flags, int sm_count, cudaStream_t st) {
+                        float* y, int* flags, int sm_count, cudaStream_t st, const EpView* ep) {
   const int TK = T * L.topk;
   if (TK <= 0 || !flags) return;
   FixArgs a{};
@@ -142,6 +169,8 @@ void launch_exact_fixup(const LayerDev& L, const float* xn, const int* idx, cons
   a.D = L.D; a.F = L.F; a.K = L.topk; a.T = T; a.e_begin = L.e_begin; a.E_local = L.e_end - L.e_begin;
   a.gu_rb = L.gu_rb; a.d_rb = L.d_rb;
   a.xn = xn; a.idx = idx; a.slot_pos = slot_pos; a.y = y; a.flags = flags;
+  a.ep_on = ep != nullptr;
+  if (ep) a.ep = *ep;
   const int grid = TK < 2 * sm_count ? TK : 2 * sm_count;
   const size_t smem = sizeof(int) * ((size_t)L.D + L.F);
   auto go = [&](auto kern) {

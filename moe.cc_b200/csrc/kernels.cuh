@@ -70,6 +70,13 @@ struct Workspace {
 //   idx, p [world*T_local*K]       every rank's top-k choice and weight
 //   y [T_local*K][D] f32           this rank's slot rows, stored by the owners
 //                                  of the slots' experts
+//   xf [T_local][D] f32            this rank's MoE inputs as given (local
+//                                  stores; the exact fix-up pass of the
+//                                  experts' owners reads them over NVLink)
+//   xflag [2 + T_local] int        [0] and [2 + t]: equal to the low 32 bits
+//                                  of seq when some token / token t of this
+//                                  rank had an activation outside the fast
+//                                  kernels' range in this call
 // base[] holds the peers' mappings (own buffer at base[rank]); the *_off
 // fields point into this call's parity.
 constexpr int kEpMaxRanks = 64;
@@ -80,8 +87,27 @@ struct EpView {
   uint8_t* base_local = nullptr;    // == base[rank]
   int world = 0, rank = 0, T_local = 0;
   unsigned long long seq = 0;
-  size_t xact_off = 0, xsum_off = 0, idx_off = 0, p_off = 0, y_off = 0;
+  unsigned long long wait_ns = 0;   // limit of each wait on the other ranks' flags
+  size_t xact_off = 0, xsum_off = 0, idx_off = 0, p_off = 0, y_off = 0, xf_off = 0, xflag_off = 0;
 };
+
+#ifdef __CUDACC__
+}  // namespace moe
+#include "pipeline.cuh"
+namespace moe {
+// One thread, once the rank's y-row stores of this call are complete: raise
+// this rank's combine flag (entry ep.rank, value ep.seq) at every rank,
+// starting with itself, after a system fence (release), so a rank that sees
+// the flag sees the rows.
+__device__ __forceinline__ void ep_raise_combine(const EpView& ep) {
+  __threadfence_system();
+  for (int i = 0; i < ep.world; ++i) {
+    const int p = (ep.rank + i) % ep.world;
+    uint8_t* pb = reinterpret_cast<uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(ep.base) + p));
+    st_release_sys(reinterpret_cast<unsigned long long*>(pb + kEpCombineFlags) + ep.rank, ep.seq);
+  }
+}
+#endif
 
 struct RouteView {
   int* n_active; int* active; int* exp_off; int* slot_list;
@@ -141,8 +167,12 @@ void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y, cudaSt
 // slot of each flagged token whose expert is local, with int32 activations
 // of any magnitude, into row slot_pos[s] (or s when slot_pos is null) of y;
 // the last CTA clears the flags. A no-op launch when nothing was flagged.
+// ep != null (expert parallel; T = all ranks' tokens, idx = all ranks' top-k):
+// tokens are also flagged by their home rank's xflag, their inputs are read
+// from its xf, y rows go to its y buffer, and the last CTA raises this rank's
+// combine flags at every rank.
 void launch_exact_fixup(const LayerDev& L, const float* xn, const int* idx, const int* slot_pos, int T,
-                        float* y, int* flags, int sm_count, cudaStream_t st);
+                        float* y, int* flags, int sm_count, cudaStream_t st, const EpView* ep = nullptr);
 void launch_combine(const float* y, const float* p, const int* idx, const float* xres,
                     float* out, int T, int D, int K, cudaStream_t st);
 void launch_quantize_rowwise(int dtype, const float* W, int rows, int cols,

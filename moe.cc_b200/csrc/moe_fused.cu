@@ -34,7 +34,7 @@
 //
 // Roles: warp 0 lane 0 = work claiming + TMA producer, warp 1 lane 0 = MMA
 // issuer, warps 2..9 = epilogue (tcgen05.ld, one weight row per thread).
-// Every wait is bounded (kWaitBudget polls): on expiry the CTA flags
+// Every wait is bounded (kWaitNs of %globaltimer): on expiry the CTA flags
 // kErrTimeout and leaves, after waiting (bounded) for its own copies.
 #include <cuda.h>
 #include "common.cuh"
@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(threads(DT), 2)
 #endif
           int v;
           while ((v = ld_acquire_gpu(ready + pos)) == 0)
-            if (++i >= kWaitBudget) break;
+            if (++i >= kWaitNs) break;
 #ifdef MOE_TIMELINE
           stall += tl_now() - w0;
 #endif
@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(threads(DT), 2)
         // one slot item: wait the slot free, expect its bytes
         auto take = [&](uint32_t bytes) -> int {
           const int st = it % a.nslots;
-          if (it >= a.nslots && !mbar_wait(&empty[st], ((it / a.nslots) - 1) & 1, kWaitBudget)) {
+          if (it >= a.nslots && !mbar_wait(&empty[st], ((it / a.nslots) - 1) & 1, kWaitNs)) {
             atomicOr(a.err, kErrTimeout); *abort_flag = 1; return -1;
           }
           mbar_arrive_expect_tx(&full[st], bytes);
@@ -264,13 +264,13 @@ __global__ void __launch_bounds__(threads(DT), 2)
       int it = 0, ik = 0;                     // slot items consumed, Q4 expanded k-chunks consumed
       for (int ul = 0;; ++ul) {
         const int ri = ul % kUnitRing;
-        if (!mbar_wait(&unit_rdy[ri], (ul / kUnitRing) & 1, kWaitBudget)) {
+        if (!mbar_wait(&unit_rdy[ri], (ul / kUnitRing) & 1, kWaitNs)) {
           atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
         }
         const int g = s_unit[ri];
         if (g < 0) break;
         const int buf = ul & 1;
-        if (ul >= 2 && !mbar_wait(&acc_empty[buf], ((ul >> 1) - 1) & 1, kWaitBudget)) {
+        if (ul >= 2 && !mbar_wait(&acc_empty[buf], ((ul >> 1) - 1) & 1, kWaitNs)) {
           atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
         }
         tc::fence_after_sync();
@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(threads(DT), 2)
           if (gu) { s1 = it % a.nslots; ph1 = (it / a.nslots) & 1; ++it; }
           const uint8_t* p0 = smem + (size_t)s0 * a.slot_bytes;
           if (!Q4) {
-            if (!mbar_wait(&full[s0], ph0, kWaitBudget) || (gu && !mbar_wait(&full[s1], ph1, kWaitBudget))) {
+            if (!mbar_wait(&full[s0], ph0, kWaitNs) || (gu && !mbar_wait(&full[s1], ph1, kWaitNs))) {
               bad = true; break;
             }
             tc::fence_after_sync();
@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(threads(DT), 2)
             // the expanders saw the slots full before releasing each k-chunk
             for (int q = 0; q < KPS; ++q, ++ik) {
               const int ab = ik % kAR;
-              if (!mbar_wait(&afull[ab], (ik / kAR) & 1, kWaitBudget)) { bad = true; break; }
+              if (!mbar_wait(&afull[ab], (ik / kAR) & 1, kWaitNs)) { bad = true; break; }
               tc::fence_after_sync();
               const uint64_t db = tc::sw128_desc(p0 + kA + q * B);
 #pragma unroll
@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(threads(DT), 2)
     int it = 0, ik = 0;
     for (int ul = 0;; ++ul) {
       const int ri = ul % kUnitRing;
-      if (!mbar_wait(&unit_rdy[ri], (ul / kUnitRing) & 1, kWaitBudget)) {
+      if (!mbar_wait(&unit_rdy[ri], (ul / kUnitRing) & 1, kWaitNs)) {
         if (lane == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; }
         break;
       }
@@ -361,11 +361,11 @@ __global__ void __launch_bounds__(threads(DT), 2)
           if (part == 1) { sm = it % a.nslots; ph = (it / a.nslots) & 1; }
           ++it;
         }
-        if (!mbar_wait(&full[sm], ph, kWaitBudget)) { bad = true; break; }
+        if (!mbar_wait(&full[sm], ph, kWaitNs)) { bad = true; break; }
         const uint8_t* prow = smem + (size_t)sm * a.slot_bytes + r * 128;
         for (int q = 0; q < KPS; ++q, ++ik) {
           const int ab = ik % kAR;
-          if (ik >= kAR && !mbar_wait(&aempty[ab], ((ik / kAR) - 1) & 1, kWaitBudget)) { bad = true; break; }
+          if (ik >= kAR && !mbar_wait(&aempty[ab], ((ik / kAR) - 1) & 1, kWaitNs)) { bad = true; break; }
           const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + ACOL + (ab * 2) * 32;
           if (gu) {
             uint32_t o[32];
@@ -394,14 +394,14 @@ __global__ void __launch_bounds__(threads(DT), 2)
     const int q = warp & 3, half = (warp - 2) >> 2, r = q * 32 + lane;
     for (int ul = 0;; ++ul) {
       const int ri = ul % kUnitRing;
-      if (!mbar_wait(&unit_rdy[ri], (ul / kUnitRing) & 1, kWaitBudget)) {
+      if (!mbar_wait(&unit_rdy[ri], (ul / kUnitRing) & 1, kWaitNs)) {
         if (lane == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; }
         break;
       }
       const int g = s_unit[ri], dtile = s_utile[ri];
       if (g < 0) break;
       const int buf = ul & 1;
-      if (!mbar_wait(&acc_full[buf], (ul >> 1) & 1, kWaitBudget)) {
+      if (!mbar_wait(&acc_full[buf], (ul >> 1) & 1, kWaitNs)) {
         if (lane == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; }
         break;
       }
@@ -500,10 +500,12 @@ __global__ void __launch_bounds__(threads(DT), 2)
   if (threadIdx.x == 0 && s_abort) {
     // let the tensor copies still in flight land before the CTA's smem goes away
     for (int i = max(0, s_issued - a.nslots); i < s_issued; ++i)
-      mbar_wait(&full[i % a.nslots], (i / a.nslots) & 1, kWaitBudget);
+      mbar_wait(&full[i % a.nslots], (i / a.nslots) & 1, kWaitNs);
   }
   // The last CTA out resets the work and completion counters for the next
-  // call and, expert-parallel, raises this rank's combine flag at every rank.
+  // call and, expert-parallel, raises this rank's combine flag at every rank,
+  // unless a token was marked out of range (by any rank's routing, or by an
+  // epilogue here): then the exact fix-up pass that follows raises them.
   if (threadIdx.x == 0) {
     if (a.ep_on) __threadfence_system(); else __threadfence();
     s_last = atomicAdd(a.ctr + 1, 1) == (int)gridDim.x - 1;
@@ -513,14 +515,8 @@ __global__ void __launch_bounds__(threads(DT), 2)
       a.ctr[1] = 0;
       a.ctr[2] = 0;
       for (int i = 0; i < ntiles; ++i) { done[i] = 0; ready[i] = 0; }
-      if (a.ep_on) {
-        __threadfence_system();
-        for (int i = 0; i < a.ep.world; ++i) {
-          const int p = (a.ep.rank + i) % a.ep.world;
-          uint8_t* pb = reinterpret_cast<uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(a.ep.base) + p));
-          st_release_sys(reinterpret_cast<unsigned long long*>(pb + kEpCombineFlags) + a.ep.rank, a.ep.seq);
-        }
-      }
+      if (a.ep_on && !(a.flags && *reinterpret_cast<volatile int*>(a.flags)))
+        ep_raise_combine(a.ep);
     }
   }
   __syncthreads();

@@ -18,7 +18,7 @@
 //                 DOWN:   y = dot/S*s (:502-503), rows for the separate
 //                         k-ordered combine (:513-517)
 // TMEM holds two accumulator buffers so the MMAs of tile i+1 overlap the
-// epilogue of tile i. Every wait is bounded (kWaitBudget polls); on expiry the
+// epilogue of tile i. Every wait is bounded (kWaitNs of %globaltimer); on expiry the
 // kernel flags kErrTimeout and leaves instead of hanging.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -99,7 +99,7 @@ struct Args {
   int w_once;                                // T <= NT: one token tile per expert, weights read once
   int ep_on; EpView ep;                      // DOWN, expert parallel: slot rows go to their owners' y buffers
   int* err;
-  int* flags;                                // GATEUP: per-token range flags (range_fail) or null
+  int* flags;                                // per-token range flags (range_fail) or null
 };
 
 template <int DT, int MODE, int NT>
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
         if (*abort_flag) return false;
         if (it < pre) return true;
         const int st = it % a.stages;
-        if (it >= a.stages && !mbar_wait(&empty[st], ((it / a.stages) - 1) & 1, kWaitBudget)) {
+        if (it >= a.stages && !mbar_wait(&empty[st], ((it / a.stages) - 1) & 1, kWaitNs)) {
           atomicOr(a.err, kErrTimeout); *abort_flag = 1; return false;
         }
         mbar_arrive_expect_tx(&full[st], bytes);
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
       int ik = 0, ul = 0;                      // k-chunks consumed, units
       for (int u = u0; u < n_units && !*abort_flag; u += ustep, ++ul) {
         const int buf = ul & 1;
-        if (ul >= 2 && !mbar_wait(&acc_empty[buf], ((ul >> 1) - 1) & 1, kWaitBudget)) {
+        if (ul >= 2 && !mbar_wait(&acc_empty[buf], ((ul >> 1) - 1) & 1, kWaitNs)) {
           atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
         }
         tc::fence_after_sync();
@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
           const int it = ik / KPS, st = it % a.stages, q = ik % KPS;   // stage and k-chunk within it
           const int ab = ik % AR;
           if (!mbar_wait(DT == 4 ? &afull[ab] : &full[st], DT == 4 ? (ik / AR) & 1 : (it / a.stages) & 1,
-                         kWaitBudget)) {
+                         kWaitNs)) {
             atomicOr(a.err, kErrTimeout); *abort_flag = 1; break;
           }
           tc::fence_after_sync();
@@ -317,8 +317,8 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
     for (int u = u0; u < n_units && !*abort_flag; u += ustep) {
       for (int kc = 0; kc < a.kchunks; ++kc, ++ik) {
         const int it = ik / KPS, st = it % a.stages, qk = ik % KPS, ab = ik % AR;
-        if (!mbar_wait(&full[st], (it / a.stages) & 1, kWaitBudget) ||
-            (ik >= AR && !mbar_wait(&aempty[ab], ((ik / AR) - 1) & 1, kWaitBudget))) {
+        if (!mbar_wait(&full[st], (it / a.stages) & 1, kWaitNs) ||
+            (ik >= AR && !mbar_wait(&aempty[ab], ((ik / AR) - 1) & 1, kWaitNs))) {
           if (lane == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; }
           break;
         }
@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
     int ul = 0;
     for (int u = u0; u < n_units; u += ustep, ++ul) {
       const int buf = ul & 1;
-      if (!mbar_wait(&acc_full[buf], (ul >> 1) & 1, kWaitBudget)) {
+      if (!mbar_wait(&acc_full[buf], (ul >> 1) & 1, kWaitNs)) {
         if (lane == 0) { atomicOr(a.err, kErrTimeout); *abort_flag = 1; }
         break;
       }
@@ -489,22 +489,19 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
     // The barrier orders the CTA's peer stores before this thread's system
     // fence; the last CTA to arrive then raises this rank's combine flag at
     // every rank (release), so a rank that sees the flag sees the rows.
+    // When a token was marked out of range the exact fix-up pass that
+    // follows raises them instead, after its own rows.
     __threadfence_system();
     int* counter = reinterpret_cast<int*>(a.ep.base_local + kEpCounter);
     if (atomicAdd(counter, 1) == (int)gridDim.x - 1) {
-      __threadfence_system();
-      for (int i = 0; i < a.ep.world; ++i) {
-        const int p = (a.ep.rank + i) % a.ep.world;
-        uint8_t* pb = reinterpret_cast<uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(a.ep.base) + p));
-        st_release_sys(reinterpret_cast<unsigned long long*>(pb + kEpCombineFlags) + a.ep.rank, a.ep.seq);
-      }
       *counter = 0;
+      if (!(a.flags && *reinterpret_cast<volatile int*>(a.flags))) ep_raise_combine(a.ep);
     }
   }
   if (threadIdx.x == 0 && s_abort) {
     // let the tensor copies still in flight land before the CTA's smem goes away
     for (int it = max(0, s_issued - a.stages); it < s_issued; ++it)
-      mbar_wait(&full[it % a.stages], (it / a.stages) & 1, kWaitBudget);
+      mbar_wait(&full[it % a.stages], (it / a.stages) & 1, kWaitNs);
   }
   __syncthreads();
   if (warp == 1) {
@@ -648,7 +645,7 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
   a.rows = L.D; a.kchunks = L.F / 128; a.n_mblk = L.D / 128;
   a.route = ws.route; a.E_local = E_local; a.TK = TK; a.max_tiles = route_max_tiles(TK, E_local, nt);
   a.slab = L.slab; a.stride = L.expert_stride; a.s0_off = L.ds_off;
-  a.ys = ys; a.T = T; a.topk = L.topk;
+  a.ys = ys; a.T = T; a.topk = L.topk; a.flags = ws.xbad;
   a.err = err;
   a.xsum = ws.xsum; a.hsum = ws.hsum; a.ep_on = ep != nullptr;
   a.w_once = T <= nt && mm::evict_first_on();

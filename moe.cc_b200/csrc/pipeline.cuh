@@ -1,7 +1,7 @@
 // pipeline.cuh — mbarrier + 1-D bulk async copy (TMA engine) primitives for
-// sm_100a, with bounded waits: a wait that exceeds its iteration budget
-// returns false instead of spinning forever, so a kernel can flag an error
-// and leave cleanly.
+// sm_100a, with bounded waits: a wait that exceeds its time limit (read from
+// the GPU's %globaltimer, in nanoseconds) returns false instead of spinning
+// forever, so a kernel can flag an error and leave cleanly.
 #pragma once
 #include <stdint.h>
 
@@ -39,11 +39,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait for phase `parity` to complete; false after `budget` polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t budget) {
-  for (uint32_t i = 0; i < budget; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
+// Nanoseconds of the GPU's global timer.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Time limit of one wait on a local event (a copy landing, a pipeline stage
+// freed, another CTA of the same kernel finishing a unit): those take
+// microseconds, so 200 ms only ever expires when something is broken.
+constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;
+
+// Wait for phase `parity` to complete; false once `limit_ns` has passed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
 }
 
 // global -> shared bulk copy (no multicast), completion counted on `bar`.
@@ -56,10 +72,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
-// Poll budget of one mbarrier wait: ~2^24 polls is far beyond any legitimate
-// copy latency (microseconds) yet ends in well under a second.
-constexpr uint32_t kWaitBudget = 1u << 24;
-
 // ---- cross-GPU flags (expert-parallel exchange over peer memory) ----------
 __device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -70,14 +82,16 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 // One thread: wait until flags[0..world) all reached seq. Bounded: a rank
-// that never arrives makes this return false after ~kWaitBudget polls per
-// flag instead of hanging the GPU.
+// that never arrives makes this return false once limit_ns has passed since
+// the wait began (one limit for the whole wait, not per flag), instead of
+// hanging the GPU.
 __device__ __forceinline__ bool wait_flags_sys(const unsigned long long* flags, int world,
-                                               unsigned long long seq) {
+                                               unsigned long long seq, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer_ns();
   for (int src = 0; src < world; ++src) {
     uint32_t i = 0;
     while (ld_acquire_sys(flags + src) < seq)
-      if (++i >= kWaitBudget) return false;
+      if ((++i & 63) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
   }
   return true;
 }

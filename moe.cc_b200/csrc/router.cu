@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
     const float* wr = sw + ee * pitch;
     float acc = 0.0f;
     for (int c = 0; c < kChunks; ++c) {
-      if (!mbar_wait(&bar[c], 0, kWaitBudget)) { ok = false; break; }
+      if (!mbar_wait(&bar[c], 0, kWaitNs)) { ok = false; break; }
       if (!mine) continue;
       // 16-k register blocks, the next block loaded before the current
       // block's 16 dependent adds, so shared-memory latency overlaps the chain
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
     const bool all = DT == 4 && blockIdx.x == 0;
     const int cf = all ? 0 : cs0 / dc, cl = all ? kChunks - 1 : (cs1 - 1) / dc;
     for (int c = cf; c <= cl && cs1 > cs0; ++c)
-      if (!mbar_wait(&bar[c], 0, kWaitBudget)) { ok = false; break; }
+      if (!mbar_wait(&bar[c], 0, kWaitNs)) { ok = false; break; }
     // expert parallel: the activations go to every rank's xact (rows of this
     // rank's tokens), starting with the next rank so the links share the load
     const int ndst = a.ep_on ? a.ep.world : 1;
@@ -153,7 +153,21 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
           bad = v < -128 || v > 127;
           ar[a.q4_mma ? q4_mma_pos(k) : q4_act_pos(k)] = (uint8_t)(v & 0xFF);
         }
-        if (bad && di == 0) range_fail(a.err, a.flags, t0 + t);
+        if (di == 0) {
+          if (a.ep_on) {
+            // the MoE input as given, for the experts' owners' exact fix-up,
+            // and this rank's out-of-range marks (this call's sequence number)
+            reinterpret_cast<float*>(a.ep.base_local + a.ep.xf_off)[(size_t)(t0 + t) * a.D + k] =
+                sx[t * pitch + k];
+            if (bad) {
+              int* xflag = reinterpret_cast<int*>(a.ep.base_local + a.ep.xflag_off);
+              xflag[2 + t0 + t] = (int)a.ep.seq;
+              xflag[0] = (int)a.ep.seq;
+            }
+          } else if (bad) {
+            range_fail(a.err, a.flags, t0 + t);
+          }
+        }
       }
       if (DT == 4 && blockIdx.x == 0) {       // Σ activation per token (Q4 zero point)
         for (int t = q0 / 32; t < nt; t += nq / 32) {
@@ -260,10 +274,15 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
                        a.ep.seq);
       }
       s_ok = wait_flags_sys(reinterpret_cast<const unsigned long long*>(a.ep.base_local + kEpDispatchFlags),
-                            a.ep.world, a.ep.seq);
+                            a.ep.world, a.ep.seq, a.ep.wait_ns);
       if (!s_ok) atomicOr(a.err, kErrTimeout);
     }
     __syncthreads();
+    // every rank's routing is done: if any rank marked a token out of range,
+    // this rank's exact fix-up pass has slots to recompute (one peer per thread)
+    if (s_ok && tid < a.ep.world &&
+        *reinterpret_cast<volatile int*>(peer_base(a.ep, tid) + a.ep.xflag_off) == (int)a.ep.seq)
+      a.flags[0] = 1;
     TK = s_ok ? a.ep.world * a.ep.T_local * a.K : 0;   // a failed wait routes nothing
     const int* all = reinterpret_cast<const int*>(a.ep.base_local + a.ep.idx_off);
     for (int s = tid; s < TK; s += kThreads) sidx[s] = __ldcg(all + s);
@@ -377,7 +396,7 @@ void launch_decode_route(const LayerDev& L, const Workspace& ws, const float* x,
   a.nt = nt; a.max_tiles = nt > 0 ? route_max_tiles(T_route * L.topk, a.E_local, nt) : 0;
   a.slot_pos = nt > 0 ? ws.slot_pos : nullptr;
   a.xact = ws.xact; a.xsum = ws.xsum; a.q4_mma = nt > 0; a.counter = counter; a.err = err;
-  a.flags = ep ? nullptr : ws.xbad;
+  a.flags = ws.xbad;
   a.ep_on = ep != nullptr;
   if (ep) a.ep = *ep;
   const size_t smem = (size_t)(rt::kE + rt::kT) * (L.D + 4) * 4;

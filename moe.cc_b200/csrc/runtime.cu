@@ -171,7 +171,8 @@ static int error_status(int h) {
   if (h) {
     // a timeout is reported first: it means some kernel's results are missing
     if (h & kErrTimeout)
-      return set_err(MOE_ERR_CUDA, "a pipelined kernel gave up waiting on a copy (bounded wait)");
+      return set_err(MOE_ERR_CUDA,
+                     "a kernel gave up waiting (bounded wait on a copy, or on another rank's flag)");
     if (h & kErrRange)
       return set_err(MOE_ERR_RANGE,
                      "an activation was NaN/inf or outside the integer range of the "
@@ -1029,9 +1030,11 @@ struct EpCtx {
   bool ready = false, connected = false;
   int cap_tokens = 0, D = 0, K = 0, world = 0;
   uint8_t* buf = nullptr;
-  size_t xact_off = 0, xsum_off = 0, idx_off = 0, p_off = 0, y_off = 0, parity_bytes = 0;
+  size_t xact_off = 0, xsum_off = 0, idx_off = 0, p_off = 0, y_off = 0, xf_off = 0, xflag_off = 0;
+  size_t parity_bytes = 0;
   void* peer_base[kEpMaxRanks] = {};
   uint8_t** d_base = nullptr;                // device array of the peers' bases
+  cudaIpcMemHandle_t own{};                  // this rank's handle (ep_setup)
   unsigned long long seq = 0;
 };
 static EpCtx g_ep;
@@ -1046,6 +1049,19 @@ static void ep_release() {
 static void ep_shutdown_hook() { ep_release(); }
 
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// Time limit of the device-side waits on the other ranks' flags (dispatch in
+// the routing kernel, combine in ep_combine): MOE_EP_WAIT_MS, default 200 ms.
+// Ranks must enter each moe_ffn_ep call within that time of one another; a
+// wait that runs out reports MOE_ERR_CUDA through moe_cuda_check_status.
+static unsigned long long ep_wait_ns() {
+  static long long ms = -1;
+  if (ms < 0) {
+    const char* e = getenv("MOE_EP_WAIT_MS");
+    ms = e && atoll(e) > 0 ? atoll(e) : 200;
+  }
+  return (unsigned long long)ms * 1000000ull;
+}
 }  // namespace moe
 
 extern "C" {
@@ -1095,6 +1111,8 @@ int moe_cuda_ep_setup(int max_tokens_local, int D, int top_k, void* ipc_handle_o
   g_ep.idx_off = o;   o = align256(o + TA * top_k * 4);
   g_ep.p_off = o;     o = align256(o + TA * top_k * 4);
   g_ep.y_off = o;     o = align256(o + (size_t)max_tokens_local * top_k * D * 4);
+  g_ep.xf_off = o;    o = align256(o + (size_t)max_tokens_local * D * 4);
+  g_ep.xflag_off = o; o = align256(o + (2 + (size_t)max_tokens_local) * 4);
   g_ep.parity_bytes = o;
   const size_t bytes = kEpHeader + 2 * o;
   if (cudaMalloc((void**)&g_ep.buf, bytes) != cudaSuccess)
@@ -1103,6 +1121,7 @@ int moe_cuda_ep_setup(int max_tokens_local, int D, int top_k, void* ipc_handle_o
   cudaIpcMemHandle_t h;
   CU(cudaIpcGetMemHandle(&h, g_ep.buf));
   memcpy(ipc_handle_out, &h, sizeof(h));
+  g_ep.own = h;
   g_ep.cap_tokens = max_tokens_local; g_ep.D = D; g_ep.K = top_k; g_ep.world = W;
   g_ep.ready = true;
   return MOE_OK;
@@ -1116,7 +1135,10 @@ int moe_cuda_ep_connect(const void* ipc_handles) {
   const cudaIpcMemHandle_t* hs = (const cudaIpcMemHandle_t*)ipc_handles;
   std::vector<uint8_t*> base(W);
   for (int p = 0; p < W; ++p) {
-    if (p == g.ep_rank) {
+    // this rank's own buffer, and any entry holding this rank's own handle
+    // (a loopback group in one process, whose waits on the other entries
+    // can only expire: used to test the bounded waits on one GPU)
+    if (p == g.ep_rank || memcmp(&hs[p], &g_ep.own, sizeof(g_ep.own)) == 0) {
       g_ep.peer_base[p] = g_ep.buf;
     } else if (!g_ep.peer_base[p]) {
       void* ptr = nullptr;
@@ -1159,6 +1181,8 @@ int moe_ffn_ep(int layer, const float* x_norm2, int T_local, float* x_inout, voi
   ep.xact_off = kEpHeader + par + g_ep.xact_off; ep.xsum_off = kEpHeader + par + g_ep.xsum_off;
   ep.idx_off = kEpHeader + par + g_ep.idx_off;   ep.p_off = kEpHeader + par + g_ep.p_off;
   ep.y_off = kEpHeader + par + g_ep.y_off;
+  ep.xf_off = kEpHeader + par + g_ep.xf_off;     ep.xflag_off = kEpHeader + par + g_ep.xflag_off;
+  ep.wait_ns = ep_wait_ns();
   // the expert kernels read all ranks' tokens from the exchange buffers
   Workspace w = g.ws;
   w.xact = g_ep.buf + ep.xact_off;
@@ -1166,9 +1190,6 @@ int moe_ffn_ep(int layer, const float* x_norm2, int T_local, float* x_inout, voi
   w.topk_idx = (int*)(g_ep.buf + ep.idx_off);
   w.topk_p = (float*)(g_ep.buf + ep.p_off);
   w.cap_T = std::min(g.ws.cap_T, W * g_ep.cap_tokens);     // rows the tensor maps may cover
-  // no exact fix-up across ranks: an out-of-range activation is reported as
-  // MOE_ERR_RANGE by moe_cuda_check_status
-  w.xbad = nullptr;
   const int fnt = fused_tile_n(L, T);
   const int nt = fnt ? fnt : mma_tile_n(T, L.dtype);
   timed("route_dispatch", st, [&] {
@@ -1186,6 +1207,10 @@ int moe_ffn_ep(int layer, const float* x_norm2, int T_local, float* x_inout, voi
       });
   }
   if (!ok) return set_err(MOE_ERR_CUDA, "tensor-core launch failed (tensor map or shared memory)");
+  // exact recomputation of out-of-range tokens' slots; raises the combine flags
+  timed("exact_fixup_ep", st, [&] {
+    launch_exact_fixup(L, nullptr, w.topk_idx, nullptr, T, nullptr, w.xbad, g.sm_count, st, &ep);
+  });
   timed("ep_combine", st, [&] { launch_ep_combine(ep, x_inout, x_inout, L.D, L.topk, g.d_err, st); });
   CU(cudaGetLastError());
   return MOE_OK;

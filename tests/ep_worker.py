@@ -19,11 +19,30 @@ import moe_cuda as mc  # noqa: E402
 import synth as sy  # noqa: E402
 
 
-def fused_exchange(rank, world, T, xn, xa):
+def fused_exchange(rank, world, T, xn, xa, skip=False):
     """moe_ffn_ep: T tokens split into world shards of T/world; three calls
     (both receive-buffer parities, growing flag sequence); returns all T rows
-    gathered from the ranks."""
+    gathered from the ranks.
+    skip: first, rank 1 leaves one call out (between steps, nothing of its own
+    in flight): rank 0's waits on its flags must run out (MOE_EP_WAIT_MS),
+    moe_cuda_check_status must report it, and after a fresh ep_setup /
+    ep_connect on both ranks the calls must be exact again."""
     Tl = T // world
+    if skip:
+        handles = [None] * world
+        dist.all_gather_object(handles, mc.ep_setup(Tl, 2048, 8))
+        mc.ep_connect(handles)
+        dist.barrier()
+        if rank == 0:
+            x = xa[:Tl].clone()
+            mc.moe_ffn_ep(0, xn[:Tl], x)
+            torch.cuda.synchronize()
+            try:
+                mc.check_status()
+                raise AssertionError("rank 0 did not report the expired wait")
+            except mc.MoeError as e:
+                assert e.code == mc.MOE_ERR_CUDA, str(e)
+        dist.barrier()                  # rank 0's kernels are done before buffers go
     handles = [None] * world
     dist.all_gather_object(handles, mc.ep_setup(Tl, 2048, 8))
     mc.ep_connect(handles)
@@ -48,6 +67,7 @@ def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     out_path, T, dt = sys.argv[1], int(sys.argv[2]), int(sys.argv[3])
     mode = sys.argv[4] if len(sys.argv) > 4 else "nccl"
+    inputs = sys.argv[5] if len(sys.argv) > 5 else "normal"
     ngpu = torch.cuda.device_count()
     dev = rank if ngpu >= world else 0
     torch.cuda.set_device(dev)
@@ -61,8 +81,13 @@ def main():
     mc.upload_layer(0, L, device_arrays=True)
     xn = sy.make_tokens_dev(torch, 501, T, 2048)
     xa = sy.make_tokens_dev(torch, 502, T, 2048)
-    if mode == "fused":
-        out = fused_exchange(rank, world, T, xn, xa)
+    if inputs == "big":
+        # tokens whose activations leave the fast kernels' integer range (Q8:
+        # |x| >= 258; Q4: |x| > 18.3, which also drives h out of range): the
+        # exact fix-up pass on the experts' owners computes their slots
+        xn[0::3, 5::97] *= 300.0 if dt == 2 else 25.0
+    if mode in ("fused", "skip"):
+        out = fused_exchange(rank, world, T, xn, xa, skip=(mode == "skip"))
     else:
         y = torch.empty(T * 8, 2048, device="cuda")
         p = torch.empty(T, 8, device="cuda")

@@ -12,12 +12,13 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def assert_matches_port(out, ref, T):
-    """Bit-exact for small batches. With many tokens a few SiLU / softmax
-    exponentials round differently in the last place (device: double exp
-    rounded once; oracle: glibc expf), so large batches are held to the
-    layer tolerance 1e-4*max|y| with at least 99.5% of outputs identical."""
-    if T <= 64:
+def assert_matches_port(out, ref, T, xn):
+    """Bit-exact for small batches of in-range tokens. With many tokens, or
+    large activations, a few SiLU / softmax exponentials round differently in
+    the last place (device: double exp rounded once; oracle: glibc expf), so
+    those are held to the layer tolerance 1e-4*max|y| with at least 99.5% of
+    outputs identical."""
+    if T <= 64 and float(np.abs(xn).max()) < 18.0:
         assert np.array_equal(out, ref)
         return
     err = float(np.abs(out - ref).max())
@@ -25,12 +26,13 @@ def assert_matches_port(out, ref, T):
     assert float(np.mean(out == ref)) >= 0.995
 
 
-@pytest.mark.parametrize("dt,T", [(2, 16), (2, 40), (2, 256)])
-def test_expert_parallel_two_ranks_matches_oracle(tmp_path, dt, T):
+@pytest.mark.parametrize("dt,T,inputs", [(2, 16, "normal"), (2, 40, "normal"), (2, 256, "normal"),
+                                         (2, 16, "big"), (3, 40, "big")])
+def test_expert_parallel_two_ranks_matches_oracle(tmp_path, dt, T, inputs):
     out = str(tmp_path / "ep.npz")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr", "127.0.0.1", "--master-port", str(29500 + T),
-           os.path.join(HERE, "ep_worker.py"), out, str(T), str(dt)]
+           "--master-addr", "127.0.0.1", "--master-port", str(29500 + T + 7 * dt + (50 if inputs == "big" else 0)),
+           os.path.join(HERE, "ep_worker.py"), out, str(T), str(dt), "nccl", inputs]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-3000:]
     from oracle.oracle import Port
@@ -39,22 +41,31 @@ def test_expert_parallel_two_ranks_matches_oracle(tmp_path, dt, T):
     for k in ("router_w", "gq", "gs", "uq", "us", "dq", "ds"):
         L[k] = z[k]
     ref, _, _, _ = Port().moe_block(z["xn"], z["xa"], L)
-    assert_matches_port(z["out"], ref, T)
+    assert_matches_port(z["out"], ref, T, z["xn"])
 
 
-@pytest.mark.parametrize("dt,T", [(2, 16), (3, 40), (2, 256)])
-def test_fused_expert_parallel_two_gpus_matches_oracle(tmp_path, dt, T):
+@pytest.mark.parametrize("dt,T,mode,inputs", [(2, 16, "fused", "normal"), (3, 40, "fused", "normal"),
+                                              (2, 256, "fused", "normal"), (2, 16, "fused", "big"),
+                                              (3, 40, "fused", "big"), (2, 16, "skip", "normal")])
+def test_fused_expert_parallel_two_gpus_matches_oracle(tmp_path, dt, T, mode, inputs):
     """moe_ffn_ep: the down GEMM stores slot rows into the owning rank's
     receive buffer over NVLink and the combine waits on the ranks' flags.
-    Needs one GPU per rank (ranks spin on one another)."""
+    "big": out-of-range tokens, recomputed by the experts' owners' exact
+    fix-up pass. "skip": rank 1 first leaves a call out; rank 0's bounded
+    waits run out and report it, then a fresh setup works. Needs one GPU per
+    rank (ranks spin on one another)."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("the fused exchange needs one GPU per rank (2 GPUs)")
     out = str(tmp_path / "epf.npz")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr", "127.0.0.1", "--master-port", str(29700 + T + dt),
-           os.path.join(HERE, "ep_worker.py"), out, str(T), str(dt), "fused"]
-    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+           "--master-addr", "127.0.0.1",
+           "--master-port", str(29700 + T + dt + (40 if inputs == "big" else 0) + (80 if mode == "skip" else 0)),
+           os.path.join(HERE, "ep_worker.py"), out, str(T), str(dt), mode, inputs]
+    # the skip case: short flag waits, and no NVLink multicast in NCCL while a
+    # rank sits a call out
+    env = dict(os.environ, MOE_EP_WAIT_MS="100", NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
     assert r.returncode == 0, r.stderr[-3000:]
     from oracle.oracle import Port
     z = np.load(out)
@@ -62,4 +73,4 @@ def test_fused_expert_parallel_two_gpus_matches_oracle(tmp_path, dt, T):
     for k in ("router_w", "gq", "gs", "uq", "us", "dq", "ds"):
         L[k] = z[k]
     ref, _, _, _ = Port().moe_block(z["xn"], z["xa"], L)
-    assert_matches_port(z["out"], ref, T)
+    assert_matches_port(z["out"], ref, T, z["xn"])
