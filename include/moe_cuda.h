@@ -54,6 +54,7 @@ typedef struct {
 #define MOE_ERR_UNSUPPORTED  5  /* valid for the reference, not built here */
 #define MOE_ERR_NOMEM        6  /* device allocation failed */
 
+#define MOE_DTYPE_F32 0   /* unquantised fp32 experts (moe_cuda_upload_layer_f32) */
 #define MOE_DTYPE_Q8 2
 #define MOE_DTYPE_Q4 3
 
@@ -64,6 +65,14 @@ typedef struct {
 #define MOE_FFN_DEVICE_PTRS 0x0 /* all pointers are device memory; async */
 #define MOE_FFN_FORCE_GEMV  0x4 /* always use the decode (GEMV) kernels */
 #define MOE_FFN_FORCE_GEMM  0x8 /* always use the grouped tcgen05 GEMM */
+#define MOE_FFN_SEQ_RESIDUAL 0x10 /* add p*y into x_inout one slot at a time,
+                                     x = ((x + p0 y0) + p1 y1) + ..., as
+                                     model.c:188 does, instead of
+                                     x + (p0 y0 + p1 y1 + ...) as
+                                     test_model_trace.c:513,517 */
+#define MOE_FFN_GIVEN_TOPK  0x20 /* topk_idx_out / topk_p_out are inputs: the
+                                    routing to use (model.c:139-141 reuse_topk),
+                                    no router or top-k is computed */
 
 /* ---- runtime -------------------------------------------------------------
  * No reference counterpart (moe.cc has no device); the reference's process
@@ -86,8 +95,11 @@ int moe_cuda_check_status(void);
 /* replaces static matmul_f32_q8, kernels.c:51 (same parameter list) */
 void matmul_f32_q8(const float* A, const int8_t* B_q, const float* B_s,
                    float* C, int M, int N, int K);
-/* replaces static matmul_f32_q4, kernels.c:96 (same parameter list; K even,
- * see DESIGN notes on the reference's odd-K read past the row) */
+/* replaces static matmul_f32_q4, kernels.c:96 (same parameter list). K must
+ * be even: with odd K the reference reads the last weight byte's low nibble
+ * and then one byte past the packed row (kernels.c:108,116-119), memory it
+ * does not own; this library returns MOE_ERR_UNSUPPORTED for odd K instead
+ * (the host-pointer form aborts with that message). */
 void matmul_f32_q4(const float* A, const uint8_t* B_q, const float* B_s,
                    float* C, int M, int N, int K);
 /* replaces matmul_adaptive, kernels.h:16-17 / kernels.c:149-181:
@@ -155,6 +167,15 @@ int moe_cuda_upload_layer_dev(int layer, const QuantizedWeight* Wg,
                               const QuantizedWeight* Wd,
                               const float* router_w, const float* router_b,
                               int E);
+/* A layer with unquantised fp32 experts, as model.c's layer_forward_f32 takes
+ * them (QwenLayerWeights Wg/Wu/Wd, model.h:41-43, used at model.c:172-187):
+ * Wg[e], Wu[e] host [F][D], Wd[e] host [D][F], e < E; router_w [E][D],
+ * router_b [E] or NULL; top_k experts per token (1..32, <= E). moe_ffn then
+ * runs the fp32 expert FFN (each output one sequential fp32 chain in k order,
+ * as matmul_f32, test_model_trace.c:213-227). No expert parallelism. */
+int moe_cuda_upload_layer_f32(int layer, const float* const* Wg, const float* const* Wu,
+                              const float* const* Wd, const float* router_w,
+                              const float* router_b, int E, int D, int F, int top_k);
 int moe_cuda_free_layer(int layer);
 /* Bytes of device memory the layer's expert slabs occupy on this rank. */
 size_t moe_cuda_layer_bytes(int layer);

@@ -4,6 +4,8 @@
 #include <stdint.h>
 #include <utility>
 
+#include "expf_ref.h"
+
 namespace moe {
 
 // Exactly-rounded scalar ops used wherever the reference's arithmetic must be
@@ -12,11 +14,9 @@ __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b)
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
 
-// expf(v) rounded once from a double-precision exp. glibc's expf (the
-// reference's, test_model_trace.c:233,485) is accurate to within about half
-// an ulp, so the two agree except where the exact value lies within a hair of
-// a rounding midpoint.
-__device__ __forceinline__ float exp_f32(float v) { return (float)exp((double)v); }
+// expf with the C library's results, bit for bit (expf_ref.h): the softmax
+// and SiLU exponentials of the reference (test_model_trace.c:233,485).
+__device__ __forceinline__ float exp_f32(float v) { return expf_ref(v); }
 
 // silu_f32 (test_model_trace.c:229-236): v / (1 + expf(-v)).
 __device__ __forceinline__ float silu_ref(float v) {

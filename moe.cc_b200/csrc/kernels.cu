@@ -971,33 +971,35 @@ void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y, cudaSt
 
 // k-ordered combine + residual as a separate pass (prefill, expert parallel)
 // out[t] = xres[t] + Σ_k p[t][k] y[t*K+k] in k order (test_model_trace.c:513,
-// :517). A slot with no expert (idx < 0: fewer than K logits that are neither
-// NaN nor -inf) adds p * 0: the reference reads an expert out of bounds
-// there, and its p is 0 (finite maximum) or NaN (no finite logit), which
-// gives 0 or NaN whatever that expert holds. idx may be null (every slot has
-// an expert).
+// :517), or with seq_residual out[t] = (xres[t] + p0 y0) + p1 y1 ... as
+// model.c:188 accumulates into x directly. A slot with no expert (idx < 0:
+// fewer than K logits that are neither NaN nor -inf) adds p * 0: the
+// reference reads an expert out of bounds there, and its p is 0 (finite
+// maximum) or NaN (no finite logit), which gives 0 or NaN whatever that
+// expert holds. idx may be null (every slot has an expert).
 __global__ void combine_kernel(const float* __restrict__ y, const float* __restrict__ p,
-                               const int* __restrict__ idx, const float* xres, float* out, int T, int D, int K) {
+                               const int* __restrict__ idx, const float* xres, float* out, int T, int D, int K,
+                               int seq) {
   pdl_wait();
   pdl_launch();
   const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= (long)T * D) return;
   const int t = (int)(q / D), n = (int)(q % D);
-  float acc = 0.0f;
+  float acc = seq ? xres[q] : 0.0f;
   for (int k = 0; k < K; ++k) {
     const int s = t * K + k;
     const float yv = (idx && idx[s] < 0) ? 0.0f : y[(size_t)s * D + n];
     acc = fadd(acc, fmul(p[s], yv));
   }
-  out[q] = fadd(xres[q], acc);
+  out[q] = seq ? acc : fadd(xres[q], acc);
 }
 
 void launch_combine(const float* y, const float* p, const int* idx, const float* xres, float* out, int T, int D,
-                    int K, cudaStream_t st) {
+                    int K, cudaStream_t st, bool seq_residual) {
   const long total = (long)T * D;
   if (total <= 0) return;
   launch_pdl(combine_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, y, p, idx, xres, out, T, D,
-             K);
+             K, seq_residual ? 1 : 0);
 }
 
 // --------------------------------------------------------------------------

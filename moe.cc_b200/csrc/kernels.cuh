@@ -9,6 +9,8 @@ namespace moe {
 // Device-resident layer (one expert-parallel shard of one MoE layer).
 // Each local expert owns one slab of `expert_stride` bytes:
 //   [gate q | up q | down q | gate s | up s | down s], parts 128 B aligned.
+// dtype 2 (Q8), 3 (Q4) or 0 (fp32 experts: gate [F][D], up [F][D] and down
+// [D][F] floats at gq_off, uq_off, dq_off; no scales).
 struct LayerDev {
   int E = 0, D = 0, F = 0, dtype = 0, topk = 8;
   int e_begin = 0, e_end = 0;         // this rank's experts [e_begin, e_end)
@@ -173,8 +175,13 @@ void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y, cudaSt
 // combine flags at every rank.
 void launch_exact_fixup(const LayerDev& L, const float* xn, const int* idx, const int* slot_pos, int T,
                         float* y, int* flags, int sm_count, cudaStream_t st, const EpView* ep = nullptr);
+// seq_residual: out = ((xres + p0 y0) + p1 y1) + ... (model.c:188) instead of
+// xres + (((0 + p0 y0) + p1 y1) + ...) (test_model_trace.c:513,517)
 void launch_combine(const float* y, const float* p, const int* idx, const float* xres,
-                    float* out, int T, int D, int K, cudaStream_t st);
+                    float* out, int T, int D, int K, cudaStream_t st, bool seq_residual = false);
+// fp32 experts (f32_experts.cu): h [T*K][F], y [T*K][D] (slot rows)
+void launch_f32_experts(const LayerDev& L, const float* xn, const int* idx, int T, float* h, float* y,
+                        cudaStream_t st);
 void launch_quantize_rowwise(int dtype, const float* W, int rows, int cols,
                              void* q, float* s, cudaStream_t st);
 void launch_synth_normal(uint64_t seed, uint64_t offset, size_t n, float std,
@@ -201,7 +208,8 @@ int fused_tile_n(const LayerDev& L, int T);
 bool launch_mma_fused(const LayerDev& L, const Workspace& ws, int T, int nt, int* err, cudaStream_t st,
                       const EpView* ep = nullptr);
 void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
-                           const float* xres, float* out, int T, int D, int K, cudaStream_t st);
+                           const float* xres, float* out, int T, int D, int K, cudaStream_t st,
+                           bool seq_residual = false);
 void launch_unsort_rows(const LayerDev& L, const Workspace& ws, int T, float* y_slots, cudaStream_t st);
 }  // namespace moe
 

@@ -661,14 +661,16 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
 // combine from expert-sorted y rows (prefill / non-fused path)
 __global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* __restrict__ slot_pos,
                                       const float* __restrict__ p, const int* __restrict__ idx,
-                                      const float* xres, float* out, int T, int D, int K) {
+                                      const float* xres, float* out, int T, int D, int K, int seq) {
   MOE_TL_START(kTlCombine);
   pdl_wait();
   pdl_launch();
   const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= (long)T * D) return;
   const int t = (int)(q / D), n = (int)(q % D);
-  float acc = 0.0f;
+  // seq: accumulate into the residual in k order (model.c:188), else add the
+  // k-ordered sum to it (test_model_trace.c:513,517)
+  float acc = seq ? xres[q] : 0.0f;
   constexpr int KF = 8;
   if (K <= KF) {
     // all slots' routing words first, then all their y values: two dependent
@@ -697,16 +699,16 @@ __global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* _
       acc = fadd(acc, fmul(p[s], idx[s] < 0 ? 0.0f : ys[(size_t)slot_pos[s] * D + n]));
     }
   }
-  out[q] = fadd(xres[q], acc);
+  out[q] = seq ? acc : fadd(xres[q], acc);
   MOE_TL_END(kTlCombine);
 }
 
 void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
-                           const float* xres, float* out, int T, int D, int K, cudaStream_t st) {
+                           const float* xres, float* out, int T, int D, int K, cudaStream_t st, bool seq_residual) {
   const long total = (long)T * D;
   if (total <= 0) return;
   launch_pdl(combine_sorted_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, ys, slot_pos, p, idx, xres,
-             out, T, D, K);
+             out, T, D, K, seq_residual ? 1 : 0);
 }
 
 // Expert-parallel output: slot-ordered rows of this rank's slots, zeros for

@@ -214,7 +214,7 @@ using namespace moe;
 namespace moe {
 static void ep_shutdown_hook();   // releases the expert-parallel buffers (defined below)
 struct Buf { void* p = nullptr; size_t cap = 0; };
-static Buf s_A, s_C, s_W, s_S, s_act, s_asum;
+static Buf s_A, s_C, s_W, s_S, s_act, s_asum, s_hf;
 
 static int grow(Buf& b, size_t bytes) {
   if (bytes <= b.cap) return MOE_OK;
@@ -345,7 +345,7 @@ int moe_cuda_shutdown(void) {
                   w.fused_ctr, w.xbad};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
-  Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum};
+  Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum, &s_hf};
   for (Buf* b : bufs) { if (b->p) cudaFree(b->p); *b = Buf{}; }
   cudaFree(g.d_err); g.d_err = nullptr;
   if (g.h_err) cudaFreeHost(g.h_err);
@@ -628,8 +628,11 @@ static void prof_drain() {
 }
 
 // Router + top-k + routing lists + token activation truncation.
-static void route_tokens(const LayerDev& L, const float* xn, int T, int nt, cudaStream_t st) {
-  if (decode_route_supported(L, T, xn)) {
+// given: w.topk_idx / w.topk_p already hold the routing (MOE_FFN_GIVEN_TOPK):
+// no router logits or top-k, only the activations and the routing lists.
+static void route_tokens(const LayerDev& L, const float* xn, int T, int nt, cudaStream_t st,
+                         bool given = false) {
+  if (!given && decode_route_supported(L, T, xn)) {
     timed("route", st, [&] {
       launch_decode_route(L, g.ws, xn, T, nt, g.ws.route_counter, g.d_err, st);
     });
@@ -639,12 +642,14 @@ static void route_tokens(const LayerDev& L, const float* xn, int T, int nt, cuda
   timed("quantize_act", st, [&] {
     launch_quantize_act(xn, T, L.D, L.dtype, w.xact, 2 * L.D, w.xsum, g.d_err, st, nt > 0, w.xbad);
   });
-  timed("router_logits", st, [&] {
-    launch_f32_seq_matmul(xn, L.router_w, L.router_b, w.logits, T, L.E, L.D, st);
-  });
-  timed("topk_softmax", st, [&] {
-    launch_topk_softmax(w.logits, T, L.E, L.topk, w.topk_idx, w.topk_p, st);
-  });
+  if (!given) {
+    timed("router_logits", st, [&] {
+      launch_f32_seq_matmul(xn, L.router_w, L.router_b, w.logits, T, L.E, L.D, st);
+    });
+    timed("topk_softmax", st, [&] {
+      launch_topk_softmax(w.logits, T, L.E, L.topk, w.topk_idx, w.topk_p, st);
+    });
+  }
   timed("route_build", st, [&] {
     if (T * L.topk > 1024)
       launch_route_build_multi(w.topk_idx, T, L.topk, L.e_begin, L.e_end - L.e_begin, w.route,
@@ -816,6 +821,52 @@ int moe_cuda_upload_layer_dev(int layer, const QuantizedWeight* Wg, const Quanti
   return upload_layer(layer, Wg, Wu, Wd, router_w, router_b, E, cudaMemcpyDeviceToDevice);
 }
 
+int moe_cuda_upload_layer_f32(int layer, const float* const* Wg, const float* const* Wu, const float* const* Wd,
+                              const float* router_w, const float* router_b, int E, int D, int F, int top_k) {
+  std::lock_guard<std::recursive_mutex> lk(g.mu);
+  int rc = ensure_init();
+  if (rc) return rc;
+  if (g.ep_world > 1) return set_err(MOE_ERR_UNSUPPORTED, "fp32 experts: no expert parallelism");
+  if (E <= 0 || D <= 0 || F <= 0 || !Wg || !Wu || !Wd || !router_w)
+    return set_err(MOE_ERR_INVALID, "moe_cuda_upload_layer_f32: bad arguments");
+  if (top_k < 1 || top_k > 32 || top_k > E || E > 256)
+    return set_err(MOE_ERR_UNSUPPORTED, "fp32 experts: top_k %d of E %d (top_k 1..32, E <= 256)", top_k, E);
+  for (int e = 0; e < E; ++e)
+    if (!Wg[e] || !Wu[e] || !Wd[e]) return set_err(MOE_ERR_INVALID, "expert %d: NULL weight", e);
+  host_graphs_reset();
+  if (g.layers.count(layer)) moe_cuda_free_layer(layer);
+  LayerDev L;
+  L.E = E; L.D = D; L.F = F; L.dtype = MOE_DTYPE_F32; L.topk = top_k;
+  L.e_begin = 0; L.e_end = E;
+  const size_t mb = sizeof(float) * (size_t)F * D;
+  L.gq_off = 0;
+  L.uq_off = align_up(mb, 128);
+  L.dq_off = L.uq_off + align_up(mb, 128);
+  L.gs_off = L.us_off = L.ds_off = 0;
+  L.expert_stride = align_up(L.dq_off + mb, 128);
+  L.bytes = L.expert_stride * (size_t)E;
+  if (cudaMalloc((void**)&L.slab, L.bytes) != cudaSuccess)
+    return set_err(MOE_ERR_NOMEM, "layer %d: %zu bytes of fp32 expert slabs", layer, L.bytes);
+  if (cudaMalloc((void**)&L.router_w, sizeof(float) * (size_t)E * D) != cudaSuccess) {
+    cudaFree(L.slab);
+    return set_err(MOE_ERR_NOMEM, "layer %d router", layer);
+  }
+  if (router_b && cudaMalloc((void**)&L.router_b, sizeof(float) * E) != cudaSuccess) {
+    cudaFree(L.slab); cudaFree(L.router_w);
+    return set_err(MOE_ERR_NOMEM, "layer %d router bias", layer);
+  }
+  g.layers[layer] = L;
+  CU(cudaMemcpy(L.router_w, router_w, sizeof(float) * (size_t)E * D, cudaMemcpyHostToDevice));
+  if (router_b) CU(cudaMemcpy(L.router_b, router_b, sizeof(float) * E, cudaMemcpyHostToDevice));
+  for (int e = 0; e < E; ++e) {
+    uint8_t* base = L.slab + (size_t)e * L.expert_stride;
+    CU(cudaMemcpy(base + L.gq_off, Wg[e], mb, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(base + L.uq_off, Wu[e], mb, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(base + L.dq_off, Wd[e], mb, cudaMemcpyHostToDevice));
+  }
+  return MOE_OK;
+}
+
 int moe_cuda_free_layer(int layer) {
   std::lock_guard<std::recursive_mutex> lk(g.mu);
   auto it = g.layers.find(layer);
@@ -858,16 +909,32 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
   const Workspace& w = g.ws;
   const size_t xb = sizeof(float) * (size_t)T * L.D;
   // The kernels of one call on stream s: read xn, update xo in place.
+  const bool given = flags & MOE_FFN_GIVEN_TOPK, seq = flags & MOE_FFN_SEQ_RESIDUAL;
+  if (given && (!topk_idx_out || !topk_p_out))
+    return set_err(MOE_ERR_INVALID, "MOE_FFN_GIVEN_TOPK needs topk_idx_out and topk_p_out (the routing)");
+  if (L.dtype == MOE_DTYPE_F32 && (rc = grow(s_hf, sizeof(float) * (size_t)T * L.topk * L.F))) return rc;
   // The combine always runs as its own kernel, after the exact fix-up pass
   // (exact.cu), which recomputes the slots of any token whose activations
   // left the fast kernels' integer range. (Fused into the down epilogue the
   // combine also left the last warp through each row block with T*K dependent
   // loads at the end of the kernel: measured 90 us vs 39 + 6 us.)
   auto enqueue = [&](const float* xn, float* xo, cudaStream_t s) -> int {
-    if (use_tensor_cores(L, flags)) {
+    if (L.dtype == MOE_DTYPE_F32) {
+      // fp32 experts: router chains + top-k softmax, the fp32 expert FFN, combine
+      if (!given) {
+        timed("router_logits", s, [&] {
+          launch_f32_seq_matmul(xn, L.router_w, L.router_b, w.logits, T, L.E, L.D, s);
+        });
+        timed("topk_softmax", s, [&] {
+          launch_topk_softmax(w.logits, T, L.E, L.topk, w.topk_idx, w.topk_p, s);
+        });
+      }
+      timed("f32_experts", s, [&] { launch_f32_experts(L, xn, w.topk_idx, T, (float*)s_hf.p, w.y, s); });
+      timed("combine", s, [&] { launch_combine(w.y, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s, seq); });
+    } else if (use_tensor_cores(L, flags)) {
       const int fnt = fused_tile_n(L, T);                 // fused gate/up + down kernel, if used
       const int nt = fnt ? fnt : mma_tile_n(T, L.dtype);
-      route_tokens(L, xn, T, nt, s);
+      route_tokens(L, xn, T, nt, s, given);
       if (T > nt) timed("gather", s, [&] { launch_mma_gather(L, w, T, nt, s); });
       bool ok = true;
       if (fnt) {
@@ -881,21 +948,28 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
         launch_exact_fixup(L, xn, w.topk_idx, w.slot_pos, T, w.y, w.xbad, g.sm_count, s);
       });
       timed("combine", s, [&] {
-        launch_combine_sorted(w.y, w.slot_pos, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s);
+        launch_combine_sorted(w.y, w.slot_pos, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s, seq);
       });
     } else {
-      route_tokens(L, xn, T, 0, s);
+      route_tokens(L, xn, T, 0, s, given);
       timed("gateup", s, [&] { run_gateup(L, w, T, s); });
       timed("down", s, [&] { run_down(L, w, T, w.y, s); });
       timed("exact_fixup", s, [&] {
         launch_exact_fixup(L, xn, w.topk_idx, nullptr, T, w.y, w.xbad, g.sm_count, s);
       });
-      timed("combine", s, [&] { launch_combine(w.y, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s); });
+      timed("combine", s, [&] { launch_combine(w.y, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s, seq); });
     }
     CU(cudaGetLastError());
     return MOE_OK;
   };
-  if (host && !st && !g_prof && e2e_graph_on())
+  const size_t kb = sizeof(int) * (size_t)T * L.topk;
+  if (given) {
+    // the caller's routing goes where the kernels read it
+    const cudaMemcpyKind in_kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    CU(cudaMemcpyAsync(w.topk_idx, topk_idx_out, kb, in_kind, st));
+    CU(cudaMemcpyAsync(w.topk_p, topk_p_out, kb, in_kind, st));
+  }
+  if (host && !st && !g_prof && !given && e2e_graph_on())
     return moe_ffn_host_graph(layer, T, flags, x_norm2, x_inout, topk_idx_out, topk_p_out, xb,
                               sizeof(int) * (size_t)T * L.topk, enqueue);
   const float* xn = x_norm2;
@@ -906,10 +980,9 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
     xn = w.xn; xo = w.xo;
   }
   if ((rc = enqueue(xn, xo, st))) return rc;
-  const size_t kb = sizeof(int) * (size_t)T * L.topk;
   const cudaMemcpyKind out_kind = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
-  if (topk_idx_out) CU(cudaMemcpyAsync(topk_idx_out, w.topk_idx, kb, out_kind, st));
-  if (topk_p_out) CU(cudaMemcpyAsync(topk_p_out, w.topk_p, kb, out_kind, st));
+  if (topk_idx_out && !given) CU(cudaMemcpyAsync(topk_idx_out, w.topk_idx, kb, out_kind, st));
+  if (topk_p_out && !given) CU(cudaMemcpyAsync(topk_p_out, w.topk_p, kb, out_kind, st));
   if (host) {
     CU(cudaMemcpyAsync(x_inout, xo, xb, cudaMemcpyDeviceToHost, st));
     return consume_stream_error(st);
@@ -925,6 +998,7 @@ int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots, int*
   if (rc) return rc;
   const LayerDev& L = *Lp;
   if (T < 0) return set_err(MOE_ERR_INVALID, "T=%d", T);
+  if (L.dtype == MOE_DTYPE_F32) return set_err(MOE_ERR_UNSUPPORTED, "moe_ffn_partial: fp32 experts (use moe_ffn)");
   if (T == 0) return MOE_OK;
   if ((rc = ensure_workspace(T, L.E, L.D, L.F, L.topk))) return rc;
   cudaStream_t st = (cudaStream_t)stream;

@@ -848,3 +848,217 @@ out:
   cudaFree(tmp);
   return rc;
 }
+
+/* ---- model.c call surface (include/moe_model.h) ------------------------------
+ * layer_forward_f32 / model_forward_f32 with model.c's parameter lists
+ * (model.c:38-58, :192-198). The CPU parts restate model.c:59-131 and
+ * :199-252 with the helpers above; the MoE block (:133-187) runs on the GPU:
+ * the fp32 experts resident (moe_cuda_upload_layer_f32), moe_ffn with
+ * MOE_FFN_SEQ_RESIDUAL (p*y added straight into x, slot by slot, :188) and,
+ * when the caller passes a routing, MOE_FFN_GIVEN_TOPK. */
+#include <pthread.h>
+#include "../../include/moe_model.h"
+
+typedef struct {
+  const float* router_w;
+  const float* wg0;
+  int E, D, F, topk, id;
+} F32Layer;
+
+static pthread_mutex_t g_f32_mu = PTHREAD_MUTEX_INITIALIZER;
+static F32Layer* g_f32;
+static int g_nf32, g_cap_f32;
+#define MOE_MODEL_LAYER_BASE 0x70000000
+
+static void model_die(const char* who, const char* msg) {
+  fprintf(stderr, "libmoe_host: %s failed: %s\n", who, msg);
+  abort();
+}
+
+/* The resident copy of a layer's fp32 experts: uploaded on first use. */
+static int f32_layer_id(const float* router_w, const float* router_b, const float** Wg, const float** Wu,
+                        const float** Wd, int E, int D, int F, int topk) {
+  pthread_mutex_lock(&g_f32_mu);
+  int id = -1;
+  for (int i = 0; i < g_nf32; ++i) {
+    const F32Layer* l = &g_f32[i];
+    if (l->router_w == router_w && l->wg0 == Wg[0] && l->E == E && l->D == D && l->F == F && l->topk == topk) {
+      id = l->id;
+      break;
+    }
+  }
+  if (id < 0) {
+    moe_cuda_init(0, 1, 0, NULL);  /* no-op (or a harmless refusal) when already initialised */
+    if (g_nf32 == g_cap_f32) {
+      const int nc = g_cap_f32 ? 2 * g_cap_f32 : 16;
+      F32Layer* nl = (F32Layer*)realloc(g_f32, sizeof(F32Layer) * (size_t)nc);
+      if (!nl) { pthread_mutex_unlock(&g_f32_mu); model_die("layer_forward_f32", "out of host memory"); }
+      g_f32 = nl;
+      g_cap_f32 = nc;
+    }
+    id = MOE_MODEL_LAYER_BASE + g_nf32;
+    const int rc = moe_cuda_upload_layer_f32(id, (const float* const*)Wg, (const float* const*)Wu,
+                                             (const float* const*)Wd, router_w, router_b, E, D, F, topk);
+    if (rc) { pthread_mutex_unlock(&g_f32_mu); model_die("layer_forward_f32 (upload)", moe_cuda_last_error()); }
+    F32Layer l = {router_w, Wg[0], E, D, F, topk, id};
+    g_f32[g_nf32++] = l;
+  }
+  pthread_mutex_unlock(&g_f32_mu);
+  return id;
+}
+
+void moe_model_release(void) {
+  pthread_mutex_lock(&g_f32_mu);
+  for (int i = 0; i < g_nf32; ++i) moe_cuda_free_layer(g_f32[i].id);
+  free(g_f32);
+  g_f32 = NULL;
+  g_nf32 = g_cap_f32 = 0;
+  pthread_mutex_unlock(&g_f32_mu);
+}
+
+/* model.c:59-131: norm1, attention over all T positions from 0, residual,
+   norm2. Causal masking only removes keys that add exactly 0. */
+static void model_attention(float* x, int T, int D, const float* rms1_w, float rms1_eps, const float* Wq,
+                            const float* bq, const float* Wk, const float* bk, const float* Wv, const float* bv,
+                            const float* Wo, const float* bo, const float* qn, const float* kn, int n_q, int n_kv,
+                            int dh, int causal, float rope_theta, const float* rms2_w, float rms2_eps,
+                            float* scratch, float* x_norm2) {
+  const int Dq = n_q * dh, Dkv = n_kv * dh, d2 = dh / 2, group = n_q / n_kv;
+  const float scale = 1.0f / sqrtf((float)dh);
+  float* Q = scratch;
+  float* K = Q + (size_t)T * Dq;
+  float* V = K + (size_t)T * Dkv;
+  float* S = V + (size_t)T * Dkv;                 /* [T][T] */
+  float* Hcat = S + (size_t)T * T;
+  float* x_norm1 = Hcat + (size_t)T * Dq;
+  float* attn_out = x_norm1 + (size_t)T * D;
+  rmsnorm_rows(x, rms1_w, T, D, rms1_eps, x_norm1);
+  mm_f32(x_norm1, Wq, Q, T, Dq, D);
+  mm_f32(x_norm1, Wk, K, T, Dkv, D);
+  mm_f32(x_norm1, Wv, V, T, Dkv, D);
+  for (int t = 0; t < T; ++t) {
+    if (bq) for (int i = 0; i < Dq; ++i) Q[(size_t)t * Dq + i] += bq[i];
+    if (bk) for (int i = 0; i < Dkv; ++i) K[(size_t)t * Dkv + i] += bk[i];
+    if (bv) for (int i = 0; i < Dkv; ++i) V[(size_t)t * Dkv + i] += bv[i];
+  }
+  float* inv_freq = (float*)malloc(sizeof(float) * (size_t)(d2 > 0 ? d2 : 1));
+  if (!inv_freq) model_die("layer_forward_f32", "out of host memory");
+  for (int i = 0; i < d2; ++i) inv_freq[i] = powf(rope_theta, -2.0f * (float)i / (float)dh);
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t) {
+    float* Qt = Q + (size_t)t * Dq;
+    float* Kt = K + (size_t)t * Dkv;
+    if (qn && kn) {                                 /* model.c:81-88, eps fixed at 1e-6 */
+      for (int h = 0; h < n_q; ++h) head_norm(Qt + (size_t)h * dh, qn, dh, 1e-6f);
+      for (int h = 0; h < n_kv; ++h) head_norm(Kt + (size_t)h * dh, kn, dh, 1e-6f);
+    }
+    for (int h = 0; h < n_q; ++h) rope_row(Qt + (size_t)h * dh, inv_freq, d2, (float)t);
+    for (int h = 0; h < n_kv; ++h) rope_row(Kt + (size_t)h * dh, inv_freq, d2, (float)t);
+  }
+  free(inv_freq);
+  /* one (head, query) per task; S row tq of the task's own head is private
+     to the task because tasks of one head never share a query row */
+  float* Sh = (float*)malloc(sizeof(float) * (size_t)n_q * T * T);
+  if (!Sh) model_die("layer_forward_f32", "out of host memory (attention scores)");
+#pragma omp parallel for schedule(dynamic, 4)
+  for (int task = 0; task < n_q * T; ++task) {
+    const int h = task / T, tq = task % T, kvh = h / group;
+    const int last = causal ? tq : T - 1;            /* later keys are -inf: exp gives 0 */
+    const float* qv = Q + (size_t)tq * Dq + (size_t)h * dh;
+    float* Sout = Sh + ((size_t)h * T + tq) * T;
+    for (int tk = 0; tk <= last; ++tk) {
+      const float* kv = K + (size_t)tk * Dkv + (size_t)kvh * dh;
+      float dot = 0.f;
+      for (int d = 0; d < dh; ++d) dot += qv[d] * kv[d];
+      Sout[tk] = dot * scale;
+    }
+    float m = Sout[0];
+    for (int i = 1; i <= last; ++i) if (Sout[i] > m) m = Sout[i];
+    float s = 0.f;
+    for (int i = 0; i <= last; ++i) { const float z = expf(Sout[i] - m); Sout[i] = z; s += z; }
+    const float inv = 1.f / (s + 1e-9f);
+    for (int i = 0; i <= last; ++i) Sout[i] *= inv;
+    float* out = Hcat + (size_t)tq * Dq + (size_t)h * dh;
+    for (int d = 0; d < dh; ++d) out[d] = 0.f;
+    for (int tk = 0; tk <= last; ++tk) {
+      const float* vv = V + (size_t)tk * Dkv + (size_t)kvh * dh;
+      const float p = Sout[tk];
+      for (int d = 0; d < dh; ++d) out[d] += p * vv[d];
+    }
+  }
+  /* the reference's S buffer holds the last head's probabilities on return */
+  if (n_q > 0) memcpy(S, Sh + (size_t)(n_q - 1) * T * T, sizeof(float) * (size_t)T * T);
+  free(Sh);
+  mm_f32(Hcat, Wo, attn_out, T, D, Dq);
+  if (bo) for (int t = 0; t < T; ++t) for (int i = 0; i < D; ++i) attn_out[(size_t)t * D + i] += bo[i];
+  for (size_t i = 0; i < (size_t)T * D; ++i) x[i] = x[i] + attn_out[i];
+  rmsnorm_rows(x, rms2_w, T, D, rms2_eps, x_norm2);
+}
+
+void layer_forward_f32(float* x, int T, int D, const float* rms1_w, float rms1_eps, const float* Wq,
+                       const float* bq, const float* Wk, const float* bk, const float* Wv, const float* bv,
+                       const float* Wo, const float* bo, const float* qn, const float* kn, int n_q, int n_kv,
+                       int head_dim, int causal, float rope_theta, const float* rms2_w, float rms2_eps,
+                       const float* router_w, const float* router_b, const float** Wg, const float** bg,
+                       const float** Wu, const float** bu, const float** Wd, const float** bd, int n_experts,
+                       int topk, int d_ff, float* scratch_attn, float* scratch_moe, int* reuse_topk_idx,
+                       float* reuse_topk_p) {
+  (void)bg; (void)bu; (void)bd; (void)scratch_moe;   /* model.c reads neither */
+  if (T <= 0) return;
+  if (!x || D <= 0 || !Wq || !Wk || !Wv || !Wo || !router_w || n_q < 1 || n_kv < 1 || n_q % n_kv ||
+      head_dim < 2 || (head_dim & 1) || !scratch_attn)
+    model_die("layer_forward_f32", "bad argument");
+  if (!Wg || !Wu || !Wd || !Wg[0])
+    model_die("layer_forward_f32", "model.c's layer takes fp32 experts (Wg/Wu/Wd, model.c:172-187)");
+  const int id = f32_layer_id(router_w, router_b, Wg, Wu, Wd, n_experts, D, d_ff, topk);
+  float* x_norm2 = (float*)malloc(sizeof(float) * (size_t)T * D);
+  if (!x_norm2) model_die("layer_forward_f32", "out of host memory");
+  model_attention(x, T, D, rms1_w, rms1_eps, Wq, bq, Wk, bk, Wv, bv, Wo, bo, qn, kn, n_q, n_kv, head_dim, causal,
+                  rope_theta, rms2_w, rms2_eps, scratch_attn, x_norm2);
+  const int given = reuse_topk_idx && reuse_topk_p;
+  const int rc = moe_ffn(id, x_norm2, x, T, given ? reuse_topk_idx : NULL, given ? reuse_topk_p : NULL,
+                         MOE_FFN_HOST_PTRS | MOE_FFN_SEQ_RESIDUAL | (given ? MOE_FFN_GIVEN_TOPK : 0), NULL);
+  free(x_norm2);
+  if (rc) model_die("layer_forward_f32 (moe_ffn)", moe_cuda_last_error());
+}
+
+void model_forward_f32(const int* ids, int T, const QwenConfig* cfg, const QwenWeights* w, int apply_softmax,
+                       float* out_logits) {
+  if (T <= 0) return;
+  if (!ids || !cfg || !w || !out_logits || !w->tok_emb || !w->final_norm_w || !w->layers)
+    model_die("model_forward_f32", "bad argument");
+  const int D = cfg->d_model, V = cfg->vocab_size, L = cfg->n_layers, dh = cfg->head_dim;
+  const int Dq = cfg->n_q * dh, Dkv = cfg->n_kv * dh;
+  const size_t attn_f = (size_t)T * (Dq + 2 * Dkv) + (size_t)T * T + (size_t)T * Dq + 2ull * T * D;
+  float* scratch = (float*)malloc(sizeof(float) * attn_f);
+  float* x = (float*)malloc(sizeof(float) * (size_t)T * D);
+  float* x_final = (float*)malloc(sizeof(float) * (size_t)T * D);
+  if (!scratch || !x || !x_final) model_die("model_forward_f32", "out of host memory");
+  for (int t = 0; t < T; ++t) {
+    if (ids[t] < 0 || ids[t] >= V) model_die("model_forward_f32", "token id out of range");
+    memcpy(x + (size_t)t * D, w->tok_emb + (size_t)ids[t] * D, sizeof(float) * (size_t)D);
+  }
+  for (int l = 0; l < L; ++l) {
+    const QwenLayerWeights* lw = &w->layers[l];
+    layer_forward_f32(x, T, D, lw->rms1_w, 1e-6f, lw->Wq, lw->bq, lw->Wk, lw->bk, lw->Wv, lw->bv, lw->Wo,
+                      lw->bo, lw->q_norm, lw->k_norm, cfg->n_q, cfg->n_kv, dh, cfg->causal, cfg->rope_theta,
+                      lw->rms2_w, 1e-6f, lw->router_w, lw->router_b, lw->Wg, lw->bg, lw->Wu, lw->bu, lw->Wd,
+                      lw->bd, cfg->n_experts, cfg->top_k, cfg->d_ff, scratch, NULL, NULL, NULL);
+  }
+  rmsnorm_rows(x, w->final_norm_w, T, D, 1e-6f, x_final);
+  mm_f32(x_final, w->lm_head ? w->lm_head : w->tok_emb, out_logits, T, V, D);
+  if (apply_softmax) {                              /* softmax_rows, model.c:10-28 */
+    for (int r = 0; r < T; ++r) {
+      float* row = out_logits + (size_t)r * V;
+      float maxv = row[0];
+      for (int c = 1; c < V; ++c) if (row[c] > maxv) maxv = row[c];
+      float sum = 0.0f;
+      for (int c = 0; c < V; ++c) { row[c] = expf(row[c] - maxv); sum += row[c]; }
+      const float inv = 1.0f / (sum + 1e-9f);
+      for (int c = 0; c < V; ++c) row[c] *= inv;
+    }
+  }
+  free(x_final);
+  free(x);
+  free(scratch);
+}

@@ -22,6 +22,8 @@ MOE_OK, MOE_ERR_INVALID, MOE_ERR_CUDA, MOE_ERR_NOT_INIT = 0, 1, 2, 3
 MOE_ERR_RANGE, MOE_ERR_UNSUPPORTED, MOE_ERR_NOMEM = 4, 5, 6
 Q8, Q4 = 2, 3
 HOST_PTRS, DEVICE_PTRS, FORCE_GEMV, FORCE_GEMM = 0x1, 0x0, 0x4, 0x8
+SEQ_RESIDUAL, GIVEN_TOPK = 0x10, 0x20
+F32 = 0
 
 # Every symbol include/moe_cuda.h declares (checked by the CPU test suite).
 EXPORTS = (
@@ -29,7 +31,7 @@ EXPORTS = (
     "matmul_f32_q8", "matmul_f32_q4", "matmul_adaptive",
     "moe_matmul_q8_dev", "moe_matmul_q4_dev", "moe_matmul_f32_dev", "moe_matmul_batched_dev",
     "moe_quantize_rowwise_q8_dev", "moe_quantize_rowwise_q4_dev",
-    "moe_cuda_upload_layer", "moe_cuda_upload_layer_dev", "moe_cuda_free_layer",
+    "moe_cuda_upload_layer", "moe_cuda_upload_layer_dev", "moe_cuda_upload_layer_f32", "moe_cuda_free_layer",
     "moe_cuda_layer_bytes", "moe_ffn", "moe_ffn_partial", "moe_ffn_combine",
     "moe_synth_normal_host", "moe_synth_normal_dev",
     "moe_cuda_profile", "moe_cuda_profile_read", "moe_matmul_q_dev_noalloc",
@@ -79,6 +81,7 @@ def lib():
             "moe_quantize_rowwise_q4_dev": ([vp, i, i, vp, vp, vp], i),
             "moe_cuda_upload_layer": ([i, vp, vp, vp, vp, vp, i], i),
             "moe_cuda_upload_layer_dev": ([i, vp, vp, vp, vp, vp, i], i),
+            "moe_cuda_upload_layer_f32": ([i, vp, vp, vp, vp, vp, i, i, i, i], i),
             "moe_cuda_free_layer": ([i], i), "moe_cuda_layer_bytes": ([i], sz),
             "moe_ffn": ([i, vp, vp, i, vp, vp, i, vp], i),
             "moe_ffn_partial": ([i, vp, i, vp, vp, vp, vp], i),
@@ -319,15 +322,34 @@ def layer_bytes(layer):
     return lib().moe_cuda_layer_bytes(layer)
 
 
-def moe_ffn_host(layer, x_norm2, x_after, topk=8):
-    """Host-pointer moe_ffn: returns (x_out, topk_idx, topk_p)."""
+def moe_ffn_host(layer, x_norm2, x_after, topk=8, flags=0, given=None):
+    """Host-pointer moe_ffn: returns (x_out, topk_idx, topk_p). given: an
+    (idx, p) routing to use (MOE_FFN_GIVEN_TOPK)."""
     x_norm2 = np.ascontiguousarray(x_norm2, np.float32)
     x = np.array(x_after, np.float32, copy=True, order="C")
     T = x.shape[0]
-    idx = np.empty((T, topk), np.int32)
-    p = np.empty((T, topk), np.float32)
-    check(lib().moe_ffn(layer, _p(x_norm2), _p(x), T, _p(idx), _p(p), HOST_PTRS, None))
+    if given is not None:
+        idx = np.ascontiguousarray(given[0], np.int32)
+        p = np.ascontiguousarray(given[1], np.float32)
+        flags |= GIVEN_TOPK
+    else:
+        idx = np.empty((T, topk), np.int32)
+        p = np.empty((T, topk), np.float32)
+    check(lib().moe_ffn(layer, _p(x_norm2), _p(x), T, _p(idx), _p(p), HOST_PTRS | flags, None))
     return x, idx, p
+
+
+def upload_layer_f32(layer, router_w, router_b, gate, up, down, top_k=8):
+    """fp32 experts: gate/up [E][F][D], down [E][D][F] host arrays
+    (moe_cuda_upload_layer_f32)."""
+    gate, up, down = (np.ascontiguousarray(a, np.float32) for a in (gate, up, down))
+    E, F, D = gate.shape
+    arr = C.c_void_p * E
+    ptrs = [arr(*[a[e].ctypes.data for e in range(E)]) for a in (gate, up, down)]
+    router_w = np.ascontiguousarray(router_w, np.float32)
+    router_b = None if router_b is None else np.ascontiguousarray(router_b, np.float32)
+    check(lib().moe_cuda_upload_layer_f32(layer, ptrs[0], ptrs[1], ptrs[2], _p(router_w), _p(router_b),
+                                          E, D, F, top_k))
 
 
 def moe_ffn_dev(layer, x_norm2, x_inout, topk_idx=None, topk_p=None, flags=0, stream=None):

@@ -18,6 +18,8 @@ EXPORTS = (
     "mh_step", "mh_generate", "mh_pick_greedy", "mh_embed", "mh_attention", "mh_moe",
     "mh_head", "mh_advance", "mh_timing", "mh_timing_reset",
 )
+# include/moe_model.h (model.c's call surface, served by the same library)
+MODEL_EXPORTS = ("layer_forward_f32", "model_forward_f32", "moe_model_release")
 
 LAYER_FIELDS = ("Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo", "q_norm", "k_norm", "rms1_w", "rms2_w")
 
@@ -56,6 +58,10 @@ def lib():
             "mh_advance": ([vp, i], i), "mh_timing": ([vp, vp, vp, vp], i),
             "mh_timing_reset": ([vp], None),
         }
+        sig["layer_forward_f32"] = ([vp, i, i, vp, f] + [vp] * 10 + [i, i, i, i, f, vp, f, vp, vp] + [vp] * 6 +
+                                    [i, i, i, vp, vp, vp, vp], None)
+        sig["model_forward_f32"] = ([vp, i, vp, vp, i, vp], None)
+        sig["moe_model_release"] = ([], None)
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
             fn.argtypes, fn.restype = args, res
@@ -181,3 +187,107 @@ class HostModel:
         cpu = C.c_double(0)
         check(lib().mh_timing(self.h, ms.ctypes.data, calls.ctypes.data, C.byref(cpu)))
         return ms, calls, cpu.value
+
+
+# ---- model.c's call surface (include/moe_model.h) ---------------------------
+
+class QwenConfig(C.Structure):
+    """model.h:9-22."""
+    _fields_ = [(n, C.c_int) for n in ("d_model", "n_layers", "head_dim", "n_q", "n_kv", "d_ff", "n_experts",
+                                       "top_k", "vocab_size", "causal")] + \
+               [("rope_theta", C.c_float), ("rms_eps", C.c_float)]
+
+
+class QwenLayerWeights(C.Structure):
+    """model.h:34-59."""
+    _fields_ = [(n, C.c_void_p) for n in LAYER_FIELDS[:10]] + \
+               [(n, C.c_void_p) for n in ("rms1_w", "rms2_w", "router_w", "router_b",
+                                           "Wg", "bg", "Wu", "bu", "Wd", "bd", "Wg_q", "Wu_q", "Wd_q")] + \
+               [("experts_quantized", C.c_int)]
+
+
+class QwenWeights(C.Structure):
+    """model.h:61-70."""
+    _fields_ = [("tok_emb", C.c_void_p), ("final_norm_w", C.c_void_p), ("lm_head", C.c_void_p),
+                ("layers", C.c_void_p)]
+
+
+def _ptr_array(arrs):
+    return (C.c_void_p * len(arrs))(*[a.ctypes.data for a in arrs])
+
+
+def model_forward_f32(ids, cfg, g, attn, moe_f32, apply_softmax=False):
+    """model_forward_f32 (model.c:192-198) through libmoe_host.so: logits
+    [T][vocab]. cfg: dict of QwenConfig fields; g: tok_emb, final_norm_w,
+    lm_head (or None); attn: per layer LAYER_FIELDS dicts; moe_f32: per layer
+    dicts router_w, router_b (or None), gate [E][F][D], up, down [E][D][F]."""
+    keep = []
+
+    def ptr(a):
+        if a is None:
+            return None
+        a = np.ascontiguousarray(a, np.float32)
+        keep.append(a)
+        return a.ctypes.data
+    L = cfg["n_layers"]
+    layers = (QwenLayerWeights * L)()
+    for l in range(L):
+        lw = layers[l]
+        for n in LAYER_FIELDS:
+            setattr(lw, n, ptr(attn[l].get(n)))
+        lw.router_w = ptr(moe_f32[l]["router_w"])
+        lw.router_b = ptr(moe_f32[l].get("router_b"))
+        for n, key in (("Wg", "gate"), ("Wu", "up"), ("Wd", "down")):
+            a = np.ascontiguousarray(moe_f32[l][key], np.float32)
+            keep.append(a)
+            arr = _ptr_array([a[e] for e in range(a.shape[0])])
+            keep.append(arr)
+            setattr(lw, n, C.addressof(arr))
+    keep.append(layers)
+    w = QwenWeights(ptr(g["tok_emb"]), ptr(g["final_norm_w"]), ptr(g.get("lm_head")), C.addressof(layers))
+    c = QwenConfig(**{k: cfg[k] for k, _ in QwenConfig._fields_})
+    ids = np.ascontiguousarray(ids, np.int32)
+    out = np.empty((len(ids), cfg["vocab_size"]), np.float32)
+    lib().model_forward_f32(ids.ctypes.data, len(ids), C.byref(c), C.byref(w), int(apply_softmax), out.ctypes.data)
+    return out
+
+
+def layer_forward_f32(x, a, rms1_eps, rms2_eps, n_q, n_kv, head_dim, causal, rope_theta, router_w, router_b,
+                      gate, up, down, top_k, reuse=None):
+    """layer_forward_f32 (model.c:38-58) on one layer, x [T][D] updated and
+    returned. a: LAYER_FIELDS dict; gate/up [E][F][D], down [E][D][F] fp32;
+    reuse: optional (idx [T][top_k] int32, p [T][top_k]) routing."""
+    x = np.array(x, np.float32, copy=True, order="C")
+    T, D = x.shape
+    keep = []
+
+    def ptr(v):
+        if v is None:
+            return None
+        v = np.ascontiguousarray(v, np.float32)
+        keep.append(v)
+        return v.ctypes.data
+    E, F = gate.shape[0], gate.shape[1]
+    arrs = []
+    for m in (gate, up, down):
+        m = np.ascontiguousarray(m, np.float32)
+        keep.append(m)
+        arrs.append(_ptr_array([m[e] for e in range(E)]))
+    Dq, Dkv = n_q * head_dim, n_kv * head_dim
+    scratch = np.zeros(T * (Dq + 2 * Dkv) + T * T + T * Dq + 2 * T * D, np.float32)
+    ri = rp = None
+    if reuse is not None:
+        ri = np.ascontiguousarray(reuse[0], np.int32)
+        rp = np.ascontiguousarray(reuse[1], np.float32)
+    lib().layer_forward_f32(x.ctypes.data, T, D, ptr(a["rms1_w"]), rms1_eps, ptr(a["Wq"]), ptr(a.get("bq")),
+                            ptr(a["Wk"]), ptr(a.get("bk")), ptr(a["Wv"]), ptr(a.get("bv")), ptr(a["Wo"]),
+                            ptr(a.get("bo")), ptr(a.get("q_norm")), ptr(a.get("k_norm")), n_q, n_kv, head_dim,
+                            causal, rope_theta, ptr(a["rms2_w"]), rms2_eps, ptr(router_w), ptr(router_b),
+                            C.addressof(arrs[0]), None, C.addressof(arrs[1]), None, C.addressof(arrs[2]), None,
+                            E, top_k, F, scratch.ctypes.data, None,
+                            None if ri is None else ri.ctypes.data, None if rp is None else rp.ctypes.data)
+    return x
+
+
+def model_release():
+    lib().moe_model_release()

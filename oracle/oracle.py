@@ -151,6 +151,68 @@ class Ref:
         assert r == 0
         return out
 
+    def mc_model_forward(self, ids, cfg, g, attn, moe_f32, apply_softmax=False):
+        """model.c's model_forward_f32 (model.c:192-252, compiled from its
+        source by oracle/ref_shim.c): logits of every row [T][vocab].
+        moe_f32: per layer dicts router_w, router_b, gate, up, down (fp32)."""
+        names = ("Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo", "q_norm", "k_norm", "rms1_w", "rms2_w")
+        keep = []
+
+        def ptr(a):
+            if a is None:
+                return None
+            a = np.ascontiguousarray(a, np.float32)
+            keep.append(a)
+            return a.ctypes.data
+        L = cfg["n_layers"]
+        ap = (C.c_void_p * (12 * L))(*[ptr(attn[l].get(n)) for l in range(L) for n in names])
+        rp = (C.c_void_p * (2 * L))(*[ptr(moe_f32[l][k]) if moe_f32[l].get(k) is not None else None
+                                      for l in range(L) for k in ("router_w", "router_b")])
+        ep = (C.c_void_p * (3 * L))(*[ptr(moe_f32[l][k]) for l in range(L) for k in ("gate", "up", "down")])
+        ids = np.ascontiguousarray(ids, np.int32)
+        T = len(ids)
+        out = np.empty((T, cfg["vocab_size"]), np.float32)
+        f = self.lib.ref_mc_model_forward
+        f.argtypes = [C.c_void_p] + [C.c_int] * 10 + [C.c_float, C.c_int] + [C.c_void_p] * 6 + [C.c_int, C.c_void_p]
+        f.restype = C.c_int
+        F, E = moe_f32[0]["gate"].shape[1], moe_f32[0]["gate"].shape[0]
+        r = f(ids.ctypes.data, T, cfg["d_model"], L, cfg["head_dim"], cfg["n_q"], cfg["n_kv"], F, E,
+              cfg["top_k"], cfg["vocab_size"], cfg["rope_theta"], cfg["causal"],
+              ptr(g["tok_emb"]), ptr(g["final_norm_w"]), ptr(g.get("lm_head")), ap, rp, ep,
+              int(apply_softmax), out.ctypes.data)
+        assert r == 0
+        return out
+
+    def mc_layer_forward(self, x, a, rms1_eps, rms2_eps, n_q, n_kv, head_dim, causal, rope_theta,
+                         router_w, router_b, gate, up, down, top_k, reuse=None):
+        """model.c's layer_forward_f32 (model.c:38-190) on one layer: x after it."""
+        names = ("Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo", "q_norm", "k_norm", "rms1_w", "rms2_w")
+        keep = []
+
+        def ptr(v):
+            if v is None:
+                return None
+            v = np.ascontiguousarray(v, np.float32)
+            keep.append(v)
+            return v.ctypes.data
+        x = np.array(x, np.float32, copy=True, order="C")
+        T, D = x.shape
+        E, F = gate.shape[0], gate.shape[1]
+        ap = (C.c_void_p * 12)(*[ptr(a.get(n)) for n in names])
+        ri = rp = None
+        if reuse is not None:
+            ri = np.ascontiguousarray(reuse[0], np.int32)
+            rp = np.ascontiguousarray(reuse[1], np.float32)
+        f = self.lib.ref_mc_layer_forward
+        f.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_float, C.c_float, C.c_int, C.c_int, C.c_int,
+                      C.c_int, C.c_float] + [C.c_void_p] * 5 + [C.c_int] * 3 + [C.c_void_p] * 2
+        f.restype = C.c_int
+        r = f(x.ctypes.data, T, D, ap, rms1_eps, rms2_eps, n_q, n_kv, head_dim, causal, rope_theta,
+              ptr(router_w), ptr(router_b), ptr(gate), ptr(up), ptr(down), E, top_k, F,
+              None if ri is None else ri.ctypes.data, None if rp is None else rp.ctypes.data)
+        assert r == 0
+        return x
+
     def matmul(self, A, q, s, N, K, dtype):
         A = np.ascontiguousarray(A, np.float32)
         M = A.shape[0]

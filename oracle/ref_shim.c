@@ -173,3 +173,101 @@ int ref_model_forward(const int* ids, int T, int D, int n_layers, int head_dim, 
   ref_prof_clear();
   return 0;
 }
+
+/*
+ * The reference's model.c, compiled from its source in this translation
+ * unit. model.c does not build on its own as shipped: model.h uses fprintf
+ * without <stdio.h>, and the helpers it calls (matmul_f32, silu_f32,
+ * rmsnorm_forward_f32, rope_apply_inplace_f32_gqa) are the static ones of
+ * test_model_trace.c included above. Its two exported names collide with
+ * test_model_trace.c's statics, so they are renamed on the way in, as is its
+ * own static softmax_rows. Its text is otherwise compiled unchanged.
+ *
+ * model_forward_f32 (model.c:212-214) sizes scratch_attn for the attention
+ * buffers only, and layer_forward_f32 then writes x_norm2 (T*D floats) and
+ * the router logits (T*E floats) past its end (model.c:130, :134). To run it
+ * without corrupting the heap, model.c's malloc calls get 16 MiB of slack.
+ */
+#include <alloca.h>   /* model.c calls alloca without declaring it */
+static void* refmc_malloc(size_t n) { return malloc(n + ((size_t)16 << 20)); }
+#define layer_forward_f32 refmc_layer_forward_f32
+#define model_forward_f32 refmc_model_forward_f32
+#define softmax_rows refmc_softmax_rows
+#define malloc(n) refmc_malloc(n)
+#include "model.c"
+#undef malloc
+#undef softmax_rows
+#undef model_forward_f32
+#undef layer_forward_f32
+
+/*
+ * model.c's model_forward_f32 on caller-provided fp32 weights: logits of all
+ * T rows [T][V] (softmaxed if apply_softmax).
+ *   attn: n_layers x 12 pointers as ref_model_forward
+ *   router: n_layers x 2 (router_w, router_b or NULL)
+ *   experts: n_layers x 3 pointers (gate [E][F][D], up [E][F][D], down
+ *            [E][D][F], fp32, contiguous per projection)
+ */
+int ref_mc_model_forward(const int* ids, int T, int D, int n_layers, int head_dim, int n_q, int n_kv,
+                         int F, int E, int top_k, int V, float rope_theta, int causal,
+                         const float* tok_emb, const float* final_norm_w, const float* lm_head,
+                         const float* const* attn, const float* const* router, const float* const* experts,
+                         int apply_softmax, float* out_logits) {
+  QwenConfig cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.d_model = D; cfg.n_layers = n_layers; cfg.head_dim = head_dim; cfg.n_q = n_q; cfg.n_kv = n_kv;
+  cfg.d_ff = F; cfg.n_experts = E; cfg.top_k = top_k; cfg.vocab_size = V; cfg.causal = causal;
+  cfg.rope_theta = rope_theta; cfg.rms_eps = 1e-6f;
+  QwenWeights w;
+  memset(&w, 0, sizeof(w));
+  w.tok_emb = tok_emb; w.final_norm_w = final_norm_w; w.lm_head = lm_head;
+  w.layers = (QwenLayerWeights*)calloc((size_t)n_layers, sizeof(QwenLayerWeights));
+  const float** ptrs = (const float**)calloc((size_t)n_layers * 3 * E, sizeof(float*));
+  for (int l = 0; l < n_layers; ++l) {
+    QwenLayerWeights* lw = &w.layers[l];
+    const float* const* a = attn + 12 * l;
+    lw->Wq = a[0]; lw->bq = a[1]; lw->Wk = a[2]; lw->bk = a[3]; lw->Wv = a[4]; lw->bv = a[5];
+    lw->Wo = a[6]; lw->bo = a[7]; lw->q_norm = a[8]; lw->k_norm = a[9]; lw->rms1_w = a[10]; lw->rms2_w = a[11];
+    lw->router_w = router[2 * l]; lw->router_b = router[2 * l + 1];
+    const float** g = ptrs + (size_t)l * 3 * E;
+    const float** u = g + E;
+    const float** d = u + E;
+    for (int e = 0; e < E; ++e) {
+      g[e] = experts[3 * l] + (size_t)e * F * D;
+      u[e] = experts[3 * l + 1] + (size_t)e * F * D;
+      d[e] = experts[3 * l + 2] + (size_t)e * D * F;
+    }
+    lw->Wg = g; lw->Wu = u; lw->Wd = d;
+  }
+  refmc_model_forward_f32(ids, T, &cfg, &w, apply_softmax, out_logits);
+  free(ptrs);
+  free(w.layers);
+  ref_prof_clear();
+  return 0;
+}
+
+/* model.c's layer_forward_f32 on one layer (fp32 experts as above), x in
+ * place; reuse_idx/reuse_p as model.c's reuse_topk_idx/p (both NULL: the
+ * layer computes its own routing). */
+int ref_mc_layer_forward(float* x, int T, int D, const float* const* a, float rms1_eps, float rms2_eps,
+                         int n_q, int n_kv, int head_dim, int causal, float rope_theta,
+                         const float* router_w, const float* router_b, const float* gate, const float* up,
+                         const float* down, int E, int top_k, int F, int* reuse_idx, float* reuse_p) {
+  const int Dq = n_q * head_dim, Dkv = n_kv * head_dim;
+  float* scratch_attn = (float*)calloc((size_t)T * (Dq + 2 * Dkv) + (size_t)T * T + (size_t)T * Dq +
+                                       4ull * T * D + (size_t)T * E, sizeof(float));
+  float* scratch_moe = (float*)calloc(2ull * T * F, sizeof(float));
+  const float** ptrs = (const float**)calloc((size_t)3 * E, sizeof(float*));
+  for (int e = 0; e < E; ++e) {
+    ptrs[e] = gate + (size_t)e * F * D;
+    ptrs[E + e] = up + (size_t)e * F * D;
+    ptrs[2 * E + e] = down + (size_t)e * D * F;
+  }
+  refmc_layer_forward_f32(x, T, D, a[10], rms1_eps, a[0], a[1], a[2], a[3], a[4], a[5], a[6], a[7], a[8], a[9],
+                          n_q, n_kv, head_dim, causal, rope_theta, a[11], rms2_eps, router_w, router_b,
+                          ptrs, NULL, ptrs + E, NULL, ptrs + 2 * E, NULL, E, top_k, F, scratch_attn,
+                          scratch_moe, reuse_idx, reuse_p);
+  free(ptrs); free(scratch_attn); free(scratch_moe);
+  ref_prof_clear();
+  return 0;
+}

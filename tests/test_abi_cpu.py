@@ -36,6 +36,15 @@ def test_host_driver_exports_every_declared_symbol():
         assert hasattr(lib, name), name
 
 
+def test_model_surface_exports_every_declared_symbol():
+    import moe_host as mh
+    names = declared(os.path.join(os.path.dirname(HDR), "moe_model.h"))
+    assert set(names) == set(mh.MODEL_EXPORTS)
+    lib = mh.lib()
+    for name in names:
+        assert hasattr(lib, name), name
+
+
 def test_calls_before_init_fail_loudly():
     import numpy as np
     lib = mc.lib()
