@@ -13,17 +13,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 def assert_matches_port(out, ref, T, xn):
-    """Bit-exact for small batches of in-range tokens. With many tokens, or
-    large activations, a few SiLU / softmax exponentials round differently in
-    the last place (device: double exp rounded once; oracle: glibc expf), so
-    those are held to the layer tolerance 1e-4*max|y| with at least 99.5% of
-    outputs identical."""
-    if T <= 64 and float(np.abs(xn).max()) < 18.0:
-        assert np.array_equal(out, ref)
-        return
+    """The layer tolerance 1e-4*max|y| (north_star's bar), then bit-exact
+    equality (integer dots, the reference's float order, libc's expf)."""
     err = float(np.abs(out - ref).max())
     assert err <= 1e-4 * float(np.abs(ref).max()), f"max-abs {err}"
-    assert float(np.mean(out == ref)) >= 0.995
+    assert np.array_equal(out, ref), f"only {float(np.mean(out == ref)):.6f} bit-identical (T={T})"
 
 
 @pytest.mark.parametrize("dt,T,inputs", [(2, 16, "normal"), (2, 40, "normal"), (2, 256, "normal"),
