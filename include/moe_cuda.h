@@ -49,8 +49,9 @@ typedef struct {
 #define MOE_ERR_INVALID      1  /* bad argument / shape / dtype */
 #define MOE_ERR_CUDA         2  /* a CUDA runtime call failed */
 #define MOE_ERR_NOT_INIT     3  /* moe_cuda_init() not called / layer missing */
-#define MOE_ERR_RANGE        4  /* an activation left the integer range the
-                                   kernels accept (see moe_ffn) or was NaN */
+#define MOE_ERR_RANGE        4  /* reserved: no entry point returns it (an
+                                   activation outside the fast kernels' integer
+                                   range is recomputed exactly on the device) */
 #define MOE_ERR_UNSUPPORTED  5  /* valid for the reference, not built here */
 #define MOE_ERR_NOMEM        6  /* device allocation failed */
 
@@ -85,7 +86,8 @@ int moe_cuda_init(int device, int ep_world, int ep_rank, const void* nccl_uid);
 int moe_cuda_shutdown(void);
 const char* moe_cuda_last_error(void);
 /* Synchronise the device and report (then clear) any error a kernel flagged
- * asynchronously (MOE_ERR_RANGE from device-pointer moe_ffn calls). */
+ * asynchronously: MOE_ERR_CUDA when a bounded device-side wait ran out (a copy
+ * that never landed, or another rank's flag that was not raised in time). */
 int moe_cuda_check_status(void);
 
 /* ---- reference kernel surface (kernels.c / kernels.h) --------------------
@@ -130,12 +132,17 @@ int moe_matmul_batched_dev(const float* A, const void* const* W_q,
  * memory-pool or allocator callback, hosts whose device memory is entirely
  * reserved up front, latency-critical paths that cannot take cudaMalloc's
  * implicit synchronisation). No counterpart in the reference. Same results as
- * moe_matmul_q8_dev/_q4_dev, bit for bit, for any input magnitude. Scratch is
- * a fixed 1 MiB + 16.25 KiB device array inside the library (held by every GPU
- * that loads it until exit): M <= 4096 and M*K <= 524288, larger calls return
- * MOE_ERR_INVALID. Needs no moe_cuda_init. The first call on each device
- * resolves the array's address (make it before any stream capture). All
- * calls share the array: calls whose GPU work overlaps race on it. */
+ * moe_matmul_q8_dev/_q4_dev, bit for bit, for any input magnitude (K = 0
+ * gives zeros). Scratch is a fixed 1 MiB + 16.25 KiB device array inside the
+ * library (held by every GPU that loads it until exit): shapes on the fast
+ * path (packed rows a multiple of 16 bytes, B_q 16-byte aligned) need
+ * M <= 4096 and M*K <= 524288, and larger ones return MOE_ERR_INVALID; other
+ * shapes use no scratch. Needs no moe_cuda_init. The first call on each
+ * device is its set-up: it resolves the array's address and, with CUDA's lazy
+ * module loading, loads the library's kernels, which allocates device memory;
+ * make that first call before any stream capture and outside any region that
+ * must not allocate. Not valid across a cudaDeviceReset. All calls share the
+ * array: calls whose GPU work overlaps race on it. */
 int moe_matmul_q_dev_noalloc(const float* A, const void* B_q, const float* B_s,
                              float* C, int M, int N, int K, int dtype,
                              void* stream);
@@ -244,12 +251,17 @@ int moe_quantize_rowwise_q4_host(const float* W, int rows, int cols, uint8_t* q,
  *   x_inout[t] = x_inout[t] + Σ_{k=0..top_k-1} p[t,k] · down_e(silu(gate_e x)·up_e x)
  * x_norm2: [T][D] fp32 input to the experts; x_inout: [T][D] fp32, holds
  * x_after on entry and x on return (test_model_trace.c:517).
- * topk_idx_out/topk_p_out: optional [T][top_k] (NULL to skip).
- * Integer range: Q8 needs |x| < 258 (trunc(127x) fits 16 bits) and
- * |silu(g)u| < 258; Q4 needs trunc(7x) in [-128,127]. Outside that the call
- * returns MOE_ERR_RANGE (device-pointer calls: reported by
- * moe_cuda_check_status) instead of a wrong answer.
- * With ep_world > 1 use moe_ffn_partial instead. */
+ * topk_idx_out/topk_p_out: optional [T][top_k] (NULL to skip), or with
+ * MOE_FFN_GIVEN_TOPK the routing to use (inputs).
+ * Any activation magnitude: the fast kernels carry trunc(127x) in 16 bits
+ * (Q8, |x| < 258) and trunc(7x) in 8 bits (Q4); a token whose x, or the h of
+ * one of its slots, leaves that range (or is NaN/inf) is marked, and an exact
+ * int32 fix-up pass on the device recomputes its slots before the combine,
+ * so every call returns the reference's result (the reference truncates with
+ * no range limit, kernels.c:66, :113).
+ * A slot with no expert (fewer than top_k logits that are neither NaN nor
+ * -inf; the reference then reads an expert out of bounds) adds p * 0.
+ * With ep_world > 1 use moe_ffn_partial or moe_ffn_ep instead. */
 int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T,
             int* topk_idx_out, float* topk_p_out, int flags, void* stream);
 
@@ -278,11 +290,22 @@ int moe_ffn_combine(const float* y_slots, const float* topk_p, float* x_inout,
  *                   ranks' tokens;
  *   expert GEMMs    as in moe_ffn; the down projection's epilogue stores each
  *                   slot row into the exchange buffer of the rank owning the
- *                   slot's token, and its last CTA raises the combine flag;
+ *                   slot's token, and its last CTA raises the combine flag
+ *                   (when no token was marked out of range);
+ *   exact fix-up    when some rank marked a token (x or h outside the fast
+ *                   integer range), the experts' owners recompute its slots
+ *                   exactly from the home rank's published inputs, store the
+ *                   rows, then raise the combine flags;
  *   combine         waits (bounded) for all ranks' combine flags, then the
  *                   k-ordered combine + residual of this rank's tokens.
- * A wait that runs out reports a timeout through moe_cuda_check_status
- * instead of hanging. Needs one GPU per rank.
+ * Each wait on another rank gives up after MOE_EP_WAIT_MS milliseconds
+ * (environment, default 200; ranks must enter each call within that time of
+ * one another) and reports MOE_ERR_CUDA through moe_cuda_check_status
+ * instead of hanging; a fresh moe_cuda_ep_setup / moe_cuda_ep_connect on
+ * every rank then starts over. Needs one GPU per rank. An entry of
+ * ep_connect's table that holds this rank's own handle maps its own buffer
+ * (a loopback group in one process, whose waits on that entry can only run
+ * out; used to test the waits on one GPU).
  *   moe_cuda_ep_setup: allocate this rank's exchange buffers for up to
  *     max_tokens_local tokens per rank of width D with top_k slots each and
  *     write its 64-byte CUDA IPC handle to ipc_handle_out. Every rank calls

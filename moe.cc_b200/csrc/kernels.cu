@@ -719,36 +719,63 @@ bool launch_gemv(int dtype, const uint8_t* const* Wq, const float* const* Ws, in
 // generic exact kernel for any shape / any activation magnitude: one thread
 // per output, int32 activation, plain integer multiply-accumulate.
 template <int DT>
-__global__ void gemv_generic_kernel(const float* __restrict__ A, const uint8_t* __restrict__ Wq,
-                                    const float* __restrict__ Ws, float* __restrict__ C, int M,
-                                    int N, int K) {
-  const long c = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= (long)M * N) return;
-  const int m = (int)(c / N), n = (int)(c % N);
-  const float* a = A + (size_t)m * K;
+__device__ __forceinline__ float exact_row(const float* __restrict__ a, const uint8_t* __restrict__ Wq,
+                                           const float* __restrict__ Ws, int n, int K) {
   unsigned acc = 0;
   if (DT == 8) {
     const int8_t* w = reinterpret_cast<const int8_t*>(Wq) + (size_t)n * K;
     for (int k = 0; k < K; ++k) acc += (unsigned)(trunc_scale(__ldg(a + k), 127.0f) * (int)w[k]);
-    C[c] = fmul(div_qscale((int)acc, true), __ldg(Ws + n));
-  } else {
-    const uint8_t* w = Wq + (size_t)n * (K / 2);
-    for (int k = 0; k < K; k += 2) {
-      const uint8_t b = w[k >> 1];
-      acc += (unsigned)(trunc_scale(__ldg(a + k), 7.0f) * ((int)(b & 0xF) - 8));
-      acc += (unsigned)(trunc_scale(__ldg(a + k + 1), 7.0f) * ((int)(b >> 4) - 8));
-    }
-    C[c] = fmul(div_qscale((int)acc, false), __ldg(Ws + n));
+    return fmul(div_qscale((int)acc, true), __ldg(Ws + n));
   }
+  const uint8_t* w = Wq + (size_t)n * (K / 2);
+  for (int k = 0; k < K; k += 2) {
+    const uint8_t b = w[k >> 1];
+    acc += (unsigned)(trunc_scale(__ldg(a + k), 7.0f) * ((int)(b & 0xF) - 8));
+    acc += (unsigned)(trunc_scale(__ldg(a + k + 1), 7.0f) * ((int)(b >> 4) - 8));
+  }
+  return fmul(div_qscale((int)acc, false), __ldg(Ws + n));
+}
+
+// only_if: when set, the kernel runs only if *only_if != 0 (the fix-up pass
+// after the fast GEMV, which marks an out-of-range activation there)
+template <int DT>
+__global__ void gemv_generic_kernel(const int* only_if, const float* __restrict__ A,
+                                    const uint8_t* __restrict__ Wq, const float* __restrict__ Ws,
+                                    float* __restrict__ C, int M, int N, int K) {
+  if (only_if && *only_if == 0) return;
+  const long c = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= (long)M * N) return;
+  const int m = (int)(c / N), n = (int)(c % N);
+  C[c] = exact_row<DT>(A + (size_t)m * K, Wq, Ws, n, K);
+}
+
+// one activation row against n_mat matrices (device pointer arrays)
+template <int DT>
+__global__ void gemv_generic_batched_kernel(const int* only_if, const float* __restrict__ A,
+                                            const uint8_t* const* __restrict__ Wq,
+                                            const float* const* __restrict__ Ws, float* __restrict__ C,
+                                            int N, int K) {
+  if (only_if && *only_if == 0) return;
+  const int n = blockIdx.x * blockDim.x + threadIdx.x, mat = blockIdx.y;
+  if (n >= N) return;
+  C[(size_t)mat * N + n] = exact_row<DT>(A, Wq[mat], Ws[mat], n, K);
 }
 
 void launch_gemv_generic(int dtype, const float* A, const uint8_t* Wq, const float* Ws, float* C,
-                         int M, int N, int K, cudaStream_t st) {
+                         int M, int N, int K, cudaStream_t st, const int* only_if) {
   const long total = (long)M * N;
   if (total <= 0) return;
   const unsigned grid = (unsigned)((total + 127) / 128);
-  if (dtype == 2) gemv_generic_kernel<8><<<grid, 128, 0, st>>>(A, Wq, Ws, C, M, N, K);
-  else gemv_generic_kernel<4><<<grid, 128, 0, st>>>(A, Wq, Ws, C, M, N, K);
+  if (dtype == 2) gemv_generic_kernel<8><<<grid, 128, 0, st>>>(only_if, A, Wq, Ws, C, M, N, K);
+  else gemv_generic_kernel<4><<<grid, 128, 0, st>>>(only_if, A, Wq, Ws, C, M, N, K);
+}
+
+void launch_gemv_generic_batched(int dtype, const float* A, const uint8_t* const* Wq, const float* const* Ws,
+                                 float* C, int n_mat, int N, int K, cudaStream_t st, const int* only_if) {
+  if (n_mat <= 0 || N <= 0) return;
+  const dim3 grid((unsigned)((N + 127) / 128), (unsigned)n_mat);
+  if (dtype == 2) gemv_generic_batched_kernel<8><<<grid, 128, 0, st>>>(only_if, A, Wq, Ws, C, N, K);
+  else gemv_generic_batched_kernel<4><<<grid, 128, 0, st>>>(only_if, A, Wq, Ws, C, N, K);
 }
 
 // --------------------------------------------------------------------------

@@ -157,9 +157,17 @@ bool launch_gemv(int dtype, const uint8_t* const* Wq, const float* const* Ws,
                  int n_mat, bool ptr_arrays_on_device, int N, int K,
                  const uint8_t* act, int act_stride, const int* asum, int M,
                  float* C, cudaStream_t st);
+// Exact kernel for any shape and activation magnitude (one thread per output,
+// int32 truncation, wrapping dot). only_if: run only if *only_if != 0 (the
+// fix-up pass after the fast GEMV).
 void launch_gemv_generic(int dtype, const float* A, const uint8_t* Wq,
                          const float* Ws, float* C, int M, int N, int K,
-                         cudaStream_t st);
+                         cudaStream_t st, const int* only_if = nullptr);
+// the same for one activation row against n_mat matrices (device arrays of
+// device pointers), C [n_mat][N]
+void launch_gemv_generic_batched(int dtype, const float* A, const uint8_t* const* Wq,
+                                 const float* const* Ws, float* C, int n_mat, int N, int K,
+                                 cudaStream_t st, const int* only_if = nullptr);
 bool fast_geometry_ok(int dtype, int K);
 void launch_gateup(const LayerDev& L, const Workspace& ws, int T, int* err,
                    cudaStream_t st);

@@ -214,7 +214,7 @@ using namespace moe;
 namespace moe {
 static void ep_shutdown_hook();   // releases the expert-parallel buffers (defined below)
 struct Buf { void* p = nullptr; size_t cap = 0; };
-static Buf s_A, s_C, s_W, s_S, s_act, s_asum, s_hf;
+static Buf s_A, s_C, s_W, s_S, s_act, s_asum, s_hf, s_flag;
 
 static int grow(Buf& b, size_t bytes) {
   if (bytes <= b.cap) return MOE_OK;
@@ -236,8 +236,10 @@ static int check_mnk(int M, int N, int K) {
   return MOE_OK;
 }
 
-// Q8/Q4 matmul on device pointers. If `exact_fallback` is set the caller
-// checks the range flag and reruns on the generic kernel.
+// Q8/Q4 matmul on device pointers: activation truncation + the fast warp GEMV,
+// then the exact fix-up pass (the generic kernel, which runs only when the
+// truncation marked an activation outside the 16-bit / 8-bit range), so the
+// result is the reference's for any activation magnitude.
 static int matmul_q_dev(int dtype, const float* A, const void* Bq, const float* Bs, float* C,
                         int M, int N, int K, cudaStream_t st) {
   int rc = check_mnk(M, N, K);
@@ -252,10 +254,14 @@ static int matmul_q_dev(int dtype, const float* A, const void* Bq, const float* 
   if (aligned && fast_geometry_ok(dtype, K)) {
     if ((rc = grow(s_act, (size_t)2 * K * M))) return rc;
     if ((rc = grow(s_asum, sizeof(int) * (size_t)M))) return rc;
-    launch_quantize_act(A, M, K, dtype, (uint8_t*)s_act.p, 2 * K, (int*)s_asum.p, g.d_err, st);
+    if ((rc = grow(s_flag, sizeof(int)))) return rc;
+    int* flag = (int*)s_flag.p;
+    CU(cudaMemsetAsync(flag, 0, sizeof(int), st));
+    launch_quantize_act(A, M, K, dtype, (uint8_t*)s_act.p, 2 * K, (int*)s_asum.p, flag, st);
     const uint8_t* wq = (const uint8_t*)Bq;
     launch_gemv(dtype, &wq, &Bs, 1, false, N, K, (const uint8_t*)s_act.p, 2 * K,
                   (const int*)s_asum.p, M, C, st);
+    launch_gemv_generic(dtype, A, wq, Bs, C, M, N, K, st, flag);
   } else {
     launch_gemv_generic(dtype, A, (const uint8_t*)Bq, Bs, C, M, N, K, st);
   }
@@ -284,14 +290,7 @@ static int matmul_q_host(int dtype, const float* A, const void* Bq, const float*
     return rc;
   CU(cudaMemcpy(s_A.p, A, sizeof(float) * (size_t)M * K, cudaMemcpyHostToDevice));
   if ((rc = matmul_q_dev(dtype, (const float*)s_A.p, dq, ds, (float*)s_C.p, M, N, K, 0))) return rc;
-  rc = consume_stream_error(0);
-  if (rc == MOE_ERR_RANGE) {
-    // Large activations: rerun on the exact int32 kernel (any magnitude).
-    launch_gemv_generic(dtype, (const float*)s_A.p, (const uint8_t*)dq, ds, (float*)s_C.p, M, N, K, 0);
-    CU(cudaGetLastError());
-    rc = MOE_OK;
-  }
-  if (rc) return rc;
+  if ((rc = consume_stream_error(0))) return rc;
   CU(cudaMemcpy(C, s_C.p, sizeof(float) * (size_t)M * N, cudaMemcpyDeviceToHost));
   return MOE_OK;
 }
@@ -345,7 +344,7 @@ int moe_cuda_shutdown(void) {
                   w.fused_ctr, w.xbad};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
-  Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum, &s_hf};
+  Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum, &s_hf, &s_flag};
   for (Buf* b : bufs) { if (b->p) cudaFree(b->p); *b = Buf{}; }
   cudaFree(g.d_err); g.d_err = nullptr;
   if (g.h_err) cudaFreeHost(g.h_err);
@@ -443,10 +442,15 @@ int moe_matmul_batched_dev(const float* A, const void* const* W_q, const float* 
   if (!fast_geometry_ok(dtype, K))
     return set_err(MOE_ERR_UNSUPPORTED, "batched matmul needs K with 16-byte rows (K=%d)", K);
   cudaStream_t st = (cudaStream_t)stream;
-  if ((rc = grow(s_act, (size_t)2 * K)) || (rc = grow(s_asum, sizeof(int)))) return rc;
-  launch_quantize_act(A, 1, K, dtype, (uint8_t*)s_act.p, 2 * K, (int*)s_asum.p, g.d_err, st);
+  if ((rc = grow(s_act, (size_t)2 * K)) || (rc = grow(s_asum, sizeof(int))) || (rc = grow(s_flag, sizeof(int))))
+    return rc;
+  int* flag = (int*)s_flag.p;
+  CU(cudaMemsetAsync(flag, 0, sizeof(int), st));
+  launch_quantize_act(A, 1, K, dtype, (uint8_t*)s_act.p, 2 * K, (int*)s_asum.p, flag, st);
   launch_gemv(dtype, (const uint8_t* const*)W_q, W_s, n_mat, true, N, K, (const uint8_t*)s_act.p,
                 2 * K, (const int*)s_asum.p, 1, C, st);
+  // exact fix-up pass, only when an activation was out of the fast range
+  launch_gemv_generic_batched(dtype, A, (const uint8_t* const*)W_q, W_s, C, n_mat, N, K, st, flag);
   CU(cudaGetLastError());
   return MOE_OK;
 }

@@ -94,14 +94,36 @@ def test_matmul_fast_path_vs_port(gpu, port, dt, MNK):
     assert np.array_equal(Cd.cpu().numpy(), y)
 
 
-def test_matmul_large_activations_stay_exact(gpu, port):
-    """|x| beyond the fast path's 16-bit limb range: the host entry reruns on
-    the exact int32 kernel, as the reference would compute it."""
+@pytest.mark.parametrize("dt", [2, 3])
+def test_matmul_large_activations_stay_exact(gpu, port, dt):
+    """|x| beyond the fast path's limb range (Q8 16 bits, Q4 8 bits): the exact
+    fix-up pass recomputes on the device, for the host entry and for the
+    device entry, as the reference computes it."""
     K, N = 512, 64
     W = synth(60, N * K, 0.02).reshape(N, K)
-    A = synth(61, 2 * K, 1.0).reshape(2, K) * 400.0
-    s, q = quant(2)(W)
-    assert np.array_equal(gpu.matmul_f32_q8(A, q, s, N, K), port.matmul(A, q, s, N, K, 2))
+    A = synth(61, 2 * K, 1.0).reshape(2, K) * (400.0 if dt == 2 else 30.0)
+    s, q = quant(dt)(W)
+    want = port.matmul(A, q, s, N, K, dt)
+    fn = gpu.matmul_f32_q8 if dt == 2 else gpu.matmul_f32_q4
+    assert np.array_equal(fn(A, q, s, N, K), want)
+    C = torch.empty(2, N, device="cuda")
+    gpu.matmul_q_dev(torch.from_numpy(A).cuda(), torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda(), C, dt)
+    torch.cuda.synchronize()
+    gpu.check_status()
+    assert np.array_equal(C.cpu().numpy(), want)
+    # the batched form, one row against two matrices
+    qs = [torch.from_numpy(q).cuda(), torch.from_numpy(q[::-1].copy()).cuda()]
+    ss = [torch.from_numpy(s).cuda(), torch.from_numpy(s[::-1].copy()).cuda()]
+    qp = torch.tensor([t.data_ptr() for t in qs], dtype=torch.int64, device="cuda")
+    sp = torch.tensor([t.data_ptr() for t in ss], dtype=torch.int64, device="cuda")
+    Cb = torch.empty(2, N, device="cuda")
+    xd = torch.from_numpy(A[:1].copy()).cuda()
+    gpu.check(gpu.lib().moe_matmul_batched_dev(xd.data_ptr(), qp.data_ptr(), sp.data_ptr(), Cb.data_ptr(),
+                                               2, N, K, dt, None))
+    torch.cuda.synchronize()
+    gpu.check_status()
+    assert np.array_equal(Cb[0].cpu().numpy(), want[0])
+    assert np.array_equal(Cb[1].cpu().numpy(), port.matmul(A[:1], q[::-1].copy(), s[::-1].copy(), N, K, dt)[0])
 
 
 def test_matmul_adaptive_unknown_dtype_zero_fills(gpu):
@@ -167,7 +189,8 @@ def qwen_layer(gpu, dt, bias):
 
 
 @pytest.mark.parametrize("dt,T,bias", [(2, 1, False), (2, 4, False), (2, 16, False), (2, 32, True),
-                                       (3, 1, False), (3, 16, False), (3, 512, True), (2, 100, True)])
+                                       (3, 1, False), (3, 16, False), (3, 512, True), (2, 100, True),
+                                       (3, 2048, True), (2, 2048, True)])
 def test_moe_ffn_qwen_shape_vs_port(gpu, port, dt, T, bias):
     lid, L = qwen_layer(gpu, dt, bias)
     xn = synth(900 + T, T * 2048, 1.0).reshape(T, 2048)

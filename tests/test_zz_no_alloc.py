@@ -52,7 +52,49 @@ def test_noalloc_matches_existing_entry_on_two_calls(gpu, dt):
     assert np.array_equal(got2.cpu().numpy(), fn(A2, q, s, N, K))
 
 
+@pytest.mark.parametrize("dt", [2, 3])
+def test_noalloc_warmed_call_allocates_nothing(gpu, dt):
+    """After the first call on the device (the set-up, which may load the
+    library's kernels), a call leaves the device's free memory unchanged."""
+    N, K = 512, 1024
+    s, q = quant(dt)(synth(330 + dt, N * K, 0.02).reshape(N, K))
+    qd, sd = torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()
+    A = torch.from_numpy(synth(331 + dt, 4 * K, 1.0).reshape(4, K)).cuda()
+    A[2, ::5] *= 800.0                    # the exact fix-up pass runs too
+    C = torch.empty(4, N, device="cuda")
+    noalloc(gpu, A, qd, sd, C, dt)        # set-up call
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        noalloc(gpu, A, qd, sd, C, dt)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    ref = torch.empty(4, N, device="cuda")
+    gpu.matmul_q_dev(A, qd, sd, ref, dt)
+    torch.cuda.synchronize()
+    assert np.array_equal(C.cpu().numpy(), ref.cpu().numpy())
+
+
+def test_noalloc_k0_gives_zeros_like_the_regular_entry(gpu):
+    """K = 0: no products, C = 0 whatever the scales hold (the regular entry
+    point zero-fills without reading B_s)."""
+    q = torch.zeros(4, 16, dtype=torch.int8, device="cuda")
+    sc = torch.full((4,), float("nan"), device="cuda")
+    A = torch.zeros(3, 16, device="cuda")
+    got = torch.full((3, 4), 7.0, device="cuda")
+    ref = torch.full((3, 4), 7.0, device="cuda")
+    gpu.check(gpu.lib().moe_matmul_q_dev_noalloc(A.data_ptr(), q.data_ptr(), sc.data_ptr(), got.data_ptr(),
+                                                 3, 4, 0, 2, None))
+    gpu.check(gpu.lib().moe_matmul_q8_dev(A.data_ptr(), q.data_ptr(), sc.data_ptr(), ref.data_ptr(), 3, 4, 0, None))
+    torch.cuda.synchronize()
+    assert np.array_equal(got.cpu().numpy(), ref.cpu().numpy())
+    assert not got.cpu().numpy().any()
+
+
 def test_noalloc_rejects_sizes_beyond_its_scratch(gpu):
+    """Fast-path shapes beyond the fixed array are refused before any work
+    (B_q = NULL is 16-byte aligned, so these shapes take the fast path)."""
     lib = gpu.lib()
     rc = lib.moe_matmul_q_dev_noalloc(None, None, None, None, 4097, 8, 64, 2, None)
     assert rc == gpu.MOE_ERR_INVALID and b"scratch" in lib.moe_cuda_last_error()
