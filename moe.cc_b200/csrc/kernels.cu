@@ -530,91 +530,87 @@ void launch_route_build(const int* idx, int T, int K, int e_begin, int e_end, in
 }
 
 // --------------------------------------------------------------------------
-// routing lists for many slots (prefill): histogram -> one-CTA scan (+ tile
-// table) -> scatter. Slots are placed by atomics, so their order within an
-// expert varies from call to call; each slot's result does not depend on it.
-// tmp = [count E | start E | fill E], kept zero between calls except start.
+// routing lists for many slots (prefill), in one CTA of 1024 threads:
+// per-expert counts by shared-memory atomics, one exclusive scan over the
+// experts (warp shuffles; active list, offsets, tensor-core tile table), then
+// each slot placed by a shared-memory atomic on its expert's fill counter.
+// Slots land in arbitrary order within an expert; no result depends on it.
 // --------------------------------------------------------------------------
-__global__ void route_hist_kernel(const int* __restrict__ idx, int TK, int e_begin, int E_local,
-                                  int* __restrict__ cnt) {
-  extern __shared__ int h[];
-  for (int i = threadIdx.x; i < E_local; i += blockDim.x) h[i] = 0;
+constexpr int kRbMaxE = kRouteBuildMaxE;
+
+__global__ void __launch_bounds__(1024) route_build_one_kernel(const int* __restrict__ idx, int TK, int e_begin,
+                                                               int E_local, int* __restrict__ route,
+                                                               int* __restrict__ hsum, int nt, int max_tiles,
+                                                               int* __restrict__ slot_pos) {
+  __shared__ int cnt[kRbMaxE], start[kRbMaxE], fill[kRbMaxE];
+  __shared__ int s_wsum[3][kRbMaxE / 32];
+  pdl_wait();
+  pdl_launch();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < E_local; i += blockDim.x) { cnt[i] = 0; fill[i] = 0; }
   __syncthreads();
-  for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < TK; s += gridDim.x * blockDim.x) {
-    const int el = idx[s] - e_begin;
-    if (el >= 0 && el < E_local) atomicAdd(&h[el], 1);
+  for (int s = tid; s < TK; s += blockDim.x) {
+    if (hsum) hsum[s] = 0;
+    const int el = __ldg(idx + s) - e_begin;
+    if (el >= 0 && el < E_local) atomicAdd(&cnt[el], 1);
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < E_local; i += blockDim.x)
-    if (h[i]) atomicAdd(&cnt[i], h[i]);
-}
-
-__global__ void route_scan_kernel(int* route, int E_local, int TK, int* tmp, int nt, int max_tiles) {
-  extern __shared__ int sm2[];
-  int* s_route = sm2;                       // n_active | active[E] | exp_off[E+1]
-  int* s_tab = sm2 + 2 + 2 * E_local;       // n_tiles | u[m] | j0[m] | cnt[m]
-  int* cnt = tmp;
-  int* start = tmp + E_local;
-  if (threadIdx.x == 0) {
-    int na = 0, off = 0, ntl = 0;
-    for (int el = 0; el < E_local; ++el) {
-      const int c = cnt[el];
-      start[el] = off;
-      if (c == 0) continue;
-      s_route[1 + na] = el;
-      s_route[1 + E_local + na] = off;
-      if (nt > 0)
-        for (int j0 = off; j0 < off + c && ntl < max_tiles; j0 += nt, ++ntl) {
-          s_tab[1 + ntl] = na;
-          s_tab[1 + max_tiles + ntl] = j0;
-          s_tab[1 + 2 * max_tiles + ntl] = min(nt, off + c - j0);
-        }
-      off += c;
-      ++na;
+  int* tab = route + 2 + 2 * E_local + TK;            // n_tiles | u[m] | j0[m] | cnt[m]
+  const int mt = max_tiles;
+  int xl = 0, xa = 0, xt = 0, c = 0, act = 0, til = 0;
+  if (tid < kRbMaxE) {
+    c = tid < E_local ? cnt[tid] : 0;
+    act = c > 0;
+    til = nt > 0 ? (c + nt - 1) / nt : 0;
+    xl = c; xa = act; xt = til;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int yl = __shfl_up_sync(0xffffffffu, xl, o), ya = __shfl_up_sync(0xffffffffu, xa, o),
+                yt = __shfl_up_sync(0xffffffffu, xt, o);
+      if (lane >= o) { xl += yl; xa += ya; xt += yt; }
     }
-    s_route[1 + E_local + na] = off;
-    s_route[0] = na;
-    s_tab[0] = ntl;
+    if (lane == 31) { s_wsum[0][warp] = xl; s_wsum[1][warp] = xa; s_wsum[2][warp] = xt; }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < 2 + 2 * E_local; i += blockDim.x) route[i] = s_route[i];
-  if (nt > 0) {
-    int* tab = route + 2 + 2 * E_local + TK;
-    for (int i = threadIdx.x; i < 1 + 3 * max_tiles; i += blockDim.x) tab[i] = s_tab[i];
+  if (tid < kRbMaxE) {
+    for (int w = 0; w < warp; ++w) { xl += s_wsum[0][w]; xa += s_wsum[1][w]; xt += s_wsum[2][w]; }
+    const int el = tid, off = xl - c, na = xa - act, ntl = xt - til;
+    if (el < E_local) {
+      start[el] = off;
+      if (c > 0) {
+        route[1 + na] = el;
+        route[1 + E_local + na] = off;
+        for (int j0 = off, k = ntl; nt > 0 && j0 < off + c && k < mt; j0 += nt, ++k) {
+          tab[1 + k] = na;
+          tab[1 + mt + k] = j0;
+          tab[1 + 2 * mt + k] = min(nt, off + c - j0);
+        }
+      }
+      if (el == E_local - 1) {
+        route[1 + E_local + xa] = xl;                    // exp_off[n_active] = routed slots
+        route[0] = xa;
+        if (nt > 0) tab[0] = xt < mt ? xt : mt;
+      }
+    }
+    if (E_local == 0 && tid == 0) { route[0] = 0; route[1] = 0; if (nt > 0) tab[0] = 0; }
   }
-  for (int i = threadIdx.x; i < E_local; i += blockDim.x) cnt[i] = 0;   // ready for the next call
-}
-
-__global__ void route_scatter_kernel(const int* __restrict__ idx, int TK, int e_begin, int E_local,
-                                     int* route, int* tmp, int* slot_pos, int* hsum) {
-  const int s = blockIdx.x * blockDim.x + threadIdx.x;
-  if (s >= TK) return;
-  if (hsum) hsum[s] = 0;
-  const int el = idx[s] - e_begin;
-  if (el < 0 || el >= E_local) return;
-  const int j = tmp[E_local + el] + atomicAdd(&tmp[2 * E_local + el], 1);
-  route[2 + 2 * E_local + j] = s;
-  if (slot_pos) slot_pos[s] = j;
-}
-
-__global__ void route_fill_reset_kernel(int* tmp, int E_local) {
-  for (int i = threadIdx.x; i < E_local; i += blockDim.x) tmp[2 * E_local + i] = 0;
+  __syncthreads();
+  int* slots = route + 2 + 2 * E_local;
+  for (int s = tid; s < TK; s += blockDim.x) {
+    const int el = __ldg(idx + s) - e_begin;
+    if (el < 0 || el >= E_local) continue;
+    const int j = start[el] + atomicAdd(&fill[el], 1);
+    slots[j] = s;
+    if (slot_pos) slot_pos[s] = j;
+  }
 }
 
 void launch_route_build_multi(const int* idx, int T, int K, int e_begin, int E_local, int* route, int* hsum,
-                              int nt, int* slot_pos, int* tmp, cudaStream_t st) {
+                              int nt, int* slot_pos, cudaStream_t st) {
   const int TK = T * K;
   const int mt = nt > 0 ? route_max_tiles(TK, E_local, nt) : 0;
-  route_hist_kernel<<<(TK + 1023) / 1024, 256, sizeof(int) * E_local, st>>>(idx, TK, e_begin, E_local, tmp);
-  const size_t smem = sizeof(int) * (2 + 2 * (size_t)E_local + 1 + 3 * (size_t)mt);
-  static size_t attr = 0;
-  if (smem > 48 * 1024 && smem > attr) {
-    cudaFuncSetAttribute(route_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = smem;
-  }
-  route_scan_kernel<<<1, 256, smem, st>>>(route, E_local, TK, tmp, nt, mt);
-  route_scatter_kernel<<<(TK + 255) / 256, 256, 0, st>>>(idx, TK, e_begin, E_local, route, tmp, slot_pos, hsum);
-  route_fill_reset_kernel<<<1, 256, 0, st>>>(tmp, E_local);
+  launch_pdl(route_build_one_kernel, dim3(1), dim3(1024), 0, st, idx, TK, e_begin, E_local, route, hsum, nt, mt,
+             slot_pos);
 }
 
 // --------------------------------------------------------------------------

@@ -41,11 +41,11 @@ struct Workspace {
   int* route = nullptr;       // n_active | active[E] | exp_off[E+1] | slot_list[T*K]
   uint8_t* xact = nullptr;    // token activations, 2*D bytes per token
   int* xsum = nullptr;        // [T]  Σ activation (Q4 zero-point correction)
+  int* xsum_s = nullptr;      // [T*K] Σ activation of each expert-sorted slot's token (gathered rows)
   uint8_t* hact = nullptr;    // slot activations, 2*F bytes per slot
   int* hsum = nullptr;        // [T*K]
   float* y = nullptr;         // [T*K][D]
   int* route_counter = nullptr;  // arrival counter of the fused routing kernel (kept zero)
-  int* route_tmp = nullptr;   // [3][E] counts / starts / fill counters of the parallel route build
   uint8_t* xs0 = nullptr;     // expert-sorted token activations, plane 0 [T*K][D]
   uint8_t* xs1 = nullptr;     //   plane 1 (Q8 high limb)
   uint8_t* hs0 = nullptr;     // expert-sorted down-projection inputs [T*K][F]
@@ -148,9 +148,10 @@ void launch_route_build(const int* idx, int T, int K, int e_begin, int e_end,
                         int* route, int E_local, int* hsum, int nt, int* slot_pos,
                         cudaStream_t st);
 int route_max_tiles(int TK, int E_local, int nt);
-// same lists for many slots, in parallel; tmp = 3 * E_local ints kept zero
+// the same lists built by 1024 threads (any slot count, E_local <= kRouteBuildMaxE)
+constexpr int kRouteBuildMaxE = 256;
 void launch_route_build_multi(const int* idx, int T, int K, int e_begin, int E_local, int* route,
-                              int* hsum, int nt, int* slot_pos, int* tmp, cudaStream_t st);
+                              int* hsum, int nt, int* slot_pos, cudaStream_t st);
 // Fast warp GEMV over n_mat matrices: C[mat][m][n]. Returns false if the
 // shape has no fast-path geometry (caller uses the generic kernel).
 bool launch_gemv(int dtype, const uint8_t* const* Wq, const float* const* Ws,

@@ -78,6 +78,7 @@ struct Args {
                                        // completion [kFusedMaxTiles] and the ready list [kFusedMaxTiles]
   int ep_on; EpView ep;
   const int* xsum; int* hsum;          // Q4 zero point: per-token Σa, per-slot Σh
+  const int* xsum_s;                   // Q4, gathered rows: the token Σa of sorted slot j
   int* err;
   int* flags;                          // per-token range flags (range_fail) or null
 };
@@ -431,7 +432,8 @@ __global__ void __launch_bounds__(threads(DT), 2)
           }
           int dg, du;
           if (Q4) {   // nibbles are stored +8: subtract 8 * Σ activation of the token (exact mod 2^32)
-            const unsigned as = 8u * (unsigned)__ldg(a.xsum + __ldg(slots + j) / a.topk);
+            const unsigned as = 8u * (unsigned)(a.tokb ? __ldg(a.xsum + __ldg(slots + j) / a.topk)
+                                                       : __ldg(a.xsum_s + j));
             dg = (int)(raw[0] - as);
             du = (int)(raw[1] - as);
           } else {
@@ -579,7 +581,7 @@ bool launch_mma_fused(const LayerDev& L, const Workspace& ws, int T, int nt, int
   a.w_once = tokb && evict_first_on() ? 1 : 0;   // gathered: an expert may have several tiles
   a.tokb = tokb ? 1 : 0;
   a.ctr = ws.fused_ctr; a.err = err; a.flags = ws.xbad;
-  a.xsum = ws.xsum; a.hsum = ws.hsum;
+  a.xsum = ws.xsum; a.hsum = ws.hsum; a.xsum_s = ws.xsum_s;
   a.ep_on = ep != nullptr;
   if (ep) a.ep = *ep;
   a.slot_bytes = fz::kA + 2 * nt * 128;

@@ -95,6 +95,7 @@ struct Args {
   float* ys;                               // DOWN output [J][D]
   int T, topk;
   const int* xsum; int* hsum;                // Q4 zero-point sums (token / slot)
+  const int* xsum_s;                         // Q4, gathered B rows: the token sum of sorted slot j
   int tokb;                                  // GATEUP: B = all T token rows (decode, T <= NT)
   int w_once;                                // T <= NT: one token tile per expert, weights read once
   int ep_on; EpView ep;                      // DOWN, expert parallel: slot rows go to their owners' y buffers
@@ -405,7 +406,8 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
         for (int m = 0; m < NM; ++m)
           dot[m] = NL == 2 ? (int)(raw[m * 2] + (raw[m * 2 + 1] << 8)) : (int)raw[m];
         if (DT == 4) {   // nibbles are stored +8: subtract 8 * Σ activation (exact mod 2^32)
-          const int as = MODE == GATEUP ? __ldg(a.xsum + __ldg(a.route + 2 + 2 * a.E_local + j) / a.topk)
+          const int as = MODE == GATEUP ? (a.tokb ? __ldg(a.xsum + __ldg(a.route + 2 + 2 * a.E_local + j) / a.topk)
+                                                  : __ldg(a.xsum_s + j))
                                         : __ldcg(a.hsum + j);
   #pragma unroll
           for (int m = 0; m < NM; ++m) dot[m] = (int)((unsigned)dot[m] - 8u * (unsigned)as);
@@ -521,24 +523,34 @@ namespace moe {
 namespace mm {
 
 // Gather the routed tokens' activation rows into expert-sorted order:
-// row j of the output planes = token slot_list[j] / topk (B operand rows).
-__global__ void gather_rows_kernel(const uint8_t* __restrict__ xact, int act_stride, int D, int nplanes,
-                                   const int* __restrict__ route, int E_local, int topk,
-                                   uint8_t* __restrict__ xs0, uint8_t* __restrict__ xs1) {
-  const int j = blockIdx.x;
+// row j of the output planes = token slot_list[j] / topk (B operand rows);
+// for Q4 also xsum_s[j] = that token's Σ activation (the zero-point term the
+// gate/up epilogue subtracts). One warp per row, 16-byte copies, rows
+// grid-strided over the CTAs.
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint8_t* __restrict__ xact, int act_stride, int D,
+                                                          int nplanes, const int* __restrict__ route, int E_local,
+                                                          int topk, uint8_t* __restrict__ xs0,
+                                                          uint8_t* __restrict__ xs1, const int* __restrict__ xsum,
+                                                          int* __restrict__ xsum_s) {
   MOE_TL_START(kTlGather);
   MOE_TL_END(kTlGather);
   pdl_wait();
   pdl_launch();
   const RouteView r = route_view(const_cast<int*>(route), E_local);
-  if (j >= r.exp_off[*r.n_active]) return;
-  const int t = r.slot_list[j] / topk;
-  const uint4* src = reinterpret_cast<const uint4*>(xact + (size_t)t * act_stride);
-  uint4* d0 = reinterpret_cast<uint4*>(xs0 + (size_t)j * D);
-  for (int i = threadIdx.x; i < D / 16; i += blockDim.x) d0[i] = src[i];
-  if (nplanes == 2) {
-    uint4* d1 = reinterpret_cast<uint4*>(xs1 + (size_t)j * D);
-    for (int i = threadIdx.x; i < D / 16; i += blockDim.x) d1[i] = src[D / 16 + i];
+  const int J = r.exp_off[*r.n_active];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int n16 = D / 16;
+  for (int j = blockIdx.x * 8 + w; j < J; j += gridDim.x * 8) {
+    const int t = r.slot_list[j] / topk;
+    const uint4* src = reinterpret_cast<const uint4*>(xact + (size_t)t * act_stride);
+    uint4* d0 = reinterpret_cast<uint4*>(xs0 + (size_t)j * D);
+    for (int i = lane; i < n16; i += 32) d0[i] = __ldg(src + i);
+    if (nplanes == 2) {
+      uint4* d1 = reinterpret_cast<uint4*>(xs1 + (size_t)j * D);
+      for (int i = lane; i < n16; i += 32) d1[i] = __ldg(src + n16 + i);
+    } else if (lane == 0) {
+      xsum_s[j] = __ldg(xsum + t);
+    }
   }
 }
 
@@ -587,8 +599,11 @@ bool mma_supported(const LayerDev& L) {
 void launch_mma_gather(const LayerDev& L, const Workspace& ws, int T, int nt, cudaStream_t st) {
   if (T <= nt) return;   // decode: the GEMM reads the token rows directly
   const int E_local = L.e_end - L.e_begin, TK = T * L.topk;
-  launch_pdl(mm::gather_rows_kernel, dim3(TK), dim3(128), 0, st, ws.xact, 2 * L.D, L.D, L.dtype == 2 ? 2 : 1, ws.route, E_local,
-                                             L.topk, ws.xs0, ws.xs1);
+  const int rows_per_cta = 8, cap = 8 * mm::sms();
+  int grid = (TK + rows_per_cta - 1) / rows_per_cta;
+  if (grid > cap) grid = cap;
+  launch_pdl(mm::gather_rows_kernel, dim3(grid), dim3(256), 0, st, ws.xact, 2 * L.D, L.D, L.dtype == 2 ? 2 : 1,
+             ws.route, E_local, L.topk, ws.xs0, ws.xs1, (const int*)ws.xsum, ws.xsum_s);
 }
 
 #define NT_SWITCH(nt, CALL) \
@@ -625,7 +640,8 @@ bool launch_mma_gateup(const LayerDev& L, const Workspace& ws, int T, int nt, in
   a.route = ws.route; a.E_local = E_local; a.TK = TK; a.max_tiles = route_max_tiles(TK, E_local, nt);
   a.slab = L.slab; a.stride = L.expert_stride; a.s0_off = L.gs_off; a.s1_off = L.us_off;
   a.F = L.F; a.hs0 = ws.hs0; a.hs1 = ws.hs1; a.err = err; a.flags = ws.xbad;
-  a.xsum = ws.xsum; a.hsum = ws.hsum; a.topk = L.topk; a.tokb = tokb; a.w_once = T <= nt && mm::evict_first_on();
+  a.xsum = ws.xsum; a.hsum = ws.hsum; a.xsum_s = ws.xsum_s;
+  a.topk = L.topk; a.tokb = tokb; a.w_once = T <= nt && mm::evict_first_on();
   const int units = a.max_tiles * a.n_mblk, gc = mm::grid_ctas(L.dtype == 2 ? 8 : 4, nt);
   const int grid = units < gc ? units : gc;
   bool ok = false;
@@ -659,6 +675,26 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
 }
 
 // combine from expert-sorted y rows (prefill / non-fused path)
+// Scalar form (any D, any alignment of xres/out): one thread per output.
+__global__ void combine_sorted_scalar_kernel(const float* __restrict__ ys, const int* __restrict__ slot_pos,
+                                             const float* __restrict__ p, const int* __restrict__ idx,
+                                             const float* xres, float* out, int T, int D, int K, int seq) {
+  pdl_wait();
+  pdl_launch();
+  const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= (long)T * D) return;
+  const int t = (int)(q / D), n = (int)(q % D);
+  float acc = seq ? xres[q] : 0.0f;
+  for (int k = 0; k < K; ++k) {
+    const int s = t * K + k;
+    acc = fadd(acc, fmul(p[s], idx[s] < 0 ? 0.0f : ys[(size_t)slot_pos[s] * D + n]));
+  }
+  out[q] = seq ? acc : fadd(xres[q], acc);
+}
+
+// One thread per 4 consecutive outputs of a token (D % 4 == 0, 16-byte
+// aligned rows): the token's routing words once, then 16-byte loads of its K
+// slot rows.
 __global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* __restrict__ slot_pos,
                                       const float* __restrict__ p, const int* __restrict__ idx,
                                       const float* xres, float* out, int T, int D, int K, int seq) {
@@ -666,20 +702,32 @@ __global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* _
   pdl_wait();
   pdl_launch();
   const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (q >= (long)T * D) return;
-  const int t = (int)(q / D), n = (int)(q % D);
+  const int D4 = D / 4;
+  if (q >= (long)T * D4) return;
+  const int t = (int)(q / D4), n = (int)(q % D4) * 4;
+  const size_t o = (size_t)t * D + n;
   // seq: accumulate into the residual in k order (model.c:188), else add the
   // k-ordered sum to it (test_model_trace.c:513,517)
-  float acc = seq ? xres[q] : 0.0f;
+  const float4 xr = *reinterpret_cast<const float4*>(xres + o);
+  float4 acc = seq ? xr : make_float4(0.f, 0.f, 0.f, 0.f);
+  auto add = [&](float pk, float4 y) {
+    acc.x = fadd(acc.x, fmul(pk, y.x));
+    acc.y = fadd(acc.y, fmul(pk, y.y));
+    acc.z = fadd(acc.z, fmul(pk, y.z));
+    acc.w = fadd(acc.w, fmul(pk, y.w));
+  };
   constexpr int KF = 8;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
   if (K <= KF) {
     // all slots' routing words first, then all their y values: two dependent
     // load rounds instead of 2K; the sum keeps the k order
     int js[KF];
-    float ps[KF], yv[KF];
+    float ps[KF];
+    float4 yv[KF];
 #pragma unroll
     for (int k = 0; k < KF; ++k) {
       js[k] = -1;
+      ps[k] = 0.f;
       if (k < K) {
         const int s = t * K + k;
         const int e = __ldg(idx + s), j = __ldg(slot_pos + s);
@@ -689,23 +737,37 @@ __global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* _
     }
     // a slot with no expert (idx < 0) adds p * 0, as combine_kernel
 #pragma unroll
-    for (int k = 0; k < KF; ++k) yv[k] = js[k] >= 0 ? __ldg(ys + (size_t)js[k] * D + n) : 0.0f;
+    for (int k = 0; k < KF; ++k)
+      yv[k] = js[k] >= 0 ? __ldg(reinterpret_cast<const float4*>(ys + (size_t)js[k] * D + n)) : zero;
 #pragma unroll
     for (int k = 0; k < KF; ++k)
-      if (k < K) acc = fadd(acc, fmul(ps[k], yv[k]));
+      if (k < K) add(ps[k], yv[k]);
   } else {
     for (int k = 0; k < K; ++k) {
       const int s = t * K + k;
-      acc = fadd(acc, fmul(p[s], idx[s] < 0 ? 0.0f : ys[(size_t)slot_pos[s] * D + n]));
+      add(p[s], idx[s] < 0 ? zero : *reinterpret_cast<const float4*>(ys + (size_t)slot_pos[s] * D + n));
     }
   }
-  out[q] = seq ? acc : fadd(xres[q], acc);
+  if (!seq) {
+    acc.x = fadd(xr.x, acc.x);
+    acc.y = fadd(xr.y, acc.y);
+    acc.z = fadd(xr.z, acc.z);
+    acc.w = fadd(xr.w, acc.w);
+  }
+  *reinterpret_cast<float4*>(out + o) = acc;
   MOE_TL_END(kTlCombine);
 }
 
 void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
                            const float* xres, float* out, int T, int D, int K, cudaStream_t st, bool seq_residual) {
-  const long total = (long)T * D;
+  if (D % 4 || ((uintptr_t)xres | (uintptr_t)out | (uintptr_t)ys) % 16) {
+    const long n1 = (long)T * D;
+    if (n1 > 0)
+      launch_pdl(combine_sorted_scalar_kernel, dim3((unsigned)((n1 + 255) / 256)), dim3(256), 0, st, ys, slot_pos, p,
+                 idx, xres, out, T, D, K, seq_residual ? 1 : 0);
+    return;
+  }
+  const long total = (long)T * (D / 4);
   if (total <= 0) return;
   launch_pdl(combine_sorted_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, ys, slot_pos, p, idx, xres,
              out, T, D, K, seq_residual ? 1 : 0);

@@ -123,8 +123,8 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   const int nF = F > w.cap_F ? F : w.cap_F, nK = K > w.cap_K ? K : w.cap_K;
   CU(cudaDeviceSynchronize());
   void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum, w.hact, w.hsum,
-                  w.y, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter, w.route_tmp,
-                  w.fused_ctr, w.xbad};
+                  w.y, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter,
+                  w.fused_ctr, w.xbad, w.xsum_s};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
   const size_t TK = (size_t)nT * nK;
@@ -143,6 +143,7 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   ALLOC(route, sizeof(int) * (2 + 2 * (size_t)nE + TK + 1 + 3 * max_tiles));
   ALLOC(xact, (size_t)2 * nD * nT);
   ALLOC(xsum, sizeof(int) * (size_t)nT);
+  ALLOC(xsum_s, sizeof(int) * TK);
   ALLOC(hact, (size_t)2 * nF * TK);
   ALLOC(hsum, sizeof(int) * TK);
   ALLOC(y, sizeof(float) * TK * nD);
@@ -152,7 +153,6 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   ALLOC(hs1, TK * nF);
   ALLOC(slot_pos, sizeof(int) * TK);
   ALLOC(route_counter, sizeof(int));
-  ALLOC(route_tmp, sizeof(int) * 3 * (size_t)nE);
   ALLOC(xn, sizeof(float) * (size_t)nT * nD);
   ALLOC(xo, sizeof(float) * (size_t)nT * nD);
   ALLOC(fused_ctr, sizeof(int) * (3 + 2 * kFusedMaxTiles));
@@ -161,7 +161,6 @@ static int ensure_workspace(int T, int E, int D, int F, int K) {
   CU(cudaMemset(w.xbad, 0, sizeof(int) * (2 + (size_t)nT)));
   CU(cudaMemset(w.fused_ctr, 0, sizeof(int) * (3 + 2 * kFusedMaxTiles)));
   CU(cudaMemset(w.route_counter, 0, sizeof(int)));
-  CU(cudaMemset(w.route_tmp, 0, sizeof(int) * 3 * (size_t)nE));
   w.cap_T = nT; w.cap_E = nE; w.cap_D = nD; w.cap_F = nF; w.cap_K = nK;
   return MOE_OK;
 }
@@ -340,8 +339,8 @@ int moe_cuda_shutdown(void) {
   g.alias.clear();
   Workspace& w = g.ws;
   void* ptrs[] = {w.logits, w.topk_idx, w.topk_p, w.route, w.xact, w.xsum, w.hact, w.hsum,
-                  w.y, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter, w.route_tmp,
-                  w.fused_ctr, w.xbad};
+                  w.y, w.xn, w.xo, w.xs0, w.xs1, w.hs0, w.hs1, w.slot_pos, w.route_counter,
+                  w.fused_ctr, w.xbad, w.xsum_s};
   for (void* p : ptrs) if (p) cudaFree(p);
   w = Workspace{};
   Buf* bufs[] = {&s_A, &s_C, &s_W, &s_S, &s_act, &s_asum, &s_hf, &s_flag};
@@ -655,13 +654,13 @@ static void route_tokens(const LayerDev& L, const float* xn, int T, int nt, cuda
     });
   }
   timed("route_build", st, [&] {
-    if (T * L.topk > 1024)
+    if (L.e_end - L.e_begin <= kRouteBuildMaxE)
       launch_route_build_multi(w.topk_idx, T, L.topk, L.e_begin, L.e_end - L.e_begin, w.route,
                                L.dtype == MOE_DTYPE_Q4 ? w.hsum : nullptr, nt,
-                               nt > 0 ? w.slot_pos : nullptr, w.route_tmp, st);
+                               nt > 0 ? w.slot_pos : nullptr, st);
     else
-    launch_route_build(w.topk_idx, T, L.topk, L.e_begin, L.e_end, w.route, L.e_end - L.e_begin,
-                       L.dtype == MOE_DTYPE_Q4 ? w.hsum : nullptr, nt, nt > 0 ? w.slot_pos : nullptr, st);
+      launch_route_build(w.topk_idx, T, L.topk, L.e_begin, L.e_end, w.route, L.e_end - L.e_begin,
+                         L.dtype == MOE_DTYPE_Q4 ? w.hsum : nullptr, nt, nt > 0 ? w.slot_pos : nullptr, st);
   });
 }
 

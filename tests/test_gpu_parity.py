@@ -325,3 +325,20 @@ def test_load_bin_layer_qwen_shape(gpu, dt, tmp_path):
             assert np.array_equal(u, v)
     gpu.free_layer(220 + dt)
     gpu.free_layer(320 + dt)
+
+
+@pytest.mark.parametrize("dt,T", [(2, 16), (3, 64)])
+def test_moe_ffn_unaligned_residual_stream(gpu, port, dt, T):
+    """x_inout 4 bytes off a 16-byte boundary (a view into a larger buffer):
+    the combine takes its scalar form, results unchanged."""
+    lid, L = qwen_layer(gpu, dt, False)
+    xn = synth(990 + T, T * 2048, 1.0).reshape(T, 2048)
+    xa = synth(991 + T, T * 2048, 1.0).reshape(T, 2048)
+    ref, ref_idx, _, _ = port.moe_block(xn, xa, L)
+    buf = torch.zeros(T * 2048 + 1, device="cuda")
+    out = buf[1:].view(T, 2048)
+    out.copy_(torch.from_numpy(xa))
+    gpu.moe_ffn_dev(lid, torch.from_numpy(xn).cuda(), out)
+    torch.cuda.synchronize()
+    gpu.check_status()
+    assert np.array_equal(out.cpu().numpy(), ref)
