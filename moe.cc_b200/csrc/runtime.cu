@@ -682,9 +682,15 @@ static void run_down(const LayerDev& L, const Workspace& w, int T, float* y, cud
 }
 
 // Tensor-core (tcgen05) expert GEMMs unless the caller forces the CUDA-core
-// GEMVs (MOE_FFN_FORCE_GEMV, or MOE_FFN_PATH=gemv in the environment).
-static bool use_tensor_cores(const LayerDev& L, int flags) {
+// GEMVs (MOE_FFN_FORCE_GEMV, or MOE_FFN_PATH=gemv in the environment), or a
+// call of at most kGemvMaxT tokens: one token's 8 experts make too few
+// 128-row GEMM units to spread over the SMs, and the warp GEMVs, which spread
+// every row over its own warp, measured faster there (T=1: 36.9 against
+// 43.3 us per step).
+constexpr int kGemvMaxT = 1;
+static bool use_tensor_cores(const LayerDev& L, int flags, int T) {
   if (flags & MOE_FFN_FORCE_GEMV) return false;
+  if (T <= kGemvMaxT && !(flags & MOE_FFN_FORCE_GEMM)) return false;
   static int env = -1;
   if (env < 0) {
     const char* e = getenv("MOE_FFN_PATH");
@@ -934,7 +940,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
       }
       timed("f32_experts", s, [&] { launch_f32_experts(L, xn, w.topk_idx, T, (float*)s_hf.p, w.y, s); });
       timed("combine", s, [&] { launch_combine(w.y, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s, seq); });
-    } else if (use_tensor_cores(L, flags)) {
+    } else if (use_tensor_cores(L, flags, T)) {
       const int fnt = fused_tile_n(L, T);                 // fused gate/up + down kernel, if used
       const int nt = fnt ? fnt : mma_tile_n(T, L.dtype);
       route_tokens(L, xn, T, nt, s, given);
@@ -1007,7 +1013,7 @@ int moe_ffn_partial(int layer, const float* x_norm2, int T, float* y_slots, int*
   cudaStream_t st = (cudaStream_t)stream;
   const Workspace& w = g.ws;
   const size_t TK = (size_t)T * L.topk;
-  if (use_tensor_cores(L, 0)) {
+  if (use_tensor_cores(L, 0, T)) {
     const int nt = mma_tile_n(T, L.dtype);
     route_tokens(L, x_norm2, T, nt, st);
     if (T > nt) timed("gather", st, [&] { launch_mma_gather(L, w, T, nt, st); });
@@ -1241,7 +1247,7 @@ int moe_ffn_ep(int layer, const float* x_norm2, int T_local, float* x_inout, voi
     return set_err(MOE_ERR_INVALID, "moe_ffn_ep: T_local=%d exceeds the buffers (%d) or the layer shape differs",
                    T_local, g_ep.cap_tokens);
   const int W = g_ep.world, T = T_local * W;
-  if (!use_tensor_cores(L, 0))
+  if (!use_tensor_cores(L, MOE_FFN_FORCE_GEMM, T))
     return set_err(MOE_ERR_UNSUPPORTED, "moe_ffn_ep needs the tensor-core path (Q8/Q4, D and F multiples of 128)");
   if (T_local == 0) return MOE_OK;
   if (!decode_route_supported(L, T, x_norm2))
