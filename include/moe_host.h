@@ -109,6 +109,19 @@ int mh_moe(MhModel* m, int layer, const float* x_norm2, float* x_after, int T);
 int mh_head(MhModel* m, const float* x, int T, float* logits);
 int mh_advance(MhModel* m, int T);
 
+/* Expert parallelism: this process is rank ep_rank of the ep_world group it
+ * passed to moe_cuda_init; the model's MoE layers hold only this rank's
+ * experts (every upload path shards them), and the model's `batch`
+ * sequences are this rank's own. mh_ep_setup allocates the exchange for up
+ * to max_rows_per_call rows per MoE call (batch x new tokens; larger steps
+ * run in chunks of that size) and writes this rank's 64-byte handle; the
+ * caller exchanges the handles (rank order) and passes all of them to
+ * mh_ep_connect. From then on every MoE block runs moe_ffn_ep: all ranks
+ * must step together, with the same batch and token counts (the reference
+ * runs on one CPU and has no counterpart). */
+int mh_ep_setup(MhModel* m, int max_rows_per_call, void* handle_out);
+int mh_ep_connect(MhModel* m, const void* handles);
+
 /* Accumulated wall time of the MoE calls per layer since the last reset
  * (ms[n_layers], calls[n_layers]; either may be NULL) and of the CPU part. */
 int mh_timing(const MhModel* m, double* moe_ms, long* moe_calls, double* cpu_ms);

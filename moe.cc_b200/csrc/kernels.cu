@@ -83,7 +83,7 @@ template <int DT>
 __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restrict__ x, int K,
                                                            uint8_t* __restrict__ act, int act_stride,
                                                            int* __restrict__ asum, int* err,
-                                                           int mma_layout, int* flags) {
+                                                           int mma_layout, int* flags, int mark) {
   const int m = blockIdx.x;
   const float* xr = x + (size_t)m * K;
   uint8_t* ar = act + (size_t)m * act_stride;
@@ -100,7 +100,10 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
       sum += a;
     }
   }
-  if (bad) range_fail(err, flags, m);
+  if (bad) {
+    if (mark) *err = mark;            // this call's mark (the GEMV compares it)
+    else range_fail(err, flags, m);
+  }
   if (DT == 4) {
     __shared__ int red[8];
     sum = warp_sum(sum);
@@ -115,12 +118,12 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
 }
 
 void launch_quantize_act(const float* x, int M, int K, int dtype, uint8_t* act, int act_stride,
-                         int* asum, int* err, cudaStream_t st, int mma_layout, int* flags) {
+                         int* asum, int* err, cudaStream_t st, int mma_layout, int* flags, int mark) {
   if (M <= 0) return;
   if (dtype == 2)
-    quantize_act_kernel<8><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err, mma_layout, flags);
+    quantize_act_kernel<8><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err, mma_layout, flags, mark);
   else
-    quantize_act_kernel<4><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err, mma_layout, flags);
+    quantize_act_kernel<4><<<M, 256, 0, st>>>(x, K, act, act_stride, asum, err, mma_layout, flags, mark);
 }
 
 // --------------------------------------------------------------------------
@@ -643,7 +646,24 @@ struct GemvArgs {
   const uint8_t* act;
   const int* asum;
   float* C;
+  const float* A;            // fp32 activations [M][K], for the exact path
+  const int* flag;           // == mark when the truncation kernel found an activation out of range
+  int mark;
 };
+
+template <int DT>
+__device__ __forceinline__ float exact_row(const float* __restrict__ a, const uint8_t* __restrict__ Wq,
+                                           const float* __restrict__ Ws, int n, int K);
+
+// the exact outputs of rows n0 .. n0+rows-1 of matrix `mat`, every m (kept
+// out of line so the fast path's registers are unaffected)
+template <int DT>
+__device__ __noinline__ void gemv_exact_outputs(const float* A, float* C, const uint8_t* W, const float* S, int M,
+                                                int N, int K, int n0, int rows) {
+  for (int m = 0; m < M; ++m)
+    for (int j = 0; j < rows; ++j)
+      if (n0 + j < N) C[(size_t)m * N + n0 + j] = exact_row<DT>(A + (size_t)m * K, W, S, n0 + j, K);
+}
 
 template <int DT, int LPR, int RPG>
 __global__ void __launch_bounds__(256) gemv_kernel(const GemvArgs a) {
@@ -659,6 +679,12 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvArgs a) {
   bool ok[RPG];
 #pragma unroll
   for (int j = 0; j < RPG; ++j) { n[j] = (item * GPW + grp) * RPG + j; ok[j] = n[j] < a.N; }
+  if (a.flag && *a.flag == a.mark) {
+    // an activation left the limb range: this warp's outputs are computed
+    // exactly instead (int32 truncation, wrapping dot), one thread per output
+    if (lig == 0) gemv_exact_outputs<DT>(a.A, a.C + (size_t)mat * a.M * a.N, W, S, a.M, a.N, a.K, n[0], RPG);
+    return;
+  }
   uint4 wr[RPG][4];
   auto load = [&](int p) {
 #pragma unroll
@@ -710,7 +736,8 @@ static void gemv_dispatch(const Geo& g, const GemvArgs& a, unsigned grid, cudaSt
 
 bool launch_gemv(int dtype, const uint8_t* const* Wq, const float* const* Ws, int n_mat,
                  bool ptr_arrays_on_device, int N, int K, const uint8_t* act, int act_stride,
-                 const int* asum, int M, float* C, cudaStream_t st) {
+                 const int* asum, int M, float* C, cudaStream_t st, const float* A, const int* flag,
+                 int mark) {
   Geo g;
   const int rb = dtype == 2 ? K : K / 2;
   if (dtype == 3 && (K & 1)) return false;
@@ -723,6 +750,7 @@ bool launch_gemv(int dtype, const uint8_t* const* Wq, const float* const* Ws, in
   const int rows_per_item = (32 / g.lpr) * RPG;
   a.items_per_mat = (N + rows_per_item - 1) / rows_per_item;
   a.M = M; a.act_stride = act_stride; a.act = act; a.asum = asum; a.C = C;
+  a.A = A; a.flag = flag; a.mark = mark;
   const long warps = (long)a.items_per_mat * n_mat;
   const unsigned grid = (unsigned)((warps + 7) / 8);
   if (dtype == 2) gemv_dispatch<8, RPG>(g, a, grid, st);
@@ -750,46 +778,22 @@ __device__ __forceinline__ float exact_row(const float* __restrict__ a, const ui
   return fmul(div_qscale((int)acc, false), __ldg(Ws + n));
 }
 
-// only_if: when set, the kernel runs only if *only_if != 0 (the fix-up pass
-// after the fast GEMV, which marks an out-of-range activation there)
 template <int DT>
-__global__ void gemv_generic_kernel(const int* only_if, const float* __restrict__ A,
-                                    const uint8_t* __restrict__ Wq, const float* __restrict__ Ws,
-                                    float* __restrict__ C, int M, int N, int K) {
-  if (only_if && *only_if == 0) return;
+__global__ void gemv_generic_kernel(const float* __restrict__ A, const uint8_t* __restrict__ Wq,
+                                    const float* __restrict__ Ws, float* __restrict__ C, int M, int N, int K) {
   const long c = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= (long)M * N) return;
   const int m = (int)(c / N), n = (int)(c % N);
   C[c] = exact_row<DT>(A + (size_t)m * K, Wq, Ws, n, K);
 }
 
-// one activation row against n_mat matrices (device pointer arrays)
-template <int DT>
-__global__ void gemv_generic_batched_kernel(const int* only_if, const float* __restrict__ A,
-                                            const uint8_t* const* __restrict__ Wq,
-                                            const float* const* __restrict__ Ws, float* __restrict__ C,
-                                            int N, int K) {
-  if (only_if && *only_if == 0) return;
-  const int n = blockIdx.x * blockDim.x + threadIdx.x, mat = blockIdx.y;
-  if (n >= N) return;
-  C[(size_t)mat * N + n] = exact_row<DT>(A, Wq[mat], Ws[mat], n, K);
-}
-
 void launch_gemv_generic(int dtype, const float* A, const uint8_t* Wq, const float* Ws, float* C,
-                         int M, int N, int K, cudaStream_t st, const int* only_if) {
+                         int M, int N, int K, cudaStream_t st) {
   const long total = (long)M * N;
   if (total <= 0) return;
   const unsigned grid = (unsigned)((total + 127) / 128);
-  if (dtype == 2) gemv_generic_kernel<8><<<grid, 128, 0, st>>>(only_if, A, Wq, Ws, C, M, N, K);
-  else gemv_generic_kernel<4><<<grid, 128, 0, st>>>(only_if, A, Wq, Ws, C, M, N, K);
-}
-
-void launch_gemv_generic_batched(int dtype, const float* A, const uint8_t* const* Wq, const float* const* Ws,
-                                 float* C, int n_mat, int N, int K, cudaStream_t st, const int* only_if) {
-  if (n_mat <= 0 || N <= 0) return;
-  const dim3 grid((unsigned)((N + 127) / 128), (unsigned)n_mat);
-  if (dtype == 2) gemv_generic_batched_kernel<8><<<grid, 128, 0, st>>>(only_if, A, Wq, Ws, C, N, K);
-  else gemv_generic_batched_kernel<4><<<grid, 128, 0, st>>>(only_if, A, Wq, Ws, C, N, K);
+  if (dtype == 2) gemv_generic_kernel<8><<<grid, 128, 0, st>>>(A, Wq, Ws, C, M, N, K);
+  else gemv_generic_kernel<4><<<grid, 128, 0, st>>>(A, Wq, Ws, C, M, N, K);
 }
 
 // --------------------------------------------------------------------------

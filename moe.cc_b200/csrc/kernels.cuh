@@ -134,10 +134,12 @@ __host__ __device__ inline RouteView route_view(int* route, int E) {
 // xact planes from fp32 rows: Q8 -> [lo K][hi K] per row, Q4 -> permuted K
 // bytes per row + rowsum. Sets err bit kErrRange on out-of-range values.
 // mma_layout: Q4 activations in the tensor-core order (q4_mma_pos)
-// flags: per-token range flags (range_fail in common.cuh) instead of kErrRange
+// flags: per-token range flags (range_fail in common.cuh) instead of kErrRange.
+// mark != 0: an out-of-range activation stores mark into *err instead (the
+// fast GEMV of the same call compares it), so *err needs no clearing
 void launch_quantize_act(const float* x, int M, int K, int dtype, uint8_t* act,
                          int act_stride, int* asum, int* err, cudaStream_t st,
-                         int mma_layout = 0, int* flags = nullptr);
+                         int mma_layout = 0, int* flags = nullptr, int mark = 0);
 // C[m][n] = sequential fp32 Σ_k A[m][k] W[n][k] (+ b[n]).
 void launch_f32_seq_matmul(const float* A, const float* W, const float* b,
                            float* C, int M, int N, int K, cudaStream_t st);
@@ -153,22 +155,22 @@ constexpr int kRouteBuildMaxE = 256;
 void launch_route_build_multi(const int* idx, int T, int K, int e_begin, int E_local, int* route,
                               int* hsum, int nt, int* slot_pos, cudaStream_t st);
 // Fast warp GEMV over n_mat matrices: C[mat][m][n]. Returns false if the
-// shape has no fast-path geometry (caller uses the generic kernel).
+// shape has no fast-path geometry (caller uses the generic kernel). With A
+// (the fp32 activations), flag and mark (launch_quantize_act's err word and
+// mark): when *flag == mark the kernel computes every output exactly from A
+// instead, so the result is the reference's for any activation magnitude.
 bool launch_gemv(int dtype, const uint8_t* const* Wq, const float* const* Ws,
                  int n_mat, bool ptr_arrays_on_device, int N, int K,
                  const uint8_t* act, int act_stride, const int* asum, int M,
-                 float* C, cudaStream_t st);
+                 float* C, cudaStream_t st, const float* A = nullptr, const int* flag = nullptr,
+                 int mark = 0);
+// a fresh nonzero mark per call (thread-safe)
+int next_range_mark();
 // Exact kernel for any shape and activation magnitude (one thread per output,
-// int32 truncation, wrapping dot). only_if: run only if *only_if != 0 (the
-// fix-up pass after the fast GEMV).
+// int32 truncation, wrapping dot).
 void launch_gemv_generic(int dtype, const float* A, const uint8_t* Wq,
                          const float* Ws, float* C, int M, int N, int K,
-                         cudaStream_t st, const int* only_if = nullptr);
-// the same for one activation row against n_mat matrices (device arrays of
-// device pointers), C [n_mat][N]
-void launch_gemv_generic_batched(int dtype, const float* A, const uint8_t* const* Wq,
-                                 const float* const* Ws, float* C, int n_mat, int N, int K,
-                                 cudaStream_t st, const int* only_if = nullptr);
+                         cudaStream_t st);
 bool fast_geometry_ok(int dtype, int K);
 void launch_gateup(const LayerDev& L, const Workspace& ws, int T, int* err,
                    cudaStream_t st);

@@ -17,7 +17,8 @@
 // of packed row, 16-byte aligned B_q); the limits apply to those shapes, the
 // others run the exact kernel directly and have none.
 // All calls share the array and it keeps the previous call's contents; the
-// error word is cleared at the start of each call. Calls whose GPU work
+// error word holds the mark of the last call that found an activation out of
+// range (each call compares its own mark). Calls whose GPU work
 // overlaps (different streams, no ordering between them) race on the array.
 // The first call on each device is the set-up: with that device current it
 // looks up the array's device address (cudaGetSymbolAddress) and keeps it.
@@ -114,15 +115,15 @@ extern "C" int moe_matmul_q_dev_noalloc(const float* A, const void* B_q, const f
   int* flag = reinterpret_cast<int*>(base);
   int* asum = reinterpret_cast<int*>(base + na::kHeaderBytes);
   uint8_t* act = base + na::kHeaderBytes + na::kSumBytes;
-  cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), st);
-  if (e == cudaSuccess) {
+  cudaError_t e = cudaSuccess;
+  {
     if (fast) {
-      // truncated activation planes in the static array, then the warp GEMV;
-      // the fix-up pass recomputes C exactly if any activation was out of range
-      launch_quantize_act(A, M, K, dtype, act, 2 * K, asum, flag, st);
+      // truncated activation planes in the static array, then the warp GEMV,
+      // which computes C exactly instead if any activation was out of range
+      const int mark = next_range_mark();   // the error word needs no clearing
+      launch_quantize_act(A, M, K, dtype, act, 2 * K, asum, flag, st, 0, nullptr, mark);
       const uint8_t* wq = static_cast<const uint8_t*>(B_q);
-      launch_gemv(dtype, &wq, &B_s, 1, false, N, K, act, 2 * K, asum, M, C, st);
-      launch_gemv_generic(dtype, A, wq, B_s, C, M, N, K, st, flag);
+      launch_gemv(dtype, &wq, &B_s, 1, false, N, K, act, 2 * K, asum, M, C, st, A, flag, mark);
     } else {
       // shapes without a fast geometry need no scratch: exact kernel directly
       launch_gemv_generic(dtype, A, static_cast<const uint8_t*>(B_q), B_s, C, M, N, K, st);

@@ -8,6 +8,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <map>
 #include <tuple>
 #include <mutex>
@@ -215,6 +216,13 @@ static void ep_shutdown_hook();   // releases the expert-parallel buffers (defin
 struct Buf { void* p = nullptr; size_t cap = 0; };
 static Buf s_A, s_C, s_W, s_S, s_act, s_asum, s_hf, s_flag;
 
+int next_range_mark() {
+  static std::atomic<unsigned> n{0};
+  unsigned v;
+  while ((v = ++n) == 0u) {}            // never 0 (0 means "no mark")
+  return (int)v;
+}
+
 static int grow(Buf& b, size_t bytes) {
   if (bytes <= b.cap) return MOE_OK;
   if (b.p) { CU(cudaDeviceSynchronize()); cudaFree(b.p); b.p = nullptr; b.cap = 0; }
@@ -236,9 +244,9 @@ static int check_mnk(int M, int N, int K) {
 }
 
 // Q8/Q4 matmul on device pointers: activation truncation + the fast warp GEMV,
-// then the exact fix-up pass (the generic kernel, which runs only when the
-// truncation marked an activation outside the 16-bit / 8-bit range), so the
-// result is the reference's for any activation magnitude.
+// which computes exactly from the fp32 activations instead when the
+// truncation marked one outside the 16-bit / 8-bit range, so the result is
+// the reference's for any activation magnitude.
 static int matmul_q_dev(int dtype, const float* A, const void* Bq, const float* Bs, float* C,
                         int M, int N, int K, cudaStream_t st) {
   int rc = check_mnk(M, N, K);
@@ -255,12 +263,11 @@ static int matmul_q_dev(int dtype, const float* A, const void* Bq, const float* 
     if ((rc = grow(s_asum, sizeof(int) * (size_t)M))) return rc;
     if ((rc = grow(s_flag, sizeof(int)))) return rc;
     int* flag = (int*)s_flag.p;
-    CU(cudaMemsetAsync(flag, 0, sizeof(int), st));
-    launch_quantize_act(A, M, K, dtype, (uint8_t*)s_act.p, 2 * K, (int*)s_asum.p, flag, st);
+    const int mark = next_range_mark();
+    launch_quantize_act(A, M, K, dtype, (uint8_t*)s_act.p, 2 * K, (int*)s_asum.p, flag, st, 0, nullptr, mark);
     const uint8_t* wq = (const uint8_t*)Bq;
     launch_gemv(dtype, &wq, &Bs, 1, false, N, K, (const uint8_t*)s_act.p, 2 * K,
-                  (const int*)s_asum.p, M, C, st);
-    launch_gemv_generic(dtype, A, wq, Bs, C, M, N, K, st, flag);
+                  (const int*)s_asum.p, M, C, st, A, flag, mark);
   } else {
     launch_gemv_generic(dtype, A, (const uint8_t*)Bq, Bs, C, M, N, K, st);
   }
@@ -444,12 +451,11 @@ int moe_matmul_batched_dev(const float* A, const void* const* W_q, const float* 
   if ((rc = grow(s_act, (size_t)2 * K)) || (rc = grow(s_asum, sizeof(int))) || (rc = grow(s_flag, sizeof(int))))
     return rc;
   int* flag = (int*)s_flag.p;
-  CU(cudaMemsetAsync(flag, 0, sizeof(int), st));
-  launch_quantize_act(A, 1, K, dtype, (uint8_t*)s_act.p, 2 * K, (int*)s_asum.p, flag, st);
+  const int mark = next_range_mark();
+  launch_quantize_act(A, 1, K, dtype, (uint8_t*)s_act.p, 2 * K, (int*)s_asum.p, flag, st, 0, nullptr, mark);
+  // (an activation out of the fast range makes the GEMV compute exactly)
   launch_gemv(dtype, (const uint8_t* const*)W_q, W_s, n_mat, true, N, K, (const uint8_t*)s_act.p,
-                2 * K, (const int*)s_asum.p, 1, C, st);
-  // exact fix-up pass, only when an activation was out of the fast range
-  launch_gemv_generic_batched(dtype, A, (const uint8_t* const*)W_q, W_s, C, n_mat, N, K, st, flag);
+                2 * K, (const int*)s_asum.p, 1, C, st, A, flag, mark);
   CU(cudaGetLastError());
   return MOE_OK;
 }

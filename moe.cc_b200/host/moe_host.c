@@ -60,6 +60,11 @@ struct MhModel {
   long* moe_calls;
   double cpu_ms;
   int moe_uploaded;
+  /* expert parallelism (mh_ep_setup / mh_ep_connect): device staging of the
+     MoE block's input and residual rows, and the stream of moe_ffn_ep */
+  int ep_on, ep_cap;
+  float *d_xn, *d_xo;
+  cudaStream_t ep_stream;
 };
 
 static _Thread_local char g_err[512];   /* per calling thread */
@@ -336,6 +341,9 @@ static void free_scratch(MhModel* m) {
 
 void mh_free(MhModel* m) {
   if (!m) return;
+  if (m->d_xn) cudaFree(m->d_xn);
+  if (m->d_xo) cudaFree(m->d_xo);
+  if (m->ep_stream) cudaStreamDestroy(m->ep_stream);
   if (m->moe_uploaded)
     for (int l = 0; l < m->c.n_layers; ++l) moe_cuda_free_layer(m->moe_base + l);
   for (int i = 0; i < m->n_owned; ++i) free(m->owned[i]);
@@ -501,9 +509,57 @@ int mh_attention(MhModel* m, int layer, const float* x, int T, float* x_after, f
   return MOE_OK;
 }
 
+/* Expert-parallel MoE block of R rows: moe_ffn_ep over the rows in chunks of
+   at most ep_cap (every rank has the same R, so the chunks line up across
+   the ranks), through device staging, then the status check. */
+static int moe_ep_rows(MhModel* m, int layer, const float* x_norm2, float* x_after, int R) {
+  const size_t D = (size_t)m->c.d_model;
+  for (int r0 = 0; r0 < R; r0 += m->ep_cap) {
+    const int n = R - r0 < m->ep_cap ? R - r0 : m->ep_cap;
+    const size_t bytes = sizeof(float) * (size_t)n * D;
+    if (cudaMemcpyAsync(m->d_xn, x_norm2 + (size_t)r0 * D, bytes, cudaMemcpyHostToDevice, m->ep_stream) ||
+        cudaMemcpyAsync(m->d_xo, x_after + (size_t)r0 * D, bytes, cudaMemcpyHostToDevice, m->ep_stream))
+      return fail(MOE_ERR_CUDA, "mh_moe: copy to the device failed");
+    int rc = moe_ffn_ep(m->moe_base + layer, m->d_xn, n, m->d_xo, m->ep_stream);
+    if (rc) return fail(rc, "moe_ffn_ep (layer %d): %s", layer, moe_cuda_last_error());
+    if (cudaMemcpyAsync(x_after + (size_t)r0 * D, m->d_xo, bytes, cudaMemcpyDeviceToHost, m->ep_stream) ||
+        cudaStreamSynchronize(m->ep_stream))
+      return fail(MOE_ERR_CUDA, "mh_moe: copy from the device failed");
+    if ((rc = moe_cuda_check_status())) return fail(rc, "moe_ffn_ep (layer %d): %s", layer, moe_cuda_last_error());
+  }
+  return MOE_OK;
+}
+
+int mh_ep_setup(MhModel* m, int max_rows_per_call, void* handle_out) {
+  if (!m || max_rows_per_call < 1 || !handle_out) return fail(MOE_ERR_INVALID, "mh_ep_setup: bad argument");
+  const size_t bytes = sizeof(float) * (size_t)max_rows_per_call * m->c.d_model;
+  if (!m->d_xn && (cudaMalloc((void**)&m->d_xn, bytes) || cudaMalloc((void**)&m->d_xo, bytes) ||
+                   cudaStreamCreateWithFlags(&m->ep_stream, cudaStreamNonBlocking)))
+    return fail(MOE_ERR_NOMEM, "mh_ep_setup: device staging of %d rows", max_rows_per_call);
+  const int rc = moe_cuda_ep_setup(max_rows_per_call, m->c.d_model, 8, handle_out);
+  if (rc) return fail(rc, "moe_cuda_ep_setup: %s", moe_cuda_last_error());
+  m->ep_cap = max_rows_per_call;
+  return MOE_OK;
+}
+
+int mh_ep_connect(MhModel* m, const void* handles) {
+  if (!m || !handles || !m->ep_cap) return fail(MOE_ERR_INVALID, "mh_ep_connect: call mh_ep_setup first");
+  const int rc = moe_cuda_ep_connect(handles);
+  if (rc) return fail(rc, "moe_cuda_ep_connect: %s", moe_cuda_last_error());
+  m->ep_on = 1;
+  return MOE_OK;
+}
+
 int mh_moe(MhModel* m, int layer, const float* x_norm2, float* x_after, int T) {
   if (!m || layer < 0 || layer >= m->c.n_layers) return fail(MOE_ERR_INVALID, "mh_moe: bad layer");
   const double t0 = now_ms();
+  if (m->ep_on) {
+    const int rc = moe_ep_rows(m, layer, x_norm2, x_after, m->batch * T);
+    if (rc) return rc;
+    m->moe_ms[layer] += now_ms() - t0;
+    m->moe_calls[layer] += 1;
+    return MOE_OK;
+  }
   const int rc = moe_ffn(m->moe_base + layer, x_norm2, x_after, m->batch * T, NULL, NULL,
                          MOE_FFN_HOST_PTRS, NULL);
   if (rc) return fail(rc, "moe_ffn (layer %d): %s", layer, moe_cuda_last_error());

@@ -16,7 +16,7 @@ EXPORTS = (
     "mh_create", "mh_free", "mh_last_error", "mh_set_globals", "mh_set_layer",
     "mh_config_from_bin", "mh_load_bin", "mh_synth", "mh_pos", "mh_reset", "mh_fill_kv",
     "mh_step", "mh_generate", "mh_pick_greedy", "mh_embed", "mh_attention", "mh_moe",
-    "mh_head", "mh_advance", "mh_timing", "mh_timing_reset",
+    "mh_head", "mh_advance", "mh_timing", "mh_timing_reset", "mh_ep_setup", "mh_ep_connect",
 )
 # include/moe_model.h (model.c's call surface, served by the same library)
 MODEL_EXPORTS = ("layer_forward_f32", "model_forward_f32", "moe_model_release")
@@ -57,6 +57,7 @@ def lib():
             "mh_moe": ([vp, i, vp, vp, i], i), "mh_head": ([vp, vp, i, vp], i),
             "mh_advance": ([vp, i], i), "mh_timing": ([vp, vp, vp, vp], i),
             "mh_timing_reset": ([vp], None),
+            "mh_ep_setup": ([vp, i, vp], i), "mh_ep_connect": ([vp, vp], i),
         }
         sig["layer_forward_f32"] = ([vp, i, i, vp, f] + [vp] * 10 + [i, i, i, i, f, vp, f, vp, vp] + [vp] * 6 +
                                     [i, i, i, vp, vp, vp, vp], None)

@@ -1,9 +1,7 @@
 """MOE_E2E_GRAPH=1 (graph replay of host-pointer moe_ffn calls) against the
 eager path: every call's outputs, top-k and weights bit for bit, across
-layers, token counts and rotating host buffers.
-
-Off by default: set MOE_TEST_E2E_GRAPH=1 to run it (the switch itself is off
-by default until this test has passed on a GPU)."""
+layers, token counts and rotating host buffers. (The switch stays off by
+default: it measured slower than the eager path.)"""
 import os
 import subprocess
 import sys
@@ -11,9 +9,7 @@ import sys
 import numpy as np
 import pytest
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("MOE_TEST_E2E_GRAPH") != "1",
-                                 reason="set MOE_TEST_E2E_GRAPH=1 to run the graph-replay comparison")]
+pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 

@@ -70,3 +70,33 @@ def test_host_synth_deterministic(gpu):
     lg = a.step(prompts[:, :1])
     assert np.isfinite(lg).all() and a.pos() == 13
     a.close(); b.close()
+
+
+@pytest.mark.parametrize("dt", ["q8", "q4"])
+def test_host_driver_expert_parallel_matches_one_gpu(tmp_path, dt):
+    """moe_generate with the experts sharded over 2 GPUs (moe_ffn_ep in every
+    MoE block, 2 of the 4 sequences per rank) greedy-decodes exactly the
+    tokens of the one-GPU run of the same model and prompts."""
+    import subprocess
+    import sys
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("expert parallelism needs one GPU per rank (2 GPUs)")
+    exe = os.path.join(os.path.dirname(mh.LIB_PATH), "moe_generate")
+    args = ["--layers", "2", "--dtype", dt, "--batch", "4", "--prompt", "6", "--steps", "5", "--seed", "3"]
+    one = subprocess.run([exe] + args + ["--out", str(tmp_path / "one")], capture_output=True, text=True,
+                         timeout=600)
+    assert one.returncode == 0, one.stderr[-2000:]
+    ep_dir = tmp_path / "ep"
+    ep_dir.mkdir()
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    two = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--no-python", "--nnodes=1",
+                          "--nproc-per-node=2", "--master-addr", "127.0.0.1",
+                          "--master-port", str(29910 + len(dt) + (dt == "q4")), exe] + args +
+                         ["--ep-dir", str(ep_dir), "--out", str(tmp_path / "two")],
+                         capture_output=True, text=True, timeout=600, env=env)
+    assert two.returncode == 0, two.stderr[-3000:]
+    want = (tmp_path / "one.0").read_text().split("\n")
+    got = (tmp_path / "two.0").read_text().split("\n")[:2] + (tmp_path / "two.1").read_text().split("\n")[:2]
+    assert want[:4] == got, (want, got)
+    assert '"ep_world": 2' in two.stdout
