@@ -612,6 +612,13 @@ def full_model_c5(world, rank, local, dist, steps=3, timeout_s=600):
         tmp = box[0]
         cmd += ["--ep-dir", tmp]
         env.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(local), NCCL_NVLS_ENABLE="0")
+        # torchrun pins OMP_NUM_THREADS=1 for its ranks; the host attention of
+        # each moe_generate rank gets an equal share of the cores instead
+        try:
+            ncpu = len(os.sched_getaffinity(0))
+        except AttributeError:
+            ncpu = os.cpu_count() or 1
+        env["OMP_NUM_THREADS"] = str(max(1, ncpu // world))
     else:
         cmd += ["--device", str(local)]
     try:
@@ -626,6 +633,9 @@ def full_model_c5(world, rank, local, dist, steps=3, timeout_s=600):
     out["workload"] = (f"configs[4]: 48-layer decoder, Q4 experts, 32 sequences in lockstep at context {ctx} "
                        f"(KV prefilled N(0,1)), experts sharded over {world} GPU(s) by expert parallelism")
     out["context"] = ctx
+    if world > 1:
+        out["note"] = ("moe_ms_per_layer_call includes waiting for the slowest rank's host attention: "
+                       "the ranks' MoE calls run in lockstep")
     out["context_rule"] = "largest of 8192/4096/2048/1024 whose host KV cache and weights fit half of free memory"
     return out
 
