@@ -400,15 +400,14 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
       const float sc1 = NM == 2 ? __ldg(reinterpret_cast<const float*>(ex + a.s1_off) + n) : 0.f;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * ACC;
       // one (row n, sorted slot j) output from its raw accumulator words
-      auto emit = [&](const int j, const uint32_t (&raw)[NM * NL]) {
+      // as: the Q4 zero-point sum of slot j (Σa of its token for gate/up, Σh
+      // of the slot for down), loaded by the caller
+      auto emit = [&](const int j, const uint32_t (&raw)[NM * NL], const int as) {
         int dot[NM];
   #pragma unroll
         for (int m = 0; m < NM; ++m)
           dot[m] = NL == 2 ? (int)(raw[m * 2] + (raw[m * 2 + 1] << 8)) : (int)raw[m];
         if (DT == 4) {   // nibbles are stored +8: subtract 8 * Σ activation (exact mod 2^32)
-          const int as = MODE == GATEUP ? (a.tokb ? __ldg(a.xsum + __ldg(a.route + 2 + 2 * a.E_local + j) / a.topk)
-                                                  : __ldg(a.xsum_s + j))
-                                        : __ldcg(a.hsum + j);
   #pragma unroll
           for (int m = 0; m < NM; ++m) dot[m] = (int)((unsigned)dot[m] - 8u * (unsigned)as);
         }
@@ -462,13 +461,23 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
 #pragma unroll
             for (int c = 1; c < 8; ++c) if ((t & 7) == c) raw[x] = v[x][c];
           }
-          emit(j, raw);
+          // decode gate/up: the token's Σa (Q4), through the slot's token index
+          emit(j, raw, DT == 4 ? __ldg(a.xsum + __ldg(a.route + 2 + 2 * a.E_local + j) / a.topk) : 0);
         }
       } else {
         for (int c0 = 8 * half; c0 < nt; c0 += 8 * kEpiPerQ) {
           uint32_t v[NM * NL][8];
 #pragma unroll
           for (int x = 0; x < NM * NL; ++x) tc::tmem_ld8(tbase + x * NT + c0, v[x]);
+          // the group's 8 zero-point sums, loaded together before any of its
+          // stores (the stores could alias them, so the compiler keeps loads
+          // after earlier stores): sorted-slot Σa for gate/up (staged by the
+          // gather), Σh for down (written by the gate/up kernel); through L2,
+          // as the producing kernel may have finished only under this launch
+          int asv[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            asv[i] = (DT == 4 && c0 + i < nt) ? __ldcg((MODE == GATEUP ? a.xsum_s : a.hsum) + j0 + c0 + i) : 0;
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -477,7 +486,7 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
             uint32_t raw[NM * NL];
 #pragma unroll
             for (int x = 0; x < NM * NL; ++x) raw[x] = v[x][i];
-            emit(j0 + jj, raw);
+            emit(j0 + jj, raw, asv[i]);
           }
         }
       }
