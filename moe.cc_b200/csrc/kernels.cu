@@ -236,7 +236,6 @@ __global__ void __launch_bounds__(256) f32_seq_tiled_kernel(const float* __restr
 // behind the chains of the tiles already there. A thread's experts are 16
 // rows apart, so shared-memory reads hit distinct banks. Each output is still
 // one sequential fp32 sum over k in ascending order.
-constexpr int kGK = 32, kGPad = kGK + 4;
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((unsigned)__cvta_generic_to_shared(dst)),
@@ -247,13 +246,14 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-template <int TT, int ET, int ST>
+template <int TT, int ET, int ST, int kGK>
 __global__ void __launch_bounds__(128) f32_seq_gemm_kernel(const float* __restrict__ A,
                                                           const float* __restrict__ W,
                                                           const float* __restrict__ b,
                                                           float* __restrict__ C, int M, int N, int K) {
-  constexpr int GT = 8 * TT, GE = 16 * ET;
-  constexpr int XL = GT * 8 / 128, WL = GE * 8 / 128;   // 16-byte copies per thread per k-tile
+  constexpr int GT = 8 * TT, GE = 16 * ET, kGPad = kGK + 4;
+  constexpr int CPR = kGK / 4;                           // 16-byte copies per row of a k-tile
+  constexpr int XL = GT * CPR / 128, WL = GE * CPR / 128; // 16-byte copies per thread per k-tile
   extern __shared__ __align__(16) float smf[];
   float* xs = smf;                                        // [ST][GT][kGPad]
   float* ws = smf + ST * GT * kGPad;                      // [ST][GE][kGPad]
@@ -272,14 +272,14 @@ __global__ void __launch_bounds__(128) f32_seq_gemm_kernel(const float* __restri
     const int sb = kt % ST, k0 = kt * kGK;
 #pragma unroll
     for (int i = 0; i < XL; ++i) {
-      const int q = tid + i * 128, row = q / 8, col = (q % 8) * 4;
+      const int q = tid + i * 128, row = q / CPR, col = (q % CPR) * 4;
       const int m = m0 + row;
       const bool v = m < M && k0 + col < K;
       cp_async16(&xs[((size_t)sb * GT + row) * kGPad + col], v ? A + (size_t)m * K + k0 + col : A, v ? 16 : 0);
     }
 #pragma unroll
     for (int i = 0; i < WL; ++i) {
-      const int q = tid + i * 128, row = q / 8, col = (q % 8) * 4;
+      const int q = tid + i * 128, row = q / CPR, col = (q % CPR) * 4;
       const int n = n0 + row;
       const bool v = n < N && k0 + col < K;
       cp_async16(&ws[((size_t)sb * GE + row) * kGPad + col], v ? W + (size_t)n * K + k0 + col : W, v ? 16 : 0);
@@ -326,16 +326,16 @@ __global__ void __launch_bounds__(128) f32_seq_gemm_kernel(const float* __restri
     }
 }
 
-template <int TT, int ET, int ST>
+template <int TT, int ET, int ST, int GK>
 static void launch_seq_gemm(dim3 grid, const float* A, const float* W, const float* b, float* C, int M, int N, int K,
                             cudaStream_t st) {
-  const size_t smem = sizeof(float) * (size_t)ST * (8 * TT + 16 * ET) * kGPad;
+  const size_t smem = sizeof(float) * (size_t)ST * (8 * TT + 16 * ET) * (GK + 4);
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(f32_seq_gemm_kernel<TT, ET, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(f32_seq_gemm_kernel<TT, ET, ST, GK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr = true;
   }
-  launch_pdl(f32_seq_gemm_kernel<TT, ET, ST>, grid, dim3(128), smem, st, A, W, b, C, M, N, K);
+  launch_pdl(f32_seq_gemm_kernel<TT, ET, ST, GK>, grid, dim3(128), smem, st, A, W, b, C, M, N, K);
 }
 
 void launch_f32_seq_matmul(const float* A, const float* W, const float* b, float* C, int M, int N,
@@ -348,9 +348,10 @@ void launch_f32_seq_matmul(const float* A, const float* W, const float* b, float
     // (measured faster than 2 x 4 at two CTAs per SM); 2 x 2 below that, so
     // the grid still spreads over the SMs
     if (M >= 2048) {
-      launch_seq_gemm<4, 4, 6>(dim3((N + 63) / 64, (M + 31) / 32), A, W, b, C, M, N, K, st);
+      launch_seq_gemm<4, 4, 6, 32>(dim3((N + 63) / 64, (M + 31) / 32), A, W, b, C, M, N, K, st);
     } else {
-      launch_seq_gemm<2, 2, 8>(dim3((N + 31) / 32, (M + 15) / 16), A, W, b, C, M, N, K, st);
+      // k-tiles of 128 here (T=512 router 39 -> 37 us; 32 stays best for 4 x 4)
+      launch_seq_gemm<2, 2, 4, 128>(dim3((N + 31) / 32, (M + 15) / 16), A, W, b, C, M, N, K, st);
     }
     return;
   }
