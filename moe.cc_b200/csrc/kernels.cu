@@ -1025,10 +1025,11 @@ void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y, cudaSt
 // expert holds. idx may be null (every slot has an expert).
 __global__ void combine_kernel(const float* __restrict__ y, const float* __restrict__ p,
                                const int* __restrict__ idx, const float* xres, float* out, int T, int D, int K,
-                               int seq) {
+                               int seq, const HostOut ho) {
   pdl_wait();
   pdl_launch();
   const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  publish_host(ho, q, (long)gridDim.x * blockDim.x);
   if (q >= (long)T * D) return;
   const int t = (int)(q / D), n = (int)(q % D);
   float acc = seq ? xres[q] : 0.0f;
@@ -1041,11 +1042,11 @@ __global__ void combine_kernel(const float* __restrict__ y, const float* __restr
 }
 
 void launch_combine(const float* y, const float* p, const int* idx, const float* xres, float* out, int T, int D,
-                    int K, cudaStream_t st, bool seq_residual) {
+                    int K, cudaStream_t st, bool seq_residual, const HostOut& ho) {
   const long total = (long)T * D;
   if (total <= 0) return;
   launch_pdl(combine_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, y, p, idx, xres, out, T, D,
-             K, seq_residual ? 1 : 0);
+             K, seq_residual ? 1 : 0, ho);
 }
 
 // --------------------------------------------------------------------------

@@ -186,10 +186,28 @@ void launch_down(const LayerDev& L, const Workspace& ws, int T, float* y, cudaSt
 // combine flags at every rank.
 void launch_exact_fixup(const LayerDev& L, const float* xn, const int* idx, const int* slot_pos, int T,
                         float* y, int* flags, int sm_count, cudaStream_t st, const EpView* ep = nullptr);
+// What a combine kernel also copies into page-locked host memory for a
+// host-pointer call, so that call needs no device-to-host copies: the top-k
+// lists (n = T*K entries; null destinations are skipped) and the call's
+// error word. The combine runs after every other kernel of the call has
+// completed, so the values it copies are final.
+struct HostOut {
+  int* idx; float* p; const int* idx_src; const float* p_src; int n;
+  const int* err_src; int* err;
+};
+// grid-strided over the combine's threads (q = global thread index)
+__device__ __forceinline__ void publish_host(const HostOut& h, long q, long nthreads) {
+  for (long i = q; i < h.n; i += nthreads) {
+    if (h.idx) h.idx[i] = h.idx_src[i];
+    if (h.p) h.p[i] = h.p_src[i];
+  }
+  if (q == 0 && h.err) *h.err = *reinterpret_cast<const volatile int*>(h.err_src);
+}
 // seq_residual: out = ((xres + p0 y0) + p1 y1) + ... (model.c:188) instead of
 // xres + (((0 + p0 y0) + p1 y1) + ...) (test_model_trace.c:513,517)
 void launch_combine(const float* y, const float* p, const int* idx, const float* xres,
-                    float* out, int T, int D, int K, cudaStream_t st, bool seq_residual = false);
+                    float* out, int T, int D, int K, cudaStream_t st, bool seq_residual = false,
+                    const HostOut& ho = HostOut{});
 // fp32 experts (f32_experts.cu): h [T*K][F], y [T*K][D] (slot rows)
 void launch_f32_experts(const LayerDev& L, const float* xn, const int* idx, int T, float* h, float* y,
                         cudaStream_t st);
@@ -220,7 +238,7 @@ bool launch_mma_fused(const LayerDev& L, const Workspace& ws, int T, int nt, int
                       const EpView* ep = nullptr);
 void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
                            const float* xres, float* out, int T, int D, int K, cudaStream_t st,
-                           bool seq_residual = false);
+                           bool seq_residual = false, const HostOut& ho = HostOut{});
 void launch_unsort_rows(const LayerDev& L, const Workspace& ws, int T, float* y_slots, cudaStream_t st);
 }  // namespace moe
 

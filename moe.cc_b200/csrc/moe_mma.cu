@@ -687,10 +687,12 @@ bool launch_mma_down(const LayerDev& L, const Workspace& ws, int T, int nt, floa
 // Scalar form (any D, any alignment of xres/out): one thread per output.
 __global__ void combine_sorted_scalar_kernel(const float* __restrict__ ys, const int* __restrict__ slot_pos,
                                              const float* __restrict__ p, const int* __restrict__ idx,
-                                             const float* xres, float* out, int T, int D, int K, int seq) {
+                                             const float* xres, float* out, int T, int D, int K, int seq,
+                                             const HostOut ho) {
   pdl_wait();
   pdl_launch();
   const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  publish_host(ho, q, (long)gridDim.x * blockDim.x);
   if (q >= (long)T * D) return;
   const int t = (int)(q / D), n = (int)(q % D);
   float acc = seq ? xres[q] : 0.0f;
@@ -706,11 +708,13 @@ __global__ void combine_sorted_scalar_kernel(const float* __restrict__ ys, const
 // slot rows.
 __global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* __restrict__ slot_pos,
                                       const float* __restrict__ p, const int* __restrict__ idx,
-                                      const float* xres, float* out, int T, int D, int K, int seq) {
+                                      const float* xres, float* out, int T, int D, int K, int seq,
+                                      const HostOut ho) {
   MOE_TL_START(kTlCombine);
   pdl_wait();
   pdl_launch();
   const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  publish_host(ho, q, (long)gridDim.x * blockDim.x);
   const int D4 = D / 4;
   if (q >= (long)T * D4) return;
   const int t = (int)(q / D4), n = (int)(q % D4) * 4;
@@ -768,18 +772,19 @@ __global__ void combine_sorted_kernel(const float* __restrict__ ys, const int* _
 }
 
 void launch_combine_sorted(const float* ys, const int* slot_pos, const float* p, const int* idx,
-                           const float* xres, float* out, int T, int D, int K, cudaStream_t st, bool seq_residual) {
+                           const float* xres, float* out, int T, int D, int K, cudaStream_t st, bool seq_residual,
+                           const HostOut& ho) {
   if (D % 4 || ((uintptr_t)xres | (uintptr_t)out | (uintptr_t)ys) % 16) {
     const long n1 = (long)T * D;
     if (n1 > 0)
       launch_pdl(combine_sorted_scalar_kernel, dim3((unsigned)((n1 + 255) / 256)), dim3(256), 0, st, ys, slot_pos, p,
-                 idx, xres, out, T, D, K, seq_residual ? 1 : 0);
+                 idx, xres, out, T, D, K, seq_residual ? 1 : 0, ho);
     return;
   }
   const long total = (long)T * (D / 4);
   if (total <= 0) return;
   launch_pdl(combine_sorted_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, ys, slot_pos, p, idx, xres,
-             out, T, D, K, seq_residual ? 1 : 0);
+             out, T, D, K, seq_residual ? 1 : 0, ho);
 }
 
 // Expert-parallel output: slot-ordered rows of this rank's slots, zeros for

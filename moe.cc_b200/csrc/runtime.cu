@@ -1,6 +1,8 @@
 // runtime.cu — host side of libmoe_cuda: the extern "C" boundary declared in
 // include/moe_cuda.h, device residency of the expert weights, the per-call
 // workspace and the orchestration of the fused MoE block.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdarg.h>
@@ -31,7 +33,8 @@ struct State {
   std::unordered_map<const void*, Alias> alias;  // host q/s pointer -> device copy
   Workspace ws;
   int* d_err = nullptr;                          // kernel-flagged errors
-  int* h_err = nullptr;                          // pinned host copy of d_err
+  int* h_err = nullptr;                          // pinned, mapped host copy of d_err
+  int* h_err_dev = nullptr;                      // h_err's device address
   std::string last_error;
   std::recursive_mutex mu;
 };
@@ -192,8 +195,8 @@ static int consume_device_error() {
 // The error flag as of the work queued on `st`: an async copy into pinned
 // host memory and one stream synchronisation (no device-wide sync), for the
 // synchronous host-pointer entry points.
-static int consume_stream_error(cudaStream_t st) {
-  CU(cudaMemcpyAsync(g.h_err, g.d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+static int consume_stream_error(cudaStream_t st, bool published = false) {
+  if (!published) CU(cudaMemcpyAsync(g.h_err, g.d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
   CU(cudaStreamSynchronize(st));
   const int h = *g.h_err;
   if (h) {
@@ -202,6 +205,41 @@ static int consume_stream_error(cudaStream_t st) {
     CU(cudaStreamSynchronize(st));
   }
   return error_status(h);
+}
+
+// The device address of [p, p + bytes) when the whole range lies in ONE
+// page-locked host allocation mapped into the device's address space
+// (cudaHostAlloc, cudaMallocHost, cudaHostRegister); null otherwise
+// (pageable memory, device memory, a range that spans allocations). Both
+// ends are looked up and must carry the same allocation id, so a kernel
+// given the address touches no unmapped page.
+static void* mapped_host_range(const void* p, size_t bytes) {
+  static PFN_cuPointerGetAttribute_v4000 get = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuPointerGetAttribute", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get = reinterpret_cast<PFN_cuPointerGetAttribute_v4000>(fn);
+  }
+  if (!get || !p || bytes == 0) return nullptr;
+  const uintptr_t first = (uintptr_t)p, last = first + bytes - 1;
+  cudaPointerAttributes a{}, b{};
+  if (cudaPointerGetAttributes(&a, (const void*)first) != cudaSuccess ||
+      cudaPointerGetAttributes(&b, (const void*)last) != cudaSuccess) {
+    cudaGetLastError();          // pageable memory on older runtimes reports an error; clear it
+    return nullptr;
+  }
+  if (a.type != cudaMemoryTypeHost || b.type != cudaMemoryTypeHost || !a.devicePointer || !b.devicePointer)
+    return nullptr;
+  unsigned long long ia = 0, ib = 0;
+  if (get(&ia, CU_POINTER_ATTRIBUTE_BUFFER_ID, (CUdeviceptr)first) != CUDA_SUCCESS ||
+      get(&ib, CU_POINTER_ATTRIBUTE_BUFFER_ID, (CUdeviceptr)last) != CUDA_SUCCESS || ia != ib)
+    return nullptr;
+  if ((uintptr_t)b.devicePointer - (uintptr_t)a.devicePointer != bytes - 1) return nullptr;
+  return a.devicePointer;
 }
 
 }  // namespace moe
@@ -324,7 +362,8 @@ int moe_cuda_init(int device, int ep_world, int ep_rank, const void* nccl_uid) {
   CU(cudaDeviceGetAttribute(&g.sm_count, cudaDevAttrMultiProcessorCount, device));
   CU(cudaMalloc((void**)&g.d_err, sizeof(int)));
   CU(cudaMemset(g.d_err, 0, sizeof(int)));
-  CU(cudaHostAlloc((void**)&g.h_err, sizeof(int), cudaHostAllocDefault));
+  CU(cudaHostAlloc((void**)&g.h_err, sizeof(int), cudaHostAllocMapped));
+  CU(cudaHostGetDevicePointer((void**)&g.h_err_dev, g.h_err, 0));
   *g.h_err = 0;
   g.device = device; g.ep_world = ep_world; g.ep_rank = ep_rank;
   g.init = true;
@@ -933,6 +972,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
   // left the fast kernels' integer range. (Fused into the down epilogue the
   // combine also left the last warp through each row block with T*K dependent
   // loads at the end of the kernel: measured 90 us vs 39 + 6 us.)
+  HostOut ho{};     // what the combine publishes to host memory (zero-copy calls below)
   auto enqueue = [&](const float* xn, float* xo, cudaStream_t s) -> int {
     if (L.dtype == MOE_DTYPE_F32) {
       // fp32 experts: router chains + top-k softmax, the fp32 expert FFN, combine
@@ -945,7 +985,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
         });
       }
       timed("f32_experts", s, [&] { launch_f32_experts(L, xn, w.topk_idx, T, (float*)s_hf.p, w.y, s); });
-      timed("combine", s, [&] { launch_combine(w.y, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s, seq); });
+      timed("combine", s, [&] { launch_combine(w.y, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s, seq, ho); });
     } else if (use_tensor_cores(L, flags, T)) {
       const int fnt = fused_tile_n(L, T);                 // fused gate/up + down kernel, if used
       const int nt = fnt ? fnt : mma_tile_n(T, L.dtype);
@@ -963,7 +1003,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
         launch_exact_fixup(L, xn, w.topk_idx, w.slot_pos, T, w.y, w.xbad, g.sm_count, s);
       });
       timed("combine", s, [&] {
-        launch_combine_sorted(w.y, w.slot_pos, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s, seq);
+        launch_combine_sorted(w.y, w.slot_pos, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s, seq, ho);
       });
     } else {
       route_tokens(L, xn, T, 0, s, given);
@@ -972,7 +1012,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
       timed("exact_fixup", s, [&] {
         launch_exact_fixup(L, xn, w.topk_idx, nullptr, T, w.y, w.xbad, g.sm_count, s);
       });
-      timed("combine", s, [&] { launch_combine(w.y, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s, seq); });
+      timed("combine", s, [&] { launch_combine(w.y, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s, seq, ho); });
     }
     CU(cudaGetLastError());
     return MOE_OK;
@@ -989,6 +1029,21 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
                               sizeof(int) * (size_t)T * L.topk, enqueue);
   const float* xn = x_norm2;
   float* xo = x_inout;
+  // Host-pointer call on page-locked buffers: the combine reads and updates
+  // x_inout in place through its mapped address and copies the top-k lists
+  // and the error word out, so the call makes one copy (x_norm2 in) and one
+  // stream synchronisation. Pageable buffers take the copies below.
+  if (host) {
+    float* zx = (float*)mapped_host_range(x_inout, xb);
+    int* zi = topk_idx_out && !given ? (int*)mapped_host_range(topk_idx_out, kb) : nullptr;
+    float* zp = topk_p_out && !given ? (float*)mapped_host_range(topk_p_out, kb) : nullptr;
+    if (zx && (zi || !topk_idx_out || given) && (zp || !topk_p_out || given)) {
+      CU(cudaMemcpyAsync(w.xn, x_norm2, xb, cudaMemcpyHostToDevice, st));
+      ho = HostOut{zi, zp, w.topk_idx, w.topk_p, (zi || zp) ? T * L.topk : 0, g.d_err, g.h_err_dev};
+      if ((rc = enqueue(w.xn, zx, st))) return rc;
+      return consume_stream_error(st, true);
+    }
+  }
   if (host) {
     CU(cudaMemcpyAsync(w.xn, x_norm2, xb, cudaMemcpyHostToDevice, st));
     CU(cudaMemcpyAsync(w.xo, x_inout, xb, cudaMemcpyHostToDevice, st));
