@@ -52,6 +52,7 @@ struct MhModel {
   float *kc, *vc;                /* [layer][batch][max_ctx][Dkv] */
   /* per-step scratch, grown to the step's rows */
   int cap_rows;
+  int pinned_rows;                 /* x, xa, xn2 came from cudaHostAlloc */
   float *xn1, *q, *k, *v, *hcat, *ao, *x, *xa, *xn2, *xlast;
   float* scores;                 /* per thread: max_ctx */
   int n_threads;
@@ -332,9 +333,28 @@ MhModel* mh_create(const MhConfig* cfg, int batch, int max_ctx, int moe_layer_ba
   return m;
 }
 
+/* The MoE block's input and residual rows (xn2, x, xa: x and xa swap every
+   layer) are page-locked and mapped, so each moe_ffn call copies xn2 in and
+   updates the residual in place through its mapped address, with no copy
+   out; plain malloc if page-locked memory is refused (the call then copies). */
+static float* rows_alloc(MhModel* m, size_t bytes) {
+  void* p = NULL;
+  if (m->pinned_rows && cudaHostAlloc(&p, bytes, cudaHostAllocMapped) == cudaSuccess) return (float*)p;
+  cudaGetLastError();
+  m->pinned_rows = 0;
+  return (float*)malloc(bytes);
+}
+
+static void rows_free(MhModel* m, float* p) {
+  if (!p) return;
+  if (cudaFreeHost(p) != cudaSuccess) { cudaGetLastError(); free(p); }
+  (void)m;
+}
+
 static void free_scratch(MhModel* m) {
-  float* s[] = {m->xn1, m->q, m->k, m->v, m->hcat, m->ao, m->x, m->xa, m->xn2, m->xlast};
+  float* s[] = {m->xn1, m->q, m->k, m->v, m->hcat, m->ao, m->xlast};
   for (size_t i = 0; i < sizeof(s) / sizeof(s[0]); ++i) free(s[i]);
+  rows_free(m, m->x); rows_free(m, m->xa); rows_free(m, m->xn2);
   m->xn1 = m->q = m->k = m->v = m->hcat = m->ao = m->x = m->xa = m->xn2 = m->xlast = NULL;
   m->cap_rows = 0;
 }
@@ -364,9 +384,10 @@ static int ensure_rows(MhModel* m, int R) {
   m->v = (float*)malloc(sizeof(float) * R * (size_t)m->Dkv);
   m->hcat = (float*)malloc(sizeof(float) * R * (size_t)m->Dq);
   m->ao = (float*)malloc(sizeof(float) * R * D);
-  m->x = (float*)malloc(sizeof(float) * R * D);
-  m->xa = (float*)malloc(sizeof(float) * R * D);
-  m->xn2 = (float*)malloc(sizeof(float) * R * D);
+  m->pinned_rows = 1;
+  m->x = rows_alloc(m, sizeof(float) * R * D);
+  m->xa = rows_alloc(m, sizeof(float) * R * D);
+  m->xn2 = rows_alloc(m, sizeof(float) * R * D);
   m->xlast = (float*)malloc(sizeof(float) * (size_t)m->batch * D);
   if (!m->xn1 || !m->q || !m->k || !m->v || !m->hcat || !m->ao || !m->x || !m->xa || !m->xn2 || !m->xlast) {
     free_scratch(m);
