@@ -358,13 +358,26 @@ __global__ void __launch_bounds__(cta_threads(DT, NT), (DT == 4 && MOE_Q4_TMEM &
           continue;
         }
         uint8_t* at = aring + (size_t)ab * NM * A_BYTES;
+        // every packed chunk of this k-chunk is loaded before the first
+        // expanded store: the compiler cannot move a shared load above a
+        // shared store it may alias, so load/store pairs would each wait out
+        // the load latency in turn
+        constexpr int NI = 512 / (kExpWarps > 0 ? kExpThreads : 128);
+        uint4 wv[NM][NI];
+#pragma unroll
+        for (int m = 0; m < NM; ++m)
+#pragma unroll
+          for (int i = 0; i < NI; ++i) {
+            const int item = ti + kExpThreads * i, r = item >> 2, c = item & 3;
+            wv[m][i] = *reinterpret_cast<const uint4*>(stg + m * A_BYTES + r * 128 +
+                                                       ((((qk << 2) + c) ^ (r & 7)) << 4));
+          }
 #pragma unroll
         for (int m = 0; m < NM; ++m) {
 #pragma unroll
-          for (int i = 0; i < 512 / (kExpWarps > 0 ? kExpThreads : 128); ++i) {
+          for (int i = 0; i < NI; ++i) {
             const int item = ti + kExpThreads * i, r = item >> 2, c = item & 3;
-            const uint4 w = *reinterpret_cast<const uint4*>(stg + m * A_BYTES + r * 128 +
-                                                            ((((qk << 2) + c) ^ (r & 7)) << 4));
+            const uint4 w = wv[m][i];
             uint8_t* dst = at + m * A_BYTES + r * 128;
             const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
             const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu,
