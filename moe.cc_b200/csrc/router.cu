@@ -55,21 +55,27 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
   MOE_TL_START(kTlRoute);
 
   // the rows arrive in kChunks column chunks, each on its own barrier, so the
-  // chains start on chunk 0 while the rest is still in flight
-  if (tid == 0) {
-    for (int c = 0; c < kChunks; ++c) mbar_init(&bar[c], 1);
-    fence_mbar_init();
+  // chains start on chunk 0 while the rest is still in flight. The copies
+  // are issued by all lanes of warp 0 (one thread issuing them one after
+  // another measured ~35 ns per copy).
+  if (tid < 32) {
+    if (tid == 0) {
+      for (int c = 0; c < kChunks; ++c) mbar_init(&bar[c], 1);
+      fence_mbar_init();
+      for (int c = 0; c < kChunks; ++c) mbar_arrive_expect_tx(&bar[c], (uint32_t)((ne + nt) * dc * 4));
+    }
+    __syncwarp();
     // the router rows are constant: they go out before the wait for the
     // previous kernel (dependent launch); the token rows after it
-    for (int c = 0; c < kChunks; ++c) {
-      mbar_arrive_expect_tx(&bar[c], (uint32_t)((ne + nt) * dc * 4));
-      for (int i = 0; i < ne; ++i)
-        bulk_g2s(sw + i * pitch + c * dc, a.W + (size_t)(e0 + i) * a.D + c * dc, dc * 4, &bar[c]);
+    for (int q = tid; q < kChunks * ne; q += 32) {
+      const int c = q / ne, i = q % ne;
+      bulk_g2s(sw + i * pitch + c * dc, a.W + (size_t)(e0 + i) * a.D + c * dc, dc * 4, &bar[c]);
     }
     pdl_wait();
-    for (int c = 0; c < kChunks; ++c)
-      for (int i = 0; i < nt; ++i)
-        bulk_g2s(sx + i * pitch + c * dc, a.x + (size_t)(t0 + i) * a.D + c * dc, dc * 4, &bar[c]);
+    for (int q = tid; q < kChunks * nt; q += 32) {
+      const int c = q / nt, i = q % nt;
+      bulk_g2s(sx + i * pitch + c * dc, a.x + (size_t)(t0 + i) * a.D + c * dc, dc * 4, &bar[c]);
+    }
   }
   pdl_wait();
   pdl_launch();
@@ -201,18 +207,20 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
   const int lane = tid & 31, warp = tid >> 5;
   int TK = a.T * a.K;
   for (int i = tid; i < a.E_local; i += kThreads) cnt[i] = 0;
-  // top-k per token: one warp per token, K rounds; each round is two warp
-  // reductions (redux.sync): the largest order-preserving key, then the lowest
-  // expert index among the lanes holding it. Keys of NaN and -inf are 0 (never
-  // chosen) and -0 is keyed as +0, so equal values tie exactly as in
-  // topk_desc's strict-'>' insertion (lower index first). Lane r keeps round
-  // r's winner; the softmax (:481-487) then runs across lanes, summing in order.
+  // top-k per token: one warp per token, K rounds. Lane l holds the
+  // contiguous experts l*PERL .. l*PERL+PERL-1, so lane order is expert order:
+  // each round takes the largest order-preserving key of the warp (redux.sync)
+  // and the lowest lane holding it (ballot), whose local pick is its lowest
+  // expert with that key. Keys of NaN and -inf are 0 (never chosen) and -0 is
+  // keyed as +0, so equal values tie exactly as in topk_desc's strict-'>'
+  // insertion (lower index first). Lane r keeps round r's winner; the softmax
+  // (:481-487) then runs across lanes, summing in order.
   constexpr int PERL = kMaxE / 32;
   for (int t = warp; t < a.T; t += kThreads / 32) {
     unsigned key[PERL];
 #pragma unroll
     for (int i = 0; i < PERL; ++i) {
-      const int e = lane + 32 * i;
+      const int e = lane * PERL + i;
       float v = e < a.E ? __ldcg(a.logits + (size_t)t * a.E + e) : -INFINITY;
       if (v == 0.0f) v = 0.0f;
       const unsigned u = __float_as_uint(v);
@@ -221,21 +229,23 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
     float myv = -INFINITY;
     int myi = -1;
     for (int r = 0; r < a.K; ++r) {
-      unsigned hk = 0; int hi = 0x7fffffff;
+      unsigned hk = key[0]; int hl = 0;
 #pragma unroll
-      for (int i = 0; i < PERL; ++i)
-        if (key[i] > hk) { hk = key[i]; hi = lane + 32 * i; }   // ascending index: first max kept
+      for (int i = 1; i < PERL; ++i)
+        if (key[i] > hk) { hk = key[i]; hl = i; }                // ascending index: first max kept
       const unsigned M = __reduce_max_sync(0xffffffffu, hk);
-      const unsigned I = __reduce_min_sync(0xffffffffu, (M != 0u && hk == M) ? (unsigned)hi : 0x7fffffffu);
-      if (lane == r && M != 0u) {
+      if (M == 0u) break;                                        // only NaN / -inf left: no expert
+      const int wl = __ffs(__ballot_sync(0xffffffffu, hk == M)) - 1;
+      const int I = __shfl_sync(0xffffffffu, lane * PERL + hl, wl);
+      if (lane == r) {
         const unsigned u = (M & 0x80000000u) ? (M & 0x7fffffffu) : ~M;
         myv = __uint_as_float(u);
-        myi = (int)I;
+        myi = I;
       }
-      if (M != 0u && (int)(I & 31) == lane) {
+      if (lane == wl) {
 #pragma unroll
         for (int i = 0; i < PERL; ++i)
-          if (lane + 32 * i == (int)I) key[i] = 0u;
+          if (i == hl) key[i] = 0u;
       }
     }
     float mx = __shfl_sync(0xffffffffu, myv, 0);
