@@ -299,21 +299,41 @@ __global__ void __launch_bounds__(128) f32_seq_gemm_kernel(const float* __restri
     const int kn = min(kGK, K - kt * kGK);
     const float* xb = xs + (size_t)sb * GT * kGPad;
     const float* wb = ws + (size_t)sb * GE * kGPad;
+    // per 4 k: the next 4 k's shared loads first, then for each k all TT x ET
+    // products before their TT x ET adds (inline PTX keeps this order; each
+    // chain stays sequential in k)
+    float4 xv[TT], wv[ET];
+#pragma unroll
+    for (int i = 0; i < TT; ++i) xv[i] = lds4(xb + (tq * TT + i) * kGPad);
+#pragma unroll
+    for (int j = 0; j < ET; ++j) wv[j] = lds4(wb + (eq + 16 * j) * kGPad);
+#pragma unroll 2
     for (int k = 0; k < kn; k += 4) {
-      float4 xv[TT], wv[ET];
+      const int kk = k + 4 < kn ? k + 4 : k;
+      float4 xn[TT], wn[ET];
 #pragma unroll
-      for (int i = 0; i < TT; ++i) xv[i] = *reinterpret_cast<const float4*>(xb + (tq * TT + i) * kGPad + k);
+      for (int i = 0; i < TT; ++i) xn[i] = lds4(xb + (tq * TT + i) * kGPad + kk);
 #pragma unroll
-      for (int j = 0; j < ET; ++j) wv[j] = *reinterpret_cast<const float4*>(wb + (eq + 16 * j) * kGPad + k);
+      for (int j = 0; j < ET; ++j) wn[j] = lds4(wb + (eq + 16 * j) * kGPad + kk);
 #pragma unroll
-      for (int i = 0; i < TT; ++i)
+      for (int c = 0; c < 4; ++c) {
+        float pr[TT][ET];
 #pragma unroll
-        for (int j = 0; j < ET; ++j) {
-          acc[i][j] = fadd(acc[i][j], fmul(xv[i].x, wv[j].x));
-          acc[i][j] = fadd(acc[i][j], fmul(xv[i].y, wv[j].y));
-          acc[i][j] = fadd(acc[i][j], fmul(xv[i].z, wv[j].z));
-          acc[i][j] = fadd(acc[i][j], fmul(xv[i].w, wv[j].w));
+        for (int i = 0; i < TT; ++i) {
+          const float xs = c == 0 ? xv[i].x : c == 1 ? xv[i].y : c == 2 ? xv[i].z : xv[i].w;
+#pragma unroll
+          for (int j = 0; j < ET; ++j)
+            pr[i][j] = mul_rn(xs, c == 0 ? wv[j].x : c == 1 ? wv[j].y : c == 2 ? wv[j].z : wv[j].w);
         }
+#pragma unroll
+        for (int i = 0; i < TT; ++i)
+#pragma unroll
+          for (int j = 0; j < ET; ++j) acc[i][j] = add_rn(acc[i][j], pr[i][j]);
+      }
+#pragma unroll
+      for (int i = 0; i < TT; ++i) xv[i] = xn[i];
+#pragma unroll
+      for (int j = 0; j < ET; ++j) wv[j] = wn[j];
     }
   }
   cp_async_wait<0>();

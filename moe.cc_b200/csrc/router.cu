@@ -40,27 +40,6 @@ struct Args {
   int ep_on; EpView ep;    // expert parallel: dispatch this rank's tokens, route all ranks' tokens
 };
 
-// Inline PTX for the chains, so the compiler keeps the order written: a
-// block's 16 products, the next block's shared-memory loads, then the block's
-// 16 dependent adds (from plain C++ the loads sank next to their uses: 6.6
-// against 4.9 cycles per add). mul.rn / add.rn: IEEE single, no contraction.
-__device__ __forceinline__ float4 lds4(const float* p) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"((unsigned)__cvta_generic_to_shared(p)));
-  return v;
-}
-__device__ __forceinline__ float mul_rn(float a, float b) {
-  float r;
-  asm volatile("mul.rn.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ float add_rn(float a, float b) {
-  float r;
-  asm volatile("add.rn.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
-  return r;
-}
-
 __device__ __forceinline__ uint8_t* peer_base(const EpView& ep, int p) {
   return reinterpret_cast<uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(ep.base) + p));
 }
