@@ -261,6 +261,11 @@ int moe_quantize_rowwise_q4_host(const float* W, int rows, int cols, uint8_t* q,
  * no range limit, kernels.c:66, :113).
  * A slot with no expert (fewer than top_k logits that are neither NaN nor
  * -inf; the reference then reads an expert out of bounds) adds p * 0.
+ * MOE_FFN_HOST_PTRS on page-locked host buffers (cudaHostAlloc,
+ * cudaMallocHost, cudaHostRegister): x_norm2 is copied in, and the combine
+ * kernel updates x_inout in place through its mapped address and writes the
+ * top-k outputs to host memory, so no copies come back; pageable buffers are
+ * copied both ways. Both give the same results.
  * With ep_world > 1 use moe_ffn_partial or moe_ffn_ep instead. */
 int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T,
             int* topk_idx_out, float* topk_p_out, int flags, void* stream);
