@@ -198,8 +198,9 @@ __global__ void __launch_bounds__(threads(DT), 2)
           const unsigned long long w0 = tl_now();
 #endif
           int v;
+          const uint64_t t0 = globaltimer_ns();   // bounded by time (kWaitNs), checked every 64 polls
           while ((v = ld_acquire_gpu(ready + pos)) == 0)
-            if (++i >= kWaitNs) break;
+            if ((++i & 63) == 0 && globaltimer_ns() - t0 > kWaitNs) break;
 #ifdef MOE_TIMELINE
           stall += tl_now() - w0;
 #endif
