@@ -248,8 +248,13 @@ bool decode_route_supported(const LayerDev& L, int T, const float* x);
 // ep != null: T = this rank's tokens; their activations and top-k go to every
 // rank's buffers, and the routing lists cover all ranks' tokens (after a
 // bounded wait on the dispatch flags)
+// res: a copy the routing kernel's spare warps make while the chains run
+// (n4 16-byte words from src to dst), e.g. a call's residual rows from
+// page-locked host memory into the device workspace
+struct RowCopy { const float* src; float* dst; long n4; };
 void launch_decode_route(const LayerDev& L, const Workspace& ws, const float* x, int T, int nt,
-                         int* counter, int* err, cudaStream_t st, const EpView* ep = nullptr);
+                         int* counter, int* err, cudaStream_t st, const EpView* ep = nullptr,
+                         const RowCopy* res = nullptr);
 }  // namespace moe
 
 namespace moe {

@@ -37,6 +37,7 @@ struct Args {
   uint8_t* xact; int* xsum; int q4_mma;
   int* counter; int* err;
   int* flags;              // per-token range flags (range_fail) or null
+  RowCopy res;             // copied by the non-chain warps of all CTAs (n4 = 0: none)
   int ep_on; EpView ep;    // expert parallel: dispatch this rank's tokens, route all ranks' tokens
 };
 
@@ -188,6 +189,14 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
         }
       }
     }
+  }
+  if (tid >= kChainThreads && a.res.n4 > 0) {
+    // spare warps: the caller's extra copy, spread over every CTA (all its
+    // loads are independent, so its latency overlaps the chains)
+    const int nq = kThreads - kChainThreads;
+    const long step = (long)nq * gridDim.x * gridDim.y;
+    for (long i = (long)(blockIdx.y * gridDim.x + blockIdx.x) * nq + (tid - kChainThreads); i < a.res.n4; i += step)
+      reinterpret_cast<float4*>(a.res.dst)[i] = __ldcv(reinterpret_cast<const float4*>(a.res.src) + i);
   }
   if (!ok && (tid & 31) == 0) atomicOr(a.err, kErrTimeout);
 
@@ -400,8 +409,9 @@ bool decode_route_supported(const LayerDev& L, int T, const float* x) {
 }
 
 void launch_decode_route(const LayerDev& L, const Workspace& ws, const float* x, int T, int nt,
-                         int* counter, int* err, cudaStream_t st, const EpView* ep) {
+                         int* counter, int* err, cudaStream_t st, const EpView* ep, const RowCopy* res) {
   rt::Args a{};
+  if (res) a.res = *res;
   a.x = x; a.W = L.router_w; a.b = L.router_b; a.T = T; a.E = L.E; a.D = L.D; a.K = L.topk;
   a.logits = ws.logits; a.idx = ws.topk_idx; a.p = ws.topk_p;
   a.route = ws.route; a.e_begin = L.e_begin; a.E_local = L.e_end - L.e_begin;

@@ -678,13 +678,15 @@ static void prof_drain() {
 // Router + top-k + routing lists + token activation truncation.
 // given: w.topk_idx / w.topk_p already hold the routing (MOE_FFN_GIVEN_TOPK):
 // no router logits or top-k, only the activations and the routing lists.
-static void route_tokens(const LayerDev& L, const float* xn, int T, int nt, cudaStream_t st,
-                         bool given = false) {
+// Routing of one call. res: an extra copy the decode routing kernel makes
+// on the side; returns whether it was made (the other routing paths skip it).
+static bool route_tokens(const LayerDev& L, const float* xn, int T, int nt, cudaStream_t st,
+                         bool given = false, const RowCopy* res = nullptr) {
   if (!given && decode_route_supported(L, T, xn)) {
     timed("route", st, [&] {
-      launch_decode_route(L, g.ws, xn, T, nt, g.ws.route_counter, g.d_err, st);
+      launch_decode_route(L, g.ws, xn, T, nt, g.ws.route_counter, g.d_err, st, nullptr, res);
     });
-    return;
+    return res != nullptr;
   }
   const Workspace& w = g.ws;
   timed("quantize_act", st, [&] {
@@ -707,6 +709,7 @@ static void route_tokens(const LayerDev& L, const float* xn, int T, int nt, cuda
       launch_route_build(w.topk_idx, T, L.topk, L.e_begin, L.e_end, w.route, L.e_end - L.e_begin,
                          L.dtype == MOE_DTYPE_Q4 ? w.hsum : nullptr, nt, nt > 0 ? w.slot_pos : nullptr, st);
   });
+  return false;
 }
 
 static int get_layer(int layer, const LayerDev** out) {
@@ -973,6 +976,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
   // combine also left the last warp through each row block with T*K dependent
   // loads at the end of the kernel: measured 90 us vs 39 + 6 us.)
   HostOut ho{};     // what the combine publishes to host memory (zero-copy calls below)
+  RowCopy zres{};   // zero-copy calls: the residual rows, host -> w.xo, by the routing kernel
   auto enqueue = [&](const float* xn, float* xo, cudaStream_t s) -> int {
     if (L.dtype == MOE_DTYPE_F32) {
       // fp32 experts: router chains + top-k softmax, the fp32 expert FFN, combine
@@ -989,7 +993,7 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
     } else if (use_tensor_cores(L, flags, T)) {
       const int fnt = fused_tile_n(L, T);                 // fused gate/up + down kernel, if used
       const int nt = fnt ? fnt : mma_tile_n(T, L.dtype);
-      route_tokens(L, xn, T, nt, s, given);
+      const float* xres = route_tokens(L, xn, T, nt, s, given, zres.n4 ? &zres : nullptr) ? zres.dst : xo;
       if (T > nt) timed("gather", s, [&] { launch_mma_gather(L, w, T, nt, s); });
       bool ok = true;
       if (fnt) {
@@ -1003,16 +1007,16 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
         launch_exact_fixup(L, xn, w.topk_idx, w.slot_pos, T, w.y, w.xbad, g.sm_count, s);
       });
       timed("combine", s, [&] {
-        launch_combine_sorted(w.y, w.slot_pos, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s, seq, ho);
+        launch_combine_sorted(w.y, w.slot_pos, w.topk_p, w.topk_idx, xres, xo, T, L.D, L.topk, s, seq, ho);
       });
     } else {
-      route_tokens(L, xn, T, 0, s, given);
+      const float* xres = route_tokens(L, xn, T, 0, s, given, zres.n4 ? &zres : nullptr) ? zres.dst : xo;
       timed("gateup", s, [&] { run_gateup(L, w, T, s); });
       timed("down", s, [&] { run_down(L, w, T, w.y, s); });
       timed("exact_fixup", s, [&] {
         launch_exact_fixup(L, xn, w.topk_idx, nullptr, T, w.y, w.xbad, g.sm_count, s);
       });
-      timed("combine", s, [&] { launch_combine(w.y, w.topk_p, w.topk_idx, xo, xo, T, L.D, L.topk, s, seq, ho); });
+      timed("combine", s, [&] { launch_combine(w.y, w.topk_p, w.topk_idx, xres, xo, T, L.D, L.topk, s, seq, ho); });
     }
     CU(cudaGetLastError());
     return MOE_OK;
@@ -1040,6 +1044,9 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
     if (zx && (zi || !topk_idx_out || given) && (zp || !topk_p_out || given)) {
       CU(cudaMemcpyAsync(w.xn, x_norm2, xb, cudaMemcpyHostToDevice, st));
       ho = HostOut{zi, zp, w.topk_idx, w.topk_p, (zi || zp) ? T * L.topk : 0, g.d_err, g.h_err_dev};
+      // the residual rows come over the host link once, while the routing
+      // chains run, and the combine reads them from HBM
+      if ((uintptr_t)zx % 16 == 0 && L.D % 4 == 0) zres = RowCopy{zx, w.xo, (long)T * L.D / 4};
       if ((rc = enqueue(w.xn, zx, st))) return rc;
       return consume_stream_error(st, true);
     }
