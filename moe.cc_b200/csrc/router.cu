@@ -206,8 +206,10 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
     __syncthreads();
     if (tid == 0) __threadfence_system();
   } else {
-    __threadfence();
+    // the barrier orders the CTA's logit and activation stores before
+    // thread 0's fence and arrival
     __syncthreads();
+    if (tid == 0) __threadfence();
   }
   if (tid == 0) s_last = atomicAdd(a.counter, 1) == (int)(gridDim.x * gridDim.y) - 1;
   __syncthreads();
@@ -228,28 +230,45 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
   // keyed as +0, so equal values tie exactly as in topk_desc's strict-'>'
   // insertion (lower index first). Lane r keeps round r's winner; the softmax
   // (:481-487) then runs across lanes, summing in order.
+  // Each lane first sorts its PERL (key, expert) pairs, larger key first and
+  // lower expert first on equal keys (a bitonic network on the 64-bit words
+  // key << 32 | ~expert), so a round only compares the lanes' heads and the
+  // winner shifts its list.
   constexpr int PERL = kMaxE / 32;
+  static_assert(PERL == 8, "bitonic network of 8");
   for (int t = warp; t < a.T; t += kThreads / 32) {
-    unsigned key[PERL];
+    unsigned long long c[PERL];
 #pragma unroll
     for (int i = 0; i < PERL; ++i) {
       const int e = lane * PERL + i;
       float v = e < a.E ? __ldcg(a.logits + (size_t)t * a.E + e) : -INFINITY;
       if (v == 0.0f) v = 0.0f;
       const unsigned u = __float_as_uint(v);
-      key[i] = !(v > -INFINITY) ? 0u : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+      const unsigned key = !(v > -INFINITY) ? 0u : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+      c[i] = ((unsigned long long)key << 32) | (unsigned)~e;
     }
+#pragma unroll
+    for (int k = 2; k <= PERL; k <<= 1)
+#pragma unroll
+      for (int j = k >> 1; j > 0; j >>= 1)
+#pragma unroll
+        for (int i = 0; i < PERL; ++i) {
+          const int l = i ^ j;
+          if (l > i) {
+            // descending where (i & k) == 0, ascending elsewhere: sorted descending at the end
+            const bool sw = ((i & k) == 0) ? (c[i] < c[l]) : (c[i] > c[l]);
+            const unsigned long long lo = sw ? c[l] : c[i], hi = sw ? c[i] : c[l];
+            c[i] = lo; c[l] = hi;
+          }
+        }
     float myv = -INFINITY;
     int myi = -1;
     for (int r = 0; r < a.K; ++r) {
-      unsigned hk = key[0]; int hl = 0;
-#pragma unroll
-      for (int i = 1; i < PERL; ++i)
-        if (key[i] > hk) { hk = key[i]; hl = i; }                // ascending index: first max kept
+      const unsigned hk = (unsigned)(c[0] >> 32);
       const unsigned M = __reduce_max_sync(0xffffffffu, hk);
       if (M == 0u) break;                                        // only NaN / -inf left: no expert
-      const int wl = __ffs(__ballot_sync(0xffffffffu, hk == M)) - 1;
-      const int I = __shfl_sync(0xffffffffu, lane * PERL + hl, wl);
+      const int wl = __ffs(__ballot_sync(0xffffffffu, hk == M)) - 1;   // lowest lane = lowest expert
+      const int I = (int)~__shfl_sync(0xffffffffu, (unsigned)c[0], wl);
       if (lane == r) {
         const unsigned u = (M & 0x80000000u) ? (M & 0x7fffffffu) : ~M;
         myv = __uint_as_float(u);
@@ -257,8 +276,8 @@ __global__ void __launch_bounds__(kThreads) decode_route_kernel(const Args a) {
       }
       if (lane == wl) {
 #pragma unroll
-        for (int i = 0; i < PERL; ++i)
-          if (i == hl) key[i] = 0u;
+        for (int i = 0; i < PERL - 1; ++i) c[i] = c[i + 1];
+        c[PERL - 1] = 0ull;
       }
     }
     float mx = __shfl_sync(0xffffffffu, myv, 0);
