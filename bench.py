@@ -333,10 +333,16 @@ def e2e_host(torch, mc, T, steps, warmup, nl):
     idx = torch.empty(T, TOPK, dtype=torch.int32).pin_memory()
     p = torch.empty(T, TOPK, dtype=torch.float32).pin_memory()
     lib = mc.lib()
+    # the buffers' addresses resolved once, as a C caller holds them; every
+    # step still passes host buffers through the C-ABI and copies in and out
+    xs_p = [x.data_ptr() for x in xs]
+    xo_p = [x.data_ptr() for x in xo]
+    idx_p, p_p, ffn = idx.data_ptr(), p.data_ptr(), lib.moe_ffn
 
     def call(i):
-        mc.check(lib.moe_ffn(i % nl, xs[i % 8].data_ptr(), xo[i % 8].data_ptr(), T, idx.data_ptr(),
-                             p.data_ptr(), mc.HOST_PTRS, None))
+        rc = ffn(i % nl, xs_p[i % 8], xo_p[i % 8], T, idx_p, p_p, mc.HOST_PTRS, None)
+        if rc:
+            mc.check(rc)
     for i in range(warmup):
         call(i)
     torch.cuda.synchronize()
