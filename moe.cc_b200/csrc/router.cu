@@ -1,13 +1,15 @@
 // router.cu — the decode-regime routing prologue in one launch.
 //
-// grid = (E/8 expert blocks) x (ceil(T/16) token blocks), 128 threads. Each
-// CTA bulk-copies its 8 router rows and 16 token rows into shared memory once
-// (1-D bulk async copies, one mbarrier), then every thread runs one exact
-// sequential fp32 chain logits[t][e] = Σ_k x[t][k]·W[e][k] (+b[e]) in k order
-// (test_model_trace.c:213-227, :465-468) straight from shared memory, and the
-// CTA truncates its slice of the token activations for the expert kernels
-// (kernels.c:66 / :113). The last CTA to finish (arrival counter) then does,
-// for all tokens: top-k (topk_desc, :275-288, as K warp arg-max rounds), the
+// grid = (E/8 expert blocks) x (ceil(T/8) token blocks), 512 threads. Each
+// CTA bulk-copies its 8 router rows and 8 token rows into shared memory once
+// (1-D bulk async copies in four column chunks, one mbarrier each), then each
+// of 64 threads runs one exact sequential fp32 chain
+// logits[t][e] = Σ_k x[t][k]·W[e][k] (+b[e]) in k order
+// (test_model_trace.c:213-227, :465-468) straight from shared memory, while
+// the other warps truncate the CTA's slice of the token activations for the
+// expert kernels (kernels.c:66 / :113). The last CTA to finish (arrival
+// counter) then does, for all tokens: top-k (topk_desc, :275-288, as K warp
+// arg-max rounds over per-lane sorted candidates), the
 // top-k softmax (:481-487), and the routing lists, tensor-core tile table and
 // slot -> expert-sorted-row map. That phase keeps its tables in shared memory
 // (per-expert counts by shared atomics, one warp-shuffle scan over experts)
