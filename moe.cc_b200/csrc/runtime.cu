@@ -1033,10 +1033,11 @@ int moe_ffn(int layer, const float* x_norm2, float* x_inout, int T, int* topk_id
                               sizeof(int) * (size_t)T * L.topk, enqueue);
   const float* xn = x_norm2;
   float* xo = x_inout;
-  // Host-pointer call on page-locked buffers: the combine reads and updates
-  // x_inout in place through its mapped address and copies the top-k lists
-  // and the error word out, so the call makes one copy (x_norm2 in) and one
-  // stream synchronisation. Pageable buffers take the copies below.
+  // Host-pointer call on page-locked buffers: x_inout is read through its
+  // mapped address (by the decode routing kernel's spare warps into HBM, else
+  // by the combine itself), the combine writes the result there and copies the
+  // top-k lists and the error word out, so the call makes one copy (x_norm2
+  // in) and one stream synchronisation. Pageable buffers take the copies below.
   if (host) {
     float* zx = (float*)mapped_host_range(x_inout, xb);
     int* zi = topk_idx_out && !given ? (int*)mapped_host_range(topk_idx_out, kb) : nullptr;
